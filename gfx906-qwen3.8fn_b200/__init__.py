@@ -1,0 +1,342 @@
+"""Host-side Python mirror of libqwen_moe_b200.so (B200 routed-MoE expert FFN).
+
+The product is the C ABI in include/qwen_moe_b200.h, implemented by CUDA
+kernels for sm_100a in csrc/.  This module binds it with ctypes and keeps the
+reference's host API names and error behaviour:
+
+* `RouteGroups`  -- src/routes.hpp:28-65 (ValueError where the reference throws
+  std::invalid_argument);
+* `GpuExpert`    -- src/gpu_expert.hpp:7-21 (check_quantization / linear / run);
+* `MoeLayer`, `MoeWeights` -- the routed-MoE FFN of src/session.hip:1412-1556
+  as one device call (`forward`), plus parity taps (`route`, `quantize_q8_1`,
+  `q4_linear`).
+
+Device memory, streams and process groups come from PyTorch; tensors are
+passed by pointer.  There is no CPU fallback: importing this module without
+the built library raises, and every call goes to the GPU.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqwen_moe_b200.so")
+
+MOE_OK, MOE_INVALID_ARGUMENT, MOE_NOT_SUPPORTED, MOE_CUDA_ERROR = 0, 1, 2, 3
+MOE_NUMERIC_ERROR, MOE_NCCL_ERROR, MOE_TIMEOUT, MOE_OUT_OF_MEMORY = 4, 5, 6, 7
+MOE_OUT_ACCUMULATE, MOE_OUT_OVERWRITE = 0, 1
+HIDDEN, INTER, EXPERTS, TOP_K = 2048, 512, 512, 10
+
+EXPORTED = [
+    "moe_status_string", "moe_abi_version", "moe_last_error_message",
+    "moe_weights_create", "moe_weights_destroy", "moe_weights_upload_expert",
+    "moe_weights_upload_shared_gate", "moe_weights_synthesize", "moe_weights_download_expert",
+    "moe_weights_expert_bytes", "moe_layer_create", "moe_layer_destroy", "moe_forward", "moe_forward_profiled",
+    "moe_route",
+    "moe_layer_read_flags", "moe_quantize_q8_1", "moe_q4_linear", "moe_expert_create",
+    "moe_expert_destroy", "moe_expert_check_quantization", "moe_expert_linear", "moe_expert_run",
+    "moe_route_groups_create", "moe_route_groups_destroy", "moe_route_groups_prepare",
+    "moe_route_groups_assignments", "moe_route_groups_counts", "moe_route_groups_message",
+]
+
+
+class MoeError(RuntimeError):
+    """A CUDA/NCCL failure reported by the library (reference: std::runtime_error)."""
+
+    def __init__(self, status, message):
+        super().__init__(f"{message} [{status}]")
+        self.status = status
+
+
+class desc_t(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int), ("inter", ctypes.c_int), ("experts", ctypes.c_int),
+                ("top_k", ctypes.c_int), ("has_shared", ctypes.c_int), ("device", ctypes.c_int),
+                ("max_tokens", ctypes.c_int)]
+
+
+_lib = None
+P, I, SZ, U64, U32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint32
+DESC_P = ctypes.POINTER(desc_t)
+
+
+def library(path=LIB_PATH):
+    """Load the CUDA library; raise if it has not been built (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with __graft_entry__.build() "
+                          "(python gfx906-qwen3.8fn_b200/build.py)")
+    L = ctypes.CDLL(path)
+    sig = {
+        "moe_status_string": (ctypes.c_char_p, [I]),
+        "moe_abi_version": (I, []),
+        "moe_last_error_message": (ctypes.c_char_p, []),
+        "moe_weights_create": (I, [DESC_P, ctypes.POINTER(P)]),
+        "moe_weights_destroy": (I, [P]),
+        "moe_weights_upload_expert": (I, [P, I, P, P, P, P]),
+        "moe_weights_upload_shared_gate": (I, [P, P, P]),
+        "moe_weights_synthesize": (I, [P, U64, U32, P]),
+        "moe_weights_download_expert": (I, [P, I, P, P, P, P]),
+        "moe_weights_expert_bytes": (SZ, [DESC_P]),
+        "moe_layer_create": (I, [DESC_P, ctypes.POINTER(P)]),
+        "moe_layer_destroy": (I, [P]),
+        "moe_forward": (I, [P, P, P, P, I, P, I, P]),
+        "moe_forward_profiled": (I, [P, P, P, P, I, P, I, P, ctypes.POINTER(P)]),
+        "moe_route": (I, [P, P, I, P, P, P, P, P, P, P]),
+        "moe_layer_read_flags": (I, [P, ctypes.POINTER(I), I, P]),
+        "moe_quantize_q8_1": (I, [P, I, I, P, P, P]),
+        "moe_q4_linear": (I, [P, I, I, P, I, P, P, P]),
+        "moe_expert_create": (I, [P, P, P, I, I, I, I, ctypes.POINTER(P)]),
+        "moe_expert_destroy": (I, [P]),
+        "moe_expert_check_quantization": (I, [P, P, SZ, P]),
+        "moe_expert_linear": (I, [P, I, I, P, I, P]),
+        "moe_expert_run": (I, [P, P, I, P, I, ctypes.POINTER(ctypes.c_double),
+                               ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
+        "moe_route_groups_create": (I, [I, I, ctypes.POINTER(P)]),
+        "moe_route_groups_destroy": (I, [P]),
+        "moe_route_groups_prepare": (I, [P, P, P, SZ, I]),
+        "moe_route_groups_assignments": (SZ, [P, P, SZ]),
+        "moe_route_groups_counts": (I, [P, P]),
+        "moe_route_groups_message": (ctypes.c_char_p, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(status, message_fn=None):
+    if status == MOE_OK:
+        return
+    L = library()
+    msg = (message_fn or L.moe_last_error_message)().decode(errors="replace")
+    if status == MOE_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    if status == MOE_NOT_SUPPORTED:
+        raise NotImplementedError(msg)
+    raise MoeError(status, f"{L.moe_status_string(status).decode()}: {msg}")
+
+
+def _ptr(t):
+    """Device/host address of a torch tensor or numpy array (None -> NULL)."""
+    if t is None:
+        return None
+    if hasattr(t, "data_ptr"):
+        return ctypes.c_void_p(t.data_ptr())
+    return ctypes.c_void_p(t.ctypes.data)
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def make_desc(hidden=HIDDEN, inter=INTER, experts=EXPERTS, top_k=TOP_K, has_shared=1, device=0, max_tokens=8):
+    return desc_t(hidden, inter, experts, top_k, has_shared, device, max_tokens)
+
+
+class MoeWeights:
+    """Device-resident Q4_0 experts of one layer (routed + shared)."""
+
+    def __init__(self, desc):
+        self.desc = desc
+        h = P()
+        check(library().moe_weights_create(ctypes.byref(desc), ctypes.byref(h)))
+        self.handle = h
+
+    def synthesize(self, seed, layer=0, stream=None):
+        check(library().moe_weights_synthesize(self.handle, seed, layer, _stream(stream)))
+
+    def upload_expert(self, expert, gate, up, down, stream=None):
+        check(library().moe_weights_upload_expert(self.handle, expert, _ptr(gate), _ptr(up), _ptr(down),
+                                                  _stream(stream)))
+
+    def upload_shared_gate(self, gate_vec, stream=None):
+        check(library().moe_weights_upload_shared_gate(self.handle, _ptr(gate_vec), _stream(stream)))
+
+    def download_expert(self, expert, stream=None):
+        import numpy as np
+        d = self.desc
+        n = d.hidden * d.inter // 32 * 18
+        g, u, w = (np.empty(n, np.uint8) for _ in range(3))
+        check(library().moe_weights_download_expert(self.handle, expert, _ptr(g), _ptr(u), _ptr(w),
+                                                    _stream(stream)))
+        return g, u, w
+
+    def close(self):
+        if getattr(self, "handle", None):
+            library().moe_weights_destroy(self.handle)
+            self.handle = None
+
+    __del__ = close
+
+
+class MoeLayer:
+    """Workspace of one routed-MoE FFN layer; `forward` is the whole hot path."""
+
+    def __init__(self, desc):
+        self.desc = desc
+        h = P()
+        check(library().moe_layer_create(ctypes.byref(desc), ctypes.byref(h)))
+        self.handle = h
+
+    def forward(self, weights, x, logits, out, accumulate=True, stream=None):
+        """out (+)= MoE(x).  x, out: fp32 cuda [T][H]; logits fp32 cuda [T][E]."""
+        T = x.shape[0]
+        flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
+        check(library().moe_forward(self.handle, weights.handle, _ptr(x), _ptr(logits), T, _ptr(out), flag,
+                                    _stream(stream)))
+
+    def forward_profiled(self, weights, x, logits, out, events, accumulate=True, stream=None):
+        """forward() recording torch.cuda.Event objects [before gate/up, before down, after down]."""
+        T = x.shape[0]
+        flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
+        ev = (P * 3)(*[e.cuda_event for e in events])
+        check(library().moe_forward_profiled(self.handle, weights.handle, _ptr(x), _ptr(logits), T, _ptr(out),
+                                             flag, _stream(stream), ev))
+
+    def route(self, logits, stream=None):
+        """GPU routing tap: dict of cuda tensors probs/ids/weights/offsets/token/rank."""
+        import torch
+        T = logits.shape[0]
+        dev = logits.device
+        r = dict(probs=torch.empty(T, EXPERTS, device=dev), ids=torch.empty(T, TOP_K, dtype=torch.int32, device=dev),
+                 weights=torch.empty(T, TOP_K, device=dev),
+                 offsets=torch.empty(EXPERTS + 1, dtype=torch.int32, device=dev),
+                 token=torch.empty(T * TOP_K, dtype=torch.int32, device=dev),
+                 rank=torch.empty(T * TOP_K, dtype=torch.int32, device=dev))
+        check(library().moe_route(self.handle, _ptr(logits), T, _ptr(r["probs"]), _ptr(r["ids"]),
+                                  _ptr(r["weights"]), _ptr(r["offsets"]), _ptr(r["token"]), _ptr(r["rank"]),
+                                  _stream(stream)))
+        return r
+
+    def read_flags(self, clear=True, stream=None):
+        f = ctypes.c_int(0)
+        check(library().moe_layer_read_flags(self.handle, ctypes.byref(f), int(clear), _stream(stream)))
+        return f.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            library().moe_layer_destroy(self.handle)
+            self.handle = None
+
+    __del__ = close
+
+
+def quantize_q8_1(x, error=None, stream=None):
+    """fp32 cuda [columns][width] -> uint8 cuda [columns][width/32*36] canonical Q8_1."""
+    import torch
+    cols, width = x.shape
+    q = torch.empty(cols, width // 32 * 36, dtype=torch.uint8, device=x.device)
+    own = error is None
+    if own:
+        error = torch.zeros(1, dtype=torch.int32, device=x.device)
+    check(library().moe_quantize_q8_1(_ptr(x), width, cols, _ptr(q), _ptr(error), _stream(stream)))
+    return q, error
+
+
+def q4_linear(w_q4_0, rows, k, xq, columns, with_dots=False, stream=None):
+    """Canonical Q4_0 (cuda uint8) x canonical Q8_1 (cuda uint8) -> fp32 [columns][rows] (+ int32 dots)."""
+    import torch
+    out = torch.empty(columns, rows, device=xq.device)
+    dots = torch.empty(columns, rows, k // 32, dtype=torch.int32, device=xq.device) if with_dots else None
+    check(library().moe_q4_linear(_ptr(w_q4_0), rows, k, _ptr(xq), columns, _ptr(out), _ptr(dots), _stream(stream)))
+    return (out, dots) if with_dots else out
+
+
+class RouteGroups:
+    """Host route grouping with the reference's contract (src/routes.hpp:28-65)."""
+
+    CHUNK1024, LAYERWISE16384 = 0, 1
+
+    def __init__(self, token_capacity, bound=CHUNK1024):
+        h = P()
+        L = library()
+        check(L.moe_route_groups_create(token_capacity, bound, ctypes.byref(h)), L.moe_route_groups_message)
+        self.handle = h
+        self.capacity = token_capacity
+
+    def prepare(self, ids, weights, tokens):
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.int32).ravel()
+        weights = np.ascontiguousarray(weights, dtype=np.float32).ravel()
+        if ids.size != weights.size:
+            raise ValueError("routes: expected exactly tokens*10 IDs and weights")
+        L = library()
+        check(L.moe_route_groups_prepare(self.handle, _ptr(ids), _ptr(weights), ids.size, tokens),
+              L.moe_route_groups_message)
+
+    def assignments(self):
+        import numpy as np
+        L = library()
+        n = L.moe_route_groups_assignments(self.handle, None, 0)
+        out = np.empty(n, dtype=[("token", "<i4"), ("rank", "<i4"), ("expert", "<i4"), ("weight", "<f4")])
+        L.moe_route_groups_assignments(self.handle, _ptr(out), n)
+        return out
+
+    def counts(self):
+        import numpy as np
+        c = np.empty(EXPERTS, np.int32)
+        library().moe_route_groups_counts(self.handle, _ptr(c))
+        return c
+
+    def group(self, expert):
+        if not 0 <= expert < EXPERTS:
+            raise ValueError("routes: group expert must be 0..511")
+        c = self.counts()
+        a = self.assignments()
+        start = int(c[:expert].sum())
+        return a[start:start + int(c[expert])]
+
+    def close(self):
+        if getattr(self, "handle", None):
+            library().moe_route_groups_destroy(self.handle)
+            self.handle = None
+
+    __del__ = close
+
+
+class GpuExpert:
+    """Single resident expert (src/gpu_expert.hpp:7-21) on the sm_100a kernels."""
+
+    def __init__(self, gate, up, down, device=0, max_columns=8, hidden=HIDDEN, inter=INTER):
+        h = P()
+        check(library().moe_expert_create(_ptr(gate), _ptr(up), _ptr(down), hidden, inter, device, max_columns,
+                                          ctypes.byref(h)))
+        self.handle, self.hidden, self.inter = h, hidden, inter
+
+    def check_quantization(self, x, expected_q8):
+        import numpy as np
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        e = np.ascontiguousarray(expected_q8)
+        st = library().moe_expert_check_quantization(self.handle, _ptr(x), x.size, _ptr(e))
+        if st == MOE_NUMERIC_ERROR:
+            raise RuntimeError("CPU/GPU Q8_1 ABI mismatch")
+        check(st)
+
+    def linear(self, down, up, q8, columns):
+        import numpy as np
+        rows = self.hidden if down else self.inter
+        out = np.empty((columns, rows), np.float32)
+        q8 = np.ascontiguousarray(q8)
+        check(library().moe_expert_linear(self.handle, int(down), int(up), _ptr(q8), columns, _ptr(out)))
+        return out
+
+    def run(self, x, columns, repeats=1):
+        import numpy as np
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty((columns, self.hidden), np.float32)
+        t = [ctypes.c_double() for _ in range(3)]
+        check(library().moe_expert_run(self.handle, _ptr(x), columns, _ptr(out), repeats, *map(ctypes.byref, t)))
+        return out, dict(upload_ms=t[0].value, resident_ms=t[1].value, completed_wall_ms=t[2].value)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            library().moe_expert_destroy(self.handle)
+            self.handle = None
+
+    __del__ = close

@@ -1,0 +1,119 @@
+// common.cuh -- shared device helpers for the sm_100a routed-MoE kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qwen_moe_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "this library is written for sm_100a (Blackwell) only"
+#endif
+
+namespace qmoe {
+
+constexpr int kTopK = 10;
+constexpr int kRouterExperts = 512;
+constexpr int kFlagInvalid = MOE_FLAG_INVALID;
+constexpr int kFlagArithmetic = MOE_FLAG_ARITHMETIC;
+
+// Planar Q8 activations used between kernels: int8 codes [rows][K] and per
+// block (d, s) decoded to fp32 [rows][K/32] -- the same information as the
+// canonical 36-byte Q8_1 blocks, rearranged so codes load as aligned 16-byte
+// vectors.
+struct Q8Planar {
+    int8_t *codes;
+    float2 *scales;
+};
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// Unsigned-byte x signed-byte 4-way dot product accumulate (dp4a.u32.s32).
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Uncentred u4 x s8 dot of one 32-element block: 16 code bytes as a uint4
+// (byte j: low nibble element j, high nibble element j+16) against 32 int8
+// activation codes as two int4 (elements 0..15, 16..31).  Exact in int32.
+__device__ __forceinline__ int block_dot(const uint4 w, const int4 xlo, const int4 xhi) {
+    int acc = 0;
+    acc = dp4a_us(w.x & 0x0f0f0f0fu, xlo.x, acc);
+    acc = dp4a_us(w.y & 0x0f0f0f0fu, xlo.y, acc);
+    acc = dp4a_us(w.z & 0x0f0f0f0fu, xlo.z, acc);
+    acc = dp4a_us(w.w & 0x0f0f0f0fu, xlo.w, acc);
+    acc = dp4a_us((w.x >> 4) & 0x0f0f0f0fu, xhi.x, acc);
+    acc = dp4a_us((w.y >> 4) & 0x0f0f0f0fu, xhi.y, acc);
+    acc = dp4a_us((w.z >> 4) & 0x0f0f0f0fu, xhi.z, acc);
+    acc = dp4a_us((w.w >> 4) & 0x0f0f0f0fu, xhi.w, acc);
+    return acc;
+}
+
+// One block's contribution with the reference's Q4_0 correction
+// d4*(dot*d8 - 8*s8) (src/quant.cpp:88-102), as two FMAs.
+__device__ __forceinline__ float block_term(int dot, float d4, float d8, float s8x8, float acc) {
+    return fmaf(d4, fmaf(static_cast<float>(dot), d8, -s8x8), acc);
+}
+
+__device__ __forceinline__ void report(int flags, int *error) {
+    if (flags) atomicOr(error, flags);
+}
+
+__device__ __forceinline__ float operand(float x, int &flags) {
+    if (!isfinite(x)) { flags |= kFlagInvalid; return 0.0f; }
+    return x;
+}
+__device__ __forceinline__ float arithmetic(float x, int &flags) {
+    if (!isfinite(x)) { flags |= kFlagArithmetic; return 0.0f; }
+    return x;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+// Quantise one 32-value block held one value per lane (lane = element).
+// Byte-identical to the reference's quantize_q8 (src/quant.cpp:275-325) for
+// valid blocks; invalid blocks yield zero and sticky flags, like
+// src/hip/linear.hip:99-150.  The raw sum uses the XOR butterfly 1,2,4,8,16.
+struct Q8Lane {
+    int8_t code;
+    uint16_t d, s;   // meaningful on every lane
+    int flags;       // block flags, identical on every lane
+};
+
+__device__ __forceinline__ Q8Lane quantize_lane(float x) {
+    int bad = !isfinite(x);
+    if (bad) x = 0.0f;
+    float amax = fabsf(x);
+    float sum = x;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, m);
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, m));
+    }
+    const float d = __fdiv_rn(amax, 127.0f);
+    const uint16_t hd = f2h(d), hs = f2h(sum);
+    const bool representable = isfinite(sum) && (hs & 0x7c00u) != 0x7c00u &&
+                               (hd & 0x7c00u) != 0x7c00u && (amax == 0.0f || d > 0.0f);
+    const float code = (!bad && representable && amax != 0.0f) ? roundf(__fdiv_rn(x, d)) : 0.0f;
+    int bad_code = !isfinite(code) || code < -127.0f || code > 127.0f;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) bad_code |= __shfl_xor_sync(0xffffffffu, bad_code, m);
+    const bool valid = !bad && representable && !bad_code;
+    Q8Lane q;
+    q.code = valid ? static_cast<int8_t>(code) : int8_t(0);
+    q.d = (valid && amax != 0.0f) ? hd : uint16_t(0);
+    q.s = (valid && amax != 0.0f) ? hs : uint16_t(0);
+    q.flags = (bad ? kFlagInvalid : 0) | ((representable && !bad_code) ? 0 : kFlagArithmetic);
+    return q;
+}
+
+}  // namespace qmoe

@@ -1,0 +1,362 @@
+// expert_kernels.cuh -- Q8_1 quantisation and the weight-streaming grouped
+// expert kernels (decode-size groups), plus the synthetic generator and
+// layout repacks.
+//
+// Weight layout (one expert, planar; same byte count as canonical Q4_0):
+//   gate codes [I][H/32][16] | up codes [I][H/32][16] | down codes [H][I/32][16]
+//   | gate scales [I][H/32] half | up scales | down scales [H][I/32] half
+// Block (r, b) of a matrix is canonical block r*(K/32)+b: its 16 code bytes
+// and its half scale, split so code rows load as aligned 16-byte vectors
+// (the reference's optional planar Q4_0 layout, src/hip/expert.hip:147-159).
+#pragma once
+#include "common.cuh"
+
+namespace qmoe {
+
+struct ExpertLayout {
+    size_t gate_codes, up_codes, down_codes, gate_scales, up_scales, down_scales, bytes;
+    int hidden, inter;
+};
+
+inline ExpertLayout make_layout(int H, int I) {
+    ExpertLayout L;
+    const size_t codes = static_cast<size_t>(H) * I / 2, scales = static_cast<size_t>(H) * I / 16;
+    L.gate_codes = 0;
+    L.up_codes = codes;
+    L.down_codes = 2 * codes;
+    L.gate_scales = 3 * codes;
+    L.up_scales = 3 * codes + scales;
+    L.down_scales = 3 * codes + 2 * scales;
+    L.bytes = 3 * codes + 3 * scales;
+    L.hidden = H;
+    L.inter = I;
+    return L;
+}
+
+// ---------------------------------------------------------------------------
+// fp32 [rows][K] -> Q8_1.  One warp per 32-value block, lane = element.
+// Writes the planar form (codes/scales) and/or canonical 36-byte blocks.
+__global__ void __launch_bounds__(256)
+quantize_kernel(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error) {
+    const size_t warp_global = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const size_t stride = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+    for (size_t b = warp_global; b < blocks; b += stride) {
+        const Q8Lane q = quantize_lane(x[b * 32 + lane]);
+        if (out.codes) {
+            out.codes[b * 32 + lane] = q.code;
+            if (lane == 0) out.scales[b] = make_float2(h2f(q.d), h2f(q.s));
+        }
+        if (canonical) {
+            uint8_t *blk = canonical + b * 36;
+            blk[4 + lane] = static_cast<uint8_t>(q.code);
+            if (lane == 0) {
+                blk[0] = q.d & 0xff; blk[1] = q.d >> 8;
+                blk[2] = q.s & 0xff; blk[3] = q.s >> 8;
+            }
+        }
+        if (lane == 0) report(q.flags, error);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Seeded synthetic Q4_0 weights, bit-identical to the oracle's generator.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ uint64_t synth_base(uint64_t seed, uint32_t layer, uint32_t expert,
+                                               uint32_t matrix) {
+    const uint64_t stream = (static_cast<uint64_t>(layer) << 32) |
+                            (static_cast<uint64_t>(expert) << 8) | matrix;
+    return mix64(seed ^ mix64(stream + 0x9e3779b97f4a7c15ull));
+}
+
+// Grid-stride over (expert, matrix, block); writes the planar layout.
+__global__ void __launch_bounds__(256)
+synth_kernel(uint8_t *base, ExpertLayout L, int experts_total, uint64_t seed, uint32_t layer) {
+    const size_t gate_blocks = static_cast<size_t>(L.inter) * (L.hidden / 32);
+    const size_t per_expert = 3 * gate_blocks;  // gate, up, down have equal block counts
+    const size_t total = per_expert * experts_total;
+    for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+         g += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint32_t e = static_cast<uint32_t>(g / per_expert);
+        const size_t rem = g % per_expert;
+        const uint32_t m = static_cast<uint32_t>(rem / gate_blocks);
+        const size_t i = rem % gate_blocks;
+        const uint64_t b = synth_base(seed, layer, e, m);
+        const uint64_t c0 = mix64(b + (i << 6) + 0), c1 = mix64(b + (i << 6) + 1);
+        uint32_t mx = 0;
+#pragma unroll 4
+        for (int j = 2; j < 34; ++j) {
+            const uint64_t r = mix64(b + (i << 6) + static_cast<uint64_t>(j));
+            const uint32_t s = static_cast<uint32_t>(r & 0xffffu) + static_cast<uint32_t>((r >> 16) & 0xffffu) +
+                               static_cast<uint32_t>((r >> 32) & 0xffffu) + static_cast<uint32_t>(r >> 48);
+            const uint32_t dev = s >= 131070u ? s - 131070u : 131070u - s;
+            mx = dev > mx ? dev : mx;
+        }
+        const uint16_t d = f2h(__fmul_rn(static_cast<float>(mx), 6.6073582e-08f));
+        uint8_t *ex = base + static_cast<size_t>(e) * L.bytes;
+        const size_t code_off = m == 0 ? L.gate_codes : m == 1 ? L.up_codes : L.down_codes;
+        const size_t scale_off = m == 0 ? L.gate_scales : m == 1 ? L.up_scales : L.down_scales;
+        reinterpret_cast<uint4 *>(ex + code_off)[i] =
+            make_uint4(static_cast<uint32_t>(c0), static_cast<uint32_t>(c0 >> 32),
+                       static_cast<uint32_t>(c1), static_cast<uint32_t>(c1 >> 32));
+        reinterpret_cast<uint16_t *>(ex + scale_off)[i] = d;
+    }
+}
+
+// canonical 18-byte blocks <-> planar (codes, scales).  dir 0: canonical ->
+// planar, dir 1: planar -> canonical.
+__global__ void __launch_bounds__(256)
+repack_kernel(uint8_t *canonical, uint8_t *codes, uint16_t *scales, size_t blocks, int dir) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < blocks;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        uint8_t *c = canonical + i * 18;
+        if (dir == 0) {
+            scales[i] = static_cast<uint16_t>(c[0] | (c[1] << 8));
+            for (int j = 0; j < 16; ++j) codes[i * 16 + j] = c[2 + j];
+        } else {
+            c[0] = scales[i] & 0xff;
+            c[1] = scales[i] >> 8;
+            for (int j = 0; j < 16; ++j) c[2 + j] = codes[i * 16 + j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Shared parameters of the grouped expert kernels.
+struct GroupParams {
+    const uint8_t *weights;     // expert 0 region; expert e at weights + e * layout.bytes
+    ExpertLayout layout;
+    Q8Planar x;                 // quantised tokens [T][H]
+    Q8Planar mid;               // middle per pair [P][I]
+    const int4 *tiles;          // {expert, first pair, count, 0}
+    const int *num_tiles;
+    const int32_t *pair_token;
+    const float *pair_weight;
+    float *out;                 // [T][H]
+    int *error;
+};
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvTile = 8;     // pairs per tile
+
+// Gate/up for one (tile, 32-row slab): warp w owns gate rows and up rows
+// slab*32 + 4w .. +3; lane l owns blocks l, l+32, ...  Results feed SiLU*up
+// and the slab's Q8_1 middle block (32 consecutive channels = one block),
+// the fused silu_up_q8_1 of the reference (src/hip/linear.hip:99-150,509-525).
+template <int NT>
+__global__ void __launch_bounds__(kGemvThreads)
+gate_up_kernel(GroupParams p) {
+    const int H = p.layout.hidden, I = p.layout.inter;
+    const int nb = H / 32, slabs = I / 32;
+    extern __shared__ __align__(16) uint8_t smem[];
+    int4 *sx = reinterpret_cast<int4 *>(smem);                          // [NT][H/16]
+    float2 *ss = reinterpret_cast<float2 *>(smem + NT * H);             // [NT][nb]
+    float *smid = reinterpret_cast<float *>(smem + NT * H + NT * nb * 8);  // [NT][32]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int total = *p.num_tiles * slabs;
+    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+        const int tile = item / slabs, slab = item % slabs;
+        const int4 td = p.tiles[tile];
+        const int e = td.x, p0 = td.y, n = td.z;
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < n * (H / 16); idx += kGemvThreads) {
+            const int j = idx / (H / 16), v = idx % (H / 16);
+            const int tok = p.pair_token[p0 + j];
+            sx[j * (H / 16) + v] = reinterpret_cast<const int4 *>(p.x.codes + static_cast<size_t>(tok) * H)[v];
+        }
+        for (int idx = threadIdx.x; idx < n * nb; idx += kGemvThreads) {
+            const int j = idx / nb, b = idx % nb;
+            const int tok = p.pair_token[p0 + j];
+            ss[j * nb + b] = p.x.scales[static_cast<size_t>(tok) * nb + b];
+        }
+        __syncthreads();
+        const uint8_t *ex = p.weights + static_cast<size_t>(e) * p.layout.bytes;
+        const uint4 *gcodes = reinterpret_cast<const uint4 *>(ex + p.layout.gate_codes);
+        const uint4 *ucodes = reinterpret_cast<const uint4 *>(ex + p.layout.up_codes);
+        const uint16_t *gsc = reinterpret_cast<const uint16_t *>(ex + p.layout.gate_scales);
+        const uint16_t *usc = reinterpret_cast<const uint16_t *>(ex + p.layout.up_scales);
+        const int row0 = slab * 32 + warp * 4;
+        float acc[8][NT];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int j = 0; j < NT; ++j) acc[r][j] = 0.0f;
+        for (int b = lane; b < nb; b += 32) {
+            uint4 wc[8];
+            float d4[8];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const size_t blk = static_cast<size_t>(row0 + r) * nb + b;
+                wc[r] = __ldg(gcodes + blk);
+                wc[4 + r] = __ldg(ucodes + blk);
+                d4[r] = h2f(__ldg(gsc + blk));
+                d4[4 + r] = h2f(__ldg(usc + blk));
+            }
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                if (j < n) {
+                    const int4 xlo = sx[j * (H / 16) + 2 * b], xhi = sx[j * (H / 16) + 2 * b + 1];
+                    const float2 sc = ss[j * nb + b];
+                    const float s8x8 = 8.0f * sc.y;
+#pragma unroll
+                    for (int r = 0; r < 8; ++r)
+                        acc[r][j] = block_term(block_dot(wc[r], xlo, xhi), d4[r], sc.x, s8x8, acc[r][j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int j = 0; j < NT; ++j) acc[r][j] = warp_sum(acc[r][j]);
+        // SiLU(gate) * up with the reference's sanitisation (session_ops.hip:250-262).
+        if (lane < 4) {
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                if (j < n) {
+                    float g = acc[0][j], u = acc[4][j];
+#pragma unroll
+                    for (int r = 1; r < 4; ++r)
+                        if (lane == r) { g = acc[r][j]; u = acc[4 + r][j]; }
+                    int flags = 0;
+                    g = operand(g, flags);
+                    u = operand(u, flags);
+                    const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), flags);
+                    const float v = arithmetic(__fmul_rn(act, u), flags);
+                    smid[j * 32 + warp * 4 + lane] = flags ? 0.0f : v;
+                    report(flags, p.error);
+                }
+            }
+        }
+        __syncthreads();
+        for (int j = warp; j < n; j += kGemvThreads / 32) {
+            const Q8Lane q = quantize_lane(smid[j * 32 + lane]);
+            const size_t pair = static_cast<size_t>(p0 + j);
+            p.mid.codes[pair * I + slab * 32 + lane] = q.code;
+            if (lane == 0) {
+                p.mid.scales[pair * slabs + slab] = make_float2(h2f(q.d), h2f(q.s));
+                report(q.flags, p.error);
+            }
+        }
+    }
+}
+
+// Down projection for one (tile, 64-row slab) with the router-weighted
+// scatter-add into out: thread t owns row slab*64 + t/4 and blocks t%4,
+// t%4+4, ...; the four partial sums meet in two shuffles, then
+// out[token][row] += weight * y (red.global.add).  Replaces the reference's
+// scatter + rank fold (src/hip/session_ops.hip:292-324,358-373).
+template <int NT>
+__global__ void __launch_bounds__(kGemvThreads)
+down_kernel(GroupParams p) {
+    const int H = p.layout.hidden, I = p.layout.inter;
+    const int nbd = I / 32, dslabs = H / 64;
+    extern __shared__ __align__(16) uint8_t smem[];
+    int4 *sm = reinterpret_cast<int4 *>(smem);                           // [NT][I/16]
+    float2 *ss = reinterpret_cast<float2 *>(smem + NT * I);              // [NT][nbd]
+    int *stok = reinterpret_cast<int *>(smem + NT * I + NT * nbd * 8);   // [NT]
+    float *swt = reinterpret_cast<float *>(stok + NT);                   // [NT]
+    const int q = threadIdx.x & 3;
+    const int total = *p.num_tiles * dslabs;
+    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+        const int tile = item / dslabs, ds = item % dslabs;
+        const int4 td = p.tiles[tile];
+        const int e = td.x, p0 = td.y, n = td.z;
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < n * (I / 16); idx += kGemvThreads) {
+            const int j = idx / (I / 16), v = idx % (I / 16);
+            sm[j * (I / 16) + v] = reinterpret_cast<const int4 *>(p.mid.codes + static_cast<size_t>(p0 + j) * I)[v];
+        }
+        for (int idx = threadIdx.x; idx < n * nbd; idx += kGemvThreads) {
+            const int j = idx / nbd, b = idx % nbd;
+            ss[j * nbd + b] = p.mid.scales[static_cast<size_t>(p0 + j) * nbd + b];
+        }
+        if (threadIdx.x < n) {
+            stok[threadIdx.x] = p.pair_token[p0 + threadIdx.x];
+            swt[threadIdx.x] = p.pair_weight[p0 + threadIdx.x];
+        }
+        __syncthreads();
+        const uint8_t *ex = p.weights + static_cast<size_t>(e) * p.layout.bytes;
+        const uint4 *dcodes = reinterpret_cast<const uint4 *>(ex + p.layout.down_codes);
+        const uint16_t *dsc = reinterpret_cast<const uint16_t *>(ex + p.layout.down_scales);
+        const int row = ds * 64 + (threadIdx.x >> 2);
+        float acc[NT];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[j] = 0.0f;
+        for (int b = q; b < nbd; b += 4) {
+            const size_t blk = static_cast<size_t>(row) * nbd + b;
+            const uint4 wc = __ldg(dcodes + blk);
+            const float d4 = h2f(__ldg(dsc + blk));
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                if (j < n) {
+                    const int4 xlo = sm[j * (I / 16) + 2 * b], xhi = sm[j * (I / 16) + 2 * b + 1];
+                    const float2 sc = ss[j * nbd + b];
+                    acc[j] = block_term(block_dot(wc, xlo, xhi), d4, sc.x, 8.0f * sc.y, acc[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 1);
+            acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 2);
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            if (j < n && (j & 3) == q) {
+                int flags = 0;
+                const float y = arithmetic(acc[j], flags);
+                const float c = arithmetic(__fmul_rn(swt[j], y), flags);
+                atomicAdd(p.out + static_cast<size_t>(stok[j]) * H + row, c);
+                report(flags, p.error);
+            }
+        }
+    }
+}
+
+// Parity tap / fixture linear: canonical or planar Q4_0 weights [rows][K/32]
+// against canonical Q8_1 [columns][K/32]; thread per (row, column) walking
+// the blocks serially.  Writes fp32 results and optionally every per-block
+// int32 dot computed by block_dot() -- the routine the production kernels use.
+__global__ void __launch_bounds__(256)
+q4_linear_kernel(const uint8_t *canonical_w, const uint8_t *codes, const uint16_t *scales, int rows,
+                 int nb, const uint8_t *xq, int columns, float *out, int32_t *dots) {
+    const size_t total = static_cast<size_t>(rows) * columns;
+    for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+         g += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(g / rows), r = static_cast<int>(g % rows);
+        float acc = 0.0f;
+        for (int b = 0; b < nb; ++b) {
+            const size_t blk = static_cast<size_t>(r) * nb + b;
+            uint4 wc;
+            uint16_t hd;
+            if (canonical_w) {
+                const uint8_t *s = canonical_w + blk * 18;
+                hd = static_cast<uint16_t>(s[0] | (s[1] << 8));
+                uint32_t wv[4];
+                for (int k = 0; k < 4; ++k)
+                    wv[k] = s[2 + 4 * k] | (s[3 + 4 * k] << 8) | (s[4 + 4 * k] << 16) | (static_cast<uint32_t>(s[5 + 4 * k]) << 24);
+                wc = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            } else {
+                wc = reinterpret_cast<const uint4 *>(codes)[blk];
+                hd = scales[blk];
+            }
+            const uint8_t *a = xq + (static_cast<size_t>(c) * nb + b) * 36;
+            int xv[8];
+            for (int k = 0; k < 8; ++k)
+                xv[k] = a[4 + 4 * k] | (a[5 + 4 * k] << 8) | (a[6 + 4 * k] << 16) | (static_cast<int>(a[7 + 4 * k]) << 24);
+            const int dot = block_dot(wc, make_int4(xv[0], xv[1], xv[2], xv[3]), make_int4(xv[4], xv[5], xv[6], xv[7]));
+            const float d8 = h2f(static_cast<uint16_t>(a[0] | (a[1] << 8)));
+            const float s8 = h2f(static_cast<uint16_t>(a[2] | (a[3] << 8)));
+            acc = block_term(dot, h2f(hd), d8, 8.0f * s8, acc);
+            if (dots) dots[(static_cast<size_t>(c) * rows + r) * nb + b] = dot;
+        }
+        out[static_cast<size_t>(c) * rows + r] = acc;
+    }
+}
+
+}  // namespace qmoe

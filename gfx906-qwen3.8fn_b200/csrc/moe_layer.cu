@@ -1,0 +1,672 @@
+// moe_layer.cu -- C ABI of the routed-MoE expert FFN (see include/qwen_moe_b200.h).
+//
+// Orchestration of one forward (all device work, no host synchronisation):
+//   quantize x -> route top-k (softmax, top-10, weights, shared gate, chunk masks)
+//   -> chunk prefix -> expert scan + tile list -> stable scatter of pairs
+//   -> gate/up + SiLU*up + Q8_1 middle -> down + weighted scatter-add.
+// Replaces the reference's Layer::ffn body (src/session.hip:1412-1556) and
+// Experts::run/run_chunk/project (src/session.hip:976-1071).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "common.cuh"
+#include "expert_kernels.cuh"
+#include "route_kernels.cuh"
+#include "tc_kernels.cuh"
+
+using namespace qmoe;
+
+namespace {
+
+thread_local char g_message[256];
+
+int fail(int status, const char *message) {
+    std::snprintf(g_message, sizeof(g_message), "%s", message);
+    return status;
+}
+
+int cuda_status(cudaError_t e, const char *where) {
+    if (e == cudaSuccess) return MOE_OK;
+    std::snprintf(g_message, sizeof(g_message), "%s: %s", where, cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? MOE_OUT_OF_MEMORY : MOE_CUDA_ERROR;
+}
+
+#define MOE_CUDA(call)                                        \
+    do {                                                      \
+        const cudaError_t _e = (call);                        \
+        if (_e != cudaSuccess) return cuda_status(_e, #call); \
+    } while (0)
+
+struct DeviceGuard {
+    int previous = -1;
+    cudaError_t status = cudaSuccess;
+    explicit DeviceGuard(int device) {
+        status = cudaGetDevice(&previous);
+        if (status == cudaSuccess && previous != device) status = cudaSetDevice(device);
+        else if (status == cudaSuccess) previous = -1;
+    }
+    ~DeviceGuard() {
+        if (previous >= 0) cudaSetDevice(previous);
+    }
+};
+
+bool aligned(const void *p, size_t a) { return p && reinterpret_cast<uintptr_t>(p) % a == 0; }
+
+bool overlap(const void *a, size_t an, const void *b, size_t bn) {
+    const auto x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + bn && y < x + an;
+}
+
+int validate_desc(const moe_layer_desc *d) {
+    if (!d) return fail(MOE_INVALID_ARGUMENT, "null layer description");
+    if (d->hidden <= 0 || d->hidden > 16384 || d->hidden % 256 || d->inter <= 0 || d->inter > 16384 ||
+        d->inter % 32)
+        return fail(MOE_INVALID_ARGUMENT, "hidden must be a multiple of 256, inter of 32, both <= 16384");
+    if (d->experts != kRouterExperts || d->top_k != kTopK)
+        return fail(MOE_NOT_SUPPORTED, "only 512 experts with top-10 routing are supported");
+    if (d->has_shared != 0 && d->has_shared != 1) return fail(MOE_INVALID_ARGUMENT, "has_shared must be 0 or 1");
+    if (d->max_tokens < 1 || d->max_tokens > 65536)
+        return fail(MOE_INVALID_ARGUMENT, "max_tokens must be 1..65536");
+    return MOE_OK;
+}
+
+// Bump allocator over one device arena.
+struct Arena {
+    uint8_t *base = nullptr;
+    size_t used = 0;
+    template <class T> T *take(size_t count) {
+        used = (used + 255) & ~size_t(255);
+        T *p = reinterpret_cast<T *>(base + used);
+        used += count * sizeof(T);
+        return p;
+    }
+};
+
+int sm_count(int device) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    return n > 0 ? n : 148;
+}
+
+}  // namespace
+
+struct moe_weights_s {
+    moe_layer_desc desc;
+    ExpertLayout layout;
+    int experts_total;       // routed + shared
+    uint8_t *base = nullptr; // experts_total * layout.bytes
+    float *gate_vec = nullptr;
+    uint8_t *staging = nullptr;  // canonical bytes of one expert (3 matrices)
+};
+
+struct moe_layer_s {
+    moe_layer_desc desc;
+    ExpertLayout layout;
+    int chunks_max, pairs_max, tiles_max, sms;
+    Arena arena;
+    Q8Planar xq, mid;
+    int32_t *ids, *base, *counts, *offsets, *pair_token, *pair_rank;
+    float *weights, *pair_weight;
+    uint32_t *masks;
+    int4 *tiles;
+    int *num_tiles;
+    int *error;
+    TcWorkspace tc;
+};
+
+namespace {
+
+int tiles_bound(int tokens, int has_shared) {
+    const int pairs = tokens * kTopK;
+    const int routed = (pairs + kGemvTile - 1) / kGemvTile + std::min(kRouterExperts, pairs);
+    return routed + (has_shared ? (tokens + kGemvTile - 1) / kGemvTile : 0);
+}
+
+size_t gate_up_smem(int H) { return static_cast<size_t>(kGemvTile) * H + kGemvTile * (H / 32) * 8 + kGemvTile * 32 * 4; }
+size_t down_smem(int I) { return static_cast<size_t>(kGemvTile) * I + kGemvTile * (I / 32) * 8 + 2 * kGemvTile * 4; }
+
+int configure_kernels(int H, int I) {
+    MOE_CUDA(cudaFuncSetAttribute(gate_up_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(gate_up_smem(H))));
+    MOE_CUDA(cudaFuncSetAttribute(down_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(down_smem(I))));
+    return MOE_OK;
+}
+
+GroupParams group_params(moe_layer_s *h, const moe_weights_s *w, float *out) {
+    GroupParams g;
+    g.weights = w->base;
+    g.layout = w->layout;
+    g.x = h->xq;
+    g.mid = h->mid;
+    g.tiles = h->tiles;
+    g.num_tiles = h->num_tiles;
+    g.pair_token = h->pair_token;
+    g.pair_weight = h->pair_weight;
+    g.out = out;
+    g.error = h->error;
+    return g;
+}
+
+// gate/up + down over the tile list already in the workspace.  `events`
+// (optional, three entries) are recorded around the two kernels.
+int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_tiles, cudaStream_t s,
+                   void *const *events = nullptr) {
+    const ExpertLayout &L = w->layout;
+    GroupParams g = group_params(h, w, out);
+    const int slabs = L.inter / 32, dslabs = L.hidden / 64;
+    const int gu_grid = std::max(1, std::min(max_tiles * slabs, h->sms * 8));
+    const int dn_grid = std::max(1, std::min(max_tiles * dslabs, h->sms * 8));
+    if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[0]), s));
+    gate_up_kernel<kGemvTile><<<gu_grid, kGemvThreads, gate_up_smem(L.hidden), s>>>(g);
+    MOE_CUDA(cudaGetLastError());
+    if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
+    down_kernel<kGemvTile><<<dn_grid, kGemvThreads, down_smem(L.inter), s>>>(g);
+    MOE_CUDA(cudaGetLastError());
+    if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[2]), s));
+    return MOE_OK;
+}
+
+int launch_quantize(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error, int sms,
+                    cudaStream_t s) {
+    const size_t warps = blocks;
+    const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((warps + 7) / 8, size_t(sms) * 16)));
+    quantize_kernel<<<grid, 256, 0, s>>>(x, blocks, out, canonical, error);
+    return cuda_status(cudaGetLastError(), "quantize_kernel");
+}
+
+int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const float *logits, int T,
+                 float *probs, cudaStream_t s) {
+    const int chunks = (T + kChunk - 1) / kChunk;
+    RouteParams rp;
+    rp.logits = logits;
+    rp.x = x;
+    rp.gate_vec = (w && h->desc.has_shared) ? w->gate_vec : nullptr;
+    rp.tokens = T;
+    rp.hidden = h->desc.hidden;
+    rp.probs = probs;
+    rp.ids = h->ids;
+    rp.weights = h->weights;
+    rp.masks = h->masks;
+    rp.pair_token = h->pair_token;
+    rp.pair_weight = h->pair_weight;
+    rp.pair_rank = h->pair_rank;
+    rp.error = h->error;
+    route_topk_kernel<<<chunks, kRouteThreads, 0, s>>>(rp);
+    MOE_CUDA(cudaGetLastError());
+    route_chunk_prefix_kernel<<<kRouterExperts / 32, 1024, 0, s>>>(h->masks, chunks, h->base, h->counts);
+    MOE_CUDA(cudaGetLastError());
+    ScanParams sp;
+    sp.counts = h->counts;
+    sp.tokens = T;
+    sp.tile = kGemvTile;
+    sp.has_shared = rp.gate_vec != nullptr;
+    sp.offsets = h->offsets;
+    sp.tiles = h->tiles;
+    sp.num_tiles = h->num_tiles;
+    sp.max_tiles = h->tiles_max;
+    sp.error = h->error;
+    route_scan_kernel<<<1, 512, 0, s>>>(sp);
+    MOE_CUDA(cudaGetLastError());
+    ScatterParams cp;
+    cp.masks = h->masks;
+    cp.base = h->base;
+    cp.offsets = h->offsets;
+    cp.ids = h->ids;
+    cp.weights = h->weights;
+    cp.pair_token = h->pair_token;
+    cp.pair_rank = h->pair_rank;
+    cp.pair_weight = h->pair_weight;
+    route_scatter_kernel<<<dim3(chunks, kRouterExperts / 256), 256, 0, s>>>(cp);
+    MOE_CUDA(cudaGetLastError());
+    return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *moe_last_error_message(void) { return g_message; }
+
+int moe_abi_version(void) { return (1 << 16) | 0; }
+
+const char *moe_status_string(int status) {
+    switch (status) {
+    case MOE_OK: return "ok";
+    case MOE_INVALID_ARGUMENT: return "invalid_argument";
+    case MOE_NOT_SUPPORTED: return "not_supported";
+    case MOE_CUDA_ERROR: return "cuda_error";
+    case MOE_NUMERIC_ERROR: return "numeric_error";
+    case MOE_NCCL_ERROR: return "nccl_error";
+    case MOE_TIMEOUT: return "timeout";
+    case MOE_OUT_OF_MEMORY: return "out_of_memory";
+    default: return "unknown";
+    }
+}
+
+size_t moe_weights_expert_bytes(const moe_layer_desc *desc) {
+    if (!desc) return 0;
+    return make_layout(desc->hidden, desc->inter).bytes;
+}
+
+// ---------------------------------------------------------------- weights --
+int moe_weights_create(const moe_layer_desc *desc, moe_weights_t *out) {
+    if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    if (const int st = validate_desc(desc)) return st;
+    DeviceGuard guard(desc->device);
+    MOE_CUDA(guard.status);
+    auto *w = new (std::nothrow) moe_weights_s();
+    if (!w) return fail(MOE_OUT_OF_MEMORY, "host allocation");
+    w->desc = *desc;
+    w->layout = make_layout(desc->hidden, desc->inter);
+    w->experts_total = desc->experts + desc->has_shared;
+    cudaError_t e = cudaMalloc(&w->base, w->layout.bytes * w->experts_total);
+    if (e == cudaSuccess) e = cudaMalloc(&w->gate_vec, sizeof(float) * desc->hidden);
+    if (e == cudaSuccess) e = cudaMalloc(&w->staging, w->layout.bytes / 16 * 18);
+    if (e == cudaSuccess) e = cudaMemset(w->gate_vec, 0, sizeof(float) * desc->hidden);
+    if (e != cudaSuccess) {
+        cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->staging);
+        delete w;
+        return cuda_status(e, "moe_weights_create");
+    }
+    *out = w;
+    return MOE_OK;
+}
+
+int moe_weights_destroy(moe_weights_t w) {
+    if (!w) return MOE_OK;
+    DeviceGuard guard(w->desc.device);
+    cudaFree(w->base);
+    cudaFree(w->gate_vec);
+    cudaFree(w->staging);
+    delete w;
+    return MOE_OK;
+}
+
+int moe_weights_upload_expert(moe_weights_t w, int expert, const void *gate, const void *up, const void *down,
+                              void *stream) {
+    if (!w || !gate || !up || !down) return fail(MOE_INVALID_ARGUMENT, "null weights argument");
+    if (expert < 0 || expert >= w->experts_total) return fail(MOE_INVALID_ARGUMENT, "expert index out of range");
+    DeviceGuard guard(w->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    const ExpertLayout &L = w->layout;
+    const size_t blocks = static_cast<size_t>(L.hidden) * L.inter / 32;  // per matrix
+    const size_t bytes = blocks * 18;
+    uint8_t *ex = w->base + static_cast<size_t>(expert) * L.bytes;
+    const void *src[3] = {gate, up, down};
+    const size_t codes[3] = {L.gate_codes, L.up_codes, L.down_codes};
+    const size_t scales[3] = {L.gate_scales, L.up_scales, L.down_scales};
+    for (int m = 0; m < 3; ++m) {
+        MOE_CUDA(cudaMemcpyAsync(w->staging, src[m], bytes, cudaMemcpyHostToDevice, s));
+        repack_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
+                                          blocks, 0);
+        MOE_CUDA(cudaGetLastError());
+        MOE_CUDA(cudaStreamSynchronize(s));  // staging is reused by the next matrix
+    }
+    return MOE_OK;
+}
+
+int moe_weights_download_expert(moe_weights_t w, int expert, void *gate, void *up, void *down, void *stream) {
+    if (!w || !gate || !up || !down) return fail(MOE_INVALID_ARGUMENT, "null weights argument");
+    if (expert < 0 || expert >= w->experts_total) return fail(MOE_INVALID_ARGUMENT, "expert index out of range");
+    DeviceGuard guard(w->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    const ExpertLayout &L = w->layout;
+    const size_t blocks = static_cast<size_t>(L.hidden) * L.inter / 32;
+    uint8_t *ex = w->base + static_cast<size_t>(expert) * L.bytes;
+    void *dst[3] = {gate, up, down};
+    const size_t codes[3] = {L.gate_codes, L.up_codes, L.down_codes};
+    const size_t scales[3] = {L.gate_scales, L.up_scales, L.down_scales};
+    for (int m = 0; m < 3; ++m) {
+        repack_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
+                                          blocks, 1);
+        MOE_CUDA(cudaGetLastError());
+        MOE_CUDA(cudaMemcpyAsync(dst[m], w->staging, blocks * 18, cudaMemcpyDeviceToHost, s));
+        MOE_CUDA(cudaStreamSynchronize(s));
+    }
+    return MOE_OK;
+}
+
+int moe_weights_upload_shared_gate(moe_weights_t w, const float *gate_vec, void *stream) {
+    if (!w || !gate_vec) return fail(MOE_INVALID_ARGUMENT, "null shared gate argument");
+    if (!w->desc.has_shared) return fail(MOE_INVALID_ARGUMENT, "layer has no shared expert");
+    DeviceGuard guard(w->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    MOE_CUDA(cudaMemcpyAsync(w->gate_vec, gate_vec, sizeof(float) * w->desc.hidden, cudaMemcpyHostToDevice, s));
+    MOE_CUDA(cudaStreamSynchronize(s));
+    return MOE_OK;
+}
+
+int moe_weights_synthesize(moe_weights_t w, uint64_t seed, uint32_t layer, void *stream) {
+    if (!w) return fail(MOE_INVALID_ARGUMENT, "null weights");
+    DeviceGuard guard(w->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    synth_kernel<<<sm_count(w->desc.device) * 8, 256, 0, s>>>(w->base, w->layout, w->experts_total, seed, layer);
+    return cuda_status(cudaGetLastError(), "synth_kernel");
+}
+
+// ------------------------------------------------------------------ layer --
+int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
+    if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    if (const int st = validate_desc(desc)) return st;
+    DeviceGuard guard(desc->device);
+    MOE_CUDA(guard.status);
+    auto *h = new (std::nothrow) moe_layer_s();
+    if (!h) return fail(MOE_OUT_OF_MEMORY, "host allocation");
+    h->desc = *desc;
+    h->layout = make_layout(desc->hidden, desc->inter);
+    h->sms = sm_count(desc->device);
+    const int T = desc->max_tokens, H = desc->hidden, I = desc->inter;
+    h->chunks_max = (T + kChunk - 1) / kChunk;
+    h->pairs_max = T * (kTopK + 1);
+    h->tiles_max = tiles_bound(T, 1);
+    // size the arena with a dry run
+    for (int pass = 0; pass < 2; ++pass) {
+        Arena &a = h->arena;
+        a.used = 0;
+        h->xq.codes = a.take<int8_t>(static_cast<size_t>(T) * H);
+        h->xq.scales = a.take<float2>(static_cast<size_t>(T) * (H / 32));
+        h->mid.codes = a.take<int8_t>(static_cast<size_t>(h->pairs_max) * I);
+        h->mid.scales = a.take<float2>(static_cast<size_t>(h->pairs_max) * (I / 32));
+        h->ids = a.take<int32_t>(static_cast<size_t>(T) * kTopK);
+        h->weights = a.take<float>(static_cast<size_t>(T) * kTopK);
+        h->masks = a.take<uint32_t>(static_cast<size_t>(h->chunks_max) * kRouterExperts);
+        h->base = a.take<int32_t>(static_cast<size_t>(h->chunks_max) * kRouterExperts);
+        h->counts = a.take<int32_t>(kRouterExperts);
+        h->offsets = a.take<int32_t>(kRouterExperts + 2);
+        h->pair_token = a.take<int32_t>(h->pairs_max);
+        h->pair_rank = a.take<int32_t>(h->pairs_max);
+        h->pair_weight = a.take<float>(h->pairs_max);
+        h->tiles = a.take<int4>(h->tiles_max);
+        h->num_tiles = a.take<int>(1);
+        h->error = a.take<int>(1);
+        tc_workspace_take(h->tc, a, T, H, I);
+        if (pass == 0) {
+            const size_t bytes = a.used + 256;
+            const cudaError_t e = cudaMalloc(&a.base, bytes);
+            if (e != cudaSuccess) { delete h; return cuda_status(e, "moe_layer_create"); }
+            cudaMemset(a.base, 0, bytes);
+        }
+    }
+    if (const int st = configure_kernels(H, I)) { cudaFree(h->arena.base); delete h; return st; }
+    if (const int st = tc_configure()) { cudaFree(h->arena.base); delete h; return st; }
+    *out = h;
+    return MOE_OK;
+}
+
+int moe_layer_destroy(moe_layer_t h) {
+    if (!h) return MOE_OK;
+    DeviceGuard guard(h->desc.device);
+    cudaFree(h->arena.base);
+    delete h;
+    return MOE_OK;
+}
+
+int moe_layer_read_flags(moe_layer_t h, int *flags, int clear, void *stream) {
+    if (!h || !flags) return fail(MOE_INVALID_ARGUMENT, "null argument");
+    DeviceGuard guard(h->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    MOE_CUDA(cudaMemcpyAsync(flags, h->error, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (clear) MOE_CUDA(cudaMemsetAsync(h->error, 0, sizeof(int), s));
+    MOE_CUDA(cudaStreamSynchronize(s));
+    return MOE_OK;
+}
+
+int moe_route(moe_layer_t h, const float *logits, int tokens, float *probs, int32_t *ids, float *weights,
+              int32_t *offsets, int32_t *token, int32_t *rank, void *stream) {
+    if (!h || !aligned(logits, 4)) return fail(MOE_INVALID_ARGUMENT, "null or misaligned logits");
+    if (tokens < 1 || tokens > h->desc.max_tokens) return fail(MOE_INVALID_ARGUMENT, "tokens outside 1..max_tokens");
+    DeviceGuard guard(h->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    if (const int st = launch_route(h, nullptr, nullptr, logits, tokens, probs, s)) return st;
+    const size_t n = static_cast<size_t>(tokens) * kTopK;
+    if (ids) MOE_CUDA(cudaMemcpyAsync(ids, h->ids, n * 4, cudaMemcpyDeviceToDevice, s));
+    if (weights) MOE_CUDA(cudaMemcpyAsync(weights, h->weights, n * 4, cudaMemcpyDeviceToDevice, s));
+    if (offsets) MOE_CUDA(cudaMemcpyAsync(offsets, h->offsets, (kRouterExperts + 1) * 4, cudaMemcpyDeviceToDevice, s));
+    if (token) MOE_CUDA(cudaMemcpyAsync(token, h->pair_token, n * 4, cudaMemcpyDeviceToDevice, s));
+    if (rank) MOE_CUDA(cudaMemcpyAsync(rank, h->pair_rank, n * 4, cudaMemcpyDeviceToDevice, s));
+    return MOE_OK;
+}
+
+int moe_forward(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens, float *out,
+                int flags, void *stream) {
+    return moe_forward_profiled(h, w, x, logits, tokens, out, flags, stream, nullptr);
+}
+
+int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens,
+                         float *out, int flags, void *stream, void *const *events) {
+    if (!h || !w) return fail(MOE_INVALID_ARGUMENT, "null layer or weights");
+    if (std::memcmp(&h->desc, &w->desc, offsetof(moe_layer_desc, device) + sizeof(int)) != 0)
+        return fail(MOE_INVALID_ARGUMENT, "layer and weights describe different shapes or devices");
+    if (tokens < 1 || tokens > h->desc.max_tokens) return fail(MOE_INVALID_ARGUMENT, "tokens outside 1..max_tokens");
+    if (!aligned(x, 16) || !aligned(logits, 16) || !aligned(out, 16))
+        return fail(MOE_INVALID_ARGUMENT, "x, logits and out must be 16-byte aligned device pointers");
+    if (flags != MOE_OUT_ACCUMULATE && flags != MOE_OUT_OVERWRITE) return fail(MOE_INVALID_ARGUMENT, "bad flags");
+    const int H = h->desc.hidden;
+    const size_t xbytes = static_cast<size_t>(tokens) * H * 4, lbytes = static_cast<size_t>(tokens) * kRouterExperts * 4;
+    if (overlap(out, xbytes, logits, lbytes)) return fail(MOE_INVALID_ARGUMENT, "out overlaps logits");
+    if (flags == MOE_OUT_OVERWRITE && overlap(out, xbytes, x, xbytes))
+        return fail(MOE_INVALID_ARGUMENT, "overwrite requires out disjoint from x (accumulate may alias exactly)");
+    if (flags == MOE_OUT_ACCUMULATE && overlap(out, xbytes, x, xbytes) && out != x)
+        return fail(MOE_INVALID_ARGUMENT, "out may alias x only exactly");
+    DeviceGuard guard(h->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
+    if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s))
+        return st;
+    if (const int st = launch_route(h, w, x, logits, tokens, nullptr, s)) return st;
+    return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events);
+}
+
+int moe_quantize_q8_1(const float *x, int width, int columns, void *q8, int *error, void *stream) {
+    if (width <= 0 || width > 16384 || width % 32 || columns <= 0 || columns > 65536)
+        return fail(MOE_INVALID_ARGUMENT, "width must be 32..16384 and a multiple of 32; columns 1..65536");
+    const size_t n = static_cast<size_t>(width) * columns;
+    if (!aligned(x, 4) || !aligned(q8, 4) || !aligned(error, 4) || overlap(q8, n / 32 * 36, x, n * 4) ||
+        overlap(error, 4, x, n * 4) || overlap(error, 4, q8, n / 32 * 36))
+        return fail(MOE_INVALID_ARGUMENT, "null, misaligned or overlapping quantize buffers");
+    int device = 0;
+    MOE_CUDA(cudaGetDevice(&device));
+    Q8Planar none{nullptr, nullptr};
+    return launch_quantize(x, n / 32, none, static_cast<uint8_t *>(q8), error, sm_count(device),
+                           static_cast<cudaStream_t>(stream));
+}
+
+int moe_q4_linear(const void *w, int rows, int k, const void *xq, int columns, float *out, int32_t *dots,
+                  void *stream) {
+    if (rows <= 0 || rows > 65536 || k <= 0 || k > 16384 || k % 32 || columns <= 0 || columns > 65536)
+        return fail(MOE_INVALID_ARGUMENT, "bad linear shape");
+    if (!aligned(w, 2) || !aligned(xq, 4) || !aligned(out, 4) || (dots && !aligned(dots, 4)))
+        return fail(MOE_INVALID_ARGUMENT, "null or misaligned linear buffers");
+    const size_t nb = k / 32;
+    if (overlap(out, static_cast<size_t>(rows) * columns * 4, w, rows * nb * 18) ||
+        overlap(out, static_cast<size_t>(rows) * columns * 4, xq, columns * nb * 36))
+        return fail(MOE_INVALID_ARGUMENT, "output overlaps an input");
+    int device = 0;
+    MOE_CUDA(cudaGetDevice(&device));
+    q4_linear_kernel<<<sm_count(device) * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t *>(w), nullptr, nullptr, rows, static_cast<int>(nb),
+        static_cast<const uint8_t *>(xq), columns, out, dots);
+    return cuda_status(cudaGetLastError(), "q4_linear_kernel");
+}
+
+// ------------------------------------------------- single-expert fixture --
+}  // extern "C"
+
+struct moe_expert_s {
+    moe_layer_desc desc;
+    moe_weights_s *w = nullptr;
+    moe_layer_s *h = nullptr;
+    int max_columns;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t begin = nullptr, end = nullptr;
+    float *x = nullptr, *y = nullptr;
+    uint8_t *q8 = nullptr;
+    double upload_ms = 0;
+};
+
+namespace {
+int expert_forward(moe_expert_s *e, int columns) {
+    moe_layer_s *h = e->h;
+    if (const int st = launch_quantize(e->x, static_cast<size_t>(columns) * e->desc.hidden / 32, h->xq, nullptr,
+                                       h->error, h->sms, e->stream))
+        return st;
+    identity_route_kernel<<<(columns + 255) / 256, 256, 0, e->stream>>>(columns, kGemvTile, h->tiles, h->num_tiles,
+                                                                        h->pair_token, h->pair_weight);
+    MOE_CUDA(cudaGetLastError());
+    MOE_CUDA(cudaMemsetAsync(e->y, 0, sizeof(float) * columns * e->desc.hidden, e->stream));
+    return launch_experts(h, e->w, e->y, (columns + kGemvTile - 1) / kGemvTile, e->stream);
+}
+}  // namespace
+
+extern "C" {
+
+int moe_expert_destroy(moe_expert_t e) {
+    if (!e) return MOE_OK;
+    DeviceGuard guard(e->desc.device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    moe_layer_destroy(e->h);
+    moe_weights_destroy(e->w);
+    cudaFree(e->x);
+    cudaFree(e->y);
+    cudaFree(e->q8);
+    if (e->begin) cudaEventDestroy(e->begin);
+    if (e->end) cudaEventDestroy(e->end);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return MOE_OK;
+}
+
+int moe_expert_create(const void *gate, const void *up, const void *down, int hidden, int inter, int device,
+                      int max_columns, moe_expert_t *out) {
+    if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    if (max_columns <= 0 || max_columns > 1024) return fail(MOE_INVALID_ARGUMENT, "max_columns must be 1..1024");
+    if (!gate || !up || !down) return fail(MOE_INVALID_ARGUMENT, "null expert weights");
+    moe_layer_desc d{hidden, inter, kRouterExperts, kTopK, 0, device, max_columns};
+    if (const int st = validate_desc(&d)) return st;
+    DeviceGuard guard(device);
+    MOE_CUDA(guard.status);
+    auto *e = new (std::nothrow) moe_expert_s();
+    if (!e) return fail(MOE_OUT_OF_MEMORY, "host allocation");
+    e->desc = d;
+    e->max_columns = max_columns;
+    // one expert region only: the fixture never routes
+    auto *w = new (std::nothrow) moe_weights_s();
+    if (!w) { delete e; return fail(MOE_OUT_OF_MEMORY, "host allocation"); }
+    w->desc = d;
+    w->layout = make_layout(hidden, inter);
+    w->experts_total = 1;
+    e->w = w;
+    int st = cuda_status(cudaMalloc(&w->base, w->layout.bytes), "cudaMalloc");
+    if (!st) st = cuda_status(cudaMalloc(&w->gate_vec, sizeof(float) * hidden), "cudaMalloc");
+    if (!st) st = cuda_status(cudaMalloc(&w->staging, w->layout.bytes / 16 * 18), "cudaMalloc");
+    if (!st) st = cuda_status(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream");
+    if (!st) st = cuda_status(cudaEventCreate(&e->begin), "event");
+    if (!st) st = cuda_status(cudaEventCreate(&e->end), "event");
+    const size_t n = static_cast<size_t>(max_columns) * std::max(hidden, inter);
+    if (!st) st = cuda_status(cudaMalloc(&e->x, n * 4), "cudaMalloc");
+    if (!st) st = cuda_status(cudaMalloc(&e->y, n * 4), "cudaMalloc");
+    if (!st) st = cuda_status(cudaMalloc(&e->q8, n / 32 * 36), "cudaMalloc");
+    if (!st) st = moe_layer_create(&d, &e->h);
+    if (!st) {
+        const auto t0 = std::chrono::steady_clock::now();
+        st = moe_weights_upload_expert(w, 0, gate, up, down, e->stream);
+        e->upload_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    }
+    if (st) { moe_expert_destroy(e); return st; }
+    *out = e;
+    return MOE_OK;
+}
+
+int moe_expert_check_quantization(moe_expert_t e, const float *input, size_t n, const void *expected) {
+    if (!e || !input || !expected) return fail(MOE_INVALID_ARGUMENT, "null argument");
+    if (n == 0 || n % 32 || n > static_cast<size_t>(e->desc.hidden) * e->max_columns)
+        return fail(MOE_INVALID_ARGUMENT, "GPU quantization span");
+    DeviceGuard guard(e->desc.device);
+    MOE_CUDA(guard.status);
+    int *err = e->h->error;
+    MOE_CUDA(cudaMemsetAsync(err, 0, 4, e->stream));
+    MOE_CUDA(cudaMemcpyAsync(e->x, input, n * 4, cudaMemcpyHostToDevice, e->stream));
+    Q8Planar none{nullptr, nullptr};
+    if (const int st = launch_quantize(e->x, n / 32, none, e->q8, err, e->h->sms, e->stream)) return st;
+    auto *result = new (std::nothrow) uint8_t[n / 32 * 36];
+    if (!result) return fail(MOE_OUT_OF_MEMORY, "host allocation");
+    int flags = 0;
+    cudaError_t ce = cudaMemcpyAsync(result, e->q8, n / 32 * 36, cudaMemcpyDeviceToHost, e->stream);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(&flags, err, 4, cudaMemcpyDeviceToHost, e->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+    int st = cuda_status(ce, "check_quantization");
+    if (!st && flags) st = fail(MOE_INVALID_ARGUMENT, "GPU activation not representable in Q8_1");
+    if (!st && std::memcmp(result, expected, n / 32 * 36)) st = fail(MOE_NUMERIC_ERROR, "CPU/GPU Q8_1 ABI mismatch");
+    delete[] result;
+    return st;
+}
+
+int moe_expert_linear(moe_expert_t e, int down, int up, const void *input, int columns, float *output) {
+    if (!e || !input || !output) return fail(MOE_INVALID_ARGUMENT, "null argument");
+    if (columns <= 0 || columns > e->max_columns) return fail(MOE_INVALID_ARGUMENT, "GPU linear span");
+    DeviceGuard guard(e->desc.device);
+    MOE_CUDA(guard.status);
+    const ExpertLayout &L = e->w->layout;
+    const int in = down ? L.inter : L.hidden, rows = down ? L.hidden : L.inter;
+    const uint8_t *ex = e->w->base;
+    const size_t co = down ? L.down_codes : up ? L.up_codes : L.gate_codes;
+    const size_t so = down ? L.down_scales : up ? L.up_scales : L.gate_scales;
+    MOE_CUDA(cudaMemcpyAsync(e->q8, input, static_cast<size_t>(columns) * (in / 32) * 36, cudaMemcpyHostToDevice,
+                             e->stream));
+    q4_linear_kernel<<<e->h->sms * 8, 256, 0, e->stream>>>(nullptr, ex + co, reinterpret_cast<const uint16_t *>(ex + so),
+                                                           rows, in / 32, e->q8, columns, e->y, nullptr);
+    MOE_CUDA(cudaGetLastError());
+    MOE_CUDA(cudaMemcpyAsync(output, e->y, static_cast<size_t>(columns) * rows * 4, cudaMemcpyDeviceToHost, e->stream));
+    MOE_CUDA(cudaStreamSynchronize(e->stream));
+    return MOE_OK;
+}
+
+int moe_expert_run(moe_expert_t e, const float *input, int columns, float *output, int repeats, double *upload_ms,
+                   double *resident_ms, double *wall_ms) {
+    if (!e || !input || !output) return fail(MOE_INVALID_ARGUMENT, "null argument");
+    if (columns <= 0 || columns > e->max_columns || repeats <= 0 || repeats > 10000)
+        return fail(MOE_INVALID_ARGUMENT, "GPU expert input/output");
+    DeviceGuard guard(e->desc.device);
+    MOE_CUDA(guard.status);
+    const size_t n = static_cast<size_t>(columns) * e->desc.hidden;
+    int *err = e->h->error;
+    MOE_CUDA(cudaMemsetAsync(err, 0, 4, e->stream));
+    MOE_CUDA(cudaMemcpyAsync(e->x, input, n * 4, cudaMemcpyHostToDevice, e->stream));
+    if (const int st = expert_forward(e, columns)) return st;  // warm-up outside timing
+    const auto t0 = std::chrono::steady_clock::now();
+    MOE_CUDA(cudaEventRecord(e->begin, e->stream));
+    for (int r = 0; r < repeats; ++r)
+        if (const int st = expert_forward(e, columns)) return st;
+    MOE_CUDA(cudaEventRecord(e->end, e->stream));
+    MOE_CUDA(cudaEventSynchronize(e->end));
+    float ms = 0;
+    MOE_CUDA(cudaEventElapsedTime(&ms, e->begin, e->end));
+    int flags = 0;
+    MOE_CUDA(cudaMemcpyAsync(&flags, err, 4, cudaMemcpyDeviceToHost, e->stream));
+    MOE_CUDA(cudaMemcpyAsync(output, e->y, n * 4, cudaMemcpyDeviceToHost, e->stream));
+    MOE_CUDA(cudaStreamSynchronize(e->stream));
+    const double wall = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (upload_ms) *upload_ms = e->upload_ms;
+    if (resident_ms) *resident_ms = ms / repeats;
+    if (wall_ms) *wall_ms = wall / repeats;
+    if (flags) return fail(MOE_NUMERIC_ERROR, "GPU expert numeric flag");
+    return MOE_OK;
+}
+
+}  // extern "C"

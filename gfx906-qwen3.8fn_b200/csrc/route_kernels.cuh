@@ -1,0 +1,322 @@
+// route_kernels.cuh -- router softmax, top-10 selection and stable grouping.
+//
+// Replaces three reference stages with device work and no host round trip:
+//  * router_softmax (src/hip/session_ops.hip:401-434),
+//  * select_routes (src/session.hip:666-687, a host partial_sort),
+//  * RouteGroups::prepare (src/routes.cpp:59-115, a host counting sort) plus
+//    the per-layer pinned upload of the {token, rank} list (src/session.hip:393-410).
+// Index results are bit-exact with the reference algorithms: every float
+// operation is a separately rounded IEEE op in the reference's order.
+#pragma once
+#include "common.cuh"
+
+namespace qmoe {
+
+constexpr int kChunk = 32;         // tokens per routing chunk (one bit each in a 32-bit mask)
+constexpr int kRouteThreads = 256; // 8 warps; each warp routes tokens w, w+8, w+16, w+24 of a chunk
+
+// Exponential used by the router softmax.  The same operation sequence is
+// the specification in the CPU oracle: Cody-Waite reduction with ln2 split
+// into an exact-product high part and a low part, degree-7 Taylor polynomial
+// of e^r in Horner form, exact power-of-two scaling in two steps.
+__device__ __forceinline__ float route_exp(float x) {
+    if (!(x == x)) return x;
+    if (x < -104.0f) return 0.0f;
+    if (x > 88.8f) return __int_as_float(0x7f800000);
+    const float n = rintf(__fmul_rn(x, 1.44269502f));
+    float r = fmaf(-n, 0.693145751953125f, x);
+    r = fmaf(-n, 1.42860677e-06f, r);
+    float p = 1.98412701e-04f;
+    p = fmaf(p, r, 1.38888892e-03f);
+    p = fmaf(p, r, 8.33333377e-03f);
+    p = fmaf(p, r, 4.16666679e-02f);
+    p = fmaf(p, r, 1.66666672e-01f);
+    p = fmaf(p, r, 5.00000000e-01f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int k = static_cast<int>(n);
+    const int k1 = k / 2, k2 = k - k1;
+    const float s1 = __int_as_float((127 + k1) << 23), s2 = __int_as_float((127 + k2) << 23);
+    return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
+struct RouteParams {
+    const float *logits;    // [T][512]
+    const float *x;         // [T][H] (shared-expert gate input); may be null without shared
+    const float *gate_vec;  // [H] or null (no shared expert)
+    int tokens, hidden;
+    float *probs;           // optional [T][512]
+    int32_t *ids;           // [T][10]
+    float *weights;         // [T][10]
+    uint32_t *masks;        // [chunks][512]: bit j set when token chunk*32+j routes to expert e
+    int32_t *pair_token;    // shared-expert pairs are written at [T*10 + t]
+    float *pair_weight;
+    int32_t *pair_rank;
+    int *error;
+};
+
+// One CTA per chunk of 32 tokens; one warp per token.
+__global__ void __launch_bounds__(kRouteThreads)
+route_topk_kernel(RouteParams p) {
+    __shared__ uint32_t smask[kRouterExperts];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int e = threadIdx.x; e < kRouterExperts; e += kRouteThreads) smask[e] = 0u;
+    __syncthreads();
+    const int chunk = blockIdx.x;
+    for (int j = warp; j < kChunk; j += kRouteThreads / 32) {
+        const int t = chunk * kChunk + j;
+        if (t >= p.tokens) break;
+        const float *row = p.logits + static_cast<size_t>(t) * kRouterExperts;
+        int flags = 0;
+        float w[16];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            w[k] = operand(row[lane + 32 * k], flags);
+            mx = fmaxf(mx, w[k]);
+        }
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+        float total = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const float shifted = arithmetic(__fsub_rn(w[k], mx), flags);
+            w[k] = arithmetic(route_exp(shifted), flags);
+            total = arithmetic(__fadd_rn(total, w[k]), flags);
+        }
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) total = __fadd_rn(total, __shfl_xor_sync(0xffffffffu, total, m));
+        total = arithmetic(total, flags);
+        if (!(total > 0.0f)) flags |= kFlagArithmetic;
+        const float inv = total > 0.0f ? arithmetic(__fdiv_rn(1.0f, total), flags) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) w[k] = arithmetic(__fmul_rn(w[k], inv), flags);
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) flags |= __shfl_xor_sync(0xffffffffu, flags, m);
+        if (flags) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) w[k] = 0.0f;
+        }
+        if (p.probs) {
+            float *prow = p.probs + static_cast<size_t>(t) * kRouterExperts;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) prow[lane + 32 * k] = w[k];
+        }
+        if (lane == 0) report(flags, p.error);
+
+        // top-10 by (probability desc, id asc): ten warp-wide arg-max rounds.
+        uint32_t taken = 0u;
+        int sel_id[kTopK];
+        float sel_p[kTopK];
+#pragma unroll
+        for (int r = 0; r < kTopK; ++r) {
+            float bv = -1.0f;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int id = lane + 32 * k;
+                if (!((taken >> k) & 1u) && (w[k] > bv || (w[k] == bv && id < bi))) { bv = w[k]; bi = id; }
+            }
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+            sel_id[r] = bi;
+            sel_p[r] = bv;
+        }
+        // Renormalisation: buckets[id % 32] accumulate in rank order, then an
+        // XOR butterfly 1..16, floor 1/16384, reciprocal, separate multiply.
+        float bucket = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kTopK; ++r)
+            if ((sel_id[r] & 31) == lane) bucket = __fadd_rn(bucket, sel_p[r]);
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) bucket = __fadd_rn(bucket, __shfl_xor_sync(0xffffffffu, bucket, m));
+        const float den = fmaxf(bucket, 1.0f / 16384.0f);
+        const float inv_den = __fdiv_rn(1.0f, den);
+#pragma unroll
+        for (int r = 0; r < kTopK; ++r) {
+            if (lane == r) {
+                p.ids[t * kTopK + r] = sel_id[r];
+                p.weights[t * kTopK + r] = __fmul_rn(sel_p[r], inv_den);
+                atomicOr(&smask[sel_id[r]], 1u << j);
+            }
+        }
+        // Shared expert: raw gate = x . gate_vec, weight = 1/(1+exp(-raw))
+        // (src/hip/session_ops.hip:376-391), written as pair T*10 + t.
+        if (p.gate_vec) {
+            const float4 *xr = reinterpret_cast<const float4 *>(p.x + static_cast<size_t>(t) * p.hidden);
+            const float4 *gv = reinterpret_cast<const float4 *>(p.gate_vec);
+            float acc = 0.0f;
+            for (int h = lane; h < p.hidden / 4; h += 32) {
+                const float4 a = xr[h], b = gv[h];
+                acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc);
+                acc = fmaf(a.z, b.z, acc); acc = fmaf(a.w, b.w, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                int f = 0;
+                const float raw = operand(acc, f);
+                const float scale = arithmetic(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-raw))), f);
+                const int pair = p.tokens * kTopK + t;
+                p.pair_token[pair] = t;
+                p.pair_weight[pair] = scale;
+                if (p.pair_rank) p.pair_rank[pair] = kTopK;
+                report(f, p.error);
+            }
+        }
+    }
+    __syncthreads();
+    uint32_t *out = p.masks + static_cast<size_t>(chunk) * kRouterExperts;
+    for (int e = threadIdx.x; e < kRouterExperts; e += kRouteThreads) out[e] = smask[e];
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim.x == 512).
+__device__ __forceinline__ int block_exclusive_scan_512(int v, int *total_out) {
+    __shared__ int warp_tot[16];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, inc, d);
+        if (lane >= d) inc += o;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < 16 ? warp_tot[lane] : 0;
+#pragma unroll
+        for (int d = 1; d < 16; d <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, w, d);
+            if (lane >= d) w += o;
+        }
+        if (lane < 16) warp_tot[lane] = w;   // inclusive warp totals
+    }
+    __syncthreads();
+    const int before = warp > 0 ? warp_tot[warp - 1] : 0;
+    if (total_out) *total_out = warp_tot[15];
+    __syncthreads();
+    return before + inc - v;
+}
+
+// Per-expert prefix over chunks.  Grid: 16 CTAs x 1024 threads; CTA b owns
+// experts 32b..32b+31 (lane = expert), warp w owns a contiguous range of
+// chunks.  base[c][e] = entries of expert e in chunks before c; counts[e] =
+// group size.
+__global__ void __launch_bounds__(1024)
+route_chunk_prefix_kernel(const uint32_t *masks, int chunks, int32_t *base, int32_t *counts) {
+    __shared__ int part[32][33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.x * 32 + lane;
+    const int per = (chunks + 31) / 32;
+    const int c0 = min(chunks, warp * per), c1 = min(chunks, c0 + per);
+    int s = 0;
+    for (int c = c0; c < c1; ++c) s += __popc(masks[static_cast<size_t>(c) * kRouterExperts + e]);
+    part[warp][lane] = s;
+    __syncthreads();
+    int run = 0;
+    for (int w = 0; w < warp; ++w) run += part[w][lane];
+    for (int c = c0; c < c1; ++c) {
+        const size_t idx = static_cast<size_t>(c) * kRouterExperts + e;
+        base[idx] = run;
+        run += __popc(masks[idx]);
+    }
+    if (warp == 31) counts[e] = run;
+}
+
+struct ScanParams {
+    const int32_t *counts;  // [512]
+    int tokens, tile;       // tile = tokens per work tile
+    int has_shared;
+    int32_t *offsets;       // [514]: 512 routed groups, shared group, end
+    int4 *tiles;            // {expert, first pair, count, 0}
+    int *num_tiles;
+    int max_tiles;
+    int *error;
+};
+
+// One CTA of 512 threads (thread = expert): exclusive scan over experts and
+// the work-tile list (tiles of at most `tile` pairs of one expert).
+__global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
+    const int e = threadIdx.x;
+    const int run = p.counts[e];
+    int total = 0;
+    const int off = block_exclusive_scan_512(run, &total);
+    p.offsets[e] = off;
+    if (e == kRouterExperts - 1) {
+        p.offsets[kRouterExperts] = total;
+        p.offsets[kRouterExperts + 1] = total + (p.has_shared ? p.tokens : 0);
+    }
+    const int ntiles = (run + p.tile - 1) / p.tile;
+    int tiles_total = 0;
+    const int toff = block_exclusive_scan_512(ntiles, &tiles_total);
+    for (int i = 0; i < ntiles; ++i) {
+        const int idx = toff + i;
+        if (idx < p.max_tiles)
+            p.tiles[idx] = make_int4(e, off + i * p.tile, min(p.tile, run - i * p.tile), 0);
+    }
+    int shared_tiles = 0;
+    if (p.has_shared) {
+        shared_tiles = (p.tokens + p.tile - 1) / p.tile;
+        for (int i = e; i < shared_tiles; i += 512) {
+            const int idx = tiles_total + i;
+            if (idx < p.max_tiles)
+                p.tiles[idx] = make_int4(kRouterExperts, total + i * p.tile,
+                                         min(p.tile, p.tokens - i * p.tile), 0);
+        }
+    }
+    if (e == 0) {
+        int n = tiles_total + shared_tiles;
+        if (n > p.max_tiles) { atomicOr(p.error, kFlagArithmetic); n = p.max_tiles; }
+        *p.num_tiles = n;
+    }
+}
+
+struct ScatterParams {
+    const uint32_t *masks;
+    const int32_t *base;
+    const int32_t *offsets;
+    const int32_t *ids;
+    const float *weights;
+    int32_t *pair_token;
+    int32_t *pair_rank;
+    float *pair_weight;
+};
+
+// Thread per (chunk, expert): stable placement by token order within the chunk.
+__global__ void __launch_bounds__(256) route_scatter_kernel(ScatterParams p) {
+    const int chunk = blockIdx.x, e = blockIdx.y * 256 + threadIdx.x;
+    const size_t idx = static_cast<size_t>(chunk) * kRouterExperts + e;
+    uint32_t m = p.masks[idx];
+    if (!m) return;
+    int pos = p.offsets[e] + p.base[idx];
+    while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1u;
+        const int t = chunk * kChunk + j;
+        int r = 0;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k)
+            if (p.ids[t * kTopK + k] == e) r = k;
+        p.pair_token[pos] = t;
+        if (p.pair_rank) p.pair_rank[pos] = r;
+        p.pair_weight[pos] = p.weights[t * kTopK + r];
+        ++pos;
+    }
+}
+
+// Single-expert fixture routing: pair t = token t of expert 0 with weight 1.
+__global__ void identity_route_kernel(int tokens, int tile, int4 *tiles, int *num_tiles,
+                                      int32_t *pair_token, float *pair_weight) {
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < tokens; t += gridDim.x * blockDim.x) {
+        pair_token[t] = t;
+        pair_weight[t] = 1.0f;
+        if (t % tile == 0) tiles[t / tile] = make_int4(0, t, min(tile, tokens - t), 0);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *num_tiles = (tokens + tile - 1) / tile;
+}
+
+}  // namespace qmoe

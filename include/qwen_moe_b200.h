@@ -1,0 +1,193 @@
+/*
+ * qwen_moe_b200.h -- C ABI of the B200 routed-MoE expert FFN library
+ * (libqwen_moe_b200.so, built for sm_100a).
+ *
+ * Conventions (mirroring the reference's borrowed-buffer launchers,
+ * src/hip/session_ops.cuh:22-48, src/hip/linear.cuh:35-45):
+ *  - every pointer named *_dev is caller-owned device memory on the handle's
+ *    device; lifetimes and cross-stream ordering are the caller's;
+ *  - every launch takes an explicit cudaStream_t (passed as void*; NULL is the
+ *    legacy default stream);
+ *  - invalid shapes, null or misaligned pointers and writable overlaps return
+ *    MOE_INVALID_ARGUMENT before anything is enqueued; a status of MOE_OK means
+ *    "enqueued", not "completed";
+ *  - no call allocates device memory except the *_create / *_weights_create
+ *    functions; no call synchronises except where stated; no C++ exception
+ *    crosses this boundary;
+ *  - numeric faults never trap: kernels OR sticky bits into a device int
+ *    (MOE_FLAG_INVALID = 1 nonfinite input, MOE_FLAG_ARITHMETIC = 2 nonfinite
+ *    or unrepresentable arithmetic), as the reference's session ops do.
+ *
+ * Q4_0 blocks are the canonical 18-byte GGML layout (half d, 16 code bytes,
+ * low nibble of byte j = element j, high nibble = element j+16); Q8_1 blocks
+ * are the reference's 36-byte ABI (half d, half raw sum, 32 int8 codes),
+ * src/quant.hpp:8-18.
+ */
+#ifndef QWEN_MOE_B200_H
+#define QWEN_MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+enum moe_status {
+    MOE_OK = 0,
+    MOE_INVALID_ARGUMENT = 1, /* reference: std::invalid_argument / hipErrorInvalidValue */
+    MOE_NOT_SUPPORTED = 2,    /* reference: hipErrorNotSupported */
+    MOE_CUDA_ERROR = 3,       /* reference: std::runtime_error from a HIP call */
+    MOE_NUMERIC_ERROR = 4,    /* a sticky numeric flag was raised */
+    MOE_NCCL_ERROR = 5,
+    MOE_TIMEOUT = 6,
+    MOE_OUT_OF_MEMORY = 7
+};
+
+enum moe_flags { MOE_FLAG_INVALID = 1, MOE_FLAG_ARITHMETIC = 2 };
+
+/* moe_forward flags */
+enum moe_forward_flags {
+    MOE_OUT_ACCUMULATE = 0, /* out += layer(x): scatter-add into a residual */
+    MOE_OUT_OVERWRITE = 1   /* out  = layer(x) */
+};
+
+/* Shape of one MoE layer.  Replaces the fixed constants of the reference's
+ * Session (src/session.hip:40, H=2560/640) and RouteGroups (src/routes.hpp:53-55,
+ * 512 experts, top-10).  Supported: hidden, inter multiples of 256 and <= 16384,
+ * experts == 512, top_k == 10. */
+typedef struct moe_layer_desc {
+    int hidden;      /* H */
+    int inter;       /* I, expert intermediate width */
+    int experts;     /* routed experts (512) */
+    int top_k;       /* 10 */
+    int has_shared;  /* 1: one shared expert with a sigmoid scalar gate */
+    int device;      /* CUDA device ordinal */
+    int max_tokens;  /* capacity of one forward */
+} moe_layer_desc;
+
+typedef struct moe_layer_s *moe_layer_t;
+typedef struct moe_weights_s *moe_weights_t;
+
+const char *moe_status_string(int status);
+/* Version of this library's ABI (major << 16 | minor). */
+int moe_abi_version(void);
+
+/* ---- weights: device-resident experts of one layer ------------------------
+ * Storage per expert is one contiguous 1,769,472-byte region (H=2048, I=512)
+ * in a planar layout: gate/up/down code bytes (16 per block, row-major
+ * blocks), then gate/up/down half scales.  Byte count equals the canonical
+ * Q4_0 size.  The shared expert is stored as expert index `experts`. */
+int moe_weights_create(const moe_layer_desc *desc, moe_weights_t *out);
+int moe_weights_destroy(moe_weights_t w);
+/* Upload one expert from canonical host Q4_0 bytes (repacked to the planar
+ * layout on the device).  Replaces the reference's expert staging
+ * (src/session.hip:957-1042): all experts stay resident.  expert == experts
+ * uploads the shared expert.  gate/up: [I][H/32] blocks, down: [H][I/32]. */
+int moe_weights_upload_expert(moe_weights_t w, int expert, const void *gate_q4_0,
+                              const void *up_q4_0, const void *down_q4_0, void *stream);
+/* Shared expert scalar gate vector (fp32 [H]), the reference's
+ * ffn_gate_inp_shexp (src/session.hip:1101, used at :1398-1402). */
+int moe_weights_upload_shared_gate(moe_weights_t w, const float *gate_vec_host, void *stream);
+/* Fill every expert (and the shared expert) with the seeded synthetic Q4_0
+ * generator on the device (bit-identical to the oracle's generator). */
+int moe_weights_synthesize(moe_weights_t w, uint64_t seed, uint32_t layer, void *stream);
+/* Copy one expert back as canonical Q4_0 bytes (host), for parity checks. */
+int moe_weights_download_expert(moe_weights_t w, int expert, void *gate_q4_0, void *up_q4_0,
+                                void *down_q4_0, void *stream);
+/* Device address of expert e's planar region (for expert-parallel sharding). */
+size_t moe_weights_expert_bytes(const moe_layer_desc *desc);
+
+/* ---- layer workspace and forward ----------------------------------------- */
+int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out);
+int moe_layer_destroy(moe_layer_t h);
+
+/* Whole routed-MoE FFN for T tokens, replacing the body of the reference's
+ * Layer::ffn (src/session.hip:1412-1556) from the router probabilities on:
+ * softmax over router logits, top-10 + renormalised weights, GPU grouping,
+ * Q8_1 quantisation of x, grouped gate/up + fused SiLU*up + Q8_1
+ * requantisation, down projection, router-weighted scatter-add of every
+ * routed expert and of the sigmoid-gated shared expert into out.
+ * x_dev fp32 [T][H]; logits_dev fp32 [T][experts]; out_dev fp32 [T][H].
+ * No host synchronisation: the call is capturable in a CUDA graph. */
+int moe_forward(moe_layer_t h, moe_weights_t w, const float *x_dev, const float *logits_dev,
+                int tokens, float *out_dev, int flags, void *stream);
+
+/* moe_forward with three caller-created CUDA events recorded on `stream`:
+ * events[0] before the gate/up kernel, events[1] between gate/up and down,
+ * events[2] after the down kernel -- the timing tap bench.py uses to measure
+ * the expert kernels' own durations on their launching stream. */
+int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x_dev, const float *logits_dev,
+                         int tokens, float *out_dev, int flags, void *stream, void *const *events);
+
+/* Routing only (parity tap for src/hip/session_ops.hip:401-434 router_softmax,
+ * src/session.hip:666-687 select_routes and src/routes.cpp:59-115 grouping).
+ * Outputs (device, any may be NULL): probs fp32 [T][experts], ids int32
+ * [T][top_k], weights fp32 [T][top_k], offsets int32 [experts+1], and the
+ * sorted assignment list as token/rank int32 [T*top_k]. */
+int moe_route(moe_layer_t h, const float *logits_dev, int tokens, float *probs_dev,
+              int32_t *ids_dev, float *weights_dev, int32_t *offsets_dev, int32_t *token_dev,
+              int32_t *rank_dev, void *stream);
+
+/* Read (and optionally clear) the sticky numeric flags of a layer.  This is
+ * the only call here that synchronises (on `stream`). */
+int moe_layer_read_flags(moe_layer_t h, int *flags_host, int clear, void *stream);
+
+/* ---- kernels exposed for parity taps ------------------------------------- */
+/* fp32 [columns][width] -> canonical Q8_1 [columns][width/32] (36-byte blocks).
+ * Same contract as the reference's launch_quantize_q8_1
+ * (src/hip/linear.cuh:89-108): failing blocks are written as zero and set
+ * sticky bits in *error_dev (caller-zeroed). */
+int moe_quantize_q8_1(const float *x_dev, int width, int columns, void *q8_dev, int *error_dev,
+                      void *stream);
+/* Q4_0 x Q8_1 linear: out[c][r] = sum_b d4*(dot*d8 - 8*s8) for canonical
+ * Q4_0 weights [rows][K/32] and canonical Q8_1 input [columns][K/32].
+ * Replaces launch_quantized_linear{,_short,_tiled} (src/hip/linear.hip:445-490).
+ * When dots_dev is non-NULL the per-block int32 dots are also written
+ * ([columns][rows][K/32]), the bit-exact parity tap. */
+int moe_q4_linear(const void *w_q4_0_dev, int rows, int k, const void *x_q8_dev, int columns,
+                  float *out_dev, int32_t *dots_dev, void *stream);
+
+/* ---- single-expert fixture API (src/gpu_expert.hpp:7-21) ---------------- */
+typedef struct moe_expert_s *moe_expert_t;
+int moe_expert_create(const void *gate_q4_0, const void *up_q4_0, const void *down_q4_0,
+                      int hidden, int inter, int device, int max_columns, moe_expert_t *out);
+int moe_expert_destroy(moe_expert_t e);
+/* Host fp32 [n] -> compare the GPU Q8_1 bytes with `expected` (host Q8_1);
+ * MOE_INVALID_ARGUMENT when the input is not representable, MOE_NUMERIC_ERROR
+ * when the bytes differ (GpuExpert::check_quantization). */
+int moe_expert_check_quantization(moe_expert_t e, const float *input, size_t n,
+                                  const void *expected_q8);
+/* One projection of host Q8_1 input (GpuExpert::linear): down selects the
+ * down matrix, else up selects up, else gate.  Output host fp32 [columns][rows]. */
+int moe_expert_linear(moe_expert_t e, int down, int up, const void *input_q8, int columns,
+                      float *output);
+/* Resident float -> Q8 -> gate/up -> SiLU*up -> Q8 -> down, host fp32 in/out
+ * [columns][hidden]; timings in milliseconds (GpuExpert::run). */
+int moe_expert_run(moe_expert_t e, const float *input, int columns, float *output, int repeats,
+                   double *upload_ms, double *resident_ms, double *wall_ms);
+
+/* ---- route grouping on the host (src/routes.hpp:28-65) ------------------- */
+typedef struct moe_route_groups_s *moe_route_groups_t;
+/* bound 0: capacity 1..1024, bound 1: capacity 1..16384 */
+int moe_route_groups_create(int token_capacity, int bound, moe_route_groups_t *out);
+int moe_route_groups_destroy(moe_route_groups_t g);
+int moe_route_groups_prepare(moe_route_groups_t g, const int32_t *ids, const float *weights,
+                             size_t n, int tokens);
+/* 16-byte records {int token, int rank, int expert, float weight}. */
+size_t moe_route_groups_assignments(moe_route_groups_t g, void *out, size_t capacity);
+int moe_route_groups_counts(moe_route_groups_t g, int32_t *out512);
+/* Message of the last rejected create/prepare on this thread. */
+const char *moe_route_groups_message(void);
+const char *moe_last_error_message(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif

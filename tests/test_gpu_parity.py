@@ -1,0 +1,249 @@
+"""GPU parity tests: the sm_100a kernels through the C ABI against the CPU
+oracle (itself pinned to the reference's own code).
+
+Bars (from the build's contract):
+* Q8_1 bytes, per-block int32 dots, routing ids/weights/probabilities and the
+  grouped (expert, token, rank) order: bit-exact;
+* layer outputs: max|err| <= 1e-3 * RMS(output) in fp32 (TOL_RMS below);
+* single linear projections: the reference's own common-Q8 gate
+  2e-4 + 2e-5*|ref| (tests/cpu_expert_test.cpp:296-324).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL_RMS = 1e-3
+H, I, E = 2048, 512, 512
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    assert t.cuda.is_available()
+    return t
+
+
+def f32bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def zipf_logits(rng, T, s=1.1):
+    """Zipf(s) route skew: -s*ln(1+pi(e)) + Gumbel noise (top-10 of Gumbel-perturbed
+    log-weights samples experts without replacement in proportion to the weights)."""
+    perm = rng.permutation(E)
+    base = -s * np.log1p(perm.astype(np.float64))
+    g = -np.log(-np.log(rng.random((T, E))))
+    return (base[None, :] + g).astype(np.float32)
+
+
+# ------------------------------------------------------------------ kernels --
+def test_quantize_bytes_match_oracle(pkg, O, torch):
+    from conftest import golden
+    g = golden("quant_cases.npz")
+    rng = np.random.default_rng(1)
+    x = np.concatenate([g["x"].reshape(-1, 32),
+                        (rng.standard_normal((4096, 32)) * 10.0 ** rng.uniform(-5, 3, (4096, 1))).astype(np.float32)])
+    x = np.ascontiguousarray(x)  # one 32-wide column per block
+    q, err = pkg.quantize_q8_1(torch.from_numpy(x).cuda())
+    want, flags = O.quantize(x)
+    assert int(err.item()) == flags == 0
+    assert np.array_equal(q.cpu().numpy().ravel(), want.view(np.uint8).ravel())
+
+
+def test_quantize_invalid_blocks(pkg, O, torch):
+    x = np.ones((2, 64), np.float32)
+    x[0, 3] = np.nan
+    x[1, 40] = 1e-45
+    q, err = pkg.quantize_q8_1(torch.from_numpy(x).cuda())
+    want, flags = O.quantize(x)
+    assert int(err.item()) == flags == 3
+    assert np.array_equal(q.cpu().numpy().ravel(), want.view(np.uint8).ravel())
+
+
+@pytest.mark.parametrize("rows,k,cols", [(512, 2048, 3), (2048, 512, 5), (96, 64, 1)])
+def test_block_dots_bit_exact(pkg, O, torch, rows, k, cols):
+    rng = np.random.default_rng(rows + cols)
+    w = O.synth_q4_0(3, 0, rows % 7, 0, rows, k // 32)
+    x = rng.standard_normal((cols, k)).astype(np.float32)
+    xq, _ = O.quantize(x)
+    out, dots = pkg.q4_linear(torch.from_numpy(w).cuda(), rows, k,
+                              torch.from_numpy(xq.view(np.uint8).reshape(cols, -1).copy()).cuda(), cols,
+                              with_dots=True)
+    assert np.array_equal(dots.cpu().numpy(), O.block_dots(w, xq, rows, k // 32))
+    ref = O.matrix_serial(w, xq, rows, k // 32)
+    got = out.cpu().numpy()
+    assert np.all(np.abs(got - ref) <= 2e-4 + 2e-5 * np.abs(ref))
+
+
+def test_synthesized_weights_match_oracle_generator(pkg, O, torch):
+    desc = pkg.make_desc(max_tokens=1)
+    w = pkg.MoeWeights(desc)
+    w.synthesize(99, 7)
+    torch.cuda.synchronize()
+    for e in (0, 255, 511, 512):
+        got = w.download_expert(e)
+        want = O.synth_expert(99, 7, e)
+        for a, b in zip(got, want):
+            assert np.array_equal(a, b), e
+
+
+def test_upload_download_roundtrip(pkg, O, torch):
+    desc = pkg.make_desc(max_tokens=1)
+    w = pkg.MoeWeights(desc)
+    g, u, d = O.synth_expert(1, 1, 1)
+    w.upload_expert(3, g, u, d)
+    for a, b in zip(w.download_expert(3), (g, u, d)):
+        assert np.array_equal(a, b)
+
+
+# ------------------------------------------------------------------ routing --
+@pytest.mark.parametrize("T,kind", [(1, "normal"), (8, "normal"), (37, "ties"), (300, "normal"),
+                                    (4096, "zipf"), (2500, "nonfinite")])
+def test_route_bit_exact(pkg, O, torch, T, kind):
+    rng = np.random.default_rng(T)
+    if kind == "zipf":
+        logits = zipf_logits(rng, T)
+    else:
+        logits = rng.standard_normal((T, E)).astype(np.float32)
+    if kind == "ties":
+        logits[0, :] = 0.0
+        logits[1, 10] = logits[1, 20] = 7.0
+        logits[2] = np.round(logits[2])
+    if kind == "nonfinite":
+        logits[5, 9] = np.inf
+        logits[77, 0] = np.nan
+    layer = pkg.MoeLayer(pkg.make_desc(max_tokens=T))
+    r = layer.route(torch.from_numpy(logits).cuda())
+    torch.cuda.synchronize()
+    probs, flags = O.router_softmax(logits)
+    ids, w = O.select_routes(probs)
+    grp = O.route_groups(ids, w)
+    assert np.array_equal(f32bits(r["probs"].cpu().numpy()), f32bits(probs))
+    assert np.array_equal(r["ids"].cpu().numpy(), ids)
+    assert np.array_equal(f32bits(r["weights"].cpu().numpy()), f32bits(w))
+    assert np.array_equal(r["offsets"].cpu().numpy(), grp["offsets"])
+    assert np.array_equal(r["token"].cpu().numpy(), grp["token"])
+    assert np.array_equal(r["rank"].cpu().numpy(), grp["rank"])
+    assert layer.read_flags() == flags
+
+
+# -------------------------------------------------------------------- layer --
+class LayerCase:
+    def __init__(self, pkg, O, torch, T, seed, logits_kind="normal", max_tokens=None):
+        self.pkg, self.O, self.T, self.seed = pkg, O, T, seed
+        rng = np.random.default_rng(seed)
+        self.x = rng.standard_normal((T, H)).astype(np.float32)
+        self.logits = zipf_logits(rng, T) if logits_kind == "zipf" else rng.standard_normal((T, E)).astype(np.float32)
+        self.gate_vec = (rng.standard_normal(H) * 0.02).astype(np.float32)
+        self.desc = pkg.make_desc(max_tokens=max_tokens or T)
+        self.weights = pkg.MoeWeights(self.desc)
+        self.weights.synthesize(seed, 0)
+        self.weights.upload_shared_gate(self.gate_vec)
+        self.layer = pkg.MoeLayer(self.desc)
+        self.xd = torch.from_numpy(self.x).cuda()
+        self.ld = torch.from_numpy(self.logits).cuda()
+
+    def oracle(self, tokens=None):
+        O, seed = self.O, self.seed
+        out, ids, w, flags = O.moe_layer(self.x, self.logits, lambda e: O.synth_expert(seed, 0, e),
+                                         O.synth_expert(seed, 0, 512), self.gate_vec, tokens)
+        return out
+
+
+def assert_close(got, want):
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    err = float(np.max(np.abs(got.astype(np.float64) - want)))
+    assert err <= TOL_RMS * rms, f"max|err|={err:.3e} rms={rms:.3e}"
+    return err / rms
+
+
+@pytest.mark.parametrize("T", [1, 8, 3, 33])
+def test_forward_matches_oracle(pkg, O, torch, T):
+    c = LayerCase(pkg, O, torch, T, seed=100 + T)
+    out = torch.zeros(T, H, device="cuda")
+    c.layer.forward(c.weights, c.xd, c.ld, out, accumulate=False)
+    torch.cuda.synchronize()
+    assert c.layer.read_flags() == 0
+    assert_close(out.cpu().numpy(), c.oracle())
+
+
+def test_forward_accumulates_into_residual_in_place(pkg, O, torch):
+    T = 8
+    c = LayerCase(pkg, O, torch, T, seed=7)
+    h = c.xd.clone()
+    c.layer.forward(c.weights, h, c.ld, h, accumulate=True)  # residual += FFN(residual)
+    torch.cuda.synchronize()
+    assert_close(h.cpu().numpy() - c.x, c.oracle())
+
+
+def test_forward_prefill_zipf_sampled_tokens(pkg, O, torch):
+    """Config 3 shape (T=4096, Zipf(1.1) routing) checked on sampled tokens:
+    each token's output depends only on its own routing, so a sample is exact."""
+    T = 4096
+    c = LayerCase(pkg, O, torch, T, seed=3, logits_kind="zipf")
+    out = torch.zeros(T, H, device="cuda")
+    c.layer.forward(c.weights, c.xd, c.ld, out, accumulate=False)
+    torch.cuda.synchronize()
+    assert c.layer.read_flags() == 0
+    sample = np.random.default_rng(0).choice(T, 16, replace=False)
+    assert_close(out.cpu().numpy()[sample], c.oracle(sample))
+
+
+def test_forward_flags_nonfinite_input(pkg, O, torch):
+    T = 4
+    c = LayerCase(pkg, O, torch, T, seed=11)
+    x = c.xd.clone()
+    x[2, 100] = float("nan")
+    out = torch.zeros(T, H, device="cuda")
+    c.layer.forward(c.weights, x, c.ld, out, accumulate=False)
+    assert c.layer.read_flags() & 1
+
+
+def test_forward_rejects_bad_arguments(pkg, O, torch):
+    c = LayerCase(pkg, O, torch, 2, seed=12)
+    out = torch.zeros(2, H, device="cuda")
+    with pytest.raises(ValueError):
+        c.layer.forward(c.weights, c.xd, c.ld, c.xd, accumulate=False)  # overwrite aliasing x
+    big = torch.zeros(3, H, device="cuda")
+    with pytest.raises(ValueError):
+        c.layer.forward(c.weights, big, torch.zeros(3, E, device="cuda"), big.clone(), accumulate=False)
+
+
+def test_forward_in_cuda_graph(pkg, O, torch):
+    T = 8
+    c = LayerCase(pkg, O, torch, T, seed=13)
+    out = torch.zeros(T, H, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        c.layer.forward(c.weights, c.xd, c.ld, out, accumulate=False, stream=s)  # warm-up
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        c.layer.forward(c.weights, c.xd, c.ld, out, accumulate=False, stream=s)
+    out.fill_(123.0)
+    g.replay()
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), c.oracle())
+
+
+# -------------------------------------------------- single-expert fixture --
+def test_gpu_expert_api(pkg, O, torch):
+    g, u, d = O.synth_expert(4, 0, 9)
+    ex = pkg.GpuExpert(g, u, d, max_columns=5)
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((5, H)).astype(np.float32)
+    xq, _ = O.quantize(x)
+    ex.check_quantization(x, xq)
+    bad = xq.copy()
+    bad[0, 0]["qs"][0] ^= 1
+    with pytest.raises(RuntimeError):
+        ex.check_quantization(x, bad)
+    for which, (w, rows, blocks) in {"gate": (g, I, H // 32), "up": (u, I, H // 32)}.items():
+        got = ex.linear(False, which == "up", xq, 5)
+        ref = O.matrix_serial(w, xq, rows, blocks)
+        assert np.all(np.abs(got - ref) <= 2e-4 + 2e-5 * np.abs(ref))
+    y, timing = ex.run(x, 5, repeats=3)
+    want, _ = O.expert_whole(g, u, d, xq)
+    assert_close(y, want)
+    assert timing["resident_ms"] > 0
