@@ -311,11 +311,14 @@ def run_ours(args, cfg):
     out_host = torch.empty(U, T, H).pin_memory()
     stream = torch.cuda.Stream(device=dev)
 
+    # Each layer reads the step's (already normalised) FFN input x and adds its
+    # output into the residual h: h = x + sum_l FFN_l(x).  Feeding h back as
+    # the next layer's input would need the model's RMS norm between layers.
     def step_device(s):
         h.copy_(x_dev)
         for u in range(U):
             for l in range(L):
-                layer.forward(weights[l], h[u], lg_dev[u, l], h[u], accumulate=True, stream=s)
+                layer.forward(weights[l], x_dev[u], lg_dev[u, l], h[u], accumulate=True, stream=s)
 
     # warm-up (eager), then capture one step into a CUDA graph
     with torch.cuda.stream(stream):
@@ -326,8 +329,9 @@ def run_ours(args, cfg):
     with torch.cuda.graph(graph, stream=stream):
         step_device(stream)
     torch.cuda.synchronize()
-    if layer.read_flags():
-        raise RuntimeError("numeric flags raised during warm-up")
+    flags = layer.read_flags()
+    if flags:
+        raise RuntimeError(f"numeric flags {flags} raised during warm-up")
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             graph.replay()
@@ -371,11 +375,17 @@ def run_ours(args, cfg):
     nprof = min(args.steps, 4)
     evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(U * L)] for _ in range(nprof)]
     with torch.cuda.stream(stream):
+        for ks in evs:              # torch creates the CUDA event on first record
+            for trio in ks:
+                for e in trio:
+                    e.record(stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
         for k in range(nprof):
             h.copy_(x_dev)
             for u in range(U):
                 for l in range(L):
-                    layer.forward_profiled(weights[l], h[u], lg_dev[u, l], h[u], evs[k][u * L + l], stream=stream)
+                    layer.forward_profiled(weights[l], x_dev[u], lg_dev[u, l], h[u], evs[k][u * L + l], stream=stream)
     torch.cuda.synchronize()
     gu = [e[0].elapsed_time(e[1]) for ks in evs for e in ks]
     dn = [e[1].elapsed_time(e[2]) for ks in evs for e in ks]

@@ -27,6 +27,18 @@ struct Q8Planar {
     float2 *scales;
 };
 
+constexpr int kGemvTile = 8;     // pairs per work tile
+
+// Work tile: up to kGemvTile consecutive pairs (one expert) of the sorted
+// assignment list, with their tokens and router weights inline so a kernel
+// needs a single 80-byte load per tile.
+struct __align__(16) TileRec {
+    int e, p0, n, pad;
+    int tok[kGemvTile];
+    float w[kGemvTile];
+};
+static_assert(sizeof(TileRec) == 80, "tile record is five 16-byte vectors");
+
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
 

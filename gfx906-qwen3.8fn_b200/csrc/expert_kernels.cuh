@@ -133,7 +133,7 @@ struct GroupParams {
     ExpertLayout layout;
     Q8Planar x;                 // quantised tokens [T][H]
     Q8Planar mid;               // middle per pair [P][I]
-    const int4 *tiles;          // {expert, first pair, count, 0}
+    const TileRec *tiles;
     const int *num_tiles;
     const int32_t *pair_token;
     const float *pair_weight;
@@ -142,7 +142,6 @@ struct GroupParams {
 };
 
 constexpr int kGemvThreads = 256;
-constexpr int kGemvTile = 8;     // pairs per tile
 
 // Gate/up for one (tile, 32-row slab): warp w owns gate rows and up rows
 // slab*32 + 4w .. +3; lane l owns blocks l, l+32, ...  Results feed SiLU*up
@@ -153,7 +152,7 @@ __global__ void __launch_bounds__(kGemvThreads)
 gate_up_kernel(GroupParams p) {
     const int H = p.layout.hidden, I = p.layout.inter;
     const int nb = H / 32, slabs = I / 32;
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     int4 *sx = reinterpret_cast<int4 *>(smem);                          // [NT][H/16]
     float2 *ss = reinterpret_cast<float2 *>(smem + NT * H);             // [NT][nb]
     float *smid = reinterpret_cast<float *>(smem + NT * H + NT * nb * 8);  // [NT][32]
@@ -161,8 +160,8 @@ gate_up_kernel(GroupParams p) {
     const int total = *p.num_tiles * slabs;
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
         const int tile = item / slabs, slab = item % slabs;
-        const int4 td = p.tiles[tile];
-        const int e = td.x, p0 = td.y, n = td.z;
+        const TileRec &td = p.tiles[tile];
+        const int e = td.e, p0 = td.p0, n = td.n;
         __syncthreads();
         for (int idx = threadIdx.x; idx < n * (H / 16); idx += kGemvThreads) {
             const int j = idx / (H / 16), v = idx % (H / 16);
@@ -255,7 +254,7 @@ __global__ void __launch_bounds__(kGemvThreads)
 down_kernel(GroupParams p) {
     const int H = p.layout.hidden, I = p.layout.inter;
     const int nbd = I / 32, dslabs = H / 64;
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     int4 *sm = reinterpret_cast<int4 *>(smem);                           // [NT][I/16]
     float2 *ss = reinterpret_cast<float2 *>(smem + NT * I);              // [NT][nbd]
     int *stok = reinterpret_cast<int *>(smem + NT * I + NT * nbd * 8);   // [NT]
@@ -264,8 +263,8 @@ down_kernel(GroupParams p) {
     const int total = *p.num_tiles * dslabs;
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
         const int tile = item / dslabs, ds = item % dslabs;
-        const int4 td = p.tiles[tile];
-        const int e = td.x, p0 = td.y, n = td.z;
+        const TileRec &td = p.tiles[tile];
+        const int e = td.e, p0 = td.p0, n = td.n;
         __syncthreads();
         for (int idx = threadIdx.x; idx < n * (I / 16); idx += kGemvThreads) {
             const int j = idx / (I / 16), v = idx % (I / 16);

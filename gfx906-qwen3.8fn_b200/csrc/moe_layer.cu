@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "expert_kernels.cuh"
 #include "route_kernels.cuh"
+#include "stream_kernels.cuh"
 #include "tc_kernels.cuh"
 
 using namespace qmoe;
@@ -113,9 +114,11 @@ struct moe_layer_s {
     int32_t *ids, *base, *counts, *offsets, *pair_token, *pair_rank;
     float *weights, *pair_weight;
     uint32_t *masks;
-    int4 *tiles;
+    TileRec *tiles;
+    int32_t *tile_off;
     int *num_tiles;
     int *error;
+    int gu_stages, dn_stages;   // shared-memory ring depth of the streaming kernels (0: not used)
     TcWorkspace tc;
 };
 
@@ -130,11 +133,24 @@ int tiles_bound(int tokens, int has_shared) {
 size_t gate_up_smem(int H) { return static_cast<size_t>(kGemvTile) * H + kGemvTile * (H / 32) * 8 + kGemvTile * 32 * 4; }
 size_t down_smem(int I) { return static_cast<size_t>(kGemvTile) * I + kGemvTile * (I / 32) * 8 + 2 * kGemvTile * 4; }
 
-int configure_kernels(int H, int I) {
+size_t stream_gu_smem(int H, int stages) { return 128 + 2 * kGemvTile * 32 * 4 + size_t(stages) * GuStage(H).bytes; }
+size_t stream_dn_smem(int I, int stages) { return 128 + size_t(stages) * DnStage(I).bytes; }
+
+int configure_kernels(moe_layer_s *h, int H, int I) {
     MOE_CUDA(cudaFuncSetAttribute(gate_up_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(gate_up_smem(H))));
     MOE_CUDA(cudaFuncSetAttribute(down_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(down_smem(I))));
+    // The streaming kernels need at least two stages in shared memory.
+    h->gu_stages = stream_stages(GuStage(H).bytes + 2048, 2);
+    h->dn_stages = stream_stages(DnStage(I).bytes, kMaxStages);
+    if (h->gu_stages < 2 || h->dn_stages < 2) h->gu_stages = h->dn_stages = 0;
+    if (h->gu_stages) {
+        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(stream_gu_smem(H, h->gu_stages))));
+        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(stream_dn_smem(I, h->dn_stages))));
+    }
     return MOE_OK;
 }
 
@@ -158,6 +174,32 @@ GroupParams group_params(moe_layer_s *h, const moe_weights_s *w, float *out) {
 int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_tiles, cudaStream_t s,
                    void *const *events = nullptr) {
     const ExpertLayout &L = w->layout;
+    if (h->gu_stages) {
+        StreamParams sp;
+        sp.weights = w->base;
+        sp.layout = L;
+        sp.x = h->xq;
+        sp.mid = h->mid;
+        sp.tiles = h->tiles;
+        sp.num_tiles = h->num_tiles;
+        sp.out = out;
+        sp.error = h->error;
+        const int gu_items = max_tiles * (L.inter / kGuRows), dn_items = max_tiles * (L.hidden / kDnRows);
+        if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[0]), s));
+        sp.stages = h->gu_stages;
+        sp.stage_bytes = GuStage(L.hidden).bytes;
+        stream_gate_up_kernel<<<std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
+                                stream_gu_smem(L.hidden, sp.stages), s>>>(sp);
+        MOE_CUDA(cudaGetLastError());
+        if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
+        sp.stages = h->dn_stages;
+        sp.stage_bytes = DnStage(L.inter).bytes;
+        stream_down_kernel<<<std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
+                             stream_dn_smem(L.inter, sp.stages), s>>>(sp);
+        MOE_CUDA(cudaGetLastError());
+        if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[2]), s));
+        return MOE_OK;
+    }
     GroupParams g = group_params(h, w, out);
     const int slabs = L.inter / 32, dslabs = L.hidden / 64;
     const int gu_grid = std::max(1, std::min(max_tiles * slabs, h->sms * 8));
@@ -208,6 +250,9 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     sp.has_shared = rp.gate_vec != nullptr;
     sp.offsets = h->offsets;
     sp.tiles = h->tiles;
+    sp.tile_off = h->tile_off;
+    sp.pair_token = h->pair_token;
+    sp.pair_weight = h->pair_weight;
     sp.num_tiles = h->num_tiles;
     sp.max_tiles = h->tiles_max;
     sp.error = h->error;
@@ -222,6 +267,9 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     cp.pair_token = h->pair_token;
     cp.pair_rank = h->pair_rank;
     cp.pair_weight = h->pair_weight;
+    cp.tiles = h->tiles;
+    cp.tile_off = h->tile_off;
+    cp.max_tiles = h->tiles_max;
     route_scatter_kernel<<<dim3(chunks, kRouterExperts / 256), 256, 0, s>>>(cp);
     MOE_CUDA(cudaGetLastError());
     return MOE_OK;
@@ -388,7 +436,8 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
         h->pair_token = a.take<int32_t>(h->pairs_max);
         h->pair_rank = a.take<int32_t>(h->pairs_max);
         h->pair_weight = a.take<float>(h->pairs_max);
-        h->tiles = a.take<int4>(h->tiles_max);
+        h->tiles = a.take<TileRec>(h->tiles_max);
+        h->tile_off = a.take<int32_t>(kRouterExperts);
         h->num_tiles = a.take<int>(1);
         h->error = a.take<int>(1);
         tc_workspace_take(h->tc, a, T, H, I);
@@ -399,7 +448,7 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
             cudaMemset(a.base, 0, bytes);
         }
     }
-    if (const int st = configure_kernels(H, I)) { cudaFree(h->arena.base); delete h; return st; }
+    if (const int st = configure_kernels(h, H, I)) { cudaFree(h->arena.base); delete h; return st; }
     if (const int st = tc_configure()) { cudaFree(h->arena.base); delete h; return st; }
     *out = h;
     return MOE_OK;

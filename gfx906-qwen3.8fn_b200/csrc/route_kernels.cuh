@@ -232,7 +232,10 @@ struct ScanParams {
     int tokens, tile;       // tile = tokens per work tile
     int has_shared;
     int32_t *offsets;       // [514]: 512 routed groups, shared group, end
-    int4 *tiles;            // {expert, first pair, count, 0}
+    TileRec *tiles;
+    int32_t *tile_off;      // [512]: first tile of each routed expert
+    const int32_t *pair_token;   // shared-expert pairs (written by route_topk)
+    const float *pair_weight;
     int *num_tiles;
     int max_tiles;
     int *error;
@@ -253,19 +256,34 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
     const int ntiles = (run + p.tile - 1) / p.tile;
     int tiles_total = 0;
     const int toff = block_exclusive_scan_512(ntiles, &tiles_total);
+    p.tile_off[e] = toff;
     for (int i = 0; i < ntiles; ++i) {
         const int idx = toff + i;
-        if (idx < p.max_tiles)
-            p.tiles[idx] = make_int4(e, off + i * p.tile, min(p.tile, run - i * p.tile), 0);
+        if (idx < p.max_tiles) {
+            TileRec &t = p.tiles[idx];
+            t.e = e;
+            t.p0 = off + i * p.tile;
+            t.n = min(p.tile, run - i * p.tile);
+            t.pad = 0;
+        }
     }
     int shared_tiles = 0;
     if (p.has_shared) {
         shared_tiles = (p.tokens + p.tile - 1) / p.tile;
         for (int i = e; i < shared_tiles; i += 512) {
             const int idx = tiles_total + i;
-            if (idx < p.max_tiles)
-                p.tiles[idx] = make_int4(kRouterExperts, total + i * p.tile,
-                                         min(p.tile, p.tokens - i * p.tile), 0);
+            if (idx < p.max_tiles) {
+                TileRec &t = p.tiles[idx];
+                t.e = kRouterExperts;
+                t.p0 = total + i * p.tile;
+                t.n = min(p.tile, p.tokens - i * p.tile);
+                t.pad = 0;
+                for (int j = 0; j < kGemvTile; ++j) {
+                    const bool live = j < t.n;
+                    t.tok[j] = live ? p.pair_token[p.tokens * kTopK + i * p.tile + j] : 0;
+                    t.w[j] = live ? p.pair_weight[p.tokens * kTopK + i * p.tile + j] : 0.0f;
+                }
+            }
         }
     }
     if (e == 0) {
@@ -284,6 +302,9 @@ struct ScatterParams {
     int32_t *pair_token;
     int32_t *pair_rank;
     float *pair_weight;
+    TileRec *tiles;
+    const int32_t *tile_off;
+    int max_tiles;
 };
 
 // Thread per (chunk, expert): stable placement by token order within the chunk.
@@ -301,20 +322,38 @@ __global__ void __launch_bounds__(256) route_scatter_kernel(ScatterParams p) {
 #pragma unroll
         for (int k = 0; k < kTopK; ++k)
             if (p.ids[t * kTopK + k] == e) r = k;
+        const float w = p.weights[t * kTopK + r];
         p.pair_token[pos] = t;
         if (p.pair_rank) p.pair_rank[pos] = r;
-        p.pair_weight[pos] = p.weights[t * kTopK + r];
+        p.pair_weight[pos] = w;
+        if (p.tiles) {
+            const int local = pos - p.offsets[e];
+            const int tile = p.tile_off[e] + local / kGemvTile;
+            if (tile < p.max_tiles) {
+                p.tiles[tile].tok[local % kGemvTile] = t;
+                p.tiles[tile].w[local % kGemvTile] = w;
+            }
+        }
         ++pos;
     }
 }
 
 // Single-expert fixture routing: pair t = token t of expert 0 with weight 1.
-__global__ void identity_route_kernel(int tokens, int tile, int4 *tiles, int *num_tiles,
+__global__ void identity_route_kernel(int tokens, int tile, TileRec *tiles, int *num_tiles,
                                       int32_t *pair_token, float *pair_weight) {
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < tokens; t += gridDim.x * blockDim.x) {
         pair_token[t] = t;
         pair_weight[t] = 1.0f;
-        if (t % tile == 0) tiles[t / tile] = make_int4(0, t, min(tile, tokens - t), 0);
+        TileRec &r = tiles[t / tile];
+        r.tok[t % tile] = t;
+        r.w[t % tile] = 1.0f;
+        if (t % tile == 0) {
+            r.e = 0;
+            r.p0 = t;
+            r.n = min(tile, tokens - t);
+            r.pad = 0;
+            for (int j = r.n; j < tile; ++j) { r.tok[j] = 0; r.w[j] = 0.0f; }
+        }
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) *num_tiles = (tokens + tile - 1) / tile;
 }

@@ -54,7 +54,8 @@ def test_quantize_bytes_match_oracle(pkg, O, torch):
 def test_quantize_invalid_blocks(pkg, O, torch):
     x = np.ones((2, 64), np.float32)
     x[0, 3] = np.nan
-    x[1, 40] = 1e-45
+    x[1, 32:] = 0.0
+    x[1, 40] = 1e-45   # whole block's original FP32 scale underflows to zero
     q, err = pkg.quantize_q8_1(torch.from_numpy(x).cuda())
     want, flags = O.quantize(x)
     assert int(err.item()) == flags == 3
