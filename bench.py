@@ -424,7 +424,7 @@ def run_ours(args, cfg):
                      "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                      "bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "down_launch_ms": dn_ms,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650 GB/s"},
-        "gpu_launches": args.steps * U * L * 7,
+        "gpu_launches": args.steps * U * L * (3 if T <= 32 else 7),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

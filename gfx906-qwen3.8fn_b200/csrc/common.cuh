@@ -27,7 +27,7 @@ struct Q8Planar {
     float2 *scales;
 };
 
-constexpr int kGemvTile = 8;     // pairs per work tile
+constexpr int kGemvTile = 4;     // pairs per work tile
 
 // Work tile: up to kGemvTile consecutive pairs (one expert) of the sorted
 // assignment list, with their tokens and router weights inline so a kernel
@@ -37,7 +37,7 @@ struct __align__(16) TileRec {
     int tok[kGemvTile];
     float w[kGemvTile];
 };
-static_assert(sizeof(TileRec) == 80, "tile record is five 16-byte vectors");
+static_assert(sizeof(TileRec) % 16 == 0, "tile record is whole 16-byte vectors");
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
@@ -65,10 +65,32 @@ __device__ __forceinline__ int block_dot(const uint4 w, const int4 xlo, const in
     return acc;
 }
 
+// Exact int -> float for |v| < 2^22: the integer added to the bit pattern of
+// 1.5 * 2^23 lands in the mantissa, and subtracting 1.5 * 2^23 is exact.
+// (An integer add and a float add instead of the quarter-rate I2F.)
+__device__ __forceinline__ float small_int_to_float(int v) {
+    return __int_as_float(v + 0x4b400000) - 12582912.0f;
+}
+
 // One block's contribution with the reference's Q4_0 correction
-// d4*(dot*d8 - 8*s8) (src/quant.cpp:88-102), as two FMAs.
+// d4*(dot*d8 - 8*s8) (src/quant.cpp:88-102), as two FMAs.  |dot| <= 32*15*128.
 __device__ __forceinline__ float block_term(int dot, float d4, float d8, float s8x8, float acc) {
-    return fmaf(d4, fmaf(static_cast<float>(dot), d8, -s8x8), acc);
+    return fmaf(d4, fmaf(small_int_to_float(dot), d8, -s8x8), acc);
+}
+
+// Block dot as two independent dp4a chains.  High nibbles are masked in place
+// (byte values 16*q) and the chain is shifted once: each partial is a multiple
+// of 16 and |partial| <= 16*240*128 < 2^31, so the result equals block_dot.
+__device__ __forceinline__ int block_dot2(const uint4 w, const int4 xlo, const int4 xhi) {
+    int a = dp4a_us(w.x & 0x0f0f0f0fu, xlo.x, 0);
+    int b = dp4a_us(w.x & 0xf0f0f0f0u, xhi.x, 0);
+    a = dp4a_us(w.y & 0x0f0f0f0fu, xlo.y, a);
+    b = dp4a_us(w.y & 0xf0f0f0f0u, xhi.y, b);
+    a = dp4a_us(w.z & 0x0f0f0f0fu, xlo.z, a);
+    b = dp4a_us(w.z & 0xf0f0f0f0u, xhi.z, b);
+    a = dp4a_us(w.w & 0x0f0f0f0fu, xlo.w, a);
+    b = dp4a_us(w.w & 0xf0f0f0f0u, xhi.w, b);
+    return a + (b >> 4);
 }
 
 __device__ __forceinline__ void report(int flags, int *error) {

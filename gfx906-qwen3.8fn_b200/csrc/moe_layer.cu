@@ -134,6 +134,7 @@ size_t gate_up_smem(int H) { return static_cast<size_t>(kGemvTile) * H + kGemvTi
 size_t down_smem(int I) { return static_cast<size_t>(kGemvTile) * I + kGemvTile * (I / 32) * 8 + 2 * kGemvTile * 4; }
 
 size_t stream_gu_smem(int H, int stages) { return 128 + 2 * kGemvTile * 32 * 4 + size_t(stages) * GuStage(H).bytes; }
+constexpr int kGuStagesMax = 3;
 size_t stream_dn_smem(int I, int stages) { return 128 + size_t(stages) * DnStage(I).bytes; }
 
 int configure_kernels(moe_layer_s *h, int H, int I) {
@@ -142,8 +143,8 @@ int configure_kernels(moe_layer_s *h, int H, int I) {
     MOE_CUDA(cudaFuncSetAttribute(down_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(down_smem(I))));
     // The streaming kernels need at least two stages in shared memory.
-    h->gu_stages = stream_stages(GuStage(H).bytes + 2048, 2);
-    h->dn_stages = stream_stages(DnStage(I).bytes, kMaxStages);
+    h->gu_stages = stream_stages(GuStage(H).bytes + 256, kGuStagesMax);
+    h->dn_stages = stream_stages(DnStage(I).bytes, 5);
     if (h->gu_stages < 2 || h->dn_stages < 2) h->gu_stages = h->dn_stages = 0;
     if (h->gu_stages) {
         MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -239,6 +240,18 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     rp.pair_weight = h->pair_weight;
     rp.pair_rank = h->pair_rank;
     rp.error = h->error;
+    if (T <= kChunk) {   // one chunk: quantise + route + group + tiles in one launch
+        SmallRouteParams sr;
+        sr.r = rp;
+        sr.xq = x ? h->xq : Q8Planar{nullptr, nullptr};
+        sr.offsets = h->offsets;
+        sr.tiles = h->tiles;
+        sr.tile_off = h->tile_off;
+        sr.num_tiles = h->num_tiles;
+        sr.max_tiles = h->tiles_max;
+        route_small_kernel<<<1, 512, 0, s>>>(sr);
+        return cuda_status(cudaGetLastError(), "route_small_kernel");
+    }
     route_topk_kernel<<<chunks, kRouteThreads, 0, s>>>(rp);
     MOE_CUDA(cudaGetLastError());
     route_chunk_prefix_kernel<<<kRouterExperts / 32, 1024, 0, s>>>(h->masks, chunks, h->base, h->counts);
@@ -515,8 +528,9 @@ int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const f
     MOE_CUDA(guard.status);
     auto s = static_cast<cudaStream_t>(stream);
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
-    if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s))
-        return st;
+    if (tokens > kChunk)   // small batches quantise inside the fused routing kernel
+        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s))
+            return st;
     if (const int st = launch_route(h, w, x, logits, tokens, nullptr, s)) return st;
     return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events);
 }

@@ -6,7 +6,11 @@
 namespace qmoe {
 
 constexpr int kFlagTimeout = 4;      // a bounded device wait gave up (see MOE_FLAG_TIMEOUT)
-constexpr uint32_t kWaitLimit = 1u << 26;  // try_wait polls before a wait is declared failed
+// Each try_wait may park the thread for up to kSuspendNs (it wakes as soon as
+// the phase completes); after kWaitLimit unsuccessful tries (>= ~2 s) the wait
+// is declared failed.
+constexpr uint32_t kSuspendNs = 1000000u;
+constexpr uint32_t kWaitLimit = 2048u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -33,10 +37,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -58,6 +62,10 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
 // Barrier among `count` threads (a multiple of 32) on hardware barrier `id` (1..15).

@@ -55,17 +55,10 @@ struct RouteParams {
     int *error;
 };
 
-// One CTA per chunk of 32 tokens; one warp per token.
-__global__ void __launch_bounds__(kRouteThreads)
-route_topk_kernel(RouteParams p) {
-    __shared__ uint32_t smask[kRouterExperts];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int e = threadIdx.x; e < kRouterExperts; e += kRouteThreads) smask[e] = 0u;
-    __syncthreads();
-    const int chunk = blockIdx.x;
-    for (int j = warp; j < kChunk; j += kRouteThreads / 32) {
-        const int t = chunk * kChunk + j;
-        if (t >= p.tokens) break;
+// Route token t with one warp: softmax, top-10, renormalised weights, the
+// chunk mask bit j in smask[expert], and the shared-expert gate.
+__device__ __forceinline__ void route_one_token(const RouteParams &p, int t, int j, uint32_t *smask, int lane) {
+    {
         const float *row = p.logits + static_cast<size_t>(t) * kRouterExperts;
         int flags = 0;
         float w[16];
@@ -168,6 +161,21 @@ route_topk_kernel(RouteParams p) {
                 report(f, p.error);
             }
         }
+    }
+}
+
+// One CTA per chunk of 32 tokens; one warp per token.
+__global__ void __launch_bounds__(kRouteThreads)
+route_topk_kernel(RouteParams p) {
+    __shared__ uint32_t smask[kRouterExperts];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int e = threadIdx.x; e < kRouterExperts; e += kRouteThreads) smask[e] = 0u;
+    __syncthreads();
+    const int chunk = blockIdx.x;
+    for (int j = warp; j < kChunk; j += kRouteThreads / 32) {
+        const int t = chunk * kChunk + j;
+        if (t >= p.tokens) break;
+        route_one_token(p, t, j, smask, lane);
     }
     __syncthreads();
     uint32_t *out = p.masks + static_cast<size_t>(chunk) * kRouterExperts;
@@ -356,6 +364,99 @@ __global__ void identity_route_kernel(int tokens, int tile, TileRec *tiles, int 
         }
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) *num_tiles = (tokens + tile - 1) / tile;
+}
+
+// ---------------------------------------------------------------------------
+// Decode-size batches (T <= 32, one routing chunk): Q8_1 quantisation of x,
+// routing, grouping and the tile list in ONE CTA of 512 threads, replacing the
+// six launches of the general path.  Same arithmetic, same outputs.
+struct SmallRouteParams {
+    RouteParams r;
+    Q8Planar xq;            // quantised x output
+    int32_t *offsets;       // [514]
+    TileRec *tiles;
+    int32_t *tile_off;
+    int *num_tiles;
+    int max_tiles;
+};
+
+__global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
+    const RouteParams &p = sp.r;
+    __shared__ uint32_t smask[kRouterExperts];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, e = threadIdx.x;
+    const int T = p.tokens, H = p.hidden;
+    smask[e] = 0u;
+    // quantise x: one warp per 32-value block
+    for (int b = warp; p.x && sp.xq.codes && b < T * (H / 32); b += 16) {
+        const Q8Lane q = quantize_lane(p.x[static_cast<size_t>(b) * 32 + lane]);
+        sp.xq.codes[static_cast<size_t>(b) * 32 + lane] = q.code;
+        if (lane == 0) {
+            sp.xq.scales[b] = make_float2(h2f(q.d), h2f(q.s));
+            report(q.flags, p.error);
+        }
+    }
+    __syncthreads();
+    for (int t = warp; t < T; t += 16) route_one_token(p, t, t, smask, lane);
+    __syncthreads();   // ids/weights (global) and smask complete
+    const uint32_t mask = smask[e];
+    const int count = __popc(mask);
+    int total = 0;
+    const int off = block_exclusive_scan_512(count, &total);
+    sp.offsets[e] = off;
+    if (e == kRouterExperts - 1) {
+        sp.offsets[kRouterExperts] = total;
+        sp.offsets[kRouterExperts + 1] = total + (p.gate_vec ? T : 0);
+    }
+    const int ntiles = (count + kGemvTile - 1) / kGemvTile;
+    int tiles_total = 0;
+    const int toff = block_exclusive_scan_512(ntiles, &tiles_total);
+    sp.tile_off[e] = toff;
+    int pos = 0;
+    for (uint32_t m = mask; m; m &= m - 1u, ++pos) {
+        const int t = __ffs(m) - 1;
+        int r = 0;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k)
+            if (p.ids[t * kTopK + k] == e) r = k;
+        const float w = p.weights[t * kTopK + r];
+        const int pair = off + pos;
+        p.pair_token[pair] = t;
+        if (p.pair_rank) p.pair_rank[pair] = r;
+        p.pair_weight[pair] = w;
+        const int tile = toff + pos / kGemvTile, slot = pos % kGemvTile;
+        if (tile < sp.max_tiles) {
+            TileRec &rec = sp.tiles[tile];
+            if (slot == 0) {
+                rec.e = e;
+                rec.p0 = pair;
+                rec.n = min(kGemvTile, count - pos);
+                rec.pad = 0;
+            }
+            rec.tok[slot] = t;
+            rec.w[slot] = w;
+        }
+    }
+    int shared_tiles = 0;
+    if (p.gate_vec) {
+        shared_tiles = (T + kGemvTile - 1) / kGemvTile;
+        if (e < shared_tiles && tiles_total + e < sp.max_tiles) {
+            TileRec &rec = sp.tiles[tiles_total + e];
+            rec.e = kRouterExperts;
+            rec.p0 = total + e * kGemvTile;
+            rec.n = min(kGemvTile, T - e * kGemvTile);
+            rec.pad = 0;
+            for (int j = 0; j < kGemvTile; ++j) {
+                const bool live = j < rec.n;
+                rec.tok[j] = live ? p.pair_token[T * kTopK + e * kGemvTile + j] : 0;
+                rec.w[j] = live ? p.pair_weight[T * kTopK + e * kGemvTile + j] : 0.0f;
+            }
+        }
+    }
+    if (e == 0) {
+        int n = tiles_total + shared_tiles;
+        if (n > sp.max_tiles) { atomicOr(p.error, kFlagArithmetic); n = sp.max_tiles; }
+        *sp.num_tiles = n;
+    }
 }
 
 }  // namespace qmoe

@@ -1,11 +1,17 @@
 // stream_kernels.cuh -- persistent weight-streaming expert kernels (decode and
 // small groups).  One CTA per SM: warp 0 is the producer, which streams each
-// work item's weight slab, activation rows and scales into a ring of
-// shared-memory stages with cp.async.bulk (completion counted on an mbarrier);
-// warps 1..8 are consumers that run the u4 x s8 dp4a dots out of shared
-// memory and release the stage on an "empty" mbarrier.  Every SM keeps one to
-// two ~90 KB stages in flight, so HBM latency is covered by bytes in flight
-// rather than by resident warps.
+// work item's weights into a ring of shared-memory stages with cp.async.bulk
+// (completion counted on an mbarrier); warps 1..8 are consumers that run the
+// u4 x s8 dp4a dots out of shared memory and release each stage on an
+// "empty" mbarrier.  Up to two gate/up stages (72 KB each) or four down
+// stages (~40 KB each) are in flight per SM while a third is consumed, so HBM
+// latency is covered by bytes in flight rather than by resident warps.
+//
+// Work is coarse per warp on purpose: a consumer lane handles 16 (gate/up)
+// or 8 (down) block-rows per stage, so the fixed per-stage work (reductions,
+// SiLU, barriers) stays small next to the dot products.  Activation rows are
+// read through L1 (prefetched before the weights arrive).  The per-item body
+// is compiled once per tile size n = 1..4.
 #pragma once
 #include "common.cuh"
 #include "expert_kernels.cuh"
@@ -14,10 +20,11 @@
 namespace qmoe {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kStreamThreads = 32 * (kConsumerWarps + 1);
+constexpr int kConsumerThreads = 32 * kConsumerWarps;
+constexpr int kStreamThreads = 32 + kConsumerThreads;
 constexpr int kGuRows = 32;    // gate rows and up rows per item: one Q8_1 middle block
 constexpr int kDnRows = 128;   // down rows per item
-constexpr int kMaxStages = 4;
+constexpr int kMaxStages = 8;  // ring slots (two mbarriers each in the first 128 bytes)
 
 struct StreamParams {
     const uint8_t *weights;
@@ -31,9 +38,9 @@ struct StreamParams {
     uint32_t stage_bytes;
 };
 
-// ---- stage layouts -------------------------------------------------------
+// ---- stage layouts (meta, then codes, then half scales) --------------------
 struct GuStage {
-    uint32_t meta, gcodes, ucodes, gsc, usc, xcodes, xsc, bytes;
+    uint32_t meta, gcodes, ucodes, gsc, usc, bytes;
     __host__ __device__ GuStage(int H) {
         const uint32_t nb = H / 32;
         meta = 0;
@@ -41,9 +48,7 @@ struct GuStage {
         ucodes = gcodes + kGuRows * nb * 16;
         gsc = ucodes + kGuRows * nb * 16;
         usc = gsc + kGuRows * nb * 2;
-        xcodes = usc + kGuRows * nb * 2;
-        xsc = xcodes + kGemvTile * H;
-        bytes = xsc + kGemvTile * nb * 8;
+        bytes = usc + kGuRows * nb * 2;
         bytes = (bytes + 127) & ~127u;
     }
 };
@@ -67,12 +72,12 @@ __device__ __forceinline__ TileRec load_tile(const TileRec *t) {
     const int4 *s = reinterpret_cast<const int4 *>(t);
     int4 *d = reinterpret_cast<int4 *>(&r);
 #pragma unroll
-    for (int i = 0; i < 5; ++i) d[i] = __ldg(s + i);
+    for (int i = 0; i < static_cast<int>(sizeof(TileRec) / 16); ++i) d[i] = __ldg(s + i);
     return r;
 }
 
-// Common producer loop: `issue(item, stage_ptr, bar, rec)` enqueues the bulk
-// copies of one item and returns their byte count.
+// Producer loop (one thread).  `issue(item, stage, bar, rec)` arms `bar` with
+// the byte count and enqueues the bulk copies of one item.
 template <class Issue>
 __device__ __forceinline__ void stream_producer(const StreamParams &p, uint8_t *stages, uint64_t *full,
                                                 uint64_t *empty, int total, int slabs, Issue issue) {
@@ -87,16 +92,85 @@ __device__ __forceinline__ void stream_producer(const StreamParams &p, uint8_t *
         const int s = i % p.stages;
         if (i >= p.stages && !mbar_wait(&empty[s], ((i / p.stages) & 1) ^ 1, p.error)) break;
         uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
-        *reinterpret_cast<TileRec *>(st) = rec;        // meta, published by the arrive below
+        *reinterpret_cast<TileRec *>(st) = rec;        // meta, published by the arrive in issue()
         issue(item, st, &full[s], rec);
     }
     // Keep the CTA alive until every issued copy has landed.
-    const int issued = i;
-    for (int k = issued - p.stages > 0 ? issued - p.stages : 0; k < issued; ++k)
+    for (int k = i - p.stages > 0 ? i - p.stages : 0; k < i; ++k)
         mbar_wait(&full[k % p.stages], (k / p.stages) & 1, p.error);
 }
 
+__device__ __forceinline__ void init_ring(uint64_t *full, uint64_t *empty, int stages) {
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
+        mbar_fence_init();
+    }
+    __syncthreads();
+}
+
 // ---- gate/up + SiLU*up + Q8_1 middle ---------------------------------------
+// Consumer warp cw owns gate rows and up rows 4cw..4cw+3 of the slab; lane l
+// owns blocks l, l+32, ...
+template <int N>
+__device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_t *st, const GuStage &L,
+                                             const int4 *const *xr, const float2 *const *sr, int cw, int lane,
+                                             uint64_t *empty_bar, float *mid) {
+    const int nb = p.layout.hidden / 32;
+    const uint4 *gc = reinterpret_cast<const uint4 *>(st + L.gcodes);
+    const uint4 *uc = reinterpret_cast<const uint4 *>(st + L.ucodes);
+    const uint16_t *gs = reinterpret_cast<const uint16_t *>(st + L.gsc);
+    const uint16_t *us = reinterpret_cast<const uint16_t *>(st + L.usc);
+    float acc[8][N];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int j = 0; j < N; ++j) acc[r][j] = 0.0f;
+    for (int b = lane; b < nb; b += 32) {
+        uint4 wc[8];
+        float d4[8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int blk = (cw * 4 + r) * nb + b;
+            wc[r] = gc[blk];
+            wc[4 + r] = uc[blk];
+            d4[r] = h2f(gs[blk]);
+            d4[4 + r] = h2f(us[blk]);
+        }
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            const int4 lo = __ldg(xr[j] + 2 * b), hi = __ldg(xr[j] + 2 * b + 1);
+            const float2 sc = __ldg(sr[j] + b);
+            const float s8x8 = 8.0f * sc.y;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) acc[r][j] = block_term(block_dot2(wc[r], lo, hi), d4[r], sc.x, s8x8, acc[r][j]);
+        }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);   // slab fully read by this warp
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int j = 0; j < N; ++j) acc[r][j] = warp_sum(acc[r][j]);
+    // SiLU(gate) * up with the reference's sanitisation (session_ops.hip:250-262):
+    // lane r < 4 finishes row 4cw + r.
+    if (lane < 4) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            float g = acc[0][j], u = acc[4][j];
+#pragma unroll
+            for (int r = 1; r < 4; ++r)
+                if (lane == r) { g = acc[r][j]; u = acc[4 + r][j]; }
+            int flags = 0;
+            g = operand(g, flags);
+            u = operand(u, flags);
+            const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), flags);
+            const float v = arithmetic(__fmul_rn(act, u), flags);
+            mid[j * 32 + cw * 4 + lane] = flags ? 0.0f : v;
+            report(flags, p.error);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kStreamThreads, 1)
 stream_gate_up_kernel(StreamParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -107,11 +181,7 @@ stream_gate_up_kernel(StreamParams p) {
     float *smid = reinterpret_cast<float *>(smem + 128);                 // [2][kGemvTile][32]
     uint8_t *stages = smem + 128 + 2 * kGemvTile * 32 * 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < p.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
-        mbar_fence_init();
-    }
-    __syncthreads();
+    init_ring(full, empty, p.stages);
     const int total = *p.num_tiles * slabs;
 
     if (warp == 0) {
@@ -121,92 +191,51 @@ stream_gate_up_kernel(StreamParams p) {
             const int slab = item % slabs;
             const uint8_t *ex = p.weights + static_cast<size_t>(rec.e) * p.layout.bytes;
             const uint32_t code_bytes = kGuRows * nb * 16, sc_bytes = kGuRows * nb * 2;
-            const uint32_t bytes = 2 * code_bytes + 2 * sc_bytes + rec.n * (H + nb * 8);
-            mbar_arrive_expect_tx(bar, bytes);
+            mbar_arrive_expect_tx(bar, 2 * code_bytes + 2 * sc_bytes);
             bulk_g2s(st + L.gcodes, ex + p.layout.gate_codes + static_cast<size_t>(slab) * code_bytes, code_bytes, bar);
             bulk_g2s(st + L.ucodes, ex + p.layout.up_codes + static_cast<size_t>(slab) * code_bytes, code_bytes, bar);
             bulk_g2s(st + L.gsc, ex + p.layout.gate_scales + static_cast<size_t>(slab) * sc_bytes, sc_bytes, bar);
             bulk_g2s(st + L.usc, ex + p.layout.up_scales + static_cast<size_t>(slab) * sc_bytes, sc_bytes, bar);
-            for (int j = 0; j < rec.n; ++j) {
-                bulk_g2s(st + L.xcodes + j * H, p.x.codes + static_cast<size_t>(rec.tok[j]) * H, H, bar);
-                bulk_g2s(st + L.xsc + j * nb * 8, p.x.scales + static_cast<size_t>(rec.tok[j]) * nb, nb * 8, bar);
-            }
         });
         return;
     }
 
     const int cw = warp - 1;
+    bool failed = false;
     int i = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++i) {
+        const TileRec rec = load_tile(p.tiles + item / slabs);
+        const int n = rec.n < kGemvTile ? rec.n : kGemvTile;
+        const int4 *xr[kGemvTile];
+        const float2 *sr[kGemvTile];
+#pragma unroll
+        for (int j = 0; j < kGemvTile; ++j) {
+            const int t = j < n ? rec.tok[j] : rec.tok[0];
+            xr[j] = reinterpret_cast<const int4 *>(p.x.codes + static_cast<size_t>(t) * H);
+            sr[j] = p.x.scales + static_cast<size_t>(t) * nb;
+            if (j < n) {   // pull the tile's activation lines into L1 while the weights stream in
+                for (int b = lane; b < nb; b += 32) prefetch_l1(xr[j] + 2 * b);
+                if (lane * 16 < nb) prefetch_l1(sr[j] + lane * 16);
+            }
+        }
         const int s = i % p.stages;
-        if (!mbar_wait(&full[s], (i / p.stages) & 1, p.error)) break;
-        const uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
-        const TileRec &meta = *reinterpret_cast<const TileRec *>(st);
-        const int n = meta.n, p0 = meta.p0, slab = item % slabs;
-        const uint4 *gc = reinterpret_cast<const uint4 *>(st + L.gcodes);
-        const uint4 *uc = reinterpret_cast<const uint4 *>(st + L.ucodes);
-        const uint16_t *gs = reinterpret_cast<const uint16_t *>(st + L.gsc);
-        const uint16_t *us = reinterpret_cast<const uint16_t *>(st + L.usc);
-        const int4 *xc = reinterpret_cast<const int4 *>(st + L.xcodes);
-        const float2 *xs = reinterpret_cast<const float2 *>(st + L.xsc);
-        float acc[8][kGemvTile];
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int j = 0; j < kGemvTile; ++j) acc[r][j] = 0.0f;
-        for (int b = lane; b < nb; b += 32) {
-            uint4 wc[8];
-            float d4[8];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int blk = (cw * 4 + r) * nb + b;
-                wc[r] = gc[blk];
-                wc[4 + r] = uc[blk];
-                d4[r] = h2f(gs[blk]);
-                d4[4 + r] = h2f(us[blk]);
-            }
-#pragma unroll
-            for (int j = 0; j < kGemvTile; ++j) {
-                if (j < n) {
-                    const int4 xlo = xc[j * (H / 16) + 2 * b], xhi = xc[j * (H / 16) + 2 * b + 1];
-                    const float2 sc = xs[j * nb + b];
-                    const float s8x8 = 8.0f * sc.y;
-#pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        acc[r][j] = block_term(block_dot(wc[r], xlo, xhi), d4[r], sc.x, s8x8, acc[r][j]);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);   // stage fully read by this warp
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int j = 0; j < kGemvTile; ++j)
-                if (j < n) acc[r][j] = warp_sum(acc[r][j]);
+        if (!failed && !mbar_wait(&full[s], (i / p.stages) & 1, p.error)) failed = true;
         float *mid = smid + (i & 1) * kGemvTile * 32;
-        if (lane < 4) {
-#pragma unroll
-            for (int j = 0; j < kGemvTile; ++j) {
-                if (j < n) {
-                    float g = acc[0][j], u = acc[4][j];
-#pragma unroll
-                    for (int r = 1; r < 4; ++r)
-                        if (lane == r) { g = acc[r][j]; u = acc[4 + r][j]; }
-                    int flags = 0;
-                    g = operand(g, flags);
-                    u = operand(u, flags);
-                    const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), flags);
-                    const float v = arithmetic(__fmul_rn(act, u), flags);
-                    mid[j * 32 + cw * 4 + lane] = flags ? 0.0f : v;
-                    report(flags, p.error);
-                }
+        if (!failed) {
+            const uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
+            switch (n) {
+            case 1: gate_up_item<1>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
+            case 2: gate_up_item<2>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
+            case 3: gate_up_item<3>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
+            default: gate_up_item<4>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
             }
         }
-        named_barrier(1, 32 * kConsumerWarps);
+        named_barrier(1, kConsumerThreads);         // every consumer warp, even after a failed wait
+        if (failed) continue;
+        const int slab = item % slabs;
         for (int j = cw; j < n; j += kConsumerWarps) {
             const Q8Lane q = quantize_lane(mid[j * 32 + lane]);
-            const size_t pair = static_cast<size_t>(p0 + j);
+            const size_t pair = static_cast<size_t>(rec.p0 + j);
             p.mid.codes[pair * I + slab * 32 + lane] = q.code;
             if (lane == 0) {
                 p.mid.scales[pair * slabs + slab] = make_float2(h2f(q.d), h2f(q.s));
@@ -217,6 +246,53 @@ stream_gate_up_kernel(StreamParams p) {
 }
 
 // ---- down + router-weighted scatter-add -------------------------------------
+// Consumer warp cw owns rows 16cw .. 16cw+15 of the 128-row slab: lane l takes
+// rows 16cw + l/4 and 16cw + 8 + l/4 and blocks l%4, l%4+4, ...; two shuffles
+// finish each row, then out[token][row] += weight * y (red.global.add).
+template <int N>
+__device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, int I, int H, int row0,
+                                          int lr0, int q, uint64_t *empty_bar, int lane, float *out, int *error) {
+    const int nb = I / 32;
+    const TileRec &meta = *reinterpret_cast<const TileRec *>(st);
+    const uint4 *dc = reinterpret_cast<const uint4 *>(st + L.dcodes);
+    const uint16_t *ds = reinterpret_cast<const uint16_t *>(st + L.dsc);
+    const int4 *mc = reinterpret_cast<const int4 *>(st + L.mcodes);
+    const float2 *ms = reinterpret_cast<const float2 *>(st + L.msc);
+    int tok[N];
+    float w[N], acc[2][N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) { tok[j] = meta.tok[j]; w[j] = meta.w[j]; acc[0][j] = 0.0f; acc[1][j] = 0.0f; }
+    for (int b = q; b < nb; b += 4) {
+        const uint4 w0 = dc[lr0 * nb + b], w1 = dc[(lr0 + 8) * nb + b];
+        const float d0 = h2f(ds[lr0 * nb + b]), d1 = h2f(ds[(lr0 + 8) * nb + b]);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            const int4 xlo = mc[j * (I / 16) + 2 * b], xhi = mc[j * (I / 16) + 2 * b + 1];
+            const float2 sc = ms[j * nb + b];
+            const float s8x8 = 8.0f * sc.y;
+            acc[0][j] = block_term(block_dot2(w0, xlo, xhi), d0, sc.x, s8x8, acc[0][j]);
+            acc[1][j] = block_term(block_dot2(w1, xlo, xhi), d1, sc.x, s8x8, acc[1][j]);
+        }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);   // stage fully read by this warp
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            float v = acc[k][j];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            if ((j & 3) == q) {
+                int flags = 0;
+                const float y = arithmetic(v, flags);
+                const float c = arithmetic(__fmul_rn(w[j], y), flags);
+                atomicAdd(out + static_cast<size_t>(tok[j]) * H + row0 + 8 * k, c);
+                report(flags, error);
+            }
+        }
+}
+
 __global__ void __launch_bounds__(kStreamThreads, 1)
 stream_down_kernel(StreamParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -226,11 +302,7 @@ stream_down_kernel(StreamParams p) {
     uint64_t *empty = full + kMaxStages;
     uint8_t *stages = smem + 128;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < p.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
-        mbar_fence_init();
-    }
-    __syncthreads();
+    init_ring(full, empty, p.stages);
     const int total = *p.num_tiles * slabs;
 
     if (warp == 0) {
@@ -251,62 +323,20 @@ stream_down_kernel(StreamParams p) {
         return;
     }
 
-    const int cw = warp - 1, half = lane >> 4, hl = lane & 15;
+    const int cw = warp - 1, q = lane & 3;
+    const int lr0 = cw * (kDnRows / kConsumerWarps) + (lane >> 2);
     int i = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++i) {
         const int s = i % p.stages;
         if (!mbar_wait(&full[s], (i / p.stages) & 1, p.error)) break;
         const uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
-        const TileRec meta = *reinterpret_cast<const TileRec *>(st);
-        const int n = meta.n, slab = item % slabs;
-        const uint4 *dc = reinterpret_cast<const uint4 *>(st + L.dcodes);
-        const uint16_t *ds = reinterpret_cast<const uint16_t *>(st + L.dsc);
-        const int4 *mc = reinterpret_cast<const int4 *>(st + L.mcodes);
-        const float2 *ms = reinterpret_cast<const float2 *>(st + L.msc);
-        float res[kDnRows / kConsumerWarps / 2][kGemvTile];
-#pragma unroll
-        for (int pass = 0; pass < kDnRows / kConsumerWarps / 2; ++pass) {
-            const int lr = cw * (kDnRows / kConsumerWarps) + pass * 2 + half;
-            float acc[kGemvTile];
-#pragma unroll
-            for (int j = 0; j < kGemvTile; ++j) acc[j] = 0.0f;
-            for (int b = hl; b < nb; b += 16) {
-                const uint4 wc = dc[lr * nb + b];
-                const float d4 = h2f(ds[lr * nb + b]);
-#pragma unroll
-                for (int j = 0; j < kGemvTile; ++j) {
-                    if (j < n) {
-                        const int4 xlo = mc[j * (I / 16) + 2 * b], xhi = mc[j * (I / 16) + 2 * b + 1];
-                        const float2 sc = ms[j * nb + b];
-                        acc[j] = block_term(block_dot(wc, xlo, xhi), d4, sc.x, 8.0f * sc.y, acc[j]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < kGemvTile; ++j) res[pass][j] = acc[j];
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-        for (int pass = 0; pass < kDnRows / kConsumerWarps / 2; ++pass) {
-            const int row = slab * kDnRows + cw * (kDnRows / kConsumerWarps) + pass * 2 + half;
-#pragma unroll
-            for (int j = 0; j < kGemvTile; ++j) {
-                if (j < n) {
-                    float v = res[pass][j];
-                    v += __shfl_xor_sync(0xffffffffu, v, 8);
-                    v += __shfl_xor_sync(0xffffffffu, v, 4);
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);
-                    if (hl == j) {
-                        int flags = 0;
-                        const float y = arithmetic(v, flags);
-                        const float c = arithmetic(__fmul_rn(meta.w[j], y), flags);
-                        atomicAdd(p.out + static_cast<size_t>(meta.tok[j]) * H + row, c);
-                        report(flags, p.error);
-                    }
-                }
-            }
+        const int n = reinterpret_cast<const TileRec *>(st)->n;
+        const int row0 = (item % slabs) * kDnRows + lr0;
+        switch (n) {
+        case 1: down_item<1>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+        case 2: down_item<2>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+        case 3: down_item<3>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+        default: down_item<4>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
         }
     }
 }
