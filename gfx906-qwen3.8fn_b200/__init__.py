@@ -83,6 +83,7 @@ def library(path=LIB_PATH):
         "moe_forward": (I, [P, P, P, P, I, P, I, P]),
         "moe_forward_profiled": (I, [P, P, P, P, I, P, I, P, ctypes.POINTER(P)]),
         "moe_route": (I, [P, P, I, P, P, P, P, P, P, P]),
+        "moe_route_noalloc": (I, [P, I, P, P, P, P, P, P, P]),
         "moe_layer_read_flags": (I, [P, ctypes.POINTER(I), I, P]),
         "moe_quantize_q8_1": (I, [P, I, I, P, P, P]),
         "moe_q4_linear": (I, [P, I, I, P, I, P, P, P]),
@@ -225,6 +226,28 @@ class MoeLayer:
             self.handle = None
 
     __del__ = close
+
+
+def route_noalloc(logits, error=None, stream=None):
+    """moe_route_noalloc: routing with no device allocation by the library.
+
+    For callers that cannot allocate device memory (work recorded under CUDA
+    stream capture, hosts whose memory belongs to another allocator).  Outputs
+    are the caller's tensors; the library's scratch is a static device array
+    limited to 1024 tokens.  Returns dict ids/weights/offsets/token/rank and
+    the error tensor."""
+    import torch
+    T = logits.shape[0]
+    dev = logits.device
+    r = dict(ids=torch.empty(T, TOP_K, dtype=torch.int32, device=dev), weights=torch.empty(T, TOP_K, device=dev),
+             offsets=torch.empty(EXPERTS + 1, dtype=torch.int32, device=dev),
+             token=torch.empty(T * TOP_K, dtype=torch.int32, device=dev),
+             rank=torch.empty(T * TOP_K, dtype=torch.int32, device=dev))
+    if error is None:
+        error = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(library().moe_route_noalloc(_ptr(logits), T, _ptr(r["ids"]), _ptr(r["weights"]), _ptr(r["offsets"]),
+                                      _ptr(r["token"]), _ptr(r["rank"]), _ptr(error), _stream(stream)))
+    return r, error
 
 
 def quantize_q8_1(x, error=None, stream=None):

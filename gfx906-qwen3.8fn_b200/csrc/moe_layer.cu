@@ -12,6 +12,7 @@
 #include <chrono>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "common.cuh"
@@ -733,3 +734,160 @@ int moe_expert_run(moe_expert_t e, const float *input, int columns, float *outpu
 }
 
 }  // extern "C"
+
+// ------------------------------------------------ allocation-free routing --
+// moe_route_noalloc is moe_route for callers that cannot allocate device
+// memory: code that enqueues its work inside CUDA stream capture (a capture
+// cannot contain cudaMalloc, and an allocation made outside it would have to
+// outlive the graph), and hosts whose device memory is owned by another
+// allocator or a fixed arena (a serving engine, a caching allocator) and that
+// therefore cannot hand this library a workspace of its own.  Its scratch is
+// one file-scope device array, sized for at most kNoAllocMaxTokens tokens,
+// that every GPU loading this library holds until the process exits.
+namespace {
+
+constexpr int kNoAllocMaxTokens = 1024;
+constexpr int kNoAllocChunks = kNoAllocMaxTokens / kChunk;
+constexpr int kNoAllocTiles = kNoAllocMaxTokens * kTopK / kGemvTile + kRouterExperts;
+
+constexpr size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct NoAllocLayout {
+    size_t masks, base, counts, offsets, pair_weight, tiles, tile_off, num_tiles, bytes;
+};
+
+constexpr NoAllocLayout noalloc_layout() {
+    NoAllocLayout L{};
+    size_t at = 0;
+    L.masks = at;        at = align256(at + sizeof(uint32_t) * kNoAllocChunks * kRouterExperts);
+    L.base = at;         at = align256(at + sizeof(int32_t) * kNoAllocChunks * kRouterExperts);
+    L.counts = at;       at = align256(at + sizeof(int32_t) * kRouterExperts);
+    L.offsets = at;      at = align256(at + sizeof(int32_t) * (kRouterExperts + 2));
+    L.pair_weight = at;  at = align256(at + sizeof(float) * kNoAllocMaxTokens * kTopK);
+    L.tiles = at;        at = align256(at + sizeof(TileRec) * kNoAllocTiles);
+    L.tile_off = at;     at = align256(at + sizeof(int32_t) * kRouterExperts);
+    L.num_tiles = at;    at = align256(at + sizeof(int));
+    L.bytes = at;
+    return L;
+}
+
+constexpr NoAllocLayout kNoAlloc = noalloc_layout();   // 326,144 bytes
+
+// The scratch itself.  In host code this name is only a handle for
+// cudaGetSymbolAddress, never a device address.
+static __device__ __align__(256) unsigned char g_route_scratch[kNoAlloc.bytes];
+
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mutex;
+void *g_noalloc_address[kNoAllocDevices] = {};
+
+// Resolve the array's address on the current device once and cache it.
+int noalloc_scratch(uint8_t **out) {
+    int device = 0;
+    MOE_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kNoAllocDevices) return fail(MOE_NOT_SUPPORTED, "device ordinal above 63");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_address[device]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
+        if (e != cudaSuccess || !p) return cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                                                       "cudaGetSymbolAddress(route scratch)");
+        g_noalloc_address[device] = p;
+    }
+    *out = static_cast<uint8_t *>(g_noalloc_address[device]);
+    return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" int moe_route_noalloc(const float *logits, int tokens, int32_t *ids, float *weights, int32_t *offsets,
+                                 int32_t *token, int32_t *rank, int *error, void *stream) {
+    if (tokens < 1 || tokens > kNoAllocMaxTokens)
+        return fail(MOE_INVALID_ARGUMENT, "moe_route_noalloc: tokens must be 1..1024 (size of its static scratch)");
+    const size_t n = static_cast<size_t>(tokens) * kTopK;
+    if (!aligned(logits, 4) || !aligned(ids, 4) || !aligned(weights, 4) || !aligned(offsets, 4) ||
+        !aligned(token, 4) || !aligned(rank, 4) || !aligned(error, 4))
+        return fail(MOE_INVALID_ARGUMENT, "moe_route_noalloc: null or misaligned pointer");
+    const size_t lbytes = static_cast<size_t>(tokens) * kRouterExperts * 4;
+    const void *outs[6] = {ids, weights, offsets, token, rank, error};
+    const size_t sizes[6] = {n * 4, n * 4, (kRouterExperts + 1) * 4, n * 4, n * 4, 4};
+    for (int i = 0; i < 6; ++i) {
+        if (overlap(outs[i], sizes[i], logits, lbytes)) return fail(MOE_INVALID_ARGUMENT, "output overlaps logits");
+        for (int j = 0; j < i; ++j)
+            if (overlap(outs[i], sizes[i], outs[j], sizes[j])) return fail(MOE_INVALID_ARGUMENT, "outputs overlap");
+    }
+    uint8_t *sc = nullptr;
+    if (const int st = noalloc_scratch(&sc)) return st;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int chunks = (tokens + kChunk - 1) / kChunk;
+    auto *masks = reinterpret_cast<uint32_t *>(sc + kNoAlloc.masks);
+    auto *base = reinterpret_cast<int32_t *>(sc + kNoAlloc.base);
+    auto *counts = reinterpret_cast<int32_t *>(sc + kNoAlloc.counts);
+    auto *offs = reinterpret_cast<int32_t *>(sc + kNoAlloc.offsets);
+    auto *pair_weight = reinterpret_cast<float *>(sc + kNoAlloc.pair_weight);
+    auto *tiles = reinterpret_cast<TileRec *>(sc + kNoAlloc.tiles);
+    auto *tile_off = reinterpret_cast<int32_t *>(sc + kNoAlloc.tile_off);
+    auto *num_tiles = reinterpret_cast<int *>(sc + kNoAlloc.num_tiles);
+    RouteParams rp;
+    rp.logits = logits;
+    rp.x = nullptr;
+    rp.gate_vec = nullptr;
+    rp.tokens = tokens;
+    rp.hidden = 0;
+    rp.probs = nullptr;
+    rp.ids = ids;
+    rp.weights = weights;
+    rp.masks = masks;
+    rp.pair_token = token;
+    rp.pair_weight = pair_weight;
+    rp.pair_rank = rank;
+    rp.error = error;
+    if (tokens <= kChunk) {
+        SmallRouteParams sr;
+        sr.r = rp;
+        sr.xq = Q8Planar{nullptr, nullptr};
+        sr.offsets = offs;
+        sr.tiles = tiles;
+        sr.tile_off = tile_off;
+        sr.num_tiles = num_tiles;
+        sr.max_tiles = kNoAllocTiles;
+        route_small_kernel<<<1, 512, 0, s>>>(sr);
+        MOE_CUDA(cudaGetLastError());
+    } else {
+        route_topk_kernel<<<chunks, kRouteThreads, 0, s>>>(rp);
+        MOE_CUDA(cudaGetLastError());
+        route_chunk_prefix_kernel<<<kRouterExperts / 32, 1024, 0, s>>>(masks, chunks, base, counts);
+        MOE_CUDA(cudaGetLastError());
+        ScanParams sp;
+        sp.counts = counts;
+        sp.tokens = tokens;
+        sp.tile = kGemvTile;
+        sp.has_shared = 0;
+        sp.offsets = offs;
+        sp.tiles = tiles;
+        sp.tile_off = tile_off;
+        sp.pair_token = token;
+        sp.pair_weight = pair_weight;
+        sp.num_tiles = num_tiles;
+        sp.max_tiles = kNoAllocTiles;
+        sp.error = error;
+        route_scan_kernel<<<1, 512, 0, s>>>(sp);
+        MOE_CUDA(cudaGetLastError());
+        ScatterParams cp;
+        cp.masks = masks;
+        cp.base = base;
+        cp.offsets = offs;
+        cp.ids = ids;
+        cp.weights = weights;
+        cp.pair_token = token;
+        cp.pair_rank = rank;
+        cp.pair_weight = pair_weight;
+        cp.tiles = tiles;
+        cp.tile_off = tile_off;
+        cp.max_tiles = kNoAllocTiles;
+        route_scatter_kernel<<<dim3(chunks, kRouterExperts / 256), 256, 0, s>>>(cp);
+        MOE_CUDA(cudaGetLastError());
+    }
+    MOE_CUDA(cudaMemcpyAsync(offsets, offs, (kRouterExperts + 1) * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+    return MOE_OK;
+}

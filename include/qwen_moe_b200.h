@@ -132,6 +132,22 @@ int moe_route(moe_layer_t h, const float *logits_dev, int tokens, float *probs_d
               int32_t *ids_dev, float *weights_dev, int32_t *offsets_dev, int32_t *token_dev,
               int32_t *rank_dev, void *stream);
 
+/* Routing that allocates nothing: the same results as moe_route (ids,
+ * weights, offsets [experts+1], sorted token/rank [T*top_k], all device
+ * memory owned by the caller; sticky bits ORed into the caller-zeroed
+ * *error_dev) for callers that cannot allocate device memory -- work enqueued
+ * inside CUDA stream capture, or hosts whose device memory belongs to another
+ * allocator.  It has no counterpart in the reference.  Its scratch is one
+ * static device array of 326,144 bytes, held by every GPU that loads the
+ * library until the process exits, which limits tokens to 1..1024 (larger
+ * counts return MOE_INVALID_ARGUMENT).  The first call on a device resolves
+ * that array's address on the current device (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  Every call shares the array:
+ * calls whose GPU work overlaps (other streams, other threads) race. */
+int moe_route_noalloc(const float *logits_dev, int tokens, int32_t *ids_dev, float *weights_dev,
+                      int32_t *offsets_dev, int32_t *token_dev, int32_t *rank_dev, int *error_dev,
+                      void *stream);
+
 /* Read (and optionally clear) the sticky numeric flags of a layer.  This is
  * the only call here that synchronises (on `stream`). */
 int moe_layer_read_flags(moe_layer_t h, int *flags_host, int clear, void *stream);
