@@ -37,12 +37,16 @@ inline ExpertLayout make_layout(int H, int I) {
 // fp32 [rows][K] -> Q8_1.  One warp per 32-value block, lane = element.
 // Writes the planar form (codes/scales) and/or canonical 36-byte blocks.
 __global__ void __launch_bounds__(256)
-quantize_kernel(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error) {
+quantize_kernel(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error, float2 *tc) {
     const size_t warp_global = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const size_t stride = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
     for (size_t b = warp_global; b < blocks; b += stride) {
         const Q8Lane q = quantize_lane(x[b * 32 + lane]);
+        if (tc) {   // (d, 8*(sum(codes)*d - s)) for the tensor-core path's centred weights
+            const int csum = __reduce_add_sync(0xffffffffu, static_cast<int>(q.code));
+            if (lane == 0) tc[b] = make_float2(h2f(q.d), 8.0f * (static_cast<float>(csum) * h2f(q.d) - h2f(q.s)));
+        }
         if (out.codes) {
             out.codes[b * 32 + lane] = q.code;
             if (lane == 0) out.scales[b] = make_float2(h2f(q.d), h2f(q.s));

@@ -173,8 +173,36 @@ GroupParams group_params(moe_layer_s *h, const moe_weights_s *w, float *out) {
 
 // gate/up + down over the tile list already in the workspace.  `events`
 // (optional, three entries) are recorded around the two kernels.
+TcParams tc_params(moe_layer_s *h, const moe_weights_s *w, float *out, bool down) {
+    TcParams t;
+    t.weights = w->base;
+    t.layout = w->layout;
+    t.act = down ? h->mid.codes : h->xq.codes;
+    t.act_tc = down ? h->tc.mid_tc : h->tc.x_tc;
+    t.act_by_token = down ? 0 : 1;
+    t.tiles = h->tc.tiles;
+    t.num_tiles = h->tc.num_tiles;
+    t.pair_token = h->pair_token;
+    t.pair_weight = h->pair_weight;
+    t.mid = h->mid;
+    t.mid_tc = h->tc.mid_tc;
+    t.out = out;
+    t.error = h->error;
+    return t;
+}
+
+// Large groups (tiles of up to 128 pairs) on the tcgen05 kernels.
+int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, bool down, cudaStream_t s) {
+    const ExpertLayout &L = w->layout;
+    const int items = tc_tiles * (down ? L.hidden / kTcN : L.inter / (kTcN / 2));
+    const int grid = std::max(1, std::min(items, h->sms));
+    if (down) tc_expert_kernel<true><<<grid, kTcThreads, TcSmem::bytes, s>>>(tc_params(h, w, out, true));
+    else tc_expert_kernel<false><<<grid, kTcThreads, TcSmem::bytes, s>>>(tc_params(h, w, out, false));
+    return cuda_status(cudaGetLastError(), "tc_expert_kernel");
+}
+
 int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_tiles, cudaStream_t s,
-                   void *const *events = nullptr) {
+                   void *const *events = nullptr, int tc_tiles = 0) {
     const ExpertLayout &L = w->layout;
     if (h->gu_stages) {
         StreamParams sp;
@@ -193,12 +221,16 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         stream_gate_up_kernel<<<std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
                                 stream_gu_smem(L.hidden, sp.stages), s>>>(sp);
         MOE_CUDA(cudaGetLastError());
+        if (tc_tiles)
+            if (const int st = launch_tc(h, w, out, tc_tiles, false, s)) return st;
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
         sp.stages = h->dn_stages;
         sp.stage_bytes = DnStage(L.inter).bytes;
         stream_down_kernel<<<std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
                              stream_dn_smem(L.inter, sp.stages), s>>>(sp);
         MOE_CUDA(cudaGetLastError());
+        if (tc_tiles)
+            if (const int st = launch_tc(h, w, out, tc_tiles, true, s)) return st;
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[2]), s));
         return MOE_OK;
     }
@@ -217,10 +249,10 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
 }
 
 int launch_quantize(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error, int sms,
-                    cudaStream_t s) {
+                    cudaStream_t s, float2 *tc = nullptr) {
     const size_t warps = blocks;
     const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((warps + 7) / 8, size_t(sms) * 16)));
-    quantize_kernel<<<grid, 256, 0, s>>>(x, blocks, out, canonical, error);
+    quantize_kernel<<<grid, 256, 0, s>>>(x, blocks, out, canonical, error, tc);
     return cuda_status(cudaGetLastError(), "quantize_kernel");
 }
 
@@ -270,6 +302,13 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     sp.num_tiles = h->num_tiles;
     sp.max_tiles = h->tiles_max;
     sp.error = h->error;
+    if (x) {   // forward: large groups go to the tensor-core kernels
+        sp.tc_min = kTcMinGroup;
+        sp.tc_tile = kTcM;
+        sp.tc_max = h->tc.max_tiles;
+        sp.tc_tiles = h->tc.tiles;
+        sp.tc_num = h->tc.num_tiles;
+    }
     route_scan_kernel<<<1, 512, 0, s>>>(sp);
     MOE_CUDA(cudaGetLastError());
     ScatterParams cp;
@@ -530,10 +569,15 @@ int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const f
     auto s = static_cast<cudaStream_t>(stream);
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
     if (tokens > kChunk)   // small batches quantise inside the fused routing kernel
-        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s))
+        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s,
+                                           h->tc.x_tc))
             return st;
     if (const int st = launch_route(h, w, x, logits, tokens, nullptr, s)) return st;
-    return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events);
+    // Upper bound on tensor-core tiles: every group of >= kTcMinGroup pairs,
+    // 128 pairs per tile (the device writes the exact count).
+    const int pairs = tokens * (kTopK + 1);
+    const int tc_tiles = tokens > kChunk ? std::min(h->tc.max_tiles, pairs / kTcMinGroup + pairs / kTcM + 1) : 0;
+    return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events, tc_tiles);
 }
 
 int moe_quantize_q8_1(const float *x, int width, int columns, void *q8, int *error, void *stream) {

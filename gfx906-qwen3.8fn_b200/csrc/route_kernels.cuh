@@ -247,6 +247,11 @@ struct ScanParams {
     int *num_tiles;
     int max_tiles;
     int *error;
+    // Groups of at least tc_min pairs (0: never) go to the tensor-core path
+    // as tiles of up to tc_tile pairs: {expert, first pair, count, 0}.
+    int tc_min = 0, tc_tile = 128, tc_max = 0;
+    int4 *tc_tiles = nullptr;
+    int *tc_num = nullptr;
 };
 
 // One CTA of 512 threads (thread = expert): exclusive scan over experts and
@@ -261,10 +266,13 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
         p.offsets[kRouterExperts] = total;
         p.offsets[kRouterExperts + 1] = total + (p.has_shared ? p.tokens : 0);
     }
-    const int ntiles = (run + p.tile - 1) / p.tile;
-    int tiles_total = 0;
+    const bool big = p.tc_min > 0 && run >= p.tc_min;
+    const int ntiles = big ? 0 : (run + p.tile - 1) / p.tile;
+    const int ntc = big ? (run + p.tc_tile - 1) / p.tc_tile : 0;
+    int tiles_total = 0, tc_total = 0;
     const int toff = block_exclusive_scan_512(ntiles, &tiles_total);
-    p.tile_off[e] = toff;
+    const int tcoff = block_exclusive_scan_512(ntc, &tc_total);
+    p.tile_off[e] = big ? -1 : toff;
     for (int i = 0; i < ntiles; ++i) {
         const int idx = toff + i;
         if (idx < p.max_tiles) {
@@ -275,8 +283,17 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
             t.pad = 0;
         }
     }
-    int shared_tiles = 0;
-    if (p.has_shared) {
+    for (int i = 0; i < ntc; ++i)
+        if (tcoff + i < p.tc_max)
+            p.tc_tiles[tcoff + i] = make_int4(e, off + i * p.tc_tile, min(p.tc_tile, run - i * p.tc_tile), 0);
+    int shared_tiles = 0, shared_tc = 0;
+    if (p.has_shared && p.tc_min > 0 && p.tokens >= p.tc_min) {
+        shared_tc = (p.tokens + p.tc_tile - 1) / p.tc_tile;
+        for (int i = e; i < shared_tc; i += 512)
+            if (tc_total + i < p.tc_max)
+                p.tc_tiles[tc_total + i] = make_int4(kRouterExperts, total + i * p.tc_tile,
+                                                     min(p.tc_tile, p.tokens - i * p.tc_tile), 0);
+    } else if (p.has_shared) {
         shared_tiles = (p.tokens + p.tile - 1) / p.tile;
         for (int i = e; i < shared_tiles; i += 512) {
             const int idx = tiles_total + i;
@@ -298,6 +315,11 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
         int n = tiles_total + shared_tiles;
         if (n > p.max_tiles) { atomicOr(p.error, kFlagArithmetic); n = p.max_tiles; }
         *p.num_tiles = n;
+        if (p.tc_num) {
+            int m = tc_total + shared_tc;
+            if (m > p.tc_max) { atomicOr(p.error, kFlagArithmetic); m = p.tc_max; }
+            *p.tc_num = m;
+        }
     }
 }
 
@@ -334,7 +356,7 @@ __global__ void __launch_bounds__(256) route_scatter_kernel(ScatterParams p) {
         p.pair_token[pos] = t;
         if (p.pair_rank) p.pair_rank[pos] = r;
         p.pair_weight[pos] = w;
-        if (p.tiles) {
+        if (p.tiles && p.tile_off[e] >= 0) {   // tensor-core groups have no small tiles
             const int local = pos - p.offsets[e];
             const int tile = p.tile_off[e] + local / kGemvTile;
             if (tile < p.max_tiles) {
