@@ -73,4 +73,18 @@ __device__ __forceinline__ void named_barrier(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also returns the OR of `v` over the participating threads.
+__device__ __forceinline__ bool named_barrier_or(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 }  // namespace qmoe

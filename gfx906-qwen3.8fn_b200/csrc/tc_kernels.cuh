@@ -1,7 +1,7 @@
 // tc_kernels.cuh -- tcgen05 (kind::i8) grouped GEMMs for large expert groups.
 //
 // One work item = (expert e, up to 128 consecutive pairs of e's group, one
-// slab of 64 weight rows).  The MMA is D[128 pairs][64 rows] += A . B^T with
+// slab of 64 weight rows).  The MMA is D[128 pairs][64 rows] = A . B^T with
 //   A = the pairs' Q8_1 activation codes (s8, gathered by pair -> token),
 //   B = the slab's Q4_0 codes unpacked to centred s8 (q - 8),
 // K = 32 per instruction = one quantisation block, so every MMA result is one
@@ -13,20 +13,24 @@
 // reference's uncentred dot is dot_c + 8*sum(x codes) (an integer identity),
 // and d4*(dot*d8 - 8*s8) = d4*(dot_c*d8 + c8) with the per-(pair, block)
 // constant c8 = 8*(sum(x codes)*d8 - s8) computed once by the quantiser.
-// Each block's TMEM columns are pre-loaded with the bit pattern of 1.5*2^23,
-// so after the integer MMA accumulates dot_c (|dot_c| <= 32*8*127 < 2^22) the
-// column holds the float 1.5*2^23 + dot_c exactly: the epilogue subtracts the
-// constant (exact) instead of converting int -> float.
+// |dot_c| <= 32*8*127 < 2^15, so each result is read from TMEM as a 16-bit
+// value (two columns per register) and turned into an exact fp32 by placing
+// it, offset by 2^15, in the mantissa of 1.5*2^23 (two logic operations and
+// one subtraction per pair of columns).
 //
-// Warp roles (21 warps):
-//   warp 0      TMEM allocation, then one lane issues the MMAs;
-//   warps 1..4  producers: gather activation rows with cp.async, load and
-//               unpack weight codes, stage per-block scales;
-//   warps 5..20 epilogue: four per TMEM lane quarter, 16 columns each; they
-//               read each block's result, re-bias its TMEM columns, scale and
-//               accumulate in fp32 registers; at the end of an item they run
-//               SiLU*up + Q8_1 requantisation (gate/up) or the router-weighted
-//               bulk reduce-add into the residual (down).
+// Warp roles (12 warps, three per SM sub-partition):
+//   warp 0      TMEM allocation, then one lane issues the MMAs, two blocks
+//               per TMEM region (4 regions of 128 columns);
+//   warps 1..3  producers: gather activation rows with cp.async, load and
+//               unpack weight codes, stage per-block scales (software-
+//               pipelined one stage ahead);
+//   warps 4..11 epilogue: two per TMEM lane quarter, 32 columns each; per
+//               region they load both blocks, release the region, and scale
+//               and accumulate in fp32 registers with packed f32x2 arithmetic
+//               while the next region's loads are in flight; at the end of an
+//               item they run SiLU*up + Q8_1 requantisation (gate/up, split
+//               over both threads of a pair row) or the router-weighted bulk
+//               reduce-add into the residual (down).
 // All barrier waits are bounded (ptx.cuh).
 #pragma once
 #include "common.cuh"
@@ -39,13 +43,16 @@ constexpr int kTcM = 128;          // pairs per tile (MMA M, TMEM lanes)
 constexpr int kTcN = 64;           // weight rows per item (MMA N, TMEM columns per block)
 constexpr int kTcKB = 4;           // quantisation blocks per pipeline stage
 constexpr int kTcStages = 6;       // shared-memory ring depth
-constexpr int kTcRegions = 8;      // TMEM block-result regions (8 x 64 = 512 columns)
-constexpr int kTcProducerWarps = 4;
-constexpr int kTcEpilogueWarps = 16;
+constexpr int kTcRegions = 4;      // TMEM regions of two block results (4 x 128 = 512 columns)
+constexpr int kTcColumns = kTcRegions * 2 * kTcN;
+constexpr int kTcProducerWarps = 3;
+constexpr int kTcEpilogueWarps = 8;   // two per TMEM lane quarter, 32 columns each
 constexpr int kTcWarps = 1 + kTcProducerWarps + kTcEpilogueWarps;
 constexpr int kTcThreads = 32 * kTcWarps;
+constexpr int kTcXchStride = 68;   // floats per exchange row (16-byte accesses by 8 lanes hit 32 banks)
 constexpr int kTcMinGroup = 16;    // groups with at least this many pairs use the tensor-core path
-constexpr uint32_t kTcBias = 0x4b400000u;   // bit pattern of 1.5 * 2^23
+constexpr float kTcUnbias = 12615680.0f;   // 1.5 * 2^23 + 2^15
+static_assert(kTcWarps % 4 == 0, "whole warps per SM sub-partition keep the register budget");
 
 // ---- PTX wrappers ------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
@@ -80,25 +87,42 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// 32 columns of this warp's lane quarter as 16-bit values, two adjacent columns
+// per register (the lower column in the low half).
+__device__ __forceinline__ void tmem_ld16p(uint32_t taddr, uint32_t *r) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.pack::16b.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-        "r"(v)
-        : "memory");
+// Both blocks of a region: columns [0, 32) of block 0 and of block 1 (64 columns on).
+__device__ __forceinline__ void tmem_ld_pair(uint32_t taddr, uint32_t (&r)[32]) {
+    tmem_ld16p(taddr, r);
+    tmem_ld16p(taddr + kTcN, r + 16);
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Wait for outstanding TMEM loads, tying the destination registers to the wait
+// so that no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld32(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                   "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
 
 __device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async8(void *dst_smem, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -141,52 +165,87 @@ __device__ __forceinline__ void unpack_centred(const uint4 w, uint4 &lo, uint4 &
     hi = make_uint4(c(w.x >> 4), c(w.y >> 4), c(w.z >> 4), c(w.w >> 4));
 }
 
-// Quantise 32 values held by one thread with the reference's rules
-// (quant.cpp:275-325): the raw sum uses the same pairwise tree as the XOR
-// butterfly 1,2,4,8,16.
-struct Q8Block {
-    uint16_t d, s;
-    int flags;
-    float c8;          // 8 * (sum(codes) * d - s) with the stored half values
+// Packed pairs of fp32 (Blackwell f32x2 arithmetic), low word = first element.
+__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t pkf2(float lo, float hi) { return pk2(__float_as_uint(lo), __float_as_uint(hi)); }
+__device__ __forceinline__ void upk2(uint64_t v, float &lo, float &hi) {
+    uint32_t a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+    lo = __uint_as_float(a);
+    hi = __uint_as_float(b);
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// Two 16-bit two's-complement dots (low half first) -> the fp32 pair
+// (kTcUnbias + v): the bit pattern 0x4b400000 + (v + 2^15) is the float
+// 1.5*2^23 + 2^15 + v exactly for |v| < 2^15.
+__device__ __forceinline__ uint64_t dot16x2(uint32_t r) {
+    return pk2((r & 0xffffu) ^ 0x4b408000u, (r >> 16) ^ 0x4b408000u);
+}
+
+// Q8_1 of one 32-value block held as two halves of 16 by two threads, with
+// the reference's rules (quant.cpp:275-325).  The maximum does not depend on
+// order and the raw sum's pairwise tree (XOR butterfly 1,2,4,8,16) is
+// (tree of values 0..15) + (tree of values 16..31), so the split block is
+// identical to one quantised by a single thread.
+struct Q8Half {
+    float amax, sum;   // over this half, non-finite values taken as 0
+    int bad;           // a value was non-finite
 };
-__device__ __forceinline__ Q8Block quantize_thread32(float (&x)[32], int8_t (&code)[32]) {
-    int bad = 0;
-    float amax = 0.0f;
-    float t[32];
+__device__ __forceinline__ Q8Half q8_half_stats(float (&x)[16]) {
+    Q8Half q{0.0f, 0.0f, 0};
+    float t[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        if (!isfinite(x[i])) { bad = 1; x[i] = 0.0f; }
-        amax = fmaxf(amax, fabsf(x[i]));
+    for (int i = 0; i < 16; ++i) {
+        if (!isfinite(x[i])) { q.bad = 1; x[i] = 0.0f; }
+        q.amax = fmaxf(q.amax, fabsf(x[i]));
         t[i] = x[i];
     }
 #pragma unroll
-    for (int m = 1; m < 32; m <<= 1)
+    for (int m = 1; m < 16; m <<= 1)
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if ((i & m) == 0 && (i & (2 * m - 1)) == 0) t[i] = __fadd_rn(t[i], t[i + m]);
-    const float sum = t[0];
+        for (int i = 0; i < 16; ++i)
+            if ((i & (2 * m - 1)) == 0) t[i] = __fadd_rn(t[i], t[i + m]);
+    q.sum = t[0];
+    return q;
+}
+struct Q8Codes {
+    uint16_t d, s;        // half scale and raw sum of the whole block
+    int representable;    // the scale and the sum fit a half
+    int bad_code;         // a code of this half fell outside [-127, 127]
+    int csum;             // sum of this half's codes
+};
+// Codes of one half given the whole block's maximum, raw sum and non-finite flag.
+__device__ __forceinline__ Q8Codes q8_half_codes(const float (&x)[16], float amax, float sum, int bad,
+                                                 int8_t (&code)[16]) {
+    Q8Codes q;
     const float d = __fdiv_rn(amax, 127.0f);
-    const uint16_t hd = f2h(d), hs = f2h(sum);
-    const bool representable = isfinite(sum) && (hs & 0x7c00u) != 0x7c00u && (hd & 0x7c00u) != 0x7c00u &&
-                               (amax == 0.0f || d > 0.0f);
-    int bad_code = 0, csum = 0;
+    q.d = f2h(d);
+    q.s = f2h(sum);
+    q.representable = isfinite(sum) && (q.s & 0x7c00u) != 0x7c00u && (q.d & 0x7c00u) != 0x7c00u &&
+                      (amax == 0.0f || d > 0.0f);
+    q.bad_code = 0;
+    q.csum = 0;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const float c = (!bad && representable && amax != 0.0f) ? roundf(__fdiv_rn(x[i], d)) : 0.0f;
-        if (!isfinite(c) || c < -127.0f || c > 127.0f) bad_code = 1;
-        code[i] = static_cast<int8_t>(isfinite(c) && c >= -127.0f && c <= 127.0f ? c : 0.0f);
+    for (int i = 0; i < 16; ++i) {
+        const float c = (!bad && q.representable && amax != 0.0f) ? roundf(__fdiv_rn(x[i], d)) : 0.0f;
+        const bool ok = isfinite(c) && c >= -127.0f && c <= 127.0f;
+        q.bad_code |= ok ? 0 : 1;
+        code[i] = static_cast<int8_t>(ok ? c : 0.0f);
+        q.csum += code[i];
     }
-    const bool valid = !bad && representable && !bad_code;
-    Q8Block q;
-    q.d = (valid && amax != 0.0f) ? hd : uint16_t(0);
-    q.s = (valid && amax != 0.0f) ? hs : uint16_t(0);
-    q.flags = (bad ? kFlagInvalid : 0) | ((representable && !bad_code) ? 0 : kFlagArithmetic);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        if (!valid) code[i] = 0;
-        csum += code[i];
-    }
-    q.c8 = 8.0f * (static_cast<float>(csum) * h2f(q.d) - h2f(q.s));
     return q;
 }
 
@@ -211,9 +270,9 @@ struct TcParams {
 struct TcStage {
     static constexpr uint32_t a = 0;                                   // kTcKB x [128 x 32] s8
     static constexpr uint32_t b = a + kTcKB * kTcM * 32;               // kTcKB x [64 x 32] s8
-    static constexpr uint32_t d4 = b + kTcKB * kTcN * 32;              // [kTcKB][64] half
-    static constexpr uint32_t sc = d4 + kTcKB * kTcN * 2;              // [128][kTcKB] float2
-    static constexpr uint32_t bytes = sc + kTcM * kTcKB * 8;
+    static constexpr uint32_t d4 = b + kTcKB * kTcN * 32;              // [kTcKB][64] fp32 weight scales
+    static constexpr uint32_t sc = d4 + kTcKB * kTcN * 4;              // [kTcKB][128] float2 (d8, c8)
+    static constexpr uint32_t bytes = sc + kTcKB * kTcM * 8;
 };
 static_assert(TcStage::bytes % 128 == 0, "stage size keeps 128-byte alignment");
 
@@ -221,9 +280,11 @@ struct TcSmem {
     static constexpr uint32_t bars = 0;                                 // 4 barrier arrays of 8
     static constexpr uint32_t tmem_slot = 256;
     static constexpr uint32_t ring = 1024;
-    static constexpr uint32_t xch = ring + kTcStages * TcStage::bytes;  // [128][64] fp32 exchange
-    static constexpr uint32_t bytes = xch + kTcM * kTcN * 4;
+    static constexpr uint32_t xch = ring + kTcStages * TcStage::bytes;  // [128][68] fp32 rows
+    static constexpr uint32_t part = xch + kTcM * kTcXchStride * 4;     // [128][2][4] half-block statistics
+    static constexpr uint32_t bytes = part + kTcM * 2 * 4 * 4;
 };
+static_assert(TcSmem::bytes <= 227 * 1024, "fits the opt-in shared memory of one CTA");
 
 // Persistent loop shared by both kernels.  `Down` selects the down projection
 // (K = I, weight slabs of the down matrix, reduce-add epilogue) versus
@@ -241,6 +302,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + TcSmem::tmem_slot);
     uint8_t *ring = smem + TcSmem::ring;
     float *xch = reinterpret_cast<float *>(smem + TcSmem::xch);
+    float *part = reinterpret_cast<float *>(smem + TcSmem::part);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -255,7 +317,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
         mbar_fence_init();
     }
     if (warp == 0) {
-        tmem_alloc(tmem_slot, kTcRegions * kTcN);
+        tmem_alloc(tmem_slot, kTcColumns);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -277,13 +339,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
                     tc_fence_after();
                     const uint32_t st = smem_u32(ring + s * TcStage::bytes);
                     for (int kb = 0; kb < kTcKB; ++kb, ++kseq) {
-                        const int r = kseq % kTcRegions;
-                        if (!mbar_wait(&tm_empty[r], (kseq / kTcRegions) & 1, p.error)) { failed = true; break; }
-                        tc_fence_after();
+                        // blocks 2h and 2h+1 of the sequence share region h % kTcRegions
+                        const int h = kseq >> 1, r = h % kTcRegions;
+                        if ((kseq & 1) == 0) {
+                            if (!mbar_wait(&tm_empty[r], (h / kTcRegions) & 1, p.error)) { failed = true; break; }
+                            tc_fence_after();
+                        }
                         const uint64_t ad = smem_desc(st + TcStage::a + kb * kTcM * 32, 128, 256);
                         const uint64_t bd = smem_desc(st + TcStage::b + kb * kTcN * 32, 128, 256);
-                        mma_i8(tmem + r * kTcN, ad, bd, idesc, 1u);
-                        mma_commit(&tm_full[r]);
+                        mma_i8(tmem + (2 * r + (kseq & 1)) * kTcN, ad, bd, idesc, 0u);
+                        if (kseq & 1) mma_commit(&tm_full[r]);
                     }
                     mma_commit(&empty[s]);   // stage s may be refilled once these MMAs are done
                 }
@@ -291,35 +356,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
         }
     } else if (warp <= kTcProducerWarps) {
         // ---------------- producers ----------------
-        const int pt = threadIdx.x - 32;   // 0..127: one pair row of A each
-        int q = 0;
-        for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
-            const int4 td = p.tiles[item / slabs];
-            const int e = td.x, p0 = td.y, n = td.z, slab = item % slabs;
-            const uint8_t *ex = p.weights + static_cast<size_t>(e) * p.layout.bytes;
-            const int arow = pt < n ? (p.act_by_token ? p.pair_token[p0 + pt] : p0 + pt) : -1;
-            for (int ks = 0; ks < ksteps; ++ks, ++q) {
-                const int s = q % kTcStages;
-                if (q >= kTcStages && !mbar_wait(&empty[s], ((q / kTcStages) & 1) ^ 1, p.error)) { failed = true; break; }
-                uint8_t *st = ring + s * TcStage::bytes;
-                const int b0 = ks * kTcKB;
-                // A: this thread's pair row, kTcKB blocks x 2 halves, plus its block scales
-                if (arow >= 0) {
-                    const int8_t *src = p.act + static_cast<size_t>(arow) * K + b0 * 32;
+        // Software pipeline over this CTA's stages g = 0, 1, ...: the weight
+        // codes of stage g+1 are loaded into registers while stage g is staged,
+        // and stage g is published (full barrier) one iteration later, after
+        // its cp.async group has landed.
+        constexpr int kProducerThreads = 32 * kTcProducerWarps;
+        constexpr int kAPer = (kTcM + kProducerThreads - 1) / kProducerThreads;
+        constexpr int kBPer = (kTcN * kTcKB + kProducerThreads - 1) / kProducerThreads;
+        const int pt = threadIdx.x - 32;
+        const int my_items = static_cast<int>(blockIdx.x) < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+        const int nstages = my_items * ksteps;
+        int4 td_next = make_int4(0, 0, 0, 0), td = td_next;
+        uint4 wn[kBPer];
+        uint16_t dn[kBPer];
+        // global loads of stage g's weight codes and scales into wn/dn
+        auto prefetch = [&](int g) {
+            const int item = blockIdx.x + (g / ksteps) * gridDim.x, ks = g % ksteps;
+            if (ks == 0) td_next = p.tiles[item / slabs];
+            const int slab = item % slabs;
+            const uint8_t *ex = p.weights + static_cast<size_t>(td_next.x) * p.layout.bytes;
 #pragma unroll
-                    for (int kb = 0; kb < kTcKB; ++kb)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            cp_async16(st + TcStage::a + kb * kTcM * 32 + tile_off(pt, h), src + kb * 32 + h * 16);
-                    const float2 *ss = p.act_tc + static_cast<size_t>(arow) * nb + b0;
-                    cp_async16(st + TcStage::sc + pt * kTcKB * 8, ss);
-                    cp_async16(st + TcStage::sc + pt * kTcKB * 8 + 16, ss + 2);
-                }
-                // B: 64 weight rows x kTcKB blocks of codes, unpacked; two (row, block) per thread
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int idx = pt + u * 128;          // 0..255
-                    const int col = idx & 63, kb = idx >> 6;
+            for (int j = 0; j < kBPer; ++j) {
+                const int idx = pt + j * kProducerThreads;
+                if (idx < kTcN * kTcKB) {
+                    const int col = idx & (kTcN - 1), kb = idx / kTcN;
                     size_t code_off, sc_off;
                     int row;
                     if (Down) {
@@ -331,123 +391,243 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
                         code_off = col < 32 ? p.layout.gate_codes : p.layout.up_codes;
                         sc_off = col < 32 ? p.layout.gate_scales : p.layout.up_scales;
                     }
-                    const size_t blk = static_cast<size_t>(row) * nb + b0 + kb;
-                    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(ex + code_off) + blk);
+                    const size_t blk = static_cast<size_t>(row) * nb + ks * kTcKB + kb;
+                    wn[j] = __ldg(reinterpret_cast<const uint4 *>(ex + code_off) + blk);
+                    dn[j] = __ldg(reinterpret_cast<const uint16_t *>(ex + sc_off) + blk);
+                }
+            }
+        };
+        int arow[kAPer];
+        if (nstages > 0) prefetch(0);
+        for (int g = 0; g < nstages; ++g) {
+            const int ks = g % ksteps, s = g % kTcStages;
+            if (ks == 0) td = td_next;
+            uint4 wc[kBPer];
+            uint16_t dc[kBPer];
+#pragma unroll
+            for (int j = 0; j < kBPer; ++j) {
+                wc[j] = wn[j];
+                dc[j] = dn[j];
+            }
+            if (g + 1 < nstages) prefetch(g + 1);
+            if (ks == 0) {
+#pragma unroll
+                for (int a = 0; a < kAPer; ++a) {
+                    const int row = pt + a * kProducerThreads;
+                    arow[a] = row < td.z ? (p.act_by_token ? p.pair_token[td.y + row] : td.y + row) : -1;
+                }
+            }
+            if (g >= kTcStages && !mbar_wait(&empty[s], ((g / kTcStages) & 1) ^ 1, p.error)) { failed = true; break; }
+            uint8_t *st = ring + s * TcStage::bytes;
+            const int b0 = ks * kTcKB;
+            // A: pair rows (kTcKB blocks x 2 halves each) plus their block scales
+#pragma unroll
+            for (int a = 0; a < kAPer; ++a) {
+                if (arow[a] < 0) continue;
+                const int row = pt + a * kProducerThreads;
+                const int8_t *src = p.act + static_cast<size_t>(arow[a]) * K + b0 * 32;
+#pragma unroll
+                for (int kb = 0; kb < kTcKB; ++kb)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        cp_async16(st + TcStage::a + kb * kTcM * 32 + tile_off(row, h), src + kb * 32 + h * 16);
+                const float2 *ss = p.act_tc + static_cast<size_t>(arow[a]) * nb + b0;
+#pragma unroll
+                for (int kb = 0; kb < kTcKB; ++kb) cp_async8(st + TcStage::sc + (kb * kTcM + row) * 8, ss + kb);
+            }
+            cp_async_commit();
+            // B: 64 weight rows x kTcKB blocks of codes, unpacked to centred s8
+#pragma unroll
+            for (int j = 0; j < kBPer; ++j) {
+                const int idx = pt + j * kProducerThreads;
+                if (idx < kTcN * kTcKB) {
+                    const int col = idx & (kTcN - 1), kb = idx / kTcN;
                     uint4 lo, hi;
-                    unpack_centred(w, lo, hi);
+                    unpack_centred(wc[j], lo, hi);
                     *reinterpret_cast<uint4 *>(st + TcStage::b + kb * kTcN * 32 + tile_off(col, 0)) = lo;
                     *reinterpret_cast<uint4 *>(st + TcStage::b + kb * kTcN * 32 + tile_off(col, 1)) = hi;
-                    reinterpret_cast<uint16_t *>(st + TcStage::d4)[kb * kTcN + col] =
-                        __ldg(reinterpret_cast<const uint16_t *>(ex + sc_off) + blk);
+                    reinterpret_cast<float *>(st + TcStage::d4)[kb * kTcN + col] = h2f(dc[j]);
                 }
-                cp_async_wait_all();
+            }
+            // publish the previous stage: its copies have landed once at most
+            // this stage's group is pending
+            if (g > 0) {
+                cp_async_wait_group1();
                 fence_proxy_async();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[s]);
+                if (lane == 0) mbar_arrive(&full[(g - 1) % kTcStages]);
             }
+        }
+        if (nstages > 0 && !failed) {
+            cp_async_wait_all();
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[(nstages - 1) % kTcStages]);
         }
     } else {
         // ---------------- epilogue ----------------
-        const int ew = warp - 1 - kTcProducerWarps;        // 0..15
+        const int ew = warp - 1 - kTcProducerWarps;        // 0..7
         const int quarter = warp & 3;                      // TMEM lane quarter this warp may access
-        const int chunk = ew >> 2;                         // 16-column chunk 0..3
+        const int chunk = ew >> 2;                         // 32-column chunk 0..1
         const int m = quarter * 32 + lane;                 // pair row of this thread
-        const uint32_t tq = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + chunk * 16;
-        // initial bias of every region, then release all regions once
-        for (int r = 0; r < kTcRegions; ++r) tmem_st16_const(tq + r * kTcN, kTcBias);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
+        const uint32_t tq = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + chunk * 32;
+        float *xrow = xch + m * kTcXchStride;
+        float *mine = part + (m * 2 + chunk) * 4;
+        const float *other = part + (m * 2 + (chunk ^ 1)) * 4;
         if (lane == 0)
-            for (int r = 0; r < kTcRegions; ++r) mbar_arrive(&tm_empty[r]);
-        int q = 0, kseq = 0, it = 0;
-        for (int item = blockIdx.x; item < total && !failed; item += gridDim.x, ++it) {
+            for (int r = 0; r < kTcRegions; ++r) mbar_arrive(&tm_empty[r]);   // every region starts free
+        const uint64_t unbias = pkf2(-kTcUnbias, -kTcUnbias);
+        int q0 = 0, h0 = 0;   // stage and block-pair sequence numbers at the start of the item
+        for (int item = blockIdx.x; item < total; item += gridDim.x, q0 += ksteps, h0 += nb / 2) {
             const int4 td = p.tiles[item / slabs];
             const int p0 = td.y, n = td.z, slab = item % slabs;
-            float acc[16];
+            const bool live = quarter * 32 < n;   // this warp's lanes hold at least one real pair
+            uint64_t acc[16];                      // 32 fp32 accumulators as packed pairs
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-            for (int ks = 0; ks < ksteps && !failed; ++ks, ++q) {
-                const int s = q % kTcStages;
+            for (int j = 0; j < 16; ++j) acc[j] = 0ull;
+            // Issue the TMEM loads of block pair h (once the MMA has committed it).
+            auto fetch = [&](int h, uint32_t(&v)[32]) -> bool {
+                const int hh = h0 + h, r = hh % kTcRegions;
+                if (!mbar_wait(&tm_full[r], (hh / kTcRegions) & 1, p.error)) return false;
+                tc_fence_after();
+                if (live) tmem_ld_pair(tq + r * 2 * kTcN, v);
+                return true;
+            };
+            // Block pair h: its loads (issued one pair earlier) land and the region
+            // is released at once; the next pair's loads are issued and run while
+            // this pair is scaled and accumulated.
+            auto step = [&](int h, uint32_t(&cur)[32], uint32_t(&nxt)[32]) -> bool {
+                const int hh = h0 + h, r = hh % kTcRegions;
+                const int q = q0 + (2 * h) / kTcKB, s = q % kTcStages, kb = (2 * h) % kTcKB;
+                tmem_wait_ld32(cur);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tm_empty[r]);
+                if (h + 1 < nb / 2 && !fetch(h + 1, nxt)) return false;
                 const uint8_t *st = ring + s * TcStage::bytes;
                 // Acquire the producers' writes of this stage's scales directly.  The
                 // phase cannot have moved on: refilling needs this warp's release below.
-                if (!mbar_wait(&full[s], (q / kTcStages) & 1, p.error)) { failed = true; break; }
-                for (int kb = 0; kb < kTcKB; ++kb, ++kseq) {
-                    const int r = kseq % kTcRegions;
-                    if (!mbar_wait(&tm_full[r], (kseq / kTcRegions) & 1, p.error)) { failed = true; break; }
-                    tc_fence_after();
-                    uint32_t v[16];
-                    tmem_ld16(tq + r * kTcN, v);
-                    tmem_wait_ld();
-                    tmem_st16_const(tq + r * kTcN, kTcBias);
-                    tmem_wait_st();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tm_empty[r]);
-                    const float2 sc = reinterpret_cast<const float2 *>(st + TcStage::sc)[m * kTcKB + kb];
-                    const uint4 *d4v = reinterpret_cast<const uint4 *>(st + TcStage::d4 + (kb * kTcN + chunk * 16) * 2);
-                    const uint4 dA = d4v[0], dB = d4v[1];
-                    const uint32_t dw[8] = {dA.x, dA.y, dA.z, dA.w, dB.x, dB.y, dB.z, dB.w};
+                if (kb == 0 && !mbar_wait(&full[s], (q / kTcStages) & 1, p.error)) return false;
+                if (live) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float d4 = h2f(static_cast<uint16_t>(dw[j >> 1] >> (16 * (j & 1))));
-                        const float t = __int_as_float(v[j]) - 12582912.0f;   // exact: the centred dot
-                        acc[j] = fmaf(d4, fmaf(t, sc.x, sc.y), acc[j]);
+                    for (int b = 0; b < 2; ++b) {
+                        const float2 sc = reinterpret_cast<const float2 *>(st + TcStage::sc)[(kb + b) * kTcM + m];
+                        const uint64_t d8 = pkf2(sc.x, sc.x), c8 = pkf2(sc.y, sc.y);
+                        const ulonglong2 *d4v = reinterpret_cast<const ulonglong2 *>(
+                            st + TcStage::d4 + ((kb + b) * kTcN + chunk * 32) * 4);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const ulonglong2 dd = d4v[j];   // weight scales of 4 columns (broadcast)
+                            // exact dot_c of 2 columns, then acc += d4 * (dot_c * d8 + c8)
+                            const uint64_t t0 = add2(dot16x2(cur[b * 16 + 2 * j]), unbias);
+                            const uint64_t t1 = add2(dot16x2(cur[b * 16 + 2 * j + 1]), unbias);
+                            acc[2 * j] = fma2(dd.x, fma2(t0, d8, c8), acc[2 * j]);
+                            acc[2 * j + 1] = fma2(dd.y, fma2(t1, d8, c8), acc[2 * j + 1]);
+                        }
                     }
                 }
-                if (failed) break;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);   // this warp is done with the stage's scales
-            }
-            if (failed) break;
-            // ---- item epilogue: exchange accumulators through shared memory ----
-#pragma unroll
-            for (int j = 0; j < 16; ++j) xch[m * kTcN + chunk * 16 + j] = acc[j];
-            named_barrier(2, 32 * kTcEpilogueWarps);
+                if (kb + 2 == kTcKB) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);   // done with the stage's scales
+                }
+                return true;
+            };
+            uint32_t va[32], vb[32];
+            bool ok = fetch(0, va);
+            for (int h = 0; h < nb / 2 && ok; h += 2) ok = step(h, va, vb) && step(h + 1, vb, va);
+            if (!ok) tmem_wait_ld();
             if (!Down) {
-                if (chunk == 0 && m < n) {
-                    float mid[32];
-                    int flags = 0;
+                // Gate (chunk 0) and up (chunk 1) accumulators meet in row m of the
+                // exchange; thread (m, chunk) then produces middle values
+                // chunk*16 .. chunk*16+15 of the slab's Q8_1 block.  The first
+                // barrier also tells every epilogue warp whether one gave up.
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) {
+                for (int j = 0; j < 8; ++j) {
+                    float a0, a1, a2, a3;
+                    upk2(acc[2 * j], a0, a1);
+                    upk2(acc[2 * j + 1], a2, a3);
+                    *reinterpret_cast<float4 *>(xrow + chunk * 32 + 4 * j) = make_float4(a0, a1, a2, a3);
+                }
+                if (named_barrier_or(2, 32 * kTcEpilogueWarps, !ok)) { failed = true; break; }
+                const bool real = m < n;
+                float mid[16];
+                int flags = 0;
+#pragma unroll
+                for (int c = 0; c < 16; c += 4) {
+                    const float4 g4 = *reinterpret_cast<const float4 *>(xrow + chunk * 16 + c);
+                    const float4 u4 = *reinterpret_cast<const float4 *>(xrow + 32 + chunk * 16 + c);
+                    const float gs[4] = {g4.x, g4.y, g4.z, g4.w}, us[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
                         int f = 0;
-                        const float g = operand(xch[m * kTcN + c], f), u = operand(xch[m * kTcN + 32 + c], f);
+                        const float g = operand(gs[k], f), u = operand(us[k], f);
                         const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), f);
                         const float val = arithmetic(__fmul_rn(act, u), f);
-                        mid[c] = f ? 0.0f : val;
-                        flags |= f;
+                        mid[c + k] = (f || !real) ? 0.0f : val;
+                        flags |= real ? f : 0;
                     }
-                    int8_t code[32];
-                    const Q8Block qb = quantize_thread32(mid, code);
-                    const size_t pair = static_cast<size_t>(p0 + m);
-                    int4 *dst = reinterpret_cast<int4 *>(p.mid.codes + pair * I + slab * 32);
-                    const int4 *srcv = reinterpret_cast<const int4 *>(code);
-                    dst[0] = srcv[0];
-                    dst[1] = srcv[1];
-                    const int mslabs = I / 32;
-                    p.mid.scales[pair * mslabs + slab] = make_float2(h2f(qb.d), h2f(qb.s));
-                    p.mid_tc[pair * mslabs + slab] = make_float2(h2f(qb.d), qb.c8);
-                    report(flags | qb.flags, p.error);
                 }
+                const Q8Half hq = q8_half_stats(mid);
+                mine[0] = __int_as_float(__float_as_int(hq.amax) | (hq.bad << 31));   // sign bit: non-finite seen
+                mine[1] = hq.sum;
+                named_barrier(2, 32 * kTcEpilogueWarps);
+                const float oa = other[0], os = other[1];
+                const int bad = hq.bad | (__float_as_int(oa) < 0 ? 1 : 0);
+                const float amax = fmaxf(hq.amax, fabsf(oa));
+                const float sum = chunk == 0 ? __fadd_rn(hq.sum, os) : __fadd_rn(os, hq.sum);
+                int8_t code[16];
+                const Q8Codes qc = q8_half_codes(mid, amax, sum, bad, code);
+                reinterpret_cast<int *>(mine)[2] = qc.csum;
+                reinterpret_cast<int *>(mine)[3] = qc.bad_code;
+                named_barrier(2, 32 * kTcEpilogueWarps);
+                const int bad_code = qc.bad_code | reinterpret_cast<const int *>(other)[3];
+                const bool valid = !bad && qc.representable && !bad_code;
+                if (real) {
+                    const size_t pair = static_cast<size_t>(p0 + m);
+                    int4 cv = *reinterpret_cast<const int4 *>(code);
+                    if (!valid) cv = make_int4(0, 0, 0, 0);
+                    *reinterpret_cast<int4 *>(p.mid.codes + pair * I + slab * 32 + chunk * 16) = cv;
+                    if (chunk == 0) {
+                        const int mslabs = I / 32;
+                        const uint16_t hd = (valid && amax != 0.0f) ? qc.d : uint16_t(0);
+                        const uint16_t hs = (valid && amax != 0.0f) ? qc.s : uint16_t(0);
+                        const int csum = valid ? qc.csum + reinterpret_cast<const int *>(other)[2] : 0;
+                        p.mid.scales[pair * mslabs + slab] = make_float2(h2f(hd), h2f(hs));
+                        p.mid_tc[pair * mslabs + slab] =
+                            make_float2(h2f(hd), 8.0f * (static_cast<float>(csum) * h2f(hd) - h2f(hs)));
+                    }
+                    report(flags | (bad ? kFlagInvalid : 0) | ((qc.representable && !bad_code) ? 0 : kFlagArithmetic),
+                           p.error);
+                }
+                // Row m's exchange words are read only by the two threads of row
+                // m before the second barrier and its statistics only after the
+                // third, so the next item may rewrite them without another barrier.
             } else {
-                if (chunk == 0 && m < n) {
+                if (!ok) { failed = true; break; }
+                // The thread's 32 columns become router-weighted contributions in
+                // its own part of row m and are reduce-added by the bulk engine;
+                // the part is rewritten only after the engine has read it.
+                if (m < n) {
                     const float w = p.pair_weight[p0 + m];
                     int flags = 0;
+                    bulk_wait_read0();
 #pragma unroll
-                    for (int c = 0; c < kTcN; ++c) {
-                        const float y = arithmetic(xch[m * kTcN + c], flags);
-                        xch[m * kTcN + c] = arithmetic(__fmul_rn(w, y), flags);
+                    for (int j = 0; j < 8; ++j) {
+                        float y[4];
+                        upk2(acc[2 * j], y[0], y[1]);
+                        upk2(acc[2 * j + 1], y[2], y[3]);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) y[k] = arithmetic(__fmul_rn(w, arithmetic(y[k], flags)), flags);
+                        *reinterpret_cast<float4 *>(xrow + chunk * 32 + 4 * j) = make_float4(y[0], y[1], y[2], y[3]);
                     }
                     fence_proxy_async();
-                    bulk_reduce_add_f32(p.out + static_cast<size_t>(p.pair_token[p0 + m]) * H + slab * kTcN,
-                                        xch + m * kTcN, kTcN * 4);
+                    bulk_reduce_add_f32(
+                        p.out + static_cast<size_t>(p.pair_token[p0 + m]) * H + slab * kTcN + chunk * 32,
+                        xrow + chunk * 32, 32 * 4);
                     bulk_commit();
-                    bulk_wait_read0();
                     report(flags, p.error);
                 }
             }
-            named_barrier(2, 32 * kTcEpilogueWarps);   // xch free for the next item
         }
         if (Down) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // reduce-adds fully done
     }
@@ -456,7 +636,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTcRegions * kTcN);
+        tmem_dealloc(tmem, kTcColumns);
     }
 }
 
