@@ -282,7 +282,9 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
         sr.tile_off = h->tile_off;
         sr.num_tiles = h->num_tiles;
         sr.max_tiles = h->tiles_max;
-        route_small_kernel<<<1, 512, 0, s>>>(sr);
+        // block 0 routes; the others quantise x (one warp per 32-value block)
+        const int qblocks = sr.xq.codes ? (T * (h->desc.hidden / 32) + 15) / 16 : 0;
+        route_small_kernel<<<1 + qblocks, 512, 0, s>>>(sr);
         return cuda_status(cudaGetLastError(), "route_small_kernel");
     }
     route_topk_kernel<<<chunks, kRouteThreads, 0, s>>>(rp);

@@ -407,16 +407,20 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
     __shared__ uint32_t smask[kRouterExperts];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, e = threadIdx.x;
     const int T = p.tokens, H = p.hidden;
-    smask[e] = 0u;
-    // quantise x: one warp per 32-value block
-    for (int b = warp; p.x && sp.xq.codes && b < T * (H / 32); b += 16) {
-        const Q8Lane q = quantize_lane(p.x[static_cast<size_t>(b) * 32 + lane]);
-        sp.xq.codes[static_cast<size_t>(b) * 32 + lane] = q.code;
-        if (lane == 0) {
-            sp.xq.scales[b] = make_float2(h2f(q.d), h2f(q.s));
-            report(q.flags, p.error);
+    if (blockIdx.x > 0) {
+        // blocks 1.. quantise x, one warp per 32-value block, alongside the routing block
+        const int stride = (gridDim.x - 1) * 16;
+        for (int b = (blockIdx.x - 1) * 16 + warp; b < T * (H / 32); b += stride) {
+            const Q8Lane q = quantize_lane(p.x[static_cast<size_t>(b) * 32 + lane]);
+            sp.xq.codes[static_cast<size_t>(b) * 32 + lane] = q.code;
+            if (lane == 0) {
+                sp.xq.scales[b] = make_float2(h2f(q.d), h2f(q.s));
+                report(q.flags, p.error);
+            }
         }
+        return;
     }
+    smask[e] = 0u;
     __syncthreads();
     for (int t = warp; t < T; t += 16) route_one_token(p, t, t, smask, lane);
     __syncthreads();   // ids/weights (global) and smask complete
