@@ -67,6 +67,17 @@ def make_logits(rng, cfg, T):
     return rng.standard_normal((T, E)).astype(np.float32)
 
 
+def profile_traffic(name):
+    """DRAM bytes (read + write) per launch recorded in a committed ncu summary."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", name)):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 class ClockSampler:
     """nvidia-smi clocks/throttle reasons sampled during the timed region."""
 
@@ -404,8 +415,26 @@ def run_ours(args, cfg):
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except Exception:
         pass
-    peak = float(peaks.get("hbm_gbs", 6650.0))
-    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    if T <= 32:
+        # decode: weight streaming, HBM-bound
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        roof = {"bound": "hbm", "kernel": "stream_gate_up_kernel", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9,
+                "peak": peak, "unit": "GB/s", "bytes_per_launch": gu_bytes,
+                "traffic": profile_traffic("stream_gate_up_decode_T8.md") if cfg["tokens"] == 8 else None,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650 GB/s"}
+    else:
+        # prefill: int8 MACs of the gate/up contraction over all routed + shared pairs
+        ops = 2.0 * T * (K_TOP + 1) * (2 * I) * H
+        bf16 = float(peaks.get("bf16_tflops", 1590.0))
+        peak = 2.0 * bf16   # dense int8 rate = 2x dense bf16 rate on B200
+        roof = {"bound": "tensor", "kernel": "gate/up launch (tc_expert_kernel + stream_gate_up_kernel)",
+                "achieved": ops / (gu_ms * 1e-3) / 1e12, "peak": peak, "unit": "TOP/s (int8)",
+                "ops_per_launch": ops,
+                "traffic": profile_traffic("tc_expert_prefill_T4096_zipf.md") if cfg["tokens"] == 4096 else None,
+                "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops (of measured)" if peaks else "2 x fallback 1590"}
+    roof["frac"] = roof["achieved"] / peak
+    roof["launch_ms"] = gu_ms
+    roof["down_launch_ms"] = dn_ms
 
     tokens_per_step = T * U * L * world
     result = {
@@ -420,11 +449,10 @@ def run_ours(args, cfg):
                    "graph": "one CUDA graph per step"},
         "e2e": {"value": tokens_per_step / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms},
-        "roofline": {"bound": "hbm", "kernel": "gate_up_kernel", "achieved": achieved, "peak": peak,
-                     "unit": "GB/s", "frac": achieved / peak, "traffic": None,
-                     "bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "down_launch_ms": dn_ms,
-                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650 GB/s"},
-        "gpu_launches": args.steps * U * L * (3 if T <= 32 else 7),
+        "roofline": roof,
+        # per layer: fused routing + 2 streaming GEMVs (T <= 32); else quantise + 4 routing
+        # kernels + streaming and tensor-core gate/up and down
+        "gpu_launches": args.steps * U * L * (3 if T <= 32 else 9),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
