@@ -36,6 +36,8 @@ EXPORTED = [
     "moe_expert_destroy", "moe_expert_check_quantization", "moe_expert_linear", "moe_expert_run",
     "moe_route_groups_create", "moe_route_groups_destroy", "moe_route_groups_prepare",
     "moe_route_groups_assignments", "moe_route_groups_counts", "moe_route_groups_message",
+    "moe_route_noalloc", "moe_ep_weights_create", "moe_ep_create", "moe_ep_destroy", "moe_ep_ipc_handle",
+    "moe_ep_open_peers", "moe_ep_forward", "moe_ep_read_flags",
 ]
 
 
@@ -99,6 +101,13 @@ def library(path=LIB_PATH):
         "moe_route_groups_assignments": (SZ, [P, P, SZ]),
         "moe_route_groups_counts": (I, [P, P]),
         "moe_route_groups_message": (ctypes.c_char_p, []),
+        "moe_ep_weights_create": (I, [DESC_P, I, I, ctypes.POINTER(P)]),
+        "moe_ep_create": (I, [DESC_P, I, I, ctypes.POINTER(P)]),
+        "moe_ep_destroy": (I, [P]),
+        "moe_ep_ipc_handle": (I, [P, P]),
+        "moe_ep_open_peers": (I, [P, P]),
+        "moe_ep_forward": (I, [P, P, P, P, I, P, I, P]),
+        "moe_ep_read_flags": (I, [P, ctypes.POINTER(I), I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -226,6 +235,76 @@ class MoeLayer:
             self.handle = None
 
     __del__ = close
+
+
+EP_HANDLE_BYTES = 64
+
+
+class EpWeights(MoeWeights):
+    """Expert shard of rank `rank` of `world`: routed experts
+    [rank*512/world, (rank+1)*512/world) as local 0.., then the shared expert."""
+
+    def __init__(self, desc, rank, world):
+        self.desc = desc
+        self.rank, self.world = rank, world
+        h = P()
+        check(library().moe_ep_weights_create(ctypes.byref(desc), rank, world, ctypes.byref(h)))
+        self.handle = h
+
+
+class EpLayer:
+    """One rank of the expert-parallel layer (one process per GPU).
+
+    Peer buffers are mapped with CUDA IPC; `connect(exchange)` takes a
+    function that all-gathers one bytes object per rank (for example
+    `exchange_handles` over a torch.distributed group)."""
+
+    def __init__(self, desc, rank, world):
+        self.desc, self.rank, self.world = desc, rank, world
+        h = P()
+        check(library().moe_ep_create(ctypes.byref(desc), rank, world, ctypes.byref(h)))
+        self.handle = h
+
+    def ipc_handle(self):
+        buf = ctypes.create_string_buffer(EP_HANDLE_BYTES)
+        check(library().moe_ep_ipc_handle(self.handle, buf))
+        return buf.raw
+
+    def open_peers(self, handles):
+        if len(handles) != self.world or any(len(b) != EP_HANDLE_BYTES for b in handles):
+            raise ValueError("need one 64-byte handle per rank, in rank order")
+        blob = ctypes.create_string_buffer(b"".join(handles), EP_HANDLE_BYTES * self.world)
+        check(library().moe_ep_open_peers(self.handle, blob))
+
+    def connect(self, exchange):
+        self.open_peers(exchange(self.ipc_handle()))
+
+    def forward(self, weights, x, logits, out, accumulate=True, stream=None):
+        T = x.shape[0]
+        flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
+        check(library().moe_ep_forward(self.handle, weights.handle, _ptr(x), _ptr(logits), T, _ptr(out), flag,
+                                       _stream(stream)))
+
+    def read_flags(self, clear=True, stream=None):
+        f = ctypes.c_int(0)
+        check(library().moe_ep_read_flags(self.handle, ctypes.byref(f), int(clear), _stream(stream)))
+        return f.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            library().moe_ep_destroy(self.handle)
+            self.handle = None
+
+    __del__ = close
+
+
+def exchange_handles(handle, group=None):
+    """All-gather one bytes object per rank over a torch.distributed group
+    (any backend): the host-side plumbing of the peer mapping."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    return out
 
 
 def route_noalloc(logits, error=None, stream=None):

@@ -1,0 +1,352 @@
+// ep_kernels.cuh -- expert parallelism over peer memory (NVLink / NVSwitch).
+//
+// Rank r of P owns routed experts [r*E/P, (r+1)*E/P) plus a replica of the
+// shared expert, and its own shard of the tokens.  One forward:
+//   1. quantise + route the rank's tokens (top-10 over all 512 experts);
+//   2. plan: for every token the set of destination ranks (ranks owning one
+//      of its experts, plus the rank itself, which runs the shared expert, so
+//      own token t is own slot t) and its slot in each destination's receive
+//      region (stable, in token order);
+//   3. dispatch: one warp per (token, destination) stores the token's Q8_1
+//      row, tensor-core block constants and its (local expert, weight) list
+//      straight into the destination's receive buffer (peer stores); the
+//      last CTA publishes, per destination, the slot count and the epoch;
+//   4. every rank waits for all P epochs, groups its received slots by local
+//      expert (the single-GPU grouping kernels over slot masks) and runs the
+//      expert kernels, accumulating each slot's weighted expert outputs into
+//      its local partial buffer;
+//   5. it publishes "done" to every peer; after all peers are done, each rank
+//      pulls, for each of its tokens, the partial rows from the destinations
+//      it used (peer loads, destinations in ascending order) and adds them
+//      into its residual.
+// Receive regions are fixed per source (slot = source * T_max + index), so no
+// global exchange of counts is needed.  Epochs live in device memory and
+// advance once per forward on every rank, so a captured CUDA graph replays
+// correctly.  Every wait on a peer is bounded (kFlagTimeout on expiry).
+#pragma once
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace qmoe {
+
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpSlotIds = kTopK;   // (local expert, weight) entries per received slot
+
+// Control words written by peers (one set per rank, in the exported arena).
+struct EpCtl {
+    uint32_t recv_epoch[kEpMaxRanks];   // by source: dispatch of this epoch complete
+    uint32_t recv_count[kEpMaxRanks];   // by source: slots written this epoch
+    uint32_t done_epoch[kEpMaxRanks];   // by destination: partial rows of this epoch final
+    uint32_t pad[8];
+};
+
+// Byte offsets inside a rank's exported arena (identical on every rank).
+struct EpLayout {
+    size_t codes, scales, tc, ids, w, partial, ctl, bytes;
+};
+inline EpLayout make_ep_layout(int H, int slots) {
+    EpLayout L;
+    size_t o = 0;
+    auto take = [&](size_t n) { const size_t r = o; o = (o + n + 255) & ~size_t(255); return r; };
+    L.ctl = take(sizeof(EpCtl));
+    L.codes = take(static_cast<size_t>(slots) * H);
+    L.scales = take(static_cast<size_t>(slots) * (H / 32) * 8);
+    L.tc = take(static_cast<size_t>(slots) * (H / 32) * 8);
+    L.ids = take(static_cast<size_t>(slots) * kEpSlotIds * 4);
+    L.w = take(static_cast<size_t>(slots) * kEpSlotIds * 4);
+    L.partial = take(static_cast<size_t>(slots) * H * 4);
+    L.bytes = o;
+    return L;
+}
+
+struct EpPeers {
+    uint8_t *base[kEpMaxRanks];   // every rank's exported arena, mapped here
+};
+
+struct EpParams {
+    EpPeers peers;
+    EpLayout L;
+    int rank, world, ecount, t_max, tokens, hidden;
+    const int32_t *ids;           // [T][10] global expert ids of this rank's tokens
+    const float *weights;         // [T][10]
+    const int8_t *xcodes;         // [T][H]
+    const float2 *xscales;        // [T][H/32]
+    const float2 *xtc;            // [T][H/32]
+    int32_t *pos;                 // [T][kEpMaxRanks] slot index in each destination
+    uint8_t *dmask;               // [T] destination ranks
+    int32_t *counts;              // [kEpMaxRanks] slots sent to each destination
+    uint32_t *epoch;              // device epoch counter (local)
+    uint32_t *blocks_done;        // dispatch completion counter (local)
+    float *out;                   // [T][H] residual (combine)
+    int *error;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Plan (one CTA of 1024 threads): destination masks and per-destination
+// exclusive positions in token order; also advances the epoch.
+__global__ void __launch_bounds__(1024) ep_plan_kernel(EpParams p) {
+    __shared__ unsigned long long wsum[2][32];
+    __shared__ int running[kEpMaxRanks];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < kEpMaxRanks) running[tid] = 0;
+    if (tid == 0) *p.epoch += 1u;
+    __syncthreads();
+    for (int c = 0; c < p.tokens; c += 1024) {
+        const int t = c + tid;
+        uint32_t mask = 0u;
+        if (t < p.tokens) {
+            mask = 1u << p.rank;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                const int e = p.ids[t * kTopK + k];
+                if (e >= 0 && e < p.ecount * p.world) mask |= 1u << (e / p.ecount);
+            }
+            p.dmask[t] = static_cast<uint8_t>(mask);
+        }
+        // 16-bit counters per destination packed in two 64-bit words
+        unsigned long long lo = 0ull, hi = 0ull;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) lo |= static_cast<unsigned long long>((mask >> d) & 1u) << (16 * d);
+#pragma unroll
+        for (int d = 0; d < 4; ++d) hi |= static_cast<unsigned long long>((mask >> (d + 4)) & 1u) << (16 * d);
+        unsigned long long ilo = lo, ihi = hi;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long a = __shfl_up_sync(0xffffffffu, ilo, o), b = __shfl_up_sync(0xffffffffu, ihi, o);
+            if (lane >= o) { ilo += a; ihi += b; }
+        }
+        if (lane == 31) { wsum[0][warp] = ilo; wsum[1][warp] = ihi; }
+        __syncthreads();
+        if (warp == 0) {
+            unsigned long long a = wsum[0][lane], b = wsum[1][lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+                if (lane >= o) { a += x; b += y; }
+            }
+            wsum[0][lane] = a;   // inclusive warp totals
+            wsum[1][lane] = b;
+        }
+        __syncthreads();
+        const unsigned long long plo = (warp ? wsum[0][warp - 1] : 0ull) + ilo - lo;
+        const unsigned long long phi = (warp ? wsum[1][warp - 1] : 0ull) + ihi - hi;
+        if (t < p.tokens) {
+#pragma unroll
+            for (int d = 0; d < kEpMaxRanks; ++d) {
+                const unsigned long long v = d < 4 ? plo >> (16 * d) : phi >> (16 * (d - 4));
+                p.pos[t * kEpMaxRanks + d] = running[d] + static_cast<int>(v & 0xffffu);
+            }
+        }
+        __syncthreads();
+        if (tid < kEpMaxRanks) {
+            const unsigned long long v = tid < 4 ? wsum[0][31] >> (16 * tid) : wsum[1][31] >> (16 * (tid - 4));
+            running[tid] += static_cast<int>(v & 0xffffu);
+        }
+        __syncthreads();
+    }
+    if (tid < kEpMaxRanks) p.counts[tid] = running[tid];
+}
+
+// Dispatch: one warp per (token, destination).  Peer stores of the row, then
+// the last CTA publishes counts and the epoch to every destination.
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
+    const int lane = threadIdx.x & 31;
+    const int H = p.hidden, nb = H / 32;
+    const int items = p.tokens * p.world;
+    for (int it = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; it < items; it += (gridDim.x * blockDim.x) >> 5) {
+        const int t = it / p.world, d = it % p.world;
+        if (!((p.dmask[t] >> d) & 1u)) continue;
+        const size_t slot = static_cast<size_t>(p.rank) * p.t_max + p.pos[t * kEpMaxRanks + d];
+        uint8_t *dst = p.peers.base[d];
+        // codes: H bytes as 16-byte vectors
+        const uint4 *sc = reinterpret_cast<const uint4 *>(p.xcodes + static_cast<size_t>(t) * H);
+        uint4 *dc = reinterpret_cast<uint4 *>(dst + p.L.codes + slot * H);
+        for (int i = lane; i < H / 16; i += 32) dc[i] = sc[i];
+        // block scales and tensor-core constants: nb float2 each
+        const uint4 *ss = reinterpret_cast<const uint4 *>(p.xscales + static_cast<size_t>(t) * nb);
+        uint4 *ds = reinterpret_cast<uint4 *>(dst + p.L.scales + slot * nb * 8);
+        const uint4 *st = reinterpret_cast<const uint4 *>(p.xtc + static_cast<size_t>(t) * nb);
+        uint4 *dt = reinterpret_cast<uint4 *>(dst + p.L.tc + slot * nb * 8);
+        for (int i = lane; i < nb / 2; i += 32) {
+            ds[i] = ss[i];
+            dt[i] = st[i];
+        }
+        // (local expert, weight) list: the routed experts d owns (the shared
+        // expert of the own tokens is added by the receiver's grouping)
+        if (lane < kEpSlotIds) {
+            int id = -1;
+            float w = 0.0f;
+            const int e = p.ids[t * kTopK + lane];
+            if (e >= 0 && e / p.ecount == d) {
+                id = e - d * p.ecount;
+                w = p.weights[t * kTopK + lane];
+            }
+            reinterpret_cast<int32_t *>(dst + p.L.ids)[slot * kEpSlotIds + lane] = id;
+            reinterpret_cast<float *>(dst + p.L.w)[slot * kEpSlotIds + lane] = w;
+        }
+    }
+    // completion: every CTA fences its peer stores before counting itself
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const uint32_t ticket = atomicAdd(p.blocks_done, 1u);
+        if (ticket == gridDim.x - 1) {
+            __threadfence_system();
+            const uint32_t epoch = *p.epoch;
+            for (int d = 0; d < p.world; ++d) {
+                EpCtl *c = reinterpret_cast<EpCtl *>(p.peers.base[d] + p.L.ctl);
+                c->recv_count[p.rank] = static_cast<uint32_t>(p.counts[d]);
+                st_release_sys(&c->recv_epoch[p.rank], epoch);
+            }
+            *p.blocks_done = 0u;
+        }
+    }
+}
+
+// Wait until every peer has published the current epoch in `flags` (one
+// lane per peer, bounded by ~2^31 cycles).
+__global__ void ep_wait_kernel(const uint32_t *flags, const uint32_t *epoch, int world, int *error) {
+    const int d = threadIdx.x;
+    if (d >= world) return;
+    const uint32_t want = *epoch;
+    const long long t0 = clock64();
+    while (ld_acquire_sys(&flags[d]) != want) {
+        if (clock64() - t0 > (1ll << 31)) {
+            atomicOr(error, kFlagTimeout);
+            return;
+        }
+        __nanosleep(64);
+    }
+}
+
+// Received slots -> chunk masks over local experts (32 slots per CTA), and
+// zeroed partial rows for the valid slots.
+struct EpGroupParams {
+    const uint8_t *arena;   // own exported arena
+    EpLayout L;
+    int t_max, slots, hidden;
+    uint32_t *masks;        // [slots/32][512]
+    float *partial;
+};
+__device__ __forceinline__ bool ep_slot_valid(const EpCtl *c, int slot, int t_max) {
+    return static_cast<uint32_t>(slot % t_max) < c->recv_count[slot / t_max];
+}
+__global__ void __launch_bounds__(256) ep_masks_kernel(EpGroupParams g) {
+    __shared__ uint32_t smask[kRouterExperts];
+    const EpCtl *c = reinterpret_cast<const EpCtl *>(g.arena + g.L.ctl);
+    const int32_t *ids = reinterpret_cast<const int32_t *>(g.arena + g.L.ids);
+    for (int e = threadIdx.x; e < kRouterExperts; e += blockDim.x) smask[e] = 0u;
+    __syncthreads();
+    const int s0 = blockIdx.x * kChunk;
+    for (int i = threadIdx.x; i < kChunk * kEpSlotIds; i += blockDim.x) {
+        const int j = i / kEpSlotIds, k = i % kEpSlotIds, slot = s0 + j;
+        if (slot < g.slots && ep_slot_valid(c, slot, g.t_max)) {
+            const int id = ids[static_cast<size_t>(slot) * kEpSlotIds + k];
+            if (id >= 0 && id < kRouterExperts) atomicOr(&smask[id], 1u << j);
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < kRouterExperts; e += blockDim.x)
+        g.masks[static_cast<size_t>(blockIdx.x) * kRouterExperts + e] = smask[e];
+    // zero the partial rows of this chunk's valid slots
+    const int H4 = g.hidden / 4;
+    for (int i = threadIdx.x; i < kChunk * H4; i += blockDim.x) {
+        const int slot = s0 + i / H4;
+        if (slot < g.slots && ep_slot_valid(c, slot, g.t_max))
+            reinterpret_cast<float4 *>(g.partial)[static_cast<size_t>(slot) * H4 + i % H4] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// Stable placement of received (slot, local expert) pairs, as
+// route_scatter_kernel but over slot lists of kEpSlotIds entries.
+struct EpScatterParams {
+    const uint8_t *arena;
+    EpLayout L;
+    const uint32_t *masks;
+    const int32_t *base;
+    const int32_t *offsets;
+    int32_t *pair_token;
+    int32_t *pair_rank;
+    float *pair_weight;
+    TileRec *tiles;
+    const int32_t *tile_off;
+    int max_tiles;
+};
+__global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterParams p) {
+    const int chunk = blockIdx.x, e = blockIdx.y * 256 + threadIdx.x;
+    const size_t idx = static_cast<size_t>(chunk) * kRouterExperts + e;
+    uint32_t m = p.masks[idx];
+    if (!m) return;
+    const int32_t *ids = reinterpret_cast<const int32_t *>(p.arena + p.L.ids);
+    const float *ws = reinterpret_cast<const float *>(p.arena + p.L.w);
+    int pos = p.offsets[e] + p.base[idx];
+    while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1u;
+        const int slot = chunk * kChunk + j;
+        int r = 0;
+#pragma unroll
+        for (int k = 0; k < kEpSlotIds; ++k)
+            if (ids[static_cast<size_t>(slot) * kEpSlotIds + k] == e) r = k;
+        const float w = ws[static_cast<size_t>(slot) * kEpSlotIds + r];
+        p.pair_token[pos] = slot;
+        if (p.pair_rank) p.pair_rank[pos] = r;
+        p.pair_weight[pos] = w;
+        if (p.tiles && p.tile_off[e] >= 0) {
+            const int local = pos - p.offsets[e];
+            const int tile = p.tile_off[e] + local / kGemvTile;
+            if (tile < p.max_tiles) {
+                p.tiles[tile].tok[local % kGemvTile] = slot;
+                p.tiles[tile].w[local % kGemvTile] = w;
+            }
+        }
+        ++pos;
+    }
+}
+
+// Publish "partial rows final" to every peer.
+__global__ void ep_done_kernel(EpPeers peers, EpLayout L, int rank, int world, const uint32_t *epoch) {
+    const int d = threadIdx.x;
+    if (d >= world) return;
+    __threadfence_system();
+    EpCtl *c = reinterpret_cast<EpCtl *>(peers.base[d] + L.ctl);
+    st_release_sys(&c->done_epoch[rank], *epoch);
+}
+
+// Combine: out[t] += sum over the token's destinations d (ascending) of the
+// partial row d holds for it.  One CTA of H/8 threads per token, 8 floats each.
+__global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
+    const int t = blockIdx.x;
+    if (t >= p.tokens) return;
+    const uint32_t mask = p.dmask[t];
+    const int H = p.hidden;
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int d = 0; d < p.world; ++d) {
+            if (!((mask >> d) & 1u)) continue;
+            const size_t slot = static_cast<size_t>(p.rank) * p.t_max + p.pos[t * kEpMaxRanks + d];
+            const float4 v = reinterpret_cast<const float4 *>(p.peers.base[d] + p.L.partial)[slot * (H / 4) + i];
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        float4 *o = reinterpret_cast<float4 *>(p.out + static_cast<size_t>(t) * H) + i;
+        float4 r = *o;
+        r.x = __fadd_rn(r.x, acc.x);
+        r.y = __fadd_rn(r.y, acc.y);
+        r.z = __fadd_rn(r.z, acc.z);
+        r.w = __fadd_rn(r.w, acc.w);
+        *o = r;
+    }
+}
+
+}  // namespace qmoe

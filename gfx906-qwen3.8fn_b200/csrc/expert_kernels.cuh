@@ -80,7 +80,8 @@ __device__ __forceinline__ uint64_t synth_base(uint64_t seed, uint32_t layer, ui
 
 // Grid-stride over (expert, matrix, block); writes the planar layout.
 __global__ void __launch_bounds__(256)
-synth_kernel(uint8_t *base, ExpertLayout L, int experts_total, uint64_t seed, uint32_t layer) {
+synth_kernel(uint8_t *base, ExpertLayout L, int experts_total, uint64_t seed, uint32_t layer, int e_first,
+             int e_count) {
     const size_t gate_blocks = static_cast<size_t>(L.inter) * (L.hidden / 32);
     const size_t per_expert = 3 * gate_blocks;  // gate, up, down have equal block counts
     const size_t total = per_expert * experts_total;
@@ -90,7 +91,9 @@ synth_kernel(uint8_t *base, ExpertLayout L, int experts_total, uint64_t seed, ui
         const size_t rem = g % per_expert;
         const uint32_t m = static_cast<uint32_t>(rem / gate_blocks);
         const size_t i = rem % gate_blocks;
-        const uint64_t b = synth_base(seed, layer, e, m);
+        // local expert e < e_count is global expert e_first + e; the one after is the shared expert
+        const uint32_t ge = e < static_cast<uint32_t>(e_count) ? static_cast<uint32_t>(e_first) + e : 512u;
+        const uint64_t b = synth_base(seed, layer, ge, m);
         const uint64_t c0 = mix64(b + (i << 6) + 0), c1 = mix64(b + (i << 6) + 1);
         uint32_t mx = 0;
 #pragma unroll 4

@@ -20,6 +20,7 @@
 #include "route_kernels.cuh"
 #include "stream_kernels.cuh"
 #include "tc_kernels.cuh"
+#include "ep_kernels.cuh"
 
 using namespace qmoe;
 
@@ -101,6 +102,8 @@ struct moe_weights_s {
     moe_layer_desc desc;
     ExpertLayout layout;
     int experts_total;       // routed + shared
+    int expert_first = 0;    // global id of local expert 0 (expert-parallel shards)
+    int expert_count = kRouterExperts;   // routed experts held; the shared expert follows
     uint8_t *base = nullptr; // experts_total * layout.bytes
     float *gate_vec = nullptr;
     uint8_t *staging = nullptr;  // canonical bytes of one expert (3 matrices)
@@ -454,7 +457,8 @@ int moe_weights_synthesize(moe_weights_t w, uint64_t seed, uint32_t layer, void 
     DeviceGuard guard(w->desc.device);
     MOE_CUDA(guard.status);
     auto s = static_cast<cudaStream_t>(stream);
-    synth_kernel<<<sm_count(w->desc.device) * 8, 256, 0, s>>>(w->base, w->layout, w->experts_total, seed, layer);
+    synth_kernel<<<sm_count(w->desc.device) * 8, 256, 0, s>>>(w->base, w->layout, w->experts_total, seed, layer,
+                                                              w->expert_first, w->expert_count);
     return cuda_status(cudaGetLastError(), "synth_kernel");
 }
 
@@ -937,3 +941,335 @@ extern "C" int moe_route_noalloc(const float *logits, int tokens, int32_t *ids, 
     MOE_CUDA(cudaMemcpyAsync(offsets, offs, (kRouterExperts + 1) * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     return MOE_OK;
 }
+
+// ------------------------------------------------- expert parallelism --
+// Rank-local state.  `tx` is an ordinary layer workspace for the rank's own
+// tokens (quantisation, routing, shared gate); `rx` views the received slots
+// as the "tokens" of the expert kernels: its x rows are the exported receive
+// buffer and its output is the exported partial buffer.
+struct moe_ep_s {
+    moe_layer_desc desc;
+    int rank = 0, world = 1, ecount = kRouterExperts, t_max = 0, slots = 0, rx_tiles = 0, rx_pairs = 0;
+    bool tc = false;                 // received groups may use the tensor-core kernels
+    moe_layer_s *tx = nullptr;
+    moe_layer_s rx;                  // views into `exported` and `local`
+    EpLayout L;
+    uint8_t *exported = nullptr;     // IPC-exported arena (EpLayout)
+    Arena local;                     // rx workspace + plan buffers
+    EpPeers peers{};
+    bool opened[kEpMaxRanks] = {};
+    int32_t *pos = nullptr, *counts = nullptr;
+    uint8_t *dmask = nullptr;
+    uint32_t *epoch = nullptr, *blocks_done = nullptr;
+};
+
+namespace {
+
+void ep_take_rx(moe_ep_s *ep, Arena &a) {
+    const int H = ep->desc.hidden, I = ep->desc.inter, S = ep->slots;
+    moe_layer_s &r = ep->rx;
+    const int pairs = ep->rx_pairs;
+    r.mid.codes = a.take<int8_t>(static_cast<size_t>(pairs) * I);
+    r.mid.scales = a.take<float2>(static_cast<size_t>(pairs) * (I / 32));
+    r.masks = a.take<uint32_t>(static_cast<size_t>(S / kChunk) * kRouterExperts);
+    r.base = a.take<int32_t>(static_cast<size_t>(S / kChunk) * kRouterExperts);
+    r.counts = a.take<int32_t>(kRouterExperts);
+    r.offsets = a.take<int32_t>(kRouterExperts + 2);
+    r.pair_token = a.take<int32_t>(pairs);
+    r.pair_rank = a.take<int32_t>(pairs);
+    r.pair_weight = a.take<float>(pairs);
+    r.tiles = a.take<TileRec>(ep->rx_tiles);
+    r.tile_off = a.take<int32_t>(kRouterExperts);
+    r.num_tiles = a.take<int>(1);
+    r.error = a.take<int>(1);
+    r.tc.mid_tc = a.take<float2>(static_cast<size_t>(pairs) * (I / 32));
+    r.tc.max_tiles = pairs / kTcM + kRouterExperts + 2 + ep->t_max / kTcM;
+    r.tc.tiles = a.take<int4>(r.tc.max_tiles);
+    r.tc.num_tiles = a.take<int>(1);
+    ep->pos = a.take<int32_t>(static_cast<size_t>(ep->t_max) * kEpMaxRanks);
+    ep->dmask = a.take<uint8_t>(ep->t_max);
+    ep->counts = a.take<int32_t>(kEpMaxRanks);
+    ep->epoch = a.take<uint32_t>(1);
+    ep->blocks_done = a.take<uint32_t>(1);
+    (void)H;
+}
+
+EpParams ep_params(moe_ep_s *ep, int tokens, float *out) {
+    EpParams p;
+    p.peers = ep->peers;
+    p.L = ep->L;
+    p.rank = ep->rank;
+    p.world = ep->world;
+    p.ecount = ep->ecount;
+    p.t_max = ep->t_max;
+    p.tokens = tokens;
+    p.hidden = ep->desc.hidden;
+    p.ids = ep->tx->ids;
+    p.weights = ep->tx->weights;
+    p.xcodes = ep->tx->xq.codes;
+    p.xscales = ep->tx->xq.scales;
+    p.xtc = ep->tx->tc.x_tc;
+    p.pos = ep->pos;
+    p.dmask = ep->dmask;
+    p.counts = ep->counts;
+    p.epoch = ep->epoch;
+    p.blocks_done = ep->blocks_done;
+    p.out = out;
+    p.error = ep->rx.error;
+    return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_ep_weights_create(const moe_layer_desc *desc, int rank, int world, moe_weights_t *out) {
+    if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    if (const int st = validate_desc(desc)) return st;
+    if (!(world == 1 || world == 2 || world == 4 || world == 8) || rank < 0 || rank >= world)
+        return fail(MOE_INVALID_ARGUMENT, "world must be 1, 2, 4 or 8 and 0 <= rank < world");
+    DeviceGuard guard(desc->device);
+    MOE_CUDA(guard.status);
+    auto *w = new (std::nothrow) moe_weights_s();
+    if (!w) return fail(MOE_OUT_OF_MEMORY, "host allocation");
+    w->desc = *desc;
+    w->layout = make_layout(desc->hidden, desc->inter);
+    w->expert_count = kRouterExperts / world;
+    w->expert_first = rank * w->expert_count;
+    w->experts_total = w->expert_count + desc->has_shared;
+    cudaError_t e = cudaMalloc(&w->base, w->layout.bytes * w->experts_total);
+    if (e == cudaSuccess) e = cudaMalloc(&w->gate_vec, sizeof(float) * desc->hidden);
+    if (e == cudaSuccess) e = cudaMalloc(&w->staging, w->layout.bytes / 16 * 18);
+    if (e == cudaSuccess) e = cudaMemset(w->gate_vec, 0, sizeof(float) * desc->hidden);
+    if (e != cudaSuccess) {
+        cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->staging);
+        delete w;
+        return cuda_status(e, "moe_ep_weights_create");
+    }
+    *out = w;
+    return MOE_OK;
+}
+
+int moe_ep_create(const moe_layer_desc *desc, int rank, int world, moe_ep_t *out) {
+    if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
+    *out = nullptr;
+    if (const int st = validate_desc(desc)) return st;
+    if (!(world == 1 || world == 2 || world == 4 || world == 8) || rank < 0 || rank >= world)
+        return fail(MOE_INVALID_ARGUMENT, "world must be 1, 2, 4 or 8 and 0 <= rank < world");
+    if (desc->max_tokens > 32768) return fail(MOE_INVALID_ARGUMENT, "expert-parallel max_tokens is 1..32768");
+    DeviceGuard guard(desc->device);
+    MOE_CUDA(guard.status);
+    auto *ep = new (std::nothrow) moe_ep_s();
+    if (!ep) return fail(MOE_OUT_OF_MEMORY, "host allocation");
+    ep->desc = *desc;
+    ep->rank = rank;
+    ep->world = world;
+    ep->ecount = kRouterExperts / world;
+    ep->t_max = (desc->max_tokens + kChunk - 1) / kChunk * kChunk;   // slot regions of whole chunks
+    ep->slots = world * ep->t_max;
+    ep->tc = ep->t_max > kChunk;
+    ep->rx_pairs = ep->slots * kTopK + ep->t_max;
+    ep->rx_tiles = ep->rx_pairs / kGemvTile + kRouterExperts + 1 + ep->t_max / kGemvTile + 1;
+    auto cleanup = [&](int st) {
+        if (ep->tx) moe_layer_destroy(ep->tx);
+        cudaFree(ep->exported);
+        cudaFree(ep->local.base);
+        delete ep;
+        return st;
+    };
+    if (const int st = moe_layer_create(desc, &ep->tx)) return cleanup(st);
+    const int H = desc->hidden, I = desc->inter;
+    ep->L = make_ep_layout(H, ep->slots);
+    cudaError_t e = cudaMalloc(&ep->exported, ep->L.bytes);
+    if (e == cudaSuccess) e = cudaMemset(ep->exported, 0, ep->L.bytes);
+    // shape stamp read back by peers before they map this arena
+    const uint32_t stamp[4] = {static_cast<uint32_t>(ep->L.bytes), static_cast<uint32_t>(ep->L.bytes >> 32),
+                               static_cast<uint32_t>(world), static_cast<uint32_t>(ep->t_max)};
+    if (e == cudaSuccess)
+        e = cudaMemcpy(ep->exported + ep->L.ctl + offsetof(EpCtl, pad), stamp, sizeof(stamp), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cleanup(cuda_status(e, "moe_ep_create"));
+    for (int pass = 0; pass < 2; ++pass) {
+        ep->local.used = 0;
+        ep_take_rx(ep, ep->local);
+        if (pass == 0) {
+            const size_t bytes = ep->local.used + 256;
+            e = cudaMalloc(&ep->local.base, bytes);
+            if (e == cudaSuccess) e = cudaMemset(ep->local.base, 0, bytes);
+            if (e != cudaSuccess) return cleanup(cuda_status(e, "moe_ep_create"));
+        }
+    }
+    moe_layer_s &r = ep->rx;
+    r.desc = *desc;
+    r.desc.max_tokens = ep->slots;
+    r.layout = make_layout(H, I);
+    r.sms = ep->tx->sms;
+    r.chunks_max = ep->slots / kChunk;
+    r.pairs_max = ep->rx_pairs;
+    r.tiles_max = ep->rx_tiles;
+    r.xq.codes = reinterpret_cast<int8_t *>(ep->exported + ep->L.codes);
+    r.xq.scales = reinterpret_cast<float2 *>(ep->exported + ep->L.scales);
+    r.tc.x_tc = reinterpret_cast<float2 *>(ep->exported + ep->L.tc);
+    r.gu_stages = ep->tx->gu_stages;
+    r.dn_stages = ep->tx->dn_stages;
+    ep->peers.base[rank] = ep->exported;
+    *out = ep;
+    return MOE_OK;
+}
+
+int moe_ep_destroy(moe_ep_t ep) {
+    if (!ep) return MOE_OK;
+    DeviceGuard guard(ep->desc.device);
+    cudaDeviceSynchronize();
+    for (int d = 0; d < ep->world; ++d)
+        if (ep->opened[d]) cudaIpcCloseMemHandle(ep->peers.base[d]);
+    if (ep->tx) moe_layer_destroy(ep->tx);
+    cudaFree(ep->exported);
+    cudaFree(ep->local.base);
+    delete ep;
+    return MOE_OK;
+}
+
+int moe_ep_ipc_handle(moe_ep_t ep, void *handle) {
+    if (!ep || !handle) return fail(MOE_INVALID_ARGUMENT, "null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == MOE_EP_HANDLE_BYTES, "IPC handle size");
+    DeviceGuard guard(ep->desc.device);
+    MOE_CUDA(guard.status);
+    cudaIpcMemHandle_t h;
+    MOE_CUDA(cudaIpcGetMemHandle(&h, ep->exported));
+    std::memcpy(handle, &h, sizeof(h));
+    return MOE_OK;
+}
+
+int moe_ep_open_peers(moe_ep_t ep, const void *handles) {
+    if (!ep || !handles) return fail(MOE_INVALID_ARGUMENT, "null argument");
+    DeviceGuard guard(ep->desc.device);
+    MOE_CUDA(guard.status);
+    for (int d = 0; d < ep->world; ++d) {
+        if (d == ep->rank || ep->opened[d]) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(handles) + static_cast<size_t>(d) * MOE_EP_HANDLE_BYTES, sizeof(h));
+        void *ptr = nullptr;
+        MOE_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        uint32_t stamp[4] = {};
+        const cudaError_t e = cudaMemcpy(stamp, static_cast<uint8_t *>(ptr) + ep->L.ctl + offsetof(EpCtl, pad),
+                                         sizeof(stamp), cudaMemcpyDeviceToHost);
+        const uint64_t bytes = stamp[0] | (static_cast<uint64_t>(stamp[1]) << 32);
+        if (e != cudaSuccess || bytes != ep->L.bytes || stamp[2] != static_cast<uint32_t>(ep->world) ||
+            stamp[3] != static_cast<uint32_t>(ep->t_max)) {
+            cudaIpcCloseMemHandle(ptr);
+            return e != cudaSuccess ? cuda_status(e, "moe_ep_open_peers")
+                                    : fail(MOE_INVALID_ARGUMENT, "a peer was created with another shape, world or max_tokens");
+        }
+        ep->peers.base[d] = static_cast<uint8_t *>(ptr);
+        ep->opened[d] = true;
+    }
+    MOE_CUDA(cudaDeviceSynchronize());
+    return MOE_OK;
+}
+
+int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *logits, int tokens, float *out,
+                   int flags, void *stream) {
+    if (!ep || !w) return fail(MOE_INVALID_ARGUMENT, "null handle or weights");
+    for (int d = 0; d < ep->world; ++d)
+        if (!ep->peers.base[d]) return fail(MOE_INVALID_ARGUMENT, "peers are not open (moe_ep_open_peers)");
+    if (w->expert_count != ep->ecount || w->expert_first != ep->rank * ep->ecount ||
+        std::memcmp(&w->desc, &ep->desc, offsetof(moe_layer_desc, device) + sizeof(int)) != 0)
+        return fail(MOE_INVALID_ARGUMENT, "weights are not this rank's expert shard of the same layer shape");
+    if (tokens < 1 || tokens > ep->desc.max_tokens) return fail(MOE_INVALID_ARGUMENT, "tokens outside 1..max_tokens");
+    if (!aligned(x, 16) || !aligned(logits, 16) || !aligned(out, 16))
+        return fail(MOE_INVALID_ARGUMENT, "x, logits and out must be 16-byte aligned device pointers");
+    if (flags != MOE_OUT_ACCUMULATE && flags != MOE_OUT_OVERWRITE) return fail(MOE_INVALID_ARGUMENT, "bad flags");
+    const int H = ep->desc.hidden;
+    const size_t xbytes = static_cast<size_t>(tokens) * H * 4, lbytes = static_cast<size_t>(tokens) * kRouterExperts * 4;
+    if (overlap(out, xbytes, logits, lbytes)) return fail(MOE_INVALID_ARGUMENT, "out overlaps logits");
+    if (flags == MOE_OUT_OVERWRITE && overlap(out, xbytes, x, xbytes))
+        return fail(MOE_INVALID_ARGUMENT, "overwrite requires out disjoint from x (accumulate may alias exactly)");
+    if (flags == MOE_OUT_ACCUMULATE && overlap(out, xbytes, x, xbytes) && out != x)
+        return fail(MOE_INVALID_ARGUMENT, "out may alias x only exactly");
+    DeviceGuard guard(ep->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    moe_layer_s *tx = ep->tx;
+    // 1. own tokens: Q8_1 (+ tensor-core constants), routing, shared gate
+    if (tokens > kChunk || ep->tc)
+        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, tx->xq, nullptr, tx->error,
+                                           tx->sms, s, tx->tc.x_tc))
+            return st;
+    if (const int st = launch_route(tx, w, x, logits, tokens, nullptr, s)) return st;
+    // 2-3. plan and dispatch (peer stores), publish epoch + counts
+    EpParams p = ep_params(ep, tokens, out);
+    ep_plan_kernel<<<1, 1024, 0, s>>>(p);
+    MOE_CUDA(cudaGetLastError());
+    const int items = tokens * ep->world;
+    ep_dispatch_kernel<<<std::max(1, std::min((items + 7) / 8, tx->sms * 4)), 256, 0, s>>>(p);
+    MOE_CUDA(cudaGetLastError());
+    // 4. all sources' slots received -> group by local expert
+    EpCtl *ctl = reinterpret_cast<EpCtl *>(ep->exported + ep->L.ctl);
+    ep_wait_kernel<<<1, 32, 0, s>>>(ctl->recv_epoch, ep->epoch, ep->world, ep->rx.error);
+    MOE_CUDA(cudaGetLastError());
+    moe_layer_s &r = ep->rx;
+    float *partial = reinterpret_cast<float *>(ep->exported + ep->L.partial);
+    const int chunks = ep->slots / kChunk;
+    EpGroupParams g{ep->exported, ep->L, ep->t_max, ep->slots, H, r.masks, partial};
+    ep_masks_kernel<<<chunks, 256, 0, s>>>(g);
+    MOE_CUDA(cudaGetLastError());
+    route_chunk_prefix_kernel<<<kRouterExperts / 32, 1024, 0, s>>>(r.masks, chunks, r.base, r.counts);
+    MOE_CUDA(cudaGetLastError());
+    ScanParams sp;
+    sp.counts = r.counts;
+    sp.tokens = tokens;          // shared-expert pairs: the own tokens
+    sp.tile = kGemvTile;
+    sp.has_shared = ep->desc.has_shared;
+    sp.offsets = r.offsets;
+    sp.tiles = r.tiles;
+    sp.tile_off = r.tile_off;
+    sp.pair_token = r.pair_token;
+    sp.pair_weight = r.pair_weight;
+    sp.num_tiles = r.num_tiles;
+    sp.max_tiles = r.tiles_max;
+    sp.error = r.error;
+    sp.shared_w = tx->pair_weight + static_cast<size_t>(tokens) * kTopK;
+    sp.shared_token0 = ep->rank * ep->t_max;
+    sp.shared_expert = ep->ecount;
+    if (ep->tc) {
+        sp.tc_min = kTcMinGroup;
+        sp.tc_tile = kTcM;
+        sp.tc_max = r.tc.max_tiles;
+        sp.tc_tiles = r.tc.tiles;
+        sp.tc_num = r.tc.num_tiles;
+    }
+    route_scan_kernel<<<1, 512, 0, s>>>(sp);
+    MOE_CUDA(cudaGetLastError());
+    EpScatterParams cp{ep->exported, ep->L, r.masks, r.base, r.offsets, r.pair_token, r.pair_rank, r.pair_weight,
+                       r.tiles, r.tile_off, r.tiles_max};
+    ep_scatter_kernel<<<dim3(chunks, kRouterExperts / 256), 256, 0, s>>>(cp);
+    MOE_CUDA(cudaGetLastError());
+    // expert kernels over the received slots, partial rows accumulated locally
+    const int tc_tiles = ep->tc ? std::min(r.tc.max_tiles, ep->rx_pairs / kTcMinGroup + ep->rx_pairs / kTcM + 1) : 0;
+    if (const int st = launch_experts(&r, w, partial, r.tiles_max, s, nullptr, tc_tiles)) return st;
+    // 5. publish done, wait for every peer, pull the partial rows
+    ep_done_kernel<<<1, 32, 0, s>>>(ep->peers, ep->L, ep->rank, ep->world, ep->epoch);
+    MOE_CUDA(cudaGetLastError());
+    ep_wait_kernel<<<1, 32, 0, s>>>(ctl->done_epoch, ep->epoch, ep->world, ep->rx.error);
+    MOE_CUDA(cudaGetLastError());
+    if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
+    ep_combine_kernel<<<tokens, 256, 0, s>>>(p);
+    return cuda_status(cudaGetLastError(), "ep_combine_kernel");
+}
+
+int moe_ep_read_flags(moe_ep_t ep, int *flags, int clear, void *stream) {
+    if (!ep || !flags) return fail(MOE_INVALID_ARGUMENT, "null argument");
+    int a = 0, b = 0;
+    if (const int st = moe_layer_read_flags(ep->tx, &a, clear, stream)) return st;
+    DeviceGuard guard(ep->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    MOE_CUDA(cudaMemcpyAsync(&b, ep->rx.error, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (clear) MOE_CUDA(cudaMemsetAsync(ep->rx.error, 0, sizeof(int), s));
+    MOE_CUDA(cudaStreamSynchronize(s));
+    *flags = a | b;
+    return MOE_OK;
+}
+
+}  // extern "C"

@@ -242,8 +242,8 @@ struct ScanParams {
     int32_t *offsets;       // [514]: 512 routed groups, shared group, end
     TileRec *tiles;
     int32_t *tile_off;      // [512]: first tile of each routed expert
-    const int32_t *pair_token;   // shared-expert pairs (written by route_topk)
-    const float *pair_weight;
+    int32_t *pair_token;    // shared-expert pairs (written by route_topk at tokens*10 + t,
+    float *pair_weight;     // or here at offsets[512] + t when shared_w is given)
     int *num_tiles;
     int max_tiles;
     int *error;
@@ -252,6 +252,12 @@ struct ScanParams {
     int tc_min = 0, tc_tile = 128, tc_max = 0;
     int4 *tc_tiles = nullptr;
     int *tc_num = nullptr;
+    // Shared-expert pairs supplied directly (expert parallelism): pair
+    // offsets[512] + i is token shared_token0 + i with weight shared_w[i], and
+    // the shared expert's weights sit at index shared_expert.
+    const float *shared_w = nullptr;
+    int shared_token0 = 0;
+    int shared_expert = kRouterExperts;
 };
 
 // One CTA of 512 threads (thread = expert): exclusive scan over experts and
@@ -287,11 +293,18 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
         if (tcoff + i < p.tc_max)
             p.tc_tiles[tcoff + i] = make_int4(e, off + i * p.tc_tile, min(p.tc_tile, run - i * p.tc_tile), 0);
     int shared_tiles = 0, shared_tc = 0;
+    // shared pair i: from route_topk at tokens*10 + i, or given directly
+    const int shared_src = p.shared_w ? total : p.tokens * kTopK;
+    if (p.has_shared && p.shared_w)
+        for (int i = e; i < p.tokens; i += 512) {
+            p.pair_token[total + i] = p.shared_token0 + i;
+            p.pair_weight[total + i] = p.shared_w[i];
+        }
     if (p.has_shared && p.tc_min > 0 && p.tokens >= p.tc_min) {
         shared_tc = (p.tokens + p.tc_tile - 1) / p.tc_tile;
         for (int i = e; i < shared_tc; i += 512)
             if (tc_total + i < p.tc_max)
-                p.tc_tiles[tc_total + i] = make_int4(kRouterExperts, total + i * p.tc_tile,
+                p.tc_tiles[tc_total + i] = make_int4(p.shared_expert, total + i * p.tc_tile,
                                                      min(p.tc_tile, p.tokens - i * p.tc_tile), 0);
     } else if (p.has_shared) {
         shared_tiles = (p.tokens + p.tile - 1) / p.tile;
@@ -299,14 +312,15 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
             const int idx = tiles_total + i;
             if (idx < p.max_tiles) {
                 TileRec &t = p.tiles[idx];
-                t.e = kRouterExperts;
+                t.e = p.shared_expert;
                 t.p0 = total + i * p.tile;
                 t.n = min(p.tile, p.tokens - i * p.tile);
                 t.pad = 0;
                 for (int j = 0; j < kGemvTile; ++j) {
                     const bool live = j < t.n;
-                    t.tok[j] = live ? p.pair_token[p.tokens * kTopK + i * p.tile + j] : 0;
-                    t.w[j] = live ? p.pair_weight[p.tokens * kTopK + i * p.tile + j] : 0.0f;
+                    const int k = i * p.tile + j;
+                    t.tok[j] = live ? (p.shared_w ? p.shared_token0 + k : p.pair_token[shared_src + k]) : 0;
+                    t.w[j] = live ? (p.shared_w ? p.shared_w[k] : p.pair_weight[shared_src + k]) : 0.0f;
                 }
             }
         }

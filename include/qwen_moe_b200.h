@@ -47,7 +47,7 @@ enum moe_status {
     MOE_OUT_OF_MEMORY = 7
 };
 
-enum moe_flags { MOE_FLAG_INVALID = 1, MOE_FLAG_ARITHMETIC = 2 };
+enum moe_flags { MOE_FLAG_INVALID = 1, MOE_FLAG_ARITHMETIC = 2, MOE_FLAG_TIMEOUT = 4 /* a bounded device wait gave up */ };
 
 /* moe_forward flags */
 enum moe_forward_flags {
@@ -151,6 +151,43 @@ int moe_route_noalloc(const float *logits_dev, int tokens, int32_t *ids_dev, flo
 /* Read (and optionally clear) the sticky numeric flags of a layer.  This is
  * the only call here that synchronises (on `stream`). */
 int moe_layer_read_flags(moe_layer_t h, int *flags_host, int clear, void *stream);
+
+/* ---- expert parallelism over peer memory ----------------------------------
+ * One process per GPU, `world` in {1, 2, 4, 8} ranks of one node with peer
+ * access (NVLink / NVSwitch).  Rank r owns routed experts
+ * [r*512/world, (r+1)*512/world) plus a replica of the shared expert, and its
+ * own tokens.  Replaces the single-device expert loop of the reference
+ * (src/session.hip:957-1071 Experts::run/run_chunk) with the expert-sharded
+ * plan of its multi-GPU design: dispatch of Q8_1 rows to the owning ranks,
+ * local grouped expert kernels, combine of pre-reduced partial rows into the
+ * owner's residual.  Transport is peer stores/loads inside this library's own
+ * kernels on CUDA IPC mappings (no NCCL); every wait on a peer is bounded and
+ * raises MOE_FLAG_TIMEOUT instead of hanging.  All ranks must call
+ * moe_ep_forward the same number of times, in the same order. */
+typedef struct moe_ep_s *moe_ep_t;
+enum { MOE_EP_HANDLE_BYTES = 64 };
+
+/* Expert-shard weights of rank `rank`: 512/world routed experts (local index
+ * i is global expert rank*512/world + i) and the shared expert at local index
+ * 512/world.  Upload, synthesis (same bits as the global experts) and
+ * download work as for moe_weights_t with local indices. */
+int moe_ep_weights_create(const moe_layer_desc *desc, int rank, int world, moe_weights_t *out);
+/* Workspace of one rank; desc->max_tokens is the per-rank token capacity. */
+int moe_ep_create(const moe_layer_desc *desc, int rank, int world, moe_ep_t *out);
+int moe_ep_destroy(moe_ep_t ep);
+/* The rank's exportable buffer as an opaque MOE_EP_HANDLE_BYTES-byte handle
+ * (cudaIpcGetMemHandle) for the caller to exchange (e.g. all-gather). */
+int moe_ep_ipc_handle(moe_ep_t ep, void *handle_host);
+/* Map every peer's buffer from the world * MOE_EP_HANDLE_BYTES handles in
+ * rank order (the own entry is ignored).  Synchronises the device. */
+int moe_ep_open_peers(moe_ep_t ep, const void *handles_host);
+/* Expert-parallel forward of this rank's T tokens (same contract as
+ * moe_forward for x, logits and out).  Capturable in a CUDA graph once the
+ * peers are open. */
+int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x_dev, const float *logits_dev, int tokens,
+                   float *out_dev, int flags, void *stream);
+/* Sticky flags of the rank (MOE_FLAG_TIMEOUT included); synchronises `stream`. */
+int moe_ep_read_flags(moe_ep_t ep, int *flags_host, int clear, void *stream);
 
 /* ---- kernels exposed for parity taps ------------------------------------- */
 /* fp32 [columns][width] -> canonical Q8_1 [columns][width/32] (36-byte blocks).

@@ -1,0 +1,112 @@
+"""Expert parallelism over peer memory (moe_ep_*).
+
+CPU: argument checks before any device call and the host-side handle
+exchange over a 2-rank gloo group.  GPU: the world-1 path (self-dispatch)
+against moe_forward on one B200, and 2 ranks on 2 B200s (skipped with fewer
+GPUs) against the single-GPU forward of the same tokens.  Bar: max|err| <=
+1e-3 * RMS(output), the layer bar; in practice only fp32 summation order
+differs."""
+import ctypes
+import multiprocessing as mp
+import socket
+
+import numpy as np
+import pytest
+
+TOL_RMS = 1e-3
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_ranks(target, world, *args, timeout=300):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, *args, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    try:
+        for _ in range(world):
+            results.append(q.get(timeout=timeout))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    return sorted(results, key=lambda r: r[0])
+
+
+def test_ep_arguments_rejected_before_device_calls(pkg):
+    L = pkg.library()
+    h = ctypes.c_void_p()
+    d = pkg.make_desc(max_tokens=8)
+    for rank, world in ((0, 3), (2, 2), (-1, 2), (0, 16)):
+        assert L.moe_ep_create(ctypes.byref(d), rank, world, ctypes.byref(h)) == pkg.MOE_INVALID_ARGUMENT
+        assert L.moe_ep_weights_create(ctypes.byref(d), rank, world, ctypes.byref(h)) == pkg.MOE_INVALID_ARGUMENT
+        assert not h.value
+    big = pkg.make_desc(max_tokens=40000)
+    assert L.moe_ep_create(ctypes.byref(big), 0, 2, ctypes.byref(h)) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_ep_forward(None, None, None, None, 1, None, 0, None) == pkg.MOE_INVALID_ARGUMENT
+
+
+def test_handle_exchange_two_ranks_gloo():
+    import ep_worker
+    res = run_ranks(ep_worker.exchange_worker, 2, timeout=120)
+    for rank, got, n in res:
+        assert got == [1, 2], (rank, got, n)
+        assert n == 64
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tokens,routing", [(8, "normal"), (100, "normal"), (300, "zipf")])
+def test_ep_world1_matches_forward(pkg, tokens, routing):
+    import torch
+    desc = pkg.make_desc(max_tokens=tokens)
+    rng = np.random.default_rng(tokens)
+    x = torch.from_numpy(rng.standard_normal((tokens, 2048)).astype(np.float32)).cuda()
+    if routing == "zipf":
+        perm = rng.permutation(512)
+        g = -np.log(-np.log(rng.random((tokens, 512))))
+        lg = (-1.1 * np.log1p(perm.astype(np.float64))[None, :] + g).astype(np.float32)
+    else:
+        lg = rng.standard_normal((tokens, 512)).astype(np.float32)
+    logits = torch.from_numpy(lg).cuda()
+    gate = (rng.standard_normal(2048) * 0.05).astype(np.float32)
+    full = pkg.MoeWeights(desc)
+    full.synthesize(3, 1)
+    full.upload_shared_gate(gate)
+    ref = torch.zeros(tokens, 2048, device="cuda")
+    pkg.MoeLayer(desc).forward(full, x, logits, ref)
+    shard = pkg.EpWeights(desc, 0, 1)
+    shard.synthesize(3, 1)
+    shard.upload_shared_gate(gate)
+    ep = pkg.EpLayer(desc, 0, 1)
+    for _ in range(3):
+        out = x.clone()
+        ep.forward(shard, x, logits, out)          # accumulate into a residual copy
+        torch.cuda.synchronize()
+        r = ref.cpu().numpy()
+        err = np.abs((out - x).cpu().numpy() - r).max()
+        rms = np.sqrt(np.mean(r.astype(np.float64) ** 2))
+        assert err <= TOL_RMS * rms, (err, rms)
+    assert ep.read_flags() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tokens,routing", [(8, "normal"), (256, "zipf")])
+def test_ep_two_ranks_match_single_gpu(tokens, routing):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import ep_worker
+    res = run_ranks(ep_worker.forward_worker, 2, tokens, routing, timeout=600)
+    for rank, flags, errs, rms in res:
+        assert flags != "error", (rank, errs)
+        assert flags == 0, (rank, flags)
+        for e in errs:
+            assert e <= TOL_RMS * rms, (rank, e, rms)
