@@ -159,6 +159,25 @@ int configure_kernels(moe_layer_s *h, int H, int I) {
     return MOE_OK;
 }
 
+// Launch with programmatic stream serialisation: the kernel may begin while
+// the preceding kernel of the stream finishes, and orders itself after it
+// with grid_dependency_wait().
+template <class... Args>
+cudaError_t launch_overlapped(void (*kernel)(Args...), int grid, int block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 GroupParams group_params(moe_layer_s *h, const moe_weights_s *w, float *out) {
     GroupParams g;
     g.weights = w->base;
@@ -221,17 +240,15 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[0]), s));
         sp.stages = h->gu_stages;
         sp.stage_bytes = GuStage(L.hidden).bytes;
-        stream_gate_up_kernel<<<std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
-                                stream_gu_smem(L.hidden, sp.stages), s>>>(sp);
-        MOE_CUDA(cudaGetLastError());
+        MOE_CUDA(launch_overlapped(stream_gate_up_kernel, std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
+                                   stream_gu_smem(L.hidden, sp.stages), s, sp));
         if (tc_tiles)
             if (const int st = launch_tc(h, w, out, tc_tiles, false, s)) return st;
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
         sp.stages = h->dn_stages;
         sp.stage_bytes = DnStage(L.inter).bytes;
-        stream_down_kernel<<<std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
-                             stream_dn_smem(L.inter, sp.stages), s>>>(sp);
-        MOE_CUDA(cudaGetLastError());
+        MOE_CUDA(launch_overlapped(stream_down_kernel, std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
+                                   stream_dn_smem(L.inter, sp.stages), s, sp));
         if (tc_tiles)
             if (const int st = launch_tc(h, w, out, tc_tiles, true, s)) return st;
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[2]), s));

@@ -68,6 +68,13 @@ __device__ __forceinline__ void prefetch_l1(const void *p) {
     asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
+// Programmatic dependent launch: wait until the preceding kernel in the stream
+// has completed and its memory is visible (returns at once when this kernel
+// was launched without the programmatic-serialisation attribute), and allow
+// the next such kernel to start launching its CTAs.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Barrier among `count` threads (a multiple of 32) on hardware barrier `id` (1..15).
 __device__ __forceinline__ void named_barrier(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

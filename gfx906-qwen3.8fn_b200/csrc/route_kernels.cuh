@@ -9,6 +9,7 @@
 // operation is a separately rounded IEEE op in the reference's order.
 #pragma once
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace qmoe {
 
@@ -55,9 +56,11 @@ struct RouteParams {
     int *error;
 };
 
-// Route token t with one warp: softmax, top-10, renormalised weights, the
-// chunk mask bit j in smask[expert], and the shared-expert gate.
-__device__ __forceinline__ void route_one_token(const RouteParams &p, int t, int j, uint32_t *smask, int lane) {
+// Route token t with one warp: softmax, top-10, renormalised weights and the
+// chunk mask bit j in smask[expert]; ids/weights also go to shared-memory
+// copies when ids_s is given.
+__device__ __forceinline__ void route_topk_token(const RouteParams &p, int t, int j, uint32_t *smask, int lane,
+                                                 int32_t *ids_s = nullptr, float *w_s = nullptr) {
     {
         const float *row = p.logits + static_cast<size_t>(t) * kRouterExperts;
         int flags = 0;
@@ -98,27 +101,42 @@ __device__ __forceinline__ void route_one_token(const RouteParams &p, int t, int
         if (lane == 0) report(flags, p.error);
 
         // top-10 by (probability desc, id asc): ten warp-wide arg-max rounds.
+        // Probabilities are non-negative, so their bit patterns (+1, 0 =
+        // taken) order like the values: one warp max picks the value, one
+        // warp min the lowest id holding it.
         uint32_t taken = 0u;
         int sel_id[kTopK];
         float sel_p[kTopK];
+        uint32_t key[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) key[k] = __float_as_uint(w[k]) + 1u;
 #pragma unroll
         for (int r = 0; r < kTopK; ++r) {
-            float bv = -1.0f;
-            int bi = 0x7fffffff;
+            // the lane's best untaken key by a 4-level tree; at every node the
+            // left operand has the lower id, so ties keep it
+            uint32_t kv[16];
+            int ki[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
-                const int id = lane + 32 * k;
-                if (!((taken >> k) & 1u) && (w[k] > bv || (w[k] == bv && id < bi))) { bv = w[k]; bi = id; }
+                kv[k] = ((taken >> k) & 1u) ? 0u : key[k];
+                ki[k] = k;
             }
 #pragma unroll
-            for (int m = 16; m > 0; m >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-            sel_id[r] = bi;
-            sel_p[r] = bv;
+            for (int w2 = 8; w2 > 0; w2 >>= 1)
+#pragma unroll
+                for (int k = 0; k < w2; ++k) {
+                    const bool right = kv[2 * k + 1] > kv[2 * k];
+                    kv[k] = right ? kv[2 * k + 1] : kv[2 * k];
+                    ki[k] = right ? ki[2 * k + 1] : ki[2 * k];
+                }
+            const uint32_t best = kv[0];
+            const int bk = ki[0];
+            const uint32_t mk = __reduce_max_sync(0xffffffffu, best);
+            const uint32_t bi = __reduce_min_sync(0xffffffffu, best == mk ? static_cast<uint32_t>(lane + 32 * bk)
+                                                                           : 0xffffffffu);
+            if (static_cast<int>(bi & 31u) == lane) taken |= 1u << (bi >> 5);
+            sel_id[r] = static_cast<int>(bi);
+            sel_p[r] = __uint_as_float(mk - 1u);
         }
         // Renormalisation: buckets[id % 32] accumulate in rank order, then an
         // XOR butterfly 1..16, floor 1/16384, reciprocal, separate multiply.
@@ -133,13 +151,23 @@ __device__ __forceinline__ void route_one_token(const RouteParams &p, int t, int
 #pragma unroll
         for (int r = 0; r < kTopK; ++r) {
             if (lane == r) {
+                const float wr = __fmul_rn(sel_p[r], inv_den);
                 p.ids[t * kTopK + r] = sel_id[r];
-                p.weights[t * kTopK + r] = __fmul_rn(sel_p[r], inv_den);
+                p.weights[t * kTopK + r] = wr;
+                if (ids_s) {
+                    ids_s[j * kTopK + r] = sel_id[r];
+                    w_s[j * kTopK + r] = wr;
+                }
                 atomicOr(&smask[sel_id[r]], 1u << j);
             }
         }
-        // Shared expert: raw gate = x . gate_vec, weight = 1/(1+exp(-raw))
-        // (src/hip/session_ops.hip:376-391), written as pair T*10 + t.
+    }
+}
+
+// Shared expert of token t with one warp: raw gate = x . gate_vec, weight =
+// 1/(1+exp(-raw)) (src/hip/session_ops.hip:376-391), written as pair T*10 + t.
+__device__ __forceinline__ void route_shared_gate(const RouteParams &p, int t, int lane) {
+    {
         if (p.gate_vec) {
             const float4 *xr = reinterpret_cast<const float4 *>(p.x + static_cast<size_t>(t) * p.hidden);
             const float4 *gv = reinterpret_cast<const float4 *>(p.gate_vec);
@@ -162,6 +190,11 @@ __device__ __forceinline__ void route_one_token(const RouteParams &p, int t, int
             }
         }
     }
+}
+
+__device__ __forceinline__ void route_one_token(const RouteParams &p, int t, int j, uint32_t *smask, int lane) {
+    route_topk_token(p, t, j, smask, lane);
+    route_shared_gate(p, t, lane);
 }
 
 // One CTA per chunk of 32 tokens; one warp per token.
@@ -434,10 +467,15 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
         }
         return;
     }
+    __shared__ int32_t ids_s[kChunk * kTopK];
+    __shared__ float w_s[kChunk * kTopK];
     smask[e] = 0u;
     __syncthreads();
-    for (int t = warp; t < T; t += 16) route_one_token(p, t, t, smask, lane);
-    __syncthreads();   // ids/weights (global) and smask complete
+    // warps 0..T-1 route token = warp (and 16 + warp); the shared gates run on
+    // the idle warps T..2T-1 in parallel when T <= 8, else after the routing
+    for (int t = warp; t < T; t += 16) route_topk_token(p, t, t, smask, lane, ids_s, w_s);
+    for (int t = T <= 8 ? warp - T : warp; t >= 0 && t < T; t += 16) route_shared_gate(p, t, lane);
+    __syncthreads();   // ids/weights (global and shared) and smask complete
     const uint32_t mask = smask[e];
     const int count = __popc(mask);
     int total = 0;
@@ -457,8 +495,8 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
         int r = 0;
 #pragma unroll
         for (int k = 0; k < kTopK; ++k)
-            if (p.ids[t * kTopK + k] == e) r = k;
-        const float w = p.weights[t * kTopK + r];
+            if (ids_s[t * kTopK + k] == e) r = k;
+        const float w = w_s[t * kTopK + r];
         const int pair = off + pos;
         p.pair_token[pair] = t;
         if (p.pair_rank) p.pair_rank[pair] = r;

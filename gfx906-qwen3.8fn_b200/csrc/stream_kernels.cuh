@@ -182,6 +182,8 @@ stream_gate_up_kernel(StreamParams p) {
     uint8_t *stages = smem + 128 + 2 * kGemvTile * 32 * 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     init_ring(full, empty, p.stages);
+    grid_dependency_wait();     // tile list and x codes of the routing kernels
+    grid_launch_dependents();   // the down kernel may take SMs as this grid's CTAs finish
     const int total = *p.num_tiles * slabs;
 
     if (warp == 0) {
@@ -306,20 +308,49 @@ stream_down_kernel(StreamParams p) {
     const int total = *p.num_tiles * slabs;
 
     if (warp == 0) {
+        // Producer.  The tile list comes from the routing kernels, which
+        // completed before the gate/up grid started, so the weights of the
+        // first ring stages stream while gate/up finishes; the middle
+        // activations of those stages are fetched after grid_dependency_wait.
         if (lane != 0) return;
-        stream_producer(p, stages, full, empty, total, slabs,
-                        [&](int item, uint8_t *st, uint64_t *bar, const TileRec &rec) {
-            const int slab = item % slabs;
-            const uint8_t *ex = p.weights + static_cast<size_t>(rec.e) * p.layout.bytes;
-            const uint32_t code_bytes = kDnRows * nb * 16, sc_bytes = kDnRows * nb * 2;
-            const uint32_t bytes = code_bytes + sc_bytes + rec.n * (I + nb * 8);
-            mbar_arrive_expect_tx(bar, bytes);
-            bulk_g2s(st + L.dcodes, ex + p.layout.down_codes + static_cast<size_t>(slab) * code_bytes, code_bytes, bar);
-            bulk_g2s(st + L.dsc, ex + p.layout.down_scales + static_cast<size_t>(slab) * sc_bytes, sc_bytes, bar);
+        const uint32_t code_bytes = kDnRows * nb * 16, sc_bytes = kDnRows * nb * 2;
+        auto issue_mid = [&](uint8_t *st, uint64_t *bar, const TileRec &rec) {
             // the tile's pairs are consecutive: one copy each for codes and scales
             bulk_g2s(st + L.mcodes, p.mid.codes + static_cast<size_t>(rec.p0) * I, rec.n * I, bar);
             bulk_g2s(st + L.msc, p.mid.scales + static_cast<size_t>(rec.p0) * nb, rec.n * nb * 8, bar);
-        });
+        };
+        bool dep = false;
+        int i = 0;
+        auto resolve = [&]() {   // wait for gate/up, then the middle rows of the stages already armed
+            grid_dependency_wait();
+            dep = true;
+            for (int k = 0; k < i; ++k) {
+                uint8_t *st = stages + static_cast<size_t>(k % p.stages) * p.stage_bytes;
+                issue_mid(st, &full[k % p.stages], *reinterpret_cast<const TileRec *>(st));
+            }
+        };
+        for (int item = blockIdx.x; item < total; item += gridDim.x, ++i) {
+            const TileRec rec = load_tile(p.tiles + item / slabs);
+            const int s = i % p.stages;
+            if (i >= p.stages) {
+                if (!dep) resolve();
+                if (!mbar_wait(&empty[s], ((i / p.stages) & 1) ^ 1, p.error)) break;
+            }
+            uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
+            *reinterpret_cast<TileRec *>(st) = rec;
+            const int slab = item % slabs;
+            const uint8_t *ex = p.weights + static_cast<size_t>(rec.e) * p.layout.bytes;
+            mbar_arrive_expect_tx(&full[s], code_bytes + sc_bytes + rec.n * (I + nb * 8));
+            bulk_g2s(st + L.dcodes, ex + p.layout.down_codes + static_cast<size_t>(slab) * code_bytes, code_bytes,
+                     &full[s]);
+            bulk_g2s(st + L.dsc, ex + p.layout.down_scales + static_cast<size_t>(slab) * sc_bytes, sc_bytes,
+                     &full[s]);
+            if (dep) issue_mid(st, &full[s], rec);
+        }
+        if (!dep) resolve();
+        // keep the CTA alive until every issued copy has landed
+        for (int k = i - p.stages > 0 ? i - p.stages : 0; k < i; ++k)
+            mbar_wait(&full[k % p.stages], (k / p.stages) & 1, p.error);
         return;
     }
 
