@@ -561,7 +561,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
                     for (int k = 0; k < 4; ++k) {
                         int f = 0;
                         const float g = operand(gs[k], f), u = operand(us[k], f);
-                        const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), f);
+                        // fast exponential and division: a few ulp from the decode kernels'
+                        // expf/IEEE form, far inside the layer tolerance
+                        const float act = arithmetic(__fdividef(g, 1.0f + __expf(-g)), f);
                         const float val = arithmetic(__fmul_rn(act, u), f);
                         mid[c + k] = (f || !real) ? 0.0f : val;
                         flags |= real ? f : 0;
