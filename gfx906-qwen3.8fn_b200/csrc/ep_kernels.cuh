@@ -227,8 +227,9 @@ __global__ void ep_wait_kernel(const uint32_t *flags, const uint32_t *epoch, int
     }
 }
 
-// Received slots -> chunk masks over local experts (32 slots per CTA), and
-// zeroed partial rows for the valid slots.
+// Received slots -> chunk masks over local experts (32 slots per CTA).  The
+// partial rows of the slots start at zero: the combine of the previous epoch
+// cleared every row it consumed.
 struct EpGroupParams {
     const uint8_t *arena;   // own exported arena
     EpLayout L;
@@ -256,13 +257,132 @@ __global__ void __launch_bounds__(256) ep_masks_kernel(EpGroupParams g) {
     __syncthreads();
     for (int e = threadIdx.x; e < kRouterExperts; e += blockDim.x)
         g.masks[static_cast<size_t>(blockIdx.x) * kRouterExperts + e] = smask[e];
-    // zero the partial rows of this chunk's valid slots
-    const int H4 = g.hidden / 4;
-    for (int i = threadIdx.x; i < kChunk * H4; i += blockDim.x) {
-        const int slot = s0 + i / H4;
-        if (slot < g.slots && ep_slot_valid(c, slot, g.t_max))
-            reinterpret_cast<float4 *>(g.partial)[static_cast<size_t>(slot) * H4 + i % H4] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// Decode-size receive side (slots <= 512, one CTA of 512 threads, thread =
+// local expert): wait for every source's dispatch, chunk masks in shared
+// memory, counts, scan, stable placement of the pairs, the own tokens'
+// shared-expert pairs and the work-tile list -- the work of ep_wait, ep_masks,
+// route_chunk_prefix, route_scan and ep_scatter in one launch.
+struct EpSmallGroupParams {
+    const uint8_t *arena;
+    EpLayout L;
+    int t_max, slots, world, tokens, has_shared, shared_token0, shared_expert;
+    const uint32_t *epoch;
+    const float *shared_w;    // [tokens] own tokens' shared-expert gate weights
+    int32_t *offsets;         // [514]
+    int32_t *pair_token;
+    int32_t *pair_rank;
+    float *pair_weight;
+    TileRec *tiles;
+    int *num_tiles;
+    int max_tiles;
+    int *error;
+};
+constexpr int kEpSmallSlots = 512;
+__global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams g) {
+    __shared__ uint32_t smask[kEpSmallSlots / kChunk][kRouterExperts];
+    __shared__ int failed;
+    const int e = threadIdx.x, lane = e & 31;
+    const EpCtl *c = reinterpret_cast<const EpCtl *>(g.arena + g.L.ctl);
+    if (e < 32) {
+        bool ok = true;
+        if (e < g.world) {
+            const uint32_t want = *g.epoch;
+            const long long t0 = clock64();
+            while (ld_acquire_sys(&c->recv_epoch[e]) != want) {
+                if (clock64() - t0 > (1ll << 31)) {
+                    atomicOr(g.error, kFlagTimeout);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (e == 0) failed = !ok;
     }
+    const int chunks = g.slots / kChunk;
+    for (int k = 0; k < chunks; ++k) smask[k][e] = 0u;
+    __syncthreads();
+    if (failed) {
+        if (e == 0) *g.num_tiles = 0;
+        return;
+    }
+    const int32_t *ids = reinterpret_cast<const int32_t *>(g.arena + g.L.ids);
+    const float *ws = reinterpret_cast<const float *>(g.arena + g.L.w);
+    for (int i = e; i < g.slots * kEpSlotIds; i += blockDim.x) {
+        const int slot = i / kEpSlotIds;
+        if (!ep_slot_valid(c, slot, g.t_max)) continue;
+        const int id = ids[i];
+        if (id >= 0 && id < kRouterExperts) atomicOr(&smask[slot / kChunk][id], 1u << (slot % kChunk));
+    }
+    __syncthreads();
+    int count = 0;
+    for (int k = 0; k < chunks; ++k) count += __popc(smask[k][e]);
+    int total = 0;
+    const int off = block_exclusive_scan_512(count, &total);
+    g.offsets[e] = off;
+    if (e == kRouterExperts - 1) {
+        g.offsets[kRouterExperts] = total;
+        g.offsets[kRouterExperts + 1] = total + (g.has_shared ? g.tokens : 0);
+    }
+    const int ntiles = (count + kGemvTile - 1) / kGemvTile;
+    int tiles_total = 0;
+    const int toff = block_exclusive_scan_512(ntiles, &tiles_total);
+    int pos = 0;
+    for (int k = 0; k < chunks; ++k)
+        for (uint32_t m = smask[k][e]; m; m &= m - 1u, ++pos) {
+            const int slot = k * kChunk + __ffs(m) - 1;
+            int r = 0;
+#pragma unroll
+            for (int q = 0; q < kEpSlotIds; ++q)
+                if (ids[slot * kEpSlotIds + q] == e) r = q;
+            const float w = ws[slot * kEpSlotIds + r];
+            const int pair = off + pos;
+            g.pair_token[pair] = slot;
+            if (g.pair_rank) g.pair_rank[pair] = r;
+            g.pair_weight[pair] = w;
+            const int tile = toff + pos / kGemvTile, j = pos % kGemvTile;
+            if (tile < g.max_tiles) {
+                TileRec &rec = g.tiles[tile];
+                if (j == 0) {
+                    rec.e = e;
+                    rec.p0 = pair;
+                    rec.n = min(kGemvTile, count - pos);
+                    rec.pad = 0;
+                }
+                rec.tok[j] = slot;
+                rec.w[j] = w;
+            }
+        }
+    int shared_tiles = 0;
+    if (g.has_shared) {
+        for (int i = e; i < g.tokens; i += blockDim.x) {
+            g.pair_token[total + i] = g.shared_token0 + i;
+            g.pair_weight[total + i] = g.shared_w[i];
+        }
+        shared_tiles = (g.tokens + kGemvTile - 1) / kGemvTile;
+        for (int i = e; i < shared_tiles; i += blockDim.x) {
+            if (tiles_total + i >= g.max_tiles) continue;
+            TileRec &rec = g.tiles[tiles_total + i];
+            rec.e = g.shared_expert;
+            rec.p0 = total + i * kGemvTile;
+            rec.n = min(kGemvTile, g.tokens - i * kGemvTile);
+            rec.pad = 0;
+            for (int j = 0; j < kGemvTile; ++j) {
+                const bool live = j < rec.n;
+                rec.tok[j] = live ? g.shared_token0 + i * kGemvTile + j : 0;
+                rec.w[j] = live ? g.shared_w[i * kGemvTile + j] : 0.0f;
+            }
+        }
+    }
+    if (e == 0) {
+        int n = tiles_total + shared_tiles;
+        if (n > g.max_tiles) { atomicOr(g.error, kFlagArithmetic); n = g.max_tiles; }
+        *g.num_tiles = n;
+    }
+    (void)lane;
 }
 
 // Stable placement of received (slot, local expert) pairs, as
@@ -321,19 +441,45 @@ __global__ void ep_done_kernel(EpPeers peers, EpLayout L, int rank, int world, c
     st_release_sys(&c->done_epoch[rank], *epoch);
 }
 
-// Combine: out[t] += sum over the token's destinations d (ascending) of the
-// partial row d holds for it.  One CTA of H/8 threads per token, 8 floats each.
+// Combine: wait until every peer has published its partial rows (bounded),
+// then out[t] += sum over the token's destinations d (ascending) of the
+// partial row d holds for it, clearing that row for the next epoch.  One CTA
+// per token.
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
+    __shared__ int ready;
     const int t = blockIdx.x;
     if (t >= p.tokens) return;
+    if (threadIdx.x < 32) {
+        const EpCtl *c = reinterpret_cast<const EpCtl *>(p.peers.base[p.rank] + p.L.ctl);
+        bool ok = true;
+        if (threadIdx.x < p.world) {
+            const uint32_t want = *p.epoch;
+            const long long t0 = clock64();
+            while (ld_acquire_sys(&c->done_epoch[threadIdx.x]) != want) {
+                if (clock64() - t0 > (1ll << 31)) {
+                    atomicOr(p.error, kFlagTimeout);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (threadIdx.x == 0) ready = ok;
+    }
+    __syncthreads();
+    if (!ready) return;
     const uint32_t mask = p.dmask[t];
     const int H = p.hidden;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 acc = zero;
         for (int d = 0; d < p.world; ++d) {
             if (!((mask >> d) & 1u)) continue;
             const size_t slot = static_cast<size_t>(p.rank) * p.t_max + p.pos[t * kEpMaxRanks + d];
-            const float4 v = reinterpret_cast<const float4 *>(p.peers.base[d] + p.L.partial)[slot * (H / 4) + i];
+            float4 *src = reinterpret_cast<float4 *>(p.peers.base[d] + p.L.partial) + slot * (H / 4) + i;
+            const float4 v = *src;
+            *src = zero;
             acc.x = __fadd_rn(acc.x, v.x);
             acc.y = __fadd_rn(acc.y, v.y);
             acc.z = __fadd_rn(acc.z, v.z);

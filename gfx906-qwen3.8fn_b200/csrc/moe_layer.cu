@@ -1223,52 +1223,77 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
     MOE_CUDA(cudaGetLastError());
     // 4. all sources' slots received -> group by local expert
     EpCtl *ctl = reinterpret_cast<EpCtl *>(ep->exported + ep->L.ctl);
-    ep_wait_kernel<<<1, 32, 0, s>>>(ctl->recv_epoch, ep->epoch, ep->world, ep->rx.error);
-    MOE_CUDA(cudaGetLastError());
     moe_layer_s &r = ep->rx;
     float *partial = reinterpret_cast<float *>(ep->exported + ep->L.partial);
-    const int chunks = ep->slots / kChunk;
-    EpGroupParams g{ep->exported, ep->L, ep->t_max, ep->slots, H, r.masks, partial};
-    ep_masks_kernel<<<chunks, 256, 0, s>>>(g);
-    MOE_CUDA(cudaGetLastError());
-    route_chunk_prefix_kernel<<<kRouterExperts / 32, 1024, 0, s>>>(r.masks, chunks, r.base, r.counts);
-    MOE_CUDA(cudaGetLastError());
-    ScanParams sp;
-    sp.counts = r.counts;
-    sp.tokens = tokens;          // shared-expert pairs: the own tokens
-    sp.tile = kGemvTile;
-    sp.has_shared = ep->desc.has_shared;
-    sp.offsets = r.offsets;
-    sp.tiles = r.tiles;
-    sp.tile_off = r.tile_off;
-    sp.pair_token = r.pair_token;
-    sp.pair_weight = r.pair_weight;
-    sp.num_tiles = r.num_tiles;
-    sp.max_tiles = r.tiles_max;
-    sp.error = r.error;
-    sp.shared_w = tx->pair_weight + static_cast<size_t>(tokens) * kTopK;
-    sp.shared_token0 = ep->rank * ep->t_max;
-    sp.shared_expert = ep->ecount;
-    if (ep->tc) {
-        sp.tc_min = kTcMinGroup;
-        sp.tc_tile = kTcM;
-        sp.tc_max = r.tc.max_tiles;
-        sp.tc_tiles = r.tc.tiles;
-        sp.tc_num = r.tc.num_tiles;
+    const float *shared_w = tx->pair_weight + static_cast<size_t>(tokens) * kTopK;
+    if (ep->slots <= kEpSmallSlots && !ep->tc) {
+        // decode sizes: wait, masks, scan, placement and tiles in one launch
+        EpSmallGroupParams g;
+        g.arena = ep->exported;
+        g.L = ep->L;
+        g.t_max = ep->t_max;
+        g.slots = ep->slots;
+        g.world = ep->world;
+        g.tokens = tokens;
+        g.has_shared = ep->desc.has_shared;
+        g.shared_token0 = ep->rank * ep->t_max;
+        g.shared_expert = ep->ecount;
+        g.epoch = ep->epoch;
+        g.shared_w = shared_w;
+        g.offsets = r.offsets;
+        g.pair_token = r.pair_token;
+        g.pair_rank = r.pair_rank;
+        g.pair_weight = r.pair_weight;
+        g.tiles = r.tiles;
+        g.num_tiles = r.num_tiles;
+        g.max_tiles = r.tiles_max;
+        g.error = r.error;
+        ep_group_small_kernel<<<1, 512, 0, s>>>(g);
+        MOE_CUDA(cudaGetLastError());
+    } else {
+        ep_wait_kernel<<<1, 32, 0, s>>>(ctl->recv_epoch, ep->epoch, ep->world, ep->rx.error);
+        MOE_CUDA(cudaGetLastError());
+        const int chunks = ep->slots / kChunk;
+        EpGroupParams g{ep->exported, ep->L, ep->t_max, ep->slots, H, r.masks, partial};
+        ep_masks_kernel<<<chunks, 256, 0, s>>>(g);
+        MOE_CUDA(cudaGetLastError());
+        route_chunk_prefix_kernel<<<kRouterExperts / 32, 1024, 0, s>>>(r.masks, chunks, r.base, r.counts);
+        MOE_CUDA(cudaGetLastError());
+        ScanParams sp;
+        sp.counts = r.counts;
+        sp.tokens = tokens;          // shared-expert pairs: the own tokens
+        sp.tile = kGemvTile;
+        sp.has_shared = ep->desc.has_shared;
+        sp.offsets = r.offsets;
+        sp.tiles = r.tiles;
+        sp.tile_off = r.tile_off;
+        sp.pair_token = r.pair_token;
+        sp.pair_weight = r.pair_weight;
+        sp.num_tiles = r.num_tiles;
+        sp.max_tiles = r.tiles_max;
+        sp.error = r.error;
+        sp.shared_w = shared_w;
+        sp.shared_token0 = ep->rank * ep->t_max;
+        sp.shared_expert = ep->ecount;
+        if (ep->tc) {
+            sp.tc_min = kTcMinGroup;
+            sp.tc_tile = kTcM;
+            sp.tc_max = r.tc.max_tiles;
+            sp.tc_tiles = r.tc.tiles;
+            sp.tc_num = r.tc.num_tiles;
+        }
+        route_scan_kernel<<<1, 512, 0, s>>>(sp);
+        MOE_CUDA(cudaGetLastError());
+        EpScatterParams cp{ep->exported, ep->L, r.masks, r.base, r.offsets, r.pair_token, r.pair_rank, r.pair_weight,
+                           r.tiles, r.tile_off, r.tiles_max};
+        ep_scatter_kernel<<<dim3(chunks, kRouterExperts / 256), 256, 0, s>>>(cp);
+        MOE_CUDA(cudaGetLastError());
     }
-    route_scan_kernel<<<1, 512, 0, s>>>(sp);
-    MOE_CUDA(cudaGetLastError());
-    EpScatterParams cp{ep->exported, ep->L, r.masks, r.base, r.offsets, r.pair_token, r.pair_rank, r.pair_weight,
-                       r.tiles, r.tile_off, r.tiles_max};
-    ep_scatter_kernel<<<dim3(chunks, kRouterExperts / 256), 256, 0, s>>>(cp);
-    MOE_CUDA(cudaGetLastError());
     // expert kernels over the received slots, partial rows accumulated locally
     const int tc_tiles = ep->tc ? std::min(r.tc.max_tiles, ep->rx_pairs / kTcMinGroup + ep->rx_pairs / kTcM + 1) : 0;
     if (const int st = launch_experts(&r, w, partial, r.tiles_max, s, nullptr, tc_tiles)) return st;
-    // 5. publish done, wait for every peer, pull the partial rows
+    // 5. publish done; the combine waits for every peer's, then pulls the partial rows
     ep_done_kernel<<<1, 32, 0, s>>>(ep->peers, ep->L, ep->rank, ep->world, ep->epoch);
-    MOE_CUDA(cudaGetLastError());
-    ep_wait_kernel<<<1, 32, 0, s>>>(ctl->done_epoch, ep->epoch, ep->world, ep->rx.error);
     MOE_CUDA(cudaGetLastError());
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
     ep_combine_kernel<<<tokens, 256, 0, s>>>(p);
