@@ -34,8 +34,7 @@ constexpr int kEpSlotIds = kTopK;   // (local expert, weight) entries per receiv
 
 // Control words written by peers (one set per rank, in the exported arena).
 struct EpCtl {
-    uint32_t recv_epoch[kEpMaxRanks];   // by source: dispatch of this epoch complete
-    uint32_t recv_count[kEpMaxRanks];   // by source: slots written this epoch
+    uint64_t recv[kEpMaxRanks];         // by source: (slots written << 32) | epoch, one release store
     uint32_t done_epoch[kEpMaxRanks];   // by destination: partial rows of this epoch final
     uint32_t pad[8];
 };
@@ -88,6 +87,20 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
 }
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys64(uint64_t *p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Publish to destination d that this rank's `count` slots of `epoch` are in
+// place (one lane per destination, after the CTA's stores are ordered before it).
+__device__ __forceinline__ void ep_publish(const EpParams &p, int d, uint32_t count, uint32_t epoch) {
+    EpCtl *c = reinterpret_cast<EpCtl *>(p.peers.base[d] + p.L.ctl);
+    st_release_sys64(&c->recv[p.rank], (static_cast<uint64_t>(count) << 32) | epoch);
 }
 
 // Plan (one CTA of 1024 threads): destination masks and per-destination
@@ -201,24 +214,91 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
         if (ticket == gridDim.x - 1) {
             __threadfence_system();
             const uint32_t epoch = *p.epoch;
-            for (int d = 0; d < p.world; ++d) {
-                EpCtl *c = reinterpret_cast<EpCtl *>(p.peers.base[d] + p.L.ctl);
-                c->recv_count[p.rank] = static_cast<uint32_t>(p.counts[d]);
-                st_release_sys(&c->recv_epoch[p.rank], epoch);
-            }
+            for (int d = 0; d < p.world; ++d) ep_publish(p, d, static_cast<uint32_t>(p.counts[d]), epoch);
             *p.blocks_done = 0u;
         }
     }
 }
 
-// Wait until every peer has published the current epoch in `flags` (one
-// lane per peer, bounded by ~2^31 cycles).
-__global__ void ep_wait_kernel(const uint32_t *flags, const uint32_t *epoch, int world, int *error) {
+// Decode sizes (T <= 32): plan and dispatch in one CTA of 1024 threads.  Warp
+// 0 plans with ballots (lane = token), every warp then copies (token,
+// destination) rows, and after a CTA barrier lane d of warp 0 publishes to
+// destination d -- the release is cumulative over the barrier, so no grid
+// ticket and no serial loop over destinations.
+__global__ void __launch_bounds__(1024) ep_plan_dispatch_small_kernel(EpParams p) {
+    __shared__ uint32_t sm_mask[32];
+    __shared__ int sm_pos[32][kEpMaxRanks];
+    __shared__ int sm_count[kEpMaxRanks];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int H = p.hidden, nb = H / 32;
+    if (warp == 0) {
+        const int t = lane;
+        uint32_t mask = 0u;
+        if (t < p.tokens) {
+            mask = 1u << p.rank;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                const int e = p.ids[t * kTopK + k];
+                if (e >= 0 && e < p.ecount * p.world) mask |= 1u << (e / p.ecount);
+            }
+            p.dmask[t] = static_cast<uint8_t>(mask);
+        }
+        sm_mask[lane] = mask;
+#pragma unroll
+        for (int d = 0; d < kEpMaxRanks; ++d) {
+            const uint32_t b = __ballot_sync(0xffffffffu, (mask >> d) & 1u);
+            const int pos = __popc(b & ((1u << lane) - 1u));
+            sm_pos[lane][d] = pos;
+            if (t < p.tokens) p.pos[t * kEpMaxRanks + d] = pos;
+            if (lane == 0) sm_count[d] = __popc(b);
+        }
+        if (lane == 0) *p.epoch += 1u;
+    }
+    __syncthreads();
+    for (int it = warp; it < p.tokens * p.world; it += 32) {
+        const int t = it / p.world, d = it % p.world;
+        if (!((sm_mask[t] >> d) & 1u)) continue;
+        const size_t slot = static_cast<size_t>(p.rank) * p.t_max + sm_pos[t][d];
+        uint8_t *dst = p.peers.base[d];
+        const uint4 *sc = reinterpret_cast<const uint4 *>(p.xcodes + static_cast<size_t>(t) * H);
+        uint4 *dc = reinterpret_cast<uint4 *>(dst + p.L.codes + slot * H);
+        for (int i = lane; i < H / 16; i += 32) dc[i] = sc[i];
+        const uint4 *ss = reinterpret_cast<const uint4 *>(p.xscales + static_cast<size_t>(t) * nb);
+        uint4 *ds = reinterpret_cast<uint4 *>(dst + p.L.scales + slot * nb * 8);
+        const uint4 *st = reinterpret_cast<const uint4 *>(p.xtc + static_cast<size_t>(t) * nb);
+        uint4 *dt = reinterpret_cast<uint4 *>(dst + p.L.tc + slot * nb * 8);
+        for (int i = lane; i < nb / 2; i += 32) {
+            ds[i] = ss[i];
+            dt[i] = st[i];
+        }
+        if (lane < kEpSlotIds) {
+            int id = -1;
+            float w = 0.0f;
+            const int e = p.ids[t * kTopK + lane];
+            if (e >= 0 && e / p.ecount == d) {
+                id = e - d * p.ecount;
+                w = p.weights[t * kTopK + lane];
+            }
+            reinterpret_cast<int32_t *>(dst + p.L.ids)[slot * kEpSlotIds + lane] = id;
+            reinterpret_cast<float *>(dst + p.L.w)[slot * kEpSlotIds + lane] = w;
+        }
+    }
+    __syncthreads();
+    if (warp == 0 && lane < p.world) {
+        __threadfence_system();
+        ep_publish(p, lane, static_cast<uint32_t>(sm_count[lane]), *p.epoch);
+    }
+    if (threadIdx.x < kEpMaxRanks) p.counts[threadIdx.x] = sm_count[threadIdx.x];
+}
+
+// Wait until every source has published the current epoch in its receive
+// word (one lane per peer, bounded by ~2^31 cycles).
+__global__ void ep_wait_kernel(const uint64_t *recv, const uint32_t *epoch, int world, int *error) {
     const int d = threadIdx.x;
     if (d >= world) return;
     const uint32_t want = *epoch;
     const long long t0 = clock64();
-    while (ld_acquire_sys(&flags[d]) != want) {
+    while (static_cast<uint32_t>(ld_acquire_sys64(&recv[d])) != want) {
         if (clock64() - t0 > (1ll << 31)) {
             atomicOr(error, kFlagTimeout);
             return;
@@ -238,7 +318,7 @@ struct EpGroupParams {
     float *partial;
 };
 __device__ __forceinline__ bool ep_slot_valid(const EpCtl *c, int slot, int t_max) {
-    return static_cast<uint32_t>(slot % t_max) < c->recv_count[slot / t_max];
+    return static_cast<uint32_t>(slot % t_max) < static_cast<uint32_t>(c->recv[slot / t_max] >> 32);
 }
 __global__ void __launch_bounds__(256) ep_masks_kernel(EpGroupParams g) {
     __shared__ uint32_t smask[kRouterExperts];
@@ -290,7 +370,7 @@ __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams 
         if (e < g.world) {
             const uint32_t want = *g.epoch;
             const long long t0 = clock64();
-            while (ld_acquire_sys(&c->recv_epoch[e]) != want) {
+            while (static_cast<uint32_t>(ld_acquire_sys64(&c->recv[e])) != want) {
                 if (clock64() - t0 > (1ll << 31)) {
                     atomicOr(g.error, kFlagTimeout);
                     ok = false;

@@ -1216,11 +1216,16 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
     if (const int st = launch_route(tx, w, x, logits, tokens, nullptr, s)) return st;
     // 2-3. plan and dispatch (peer stores), publish epoch + counts
     EpParams p = ep_params(ep, tokens, out);
-    ep_plan_kernel<<<1, 1024, 0, s>>>(p);
-    MOE_CUDA(cudaGetLastError());
-    const int items = tokens * ep->world;
-    ep_dispatch_kernel<<<std::max(1, std::min((items + 7) / 8, tx->sms * 4)), 256, 0, s>>>(p);
-    MOE_CUDA(cudaGetLastError());
+    if (tokens <= 32) {
+        ep_plan_dispatch_small_kernel<<<1, 1024, 0, s>>>(p);
+        MOE_CUDA(cudaGetLastError());
+    } else {
+        ep_plan_kernel<<<1, 1024, 0, s>>>(p);
+        MOE_CUDA(cudaGetLastError());
+        const int items = tokens * ep->world;
+        ep_dispatch_kernel<<<std::max(1, std::min((items + 7) / 8, tx->sms * 4)), 256, 0, s>>>(p);
+        MOE_CUDA(cudaGetLastError());
+    }
     // 4. all sources' slots received -> group by local expert
     EpCtl *ctl = reinterpret_cast<EpCtl *>(ep->exported + ep->L.ctl);
     moe_layer_s &r = ep->rx;
@@ -1251,7 +1256,7 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
         ep_group_small_kernel<<<1, 512, 0, s>>>(g);
         MOE_CUDA(cudaGetLastError());
     } else {
-        ep_wait_kernel<<<1, 32, 0, s>>>(ctl->recv_epoch, ep->epoch, ep->world, ep->rx.error);
+        ep_wait_kernel<<<1, 32, 0, s>>>(ctl->recv, ep->epoch, ep->world, ep->rx.error);
         MOE_CUDA(cudaGetLastError());
         const int chunks = ep->slots / kChunk;
         EpGroupParams g{ep->exported, ep->L, ep->t_max, ep->slots, H, r.masks, partial};
