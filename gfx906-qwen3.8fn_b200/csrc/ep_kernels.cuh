@@ -284,10 +284,8 @@ __global__ void __launch_bounds__(1024) ep_plan_dispatch_small_kernel(EpParams p
         }
     }
     __syncthreads();
-    if (warp == 0 && lane < p.world) {
-        __threadfence_system();
+    if (warp == 0 && lane < p.world)   // the system-scope release orders the whole CTA's stores (barrier above)
         ep_publish(p, lane, static_cast<uint32_t>(sm_count[lane]), *p.epoch);
-    }
     if (threadIdx.x < kEpMaxRanks) p.counts[threadIdx.x] = sm_count[threadIdx.x];
 }
 
