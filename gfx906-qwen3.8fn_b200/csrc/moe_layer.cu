@@ -199,15 +199,14 @@ TcParams tc_params(moe_layer_s *h, const moe_weights_s *w, float *out, bool down
     TcParams t;
     t.weights = w->base;
     t.layout = w->layout;
-    t.act = down ? h->mid.codes : h->xq.codes;
-    t.act_tc = down ? h->tc.mid_tc : h->tc.x_tc;
-    t.act_by_token = down ? 0 : 1;
+    t.a_arr = down ? h->tc.a_dn : h->tc.a_gu;
+    t.sc_arr = down ? h->tc.sc_dn : h->tc.sc_gu;
     t.tiles = h->tc.tiles;
     t.num_tiles = h->tc.num_tiles;
     t.pair_token = h->pair_token;
     t.pair_weight = h->pair_weight;
-    t.mid = h->mid;
-    t.mid_tc = h->tc.mid_tc;
+    t.mid_arr = h->tc.a_dn;
+    t.mid_sc_arr = h->tc.sc_dn;
     t.out = out;
     t.error = h->error;
     return t;
@@ -242,8 +241,13 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         sp.stage_bytes = GuStage(L.hidden).bytes;
         MOE_CUDA(launch_overlapped(stream_gate_up_kernel, std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
                                    stream_gu_smem(L.hidden, sp.stages), s, sp));
-        if (tc_tiles)
+        if (tc_tiles) {
+            tc_gather_kernel<<<dim3(std::min(tc_tiles, h->sms * 2), L.hidden / 256), kTcM, 0, s>>>(
+                h->tc.tiles, h->tc.num_tiles, h->pair_token, h->xq.codes, h->tc.x_tc, L.hidden, h->tc.a_gu,
+                h->tc.sc_gu);
+            MOE_CUDA(cudaGetLastError());
             if (const int st = launch_tc(h, w, out, tc_tiles, false, s)) return st;
+        }
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
         sp.stages = h->dn_stages;
         sp.stage_bytes = DnStage(L.inter).bytes;
@@ -516,7 +520,7 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
         h->tile_off = a.take<int32_t>(kRouterExperts);
         h->num_tiles = a.take<int>(1);
         h->error = a.take<int>(1);
-        tc_workspace_take(h->tc, a, T, H, I);
+        tc_workspace_take(h->tc, a, T, H, I, T > kChunk);
         if (pass == 0) {
             const size_t bytes = a.used + 256;
             const cudaError_t e = cudaMalloc(&a.base, bytes);
@@ -999,10 +1003,18 @@ void ep_take_rx(moe_ep_s *ep, Arena &a) {
     r.tile_off = a.take<int32_t>(kRouterExperts);
     r.num_tiles = a.take<int>(1);
     r.error = a.take<int>(1);
-    r.tc.mid_tc = a.take<float2>(static_cast<size_t>(pairs) * (I / 32));
     r.tc.max_tiles = pairs / kTcM + kRouterExperts + 2 + ep->t_max / kTcM;
     r.tc.tiles = a.take<int4>(r.tc.max_tiles);
     r.tc.num_tiles = a.take<int>(1);
+    r.tc.a_gu = r.tc.a_dn = nullptr;
+    r.tc.sc_gu = r.tc.sc_dn = nullptr;
+    if (ep->tc) {
+        const size_t bg = static_cast<size_t>(r.tc.max_tiles) * (H / 32), bd = static_cast<size_t>(r.tc.max_tiles) * (I / 32);
+        r.tc.a_gu = a.take<uint8_t>(bg * kTcM * 32);
+        r.tc.sc_gu = a.take<float2>(bg * kTcM);
+        r.tc.a_dn = a.take<uint8_t>(bd * kTcM * 32);
+        r.tc.sc_dn = a.take<float2>(bd * kTcM);
+    }
     ep->pos = a.take<int32_t>(static_cast<size_t>(ep->t_max) * kEpMaxRanks);
     ep->dmask = a.take<uint8_t>(ep->t_max);
     ep->counts = a.take<int32_t>(kEpMaxRanks);

@@ -253,15 +253,18 @@ __device__ __forceinline__ Q8Codes q8_half_codes(const float (&x)[16], float ama
 struct TcParams {
     const uint8_t *weights;
     ExpertLayout layout;
-    const int8_t *act;          // gate/up: x codes [T][H];  down: middle codes [pairs][I]
-    const float2 *act_tc;       // per (row of act, block): (d8, c8)
-    int act_by_token;           // 1: A row = pair_token[pair] (gate/up), 0: A row = pair (down)
+    // A operand and its per-(row, block) constants (d8, c8), pre-arranged per
+    // tile so that each stage is one contiguous run: block b of tile t at
+    // a_arr + (t*nb + b)*4096 in the K-major core-matrix layout of TcStage::a,
+    // constants at sc_arr + (t*nb + b)*128.
+    const uint8_t *a_arr;
+    const float2 *sc_arr;
     const int4 *tiles;          // {expert, first pair, count, 0}
     const int *num_tiles;
     const int32_t *pair_token;
     const float *pair_weight;
-    Q8Planar mid;               // gate/up output
-    float2 *mid_tc;             // gate/up output (d8, c8) per (pair, block)
+    uint8_t *mid_arr;           // gate/up output: the down kernel's a_arr
+    float2 *mid_sc_arr;         // gate/up output: the down kernel's sc_arr
     float *out;                 // down output [T][H]
     int *error;
 };
@@ -356,17 +359,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
         }
     } else if (warp <= kTcProducerWarps) {
         // ---------------- producers ----------------
-        // Software pipeline over this CTA's stages g = 0, 1, ...: the weight
-        // codes of stage g+1 are loaded into registers while stage g is staged,
-        // and stage g is published (full barrier) one iteration later, after
-        // its cp.async group has landed.
+        // A and its block constants are one contiguous 16 KB + 4 KB run per stage
+        // in the pre-arranged buffers: one thread issues them as bulk copies
+        // counted on the stage's full barrier.  The producer warps load (one
+        // stage ahead, into registers), unpack and store the weight codes.
         constexpr int kProducerThreads = 32 * kTcProducerWarps;
-        constexpr int kAPer = (kTcM + kProducerThreads - 1) / kProducerThreads;
         constexpr int kBPer = (kTcN * kTcKB + kProducerThreads - 1) / kProducerThreads;
         const int pt = threadIdx.x - 32;
         const int my_items = static_cast<int>(blockIdx.x) < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
         const int nstages = my_items * ksteps;
-        int4 td_next = make_int4(0, 0, 0, 0), td = td_next;
+        int4 td_next = make_int4(0, 0, 0, 0);
         uint4 wn[kBPer];
         uint16_t dn[kBPer];
         // global loads of stage g's weight codes and scales into wn/dn
@@ -397,11 +399,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
                 }
             }
         };
-        int arow[kAPer];
         if (nstages > 0) prefetch(0);
         for (int g = 0; g < nstages; ++g) {
             const int ks = g % ksteps, s = g % kTcStages;
-            if (ks == 0) td = td_next;
+            const int tile = (blockIdx.x + (g / ksteps) * gridDim.x) / slabs;
             uint4 wc[kBPer];
             uint16_t dc[kBPer];
 #pragma unroll
@@ -410,32 +411,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
                 dc[j] = dn[j];
             }
             if (g + 1 < nstages) prefetch(g + 1);
-            if (ks == 0) {
-#pragma unroll
-                for (int a = 0; a < kAPer; ++a) {
-                    const int row = pt + a * kProducerThreads;
-                    arow[a] = row < td.z ? (p.act_by_token ? p.pair_token[td.y + row] : td.y + row) : -1;
-                }
-            }
             if (g >= kTcStages && !mbar_wait(&empty[s], ((g / kTcStages) & 1) ^ 1, p.error)) { failed = true; break; }
             uint8_t *st = ring + s * TcStage::bytes;
-            const int b0 = ks * kTcKB;
-            // A: pair rows (kTcKB blocks x 2 halves each) plus their block scales
-#pragma unroll
-            for (int a = 0; a < kAPer; ++a) {
-                if (arow[a] < 0) continue;
-                const int row = pt + a * kProducerThreads;
-                const int8_t *src = p.act + static_cast<size_t>(arow[a]) * K + b0 * 32;
-#pragma unroll
-                for (int kb = 0; kb < kTcKB; ++kb)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        cp_async16(st + TcStage::a + kb * kTcM * 32 + tile_off(row, h), src + kb * 32 + h * 16);
-                const float2 *ss = p.act_tc + static_cast<size_t>(arow[a]) * nb + b0;
-#pragma unroll
-                for (int kb = 0; kb < kTcKB; ++kb) cp_async8(st + TcStage::sc + (kb * kTcM + row) * 8, ss + kb);
+            if (pt == 0) {
+                const size_t blk0 = static_cast<size_t>(tile) * nb + static_cast<size_t>(ks) * kTcKB;
+                mbar_expect_tx(&full[s], kTcKB * kTcM * 32 + kTcKB * kTcM * 8);
+                bulk_g2s(st + TcStage::a, p.a_arr + blk0 * (kTcM * 32), kTcKB * kTcM * 32, &full[s]);
+                bulk_g2s(st + TcStage::sc, p.sc_arr + blk0 * kTcM, kTcKB * kTcM * 8, &full[s]);
             }
-            cp_async_commit();
             // B: 64 weight rows x kTcKB blocks of codes, unpacked to centred s8
 #pragma unroll
             for (int j = 0; j < kBPer; ++j) {
@@ -449,20 +432,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
                     reinterpret_cast<float *>(st + TcStage::d4)[kb * kTcN + col] = h2f(dc[j]);
                 }
             }
-            // publish the previous stage: its copies have landed once at most
-            // this stage's group is pending
-            if (g > 0) {
-                cp_async_wait_group1();
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[(g - 1) % kTcStages]);
-            }
-        }
-        if (nstages > 0 && !failed) {
-            cp_async_wait_all();
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&full[(nstages - 1) % kTcStages]);
+            if (lane == 0) mbar_arrive(&full[s]);
         }
     } else {
         // ---------------- epilogue ----------------
@@ -585,17 +557,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
                 const int bad_code = qc.bad_code | reinterpret_cast<const int *>(other)[3];
                 const bool valid = !bad && qc.representable && !bad_code;
                 if (real) {
-                    const size_t pair = static_cast<size_t>(p0 + m);
+                    // middle block `slab` of this tile in the down kernel's A layout
+                    const size_t mblk = static_cast<size_t>(item / slabs) * (I / 32) + slab;
                     int4 cv = *reinterpret_cast<const int4 *>(code);
                     if (!valid) cv = make_int4(0, 0, 0, 0);
-                    *reinterpret_cast<int4 *>(p.mid.codes + pair * I + slab * 32 + chunk * 16) = cv;
+                    *reinterpret_cast<int4 *>(p.mid_arr + mblk * (kTcM * 32) + tile_off(m, chunk)) = cv;
                     if (chunk == 0) {
-                        const int mslabs = I / 32;
                         const uint16_t hd = (valid && amax != 0.0f) ? qc.d : uint16_t(0);
                         const uint16_t hs = (valid && amax != 0.0f) ? qc.s : uint16_t(0);
                         const int csum = valid ? qc.csum + reinterpret_cast<const int *>(other)[2] : 0;
-                        p.mid.scales[pair * mslabs + slab] = make_float2(h2f(hd), h2f(hs));
-                        p.mid_tc[pair * mslabs + slab] =
+                        p.mid_sc_arr[mblk * kTcM + m] =
                             make_float2(h2f(hd), 8.0f * (static_cast<float>(csum) * h2f(hd) - h2f(hs)));
                     }
                     report(flags | (bad ? kFlagInvalid : 0) | ((qc.representable && !bad_code) ? 0 : kFlagArithmetic),
@@ -644,20 +615,61 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(TcParams p) {
 
 struct TcWorkspace {
     float2 *x_tc;       // (d8, c8) of the quantised input [T][H/32]
-    float2 *mid_tc;     // (d8, c8) of the middle [pairs][I/32]
     int4 *tiles;        // tensor-core tile list
     int *num_tiles;
     int max_tiles;
+    // pre-arranged A operands (see TcParams): gate/up from x, down from the
+    // gate/up epilogue; null when the workspace never runs the tensor-core path
+    uint8_t *a_gu, *a_dn;
+    float2 *sc_gu, *sc_dn;
 };
 
 template <class ArenaT>
-inline void tc_workspace_take(TcWorkspace &w, ArenaT &a, int T, int H, int I) {
+inline void tc_workspace_take(TcWorkspace &w, ArenaT &a, int T, int H, int I, bool tc_used) {
     const int pairs = T * (kTopK + 1);
     w.x_tc = a.template take<float2>(static_cast<size_t>(T) * (H / 32));
-    w.mid_tc = a.template take<float2>(static_cast<size_t>(pairs) * (I / 32));
     w.max_tiles = (pairs + kTcM - 1) / kTcM + kRouterExperts + 1;
     w.tiles = a.template take<int4>(w.max_tiles);
     w.num_tiles = a.template take<int>(1);
+    w.a_gu = w.a_dn = nullptr;
+    w.sc_gu = w.sc_dn = nullptr;
+    if (tc_used) {
+        const size_t bg = static_cast<size_t>(w.max_tiles) * (H / 32), bd = static_cast<size_t>(w.max_tiles) * (I / 32);
+        w.a_gu = a.template take<uint8_t>(bg * kTcM * 32);
+        w.sc_gu = a.template take<float2>(bg * kTcM);
+        w.a_dn = a.template take<uint8_t>(bd * kTcM * 32);
+        w.sc_dn = a.template take<float2>(bd * kTcM);
+    }
+}
+
+// Gate/up A operand of every tensor-core tile: row r of tile t is the Q8_1
+// codes (and constants) of token pair_token[p0 + r], written block by block
+// into the arranged layout.  CTA (t, g): 128 threads (rows) x blocks 8g..8g+7.
+__global__ void __launch_bounds__(kTcM) tc_gather_kernel(const int4 *tiles, const int *num_tiles,
+                                                         const int32_t *pair_token, const int8_t *xcodes,
+                                                         const float2 *xtc, int H, uint8_t *a_arr, float2 *sc_arr) {
+    const int nb = H / 32, row = threadIdx.x, b0 = blockIdx.y * 8;
+    for (int t = blockIdx.x; t < *num_tiles; t += gridDim.x) {
+        const int4 td = tiles[t];
+        if (row >= td.z) continue;
+        const int token = pair_token[td.y + row];
+        const uint4 *src = reinterpret_cast<const uint4 *>(xcodes + static_cast<size_t>(token) * H) + 2 * b0;
+        const float2 *ssrc = xtc + static_cast<size_t>(token) * nb + b0;
+        uint4 v[16];
+        float2 c[8];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = src[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) c[i] = ssrc[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const size_t blk = static_cast<size_t>(t) * nb + b0 + i;
+            uint8_t *dst = a_arr + blk * (kTcM * 32);
+            *reinterpret_cast<uint4 *>(dst + tile_off(row, 0)) = v[2 * i];
+            *reinterpret_cast<uint4 *>(dst + tile_off(row, 1)) = v[2 * i + 1];
+            sc_arr[blk * kTcM + row] = c[i];
+        }
+    }
 }
 
 inline int tc_configure() {
