@@ -550,18 +550,29 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
     const uint32_t mask = p.dmask[t];
     const int H = p.hidden;
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 *rows[kEpMaxRanks];   // this token's partial row on every destination (null: not used)
+#pragma unroll
+    for (int d = 0; d < kEpMaxRanks; ++d) {
+        const bool use = d < p.world && ((mask >> d) & 1u);
+        const size_t slot = static_cast<size_t>(p.rank) * p.t_max + (use ? p.pos[t * kEpMaxRanks + d] : 0);
+        rows[d] = use ? reinterpret_cast<float4 *>(p.peers.base[d] + p.L.partial) + slot * (H / 4) : nullptr;
+    }
     for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        // all remote loads first (one NVLink round trip), then the in-order sum
+        float4 v[kEpMaxRanks];
+#pragma unroll
+        for (int d = 0; d < kEpMaxRanks; ++d) v[d] = rows[d] ? rows[d][i] : zero;
+#pragma unroll
+        for (int d = 0; d < kEpMaxRanks; ++d)
+            if (rows[d]) rows[d][i] = zero;
         float4 acc = zero;
-        for (int d = 0; d < p.world; ++d) {
-            if (!((mask >> d) & 1u)) continue;
-            const size_t slot = static_cast<size_t>(p.rank) * p.t_max + p.pos[t * kEpMaxRanks + d];
-            float4 *src = reinterpret_cast<float4 *>(p.peers.base[d] + p.L.partial) + slot * (H / 4) + i;
-            const float4 v = *src;
-            *src = zero;
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+#pragma unroll
+        for (int d = 0; d < kEpMaxRanks; ++d) {
+            if (!rows[d]) continue;
+            acc.x = __fadd_rn(acc.x, v[d].x);
+            acc.y = __fadd_rn(acc.y, v[d].y);
+            acc.z = __fadd_rn(acc.z, v[d].z);
+            acc.w = __fadd_rn(acc.w, v[d].w);
         }
         float4 *o = reinterpret_cast<float4 *>(p.out + static_cast<size_t>(t) * H) + i;
         float4 r = *o;
