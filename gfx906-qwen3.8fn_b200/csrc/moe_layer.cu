@@ -281,7 +281,7 @@ int launch_quantize(const float *x, size_t blocks, Q8Planar out, uint8_t *canoni
 }
 
 int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const float *logits, int T,
-                 float *probs, cudaStream_t s) {
+                 float *probs, cudaStream_t s, const EpParams *ep = nullptr, uint32_t *quant_done = nullptr) {
     const int chunks = (T + kChunk - 1) / kChunk;
     RouteParams rp;
     rp.logits = logits;
@@ -306,6 +306,11 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
         sr.tile_off = h->tile_off;
         sr.num_tiles = h->num_tiles;
         sr.max_tiles = h->tiles_max;
+        if (ep) {
+            sr.ep_on = 1;
+            sr.ep = *ep;
+            sr.quant_done = quant_done;
+        }
         // block 0 routes; the others quantise x (one warp per 32-value block)
         const int qblocks = sr.xq.codes ? (T * (h->desc.hidden / 32) + 15) / 16 : 0;
         route_small_kernel<<<1 + qblocks, 512, 0, s>>>(sr);
@@ -981,7 +986,7 @@ struct moe_ep_s {
     bool opened[kEpMaxRanks] = {};
     int32_t *pos = nullptr, *counts = nullptr;
     uint8_t *dmask = nullptr;
-    uint32_t *epoch = nullptr, *blocks_done = nullptr;
+    uint32_t *epoch = nullptr, *blocks_done = nullptr, *quant_done = nullptr;
 };
 
 namespace {
@@ -1020,6 +1025,7 @@ void ep_take_rx(moe_ep_s *ep, Arena &a) {
     ep->counts = a.take<int32_t>(kEpMaxRanks);
     ep->epoch = a.take<uint32_t>(1);
     ep->blocks_done = a.take<uint32_t>(1);
+    ep->quant_done = a.take<uint32_t>(1);
     (void)H;
 }
 
@@ -1225,13 +1231,19 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
         if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, tx->xq, nullptr, tx->error,
                                            tx->sms, s, tx->tc.x_tc))
             return st;
-    if (const int st = launch_route(tx, w, x, logits, tokens, nullptr, s)) return st;
-    // 2-3. plan and dispatch (peer stores), publish epoch + counts
     EpParams p = ep_params(ep, tokens, out);
-    if (tokens <= 32) {
+    if (tokens <= kChunk && !ep->tc) {
+        // 2-3. decode sizes: the routing launch quantises, stores every row in every
+        // rank at the token's fixed slot, writes each destination's expert lists
+        // and publishes the epoch
+        if (const int st = launch_route(tx, w, x, logits, tokens, nullptr, s, &p, ep->quant_done)) return st;
+    } else if (tokens <= 32) {
+        if (const int st = launch_route(tx, w, x, logits, tokens, nullptr, s)) return st;
+        // 2-3. plan and dispatch (peer stores), publish epoch + counts
         ep_plan_dispatch_small_kernel<<<1, 1024, 0, s>>>(p);
         MOE_CUDA(cudaGetLastError());
     } else {
+        if (const int st = launch_route(tx, w, x, logits, tokens, nullptr, s)) return st;
         ep_plan_kernel<<<1, 1024, 0, s>>>(p);
         MOE_CUDA(cudaGetLastError());
         const int items = tokens * ep->world;

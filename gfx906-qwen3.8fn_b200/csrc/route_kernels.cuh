@@ -9,6 +9,7 @@
 // operation is a separately rounded IEEE op in the reference's order.
 #pragma once
 #include "common.cuh"
+#include "ep_common.cuh"
 #include "ptx.cuh"
 
 namespace qmoe {
@@ -441,6 +442,13 @@ __global__ void identity_route_kernel(int tokens, int tile, TileRec *tiles, int 
 // six launches of the general path.  Same arithmetic, same outputs.
 struct SmallRouteParams {
     RouteParams r;
+    // Expert parallelism (ep_on): the quantising CTAs also store every row into
+    // every rank's receive buffer at slot rank*t_max + token, and the routing
+    // CTA writes each destination's (local expert, weight) lists and publishes
+    // the epoch once all rows are in place -- dispatch without its own launch.
+    int ep_on = 0;
+    EpParams ep;
+    uint32_t *quant_done = nullptr;   // quantising CTAs finished (rewound by the routing CTA)
     Q8Planar xq;            // quantised x output
     int32_t *offsets;       // [514]
     TileRec *tiles;
@@ -456,13 +464,31 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
     const int T = p.tokens, H = p.hidden;
     if (blockIdx.x > 0) {
         // blocks 1.. quantise x, one warp per 32-value block, alongside the routing block
-        const int stride = (gridDim.x - 1) * 16;
-        for (int b = (blockIdx.x - 1) * 16 + warp; b < T * (H / 32); b += stride) {
+        const int stride = (gridDim.x - 1) * 16, nb = H / 32;
+        for (int b = (blockIdx.x - 1) * 16 + warp; b < T * nb; b += stride) {
             const Q8Lane q = quantize_lane(p.x[static_cast<size_t>(b) * 32 + lane]);
             sp.xq.codes[static_cast<size_t>(b) * 32 + lane] = q.code;
             if (lane == 0) {
                 sp.xq.scales[b] = make_float2(h2f(q.d), h2f(q.s));
                 report(q.flags, p.error);
+            }
+            if (sp.ep_on) {   // the row block into every rank's receive buffer (fixed slot)
+                const int t = b / nb, j = b % nb;
+                const size_t slot = static_cast<size_t>(sp.ep.rank) * sp.ep.t_max + t;
+                for (int d = 0; d < sp.ep.world; ++d) {
+                    uint8_t *base = sp.ep.peers.base[d];
+                    reinterpret_cast<int8_t *>(base + sp.ep.L.codes)[slot * H + j * 32 + lane] = q.code;
+                    if (lane == 0)
+                        reinterpret_cast<float2 *>(base + sp.ep.L.scales)[slot * nb + j] =
+                            make_float2(h2f(q.d), h2f(q.s));
+                }
+            }
+        }
+        if (sp.ep_on) {
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence_system();
+                atomicAdd(sp.quant_done, 1u);
             }
         }
         return;
@@ -471,11 +497,46 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
     __shared__ float w_s[kChunk * kTopK];
     smask[e] = 0u;
     __syncthreads();
+    if (sp.ep_on && e == 0) *sp.ep.epoch += 1u;
     // warps 0..T-1 route token = warp (and 16 + warp); the shared gates run on
     // the idle warps T..2T-1 in parallel when T <= 8, else after the routing
     for (int t = warp; t < T; t += 16) route_topk_token(p, t, t, smask, lane, ids_s, w_s);
     for (int t = T <= 8 ? warp - T : warp; t >= 0 && t < T; t += 16) route_shared_gate(p, t, lane);
     __syncthreads();   // ids/weights (global and shared) and smask complete
+    if (sp.ep_on) {
+        const EpParams &ep = sp.ep;
+        // each destination's (local expert, weight) lists of this rank's tokens
+        for (int i = e; i < T * ep.world * kTopK; i += blockDim.x) {
+            const int k = i % kTopK, d = (i / kTopK) % ep.world, t = i / (kTopK * ep.world);
+            const int gid = ids_s[t * kTopK + k];
+            const bool own = gid >= 0 && gid / ep.ecount == d;
+            const size_t slot = static_cast<size_t>(ep.rank) * ep.t_max + t;
+            reinterpret_cast<int32_t *>(ep.peers.base[d] + ep.L.ids)[slot * kEpSlotIds + k] = own ? gid - d * ep.ecount : -1;
+            reinterpret_cast<float *>(ep.peers.base[d] + ep.L.w)[slot * kEpSlotIds + k] = own ? w_s[t * kTopK + k] : 0.0f;
+        }
+        // destinations and slots for the combine: token t sits at index t in every region
+        if (e < T) {
+            uint32_t mask = 1u << ep.rank;
+            for (int k = 0; k < kTopK; ++k) {
+                const int gid = ids_s[e * kTopK + k];
+                if (gid >= 0 && gid < ep.ecount * ep.world) mask |= 1u << (gid / ep.ecount);
+            }
+            ep.dmask[e] = static_cast<uint8_t>(mask);
+            for (int d = 0; d < kEpMaxRanks; ++d) ep.pos[e * kEpMaxRanks + d] = e;
+        }
+        // every quantising CTA has stored its rows (and fenced them system-wide)
+        if (e == 0) {
+            const long long t0 = clock64();
+            while (ld_acquire_gpu_u32(sp.quant_done) != gridDim.x - 1) {
+                if (clock64() - t0 > (1ll << 31)) { atomicOr(p.error, kFlagTimeout); break; }
+                __nanosleep(32);
+            }
+            *sp.quant_done = 0u;
+        }
+        __syncthreads();
+        if (e < ep.world) ep_publish(ep, e, static_cast<uint32_t>(T), *ep.epoch);
+        return;
+    }
     const uint32_t mask = smask[e];
     const int count = __popc(mask);
     int total = 0;
