@@ -520,7 +520,7 @@ def ep_result(args, cfg, world, rank, ms, e2e_ms, h2d, d2h, clk, lg_host, T, U, 
             "bytes_per_step_rank": step_bytes,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650 GB/s"}
     tokens_per_step = T * U * L * world
-    per_layer = (6 if T <= 32 else 18)
+    per_layer = (5 if T <= 32 else 17)
     return {
         "metric": METRIC, "value": tokens_per_step / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -535,8 +535,8 @@ def ep_result(args, cfg, world, rank, ms, e2e_ms, h2d, d2h, clk, lg_host, T, U, 
         "e2e": {"value": tokens_per_step / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms},
         "roofline": roof,
-        # per layer (T <= 32): routing+dispatch, grouping, 2 expert kernels, done, combine;
-        # larger T: quantise, 4 routing, plan, dispatch, wait, 4 grouping, 4 expert kernels, done, combine
+        # per layer (T <= 32): routing+dispatch, grouping, 2 expert kernels, done+combine;
+        # larger T: quantise, 4 routing, plan, dispatch, wait, 4 grouping, 4 expert kernels, done+combine
         "gpu_launches": args.steps * U * L * per_layer,
         "clocks": clk,
     }

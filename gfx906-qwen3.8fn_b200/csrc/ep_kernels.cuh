@@ -447,13 +447,21 @@ __global__ void ep_done_kernel(EpPeers peers, EpLayout L, int rank, int world, c
     st_release_sys(&c->done_epoch[rank], *epoch);
 }
 
-// Combine: wait until every peer has published its partial rows (bounded),
+// Combine: publish this rank's "partials final", wait until every peer has
+// published its own (bounded),
 // then out[t] += sum over the token's destinations d (ascending) of the
 // partial row d holds for it, clearing that row for the next epoch.  One CTA
 // per token.
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
     __shared__ int ready;
     const int t = blockIdx.x;
+    // This rank's partial rows are final (the expert kernels before this launch
+    // completed): CTA 0 publishes that to every peer first.
+    if (t == 0 && threadIdx.x < p.world) {
+        __threadfence_system();
+        EpCtl *c = reinterpret_cast<EpCtl *>(p.peers.base[threadIdx.x] + p.L.ctl);
+        st_release_sys(&c->done_epoch[p.rank], *p.epoch);
+    }
     if (t >= p.tokens) return;
     if (threadIdx.x < 32) {
         const EpCtl *c = reinterpret_cast<const EpCtl *>(p.peers.base[p.rank] + p.L.ctl);

@@ -1321,9 +1321,7 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
     // expert kernels over the received slots, partial rows accumulated locally
     const int tc_tiles = ep->tc ? std::min(r.tc.max_tiles, ep->rx_pairs / kTcMinGroup + ep->rx_pairs / kTcM + 1) : 0;
     if (const int st = launch_experts(&r, w, partial, r.tiles_max, s, nullptr, tc_tiles)) return st;
-    // 5. publish done; the combine waits for every peer's, then pulls the partial rows
-    ep_done_kernel<<<1, 32, 0, s>>>(ep->peers, ep->L, ep->rank, ep->world, ep->epoch);
-    MOE_CUDA(cudaGetLastError());
+    // 5. the combine publishes "done", waits for every peer's, then pulls the partial rows
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
     ep_combine_kernel<<<tokens, 256, 0, s>>>(p);
     return cuda_status(cudaGetLastError(), "ep_combine_kernel");
