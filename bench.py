@@ -30,7 +30,6 @@ import argparse
 import json
 import math
 import os
-import subprocess
 import sys
 import time
 
@@ -79,53 +78,79 @@ def profile_traffic(name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event reasons sampled through NVML every 2 ms while the
+    timed region runs (a decode step's timed region is tens of milliseconds, shorter
+    than nvidia-smi's start-up), recorded as csv lines in the order of nvidia-smi's
+    --query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.*."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.002
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    # NVML clocks-event reason bits, in NAMES order
+    BITS = (0x8, 0x40, 0x20, 0x4)
 
     def __init__(self, device):
         self.device = device
-        self.proc = None
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_dev{device}.csv")
+        self.thread = None
+        self.rows = []
+
+    def _handle(self, nvml):
+        import torch
+        try:
+            p = torch.cuda.get_device_properties(self.device)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return nvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def start(self):
+        import threading
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+            import pynvml as nvml
+            nvml.nvmlInit()
+            h = self._handle(nvml)
+            mx = nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
+            self.thread = None
+            return
+        self.stop_evt = threading.Event()
+        self.rows = []
+
+        def run():
+            while True:
+                try:
+                    sm = nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM)
+                    rs = nvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    pw = nvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    self.rows.append((sm, mx, pw, rs))
+                except Exception:
+                    pass
+                if self.stop_evt.wait(self.PERIOD_S):
+                    break
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+        # the first sample lands before the timed region starts
+        while not self.rows and self.thread.is_alive():
+            time.sleep(0.0005)
 
     def stop(self):
-        if not self.proc:
+        if not self.thread:
             return None
-        self.proc.terminate()
+        self.stop_evt.set()
+        self.thread.join(timeout=5)
         try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.fh.close()
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            with open(self.path, "w") as fh:
+                for sm, mx, pw, rs in self.rows:
+                    flags = ["Active" if rs & b else "Not Active" for b in self.BITS]
+                    fh.write(f"{self.device}, {sm}, {mx}, {pw:.2f}, 0x{rs:016x}, " + ", ".join(flags) + "\n")
+        except OSError:
+            pass
+        if not self.rows:
             return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = sorted({n for _, _, _, rs in self.rows for n, b in zip(self.NAMES, self.BITS) if rs & b})
+        return {"sm_mhz": float(np.median([r[0] for r in self.rows])), "sm_max_mhz": float(self.rows[0][1]),
+                "reasons": reasons, "samples": len(self.rows), "source": "NVML, 2 ms period"}
 
 
 def dist_setup(args):

@@ -438,18 +438,8 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterParams p) {
     }
 }
 
-// Publish "partial rows final" to every peer.
-__global__ void ep_done_kernel(EpPeers peers, EpLayout L, int rank, int world, const uint32_t *epoch) {
-    const int d = threadIdx.x;
-    if (d >= world) return;
-    __threadfence_system();
-    EpCtl *c = reinterpret_cast<EpCtl *>(peers.base[d] + L.ctl);
-    st_release_sys(&c->done_epoch[rank], *epoch);
-}
-
 // Combine: publish this rank's "partials final", wait until every peer has
-// published its own (bounded),
-// then out[t] += sum over the token's destinations d (ascending) of the
+// published its own (bounded), then out[t] += sum over the token's destinations d (ascending) of the
 // partial row d holds for it, clearing that row for the next epoch.  One CTA
 // per token.
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {

@@ -24,6 +24,10 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kStreamThreads = 32 + kConsumerThreads;
 constexpr int kGuRows = 32;    // gate rows and up rows per item: one Q8_1 middle block
 constexpr int kDnRows = 128;   // down rows per item
+constexpr int kGuWarpRows = kGuRows / kConsumerWarps;         // gate (and up) rows per consumer warp
+constexpr int kDnLaneRows = kDnRows / (8 * kConsumerWarps);   // down rows per consumer lane
+static_assert(kGuWarpRows >= 1 && kGuRows % kConsumerWarps == 0, "gate/up rows split evenly over warps");
+static_assert(kDnLaneRows >= 1 && kDnRows % (8 * kConsumerWarps) == 0, "down rows split evenly over lanes");
 constexpr int kMaxStages = 8;  // ring slots (two mbarriers each in the first 128 bytes)
 
 struct StreamParams {
@@ -109,8 +113,8 @@ __device__ __forceinline__ void init_ring(uint64_t *full, uint64_t *empty, int s
 }
 
 // ---- gate/up + SiLU*up + Q8_1 middle ---------------------------------------
-// Consumer warp cw owns gate rows and up rows 4cw..4cw+3 of the slab; lane l
-// owns blocks l, l+32, ...
+// Consumer warp cw owns gate rows and up rows R*cw .. R*cw+R-1 of the slab
+// (R = kGuWarpRows); lane l owns blocks l, l+32, ...
 template <int N>
 __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_t *st, const GuStage &L,
                                              const int4 *const *xr, const float2 *const *sr, int cw, int lane,
@@ -120,21 +124,22 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
     const uint4 *uc = reinterpret_cast<const uint4 *>(st + L.ucodes);
     const uint16_t *gs = reinterpret_cast<const uint16_t *>(st + L.gsc);
     const uint16_t *us = reinterpret_cast<const uint16_t *>(st + L.usc);
-    float acc[8][N];
+    constexpr int R = kGuWarpRows;
+    float acc[2 * R][N];
 #pragma unroll
-    for (int r = 0; r < 8; ++r)
+    for (int r = 0; r < 2 * R; ++r)
 #pragma unroll
         for (int j = 0; j < N; ++j) acc[r][j] = 0.0f;
     for (int b = lane; b < nb; b += 32) {
-        uint4 wc[8];
-        float d4[8];
+        uint4 wc[2 * R];
+        float d4[2 * R];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int blk = (cw * 4 + r) * nb + b;
+        for (int r = 0; r < R; ++r) {
+            const int blk = (cw * R + r) * nb + b;
             wc[r] = gc[blk];
-            wc[4 + r] = uc[blk];
+            wc[R + r] = uc[blk];
             d4[r] = h2f(gs[blk]);
-            d4[4 + r] = h2f(us[blk]);
+            d4[R + r] = h2f(us[blk]);
         }
 #pragma unroll
         for (int j = 0; j < N; ++j) {
@@ -142,30 +147,30 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
             const float2 sc = __ldg(sr[j] + b);
             const float s8x8 = 8.0f * sc.y;
 #pragma unroll
-            for (int r = 0; r < 8; ++r) acc[r][j] = block_term(block_dot2(wc[r], lo, hi), d4[r], sc.x, s8x8, acc[r][j]);
+            for (int r = 0; r < 2 * R; ++r) acc[r][j] = block_term(block_dot2(wc[r], lo, hi), d4[r], sc.x, s8x8, acc[r][j]);
         }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar);   // slab fully read by this warp
 #pragma unroll
-    for (int r = 0; r < 8; ++r)
+    for (int r = 0; r < 2 * R; ++r)
 #pragma unroll
         for (int j = 0; j < N; ++j) acc[r][j] = warp_sum(acc[r][j]);
     // SiLU(gate) * up with the reference's sanitisation (session_ops.hip:250-262):
-    // lane r < 4 finishes row 4cw + r.
-    if (lane < 4) {
+    // lane r < R finishes row R*cw + r.
+    if (lane < R) {
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-            float g = acc[0][j], u = acc[4][j];
+            float g = acc[0][j], u = acc[R][j];
 #pragma unroll
-            for (int r = 1; r < 4; ++r)
-                if (lane == r) { g = acc[r][j]; u = acc[4 + r][j]; }
+            for (int r = 1; r < R; ++r)
+                if (lane == r) { g = acc[r][j]; u = acc[R + r][j]; }
             int flags = 0;
             g = operand(g, flags);
             u = operand(u, flags);
             const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), flags);
             const float v = arithmetic(__fmul_rn(act, u), flags);
-            mid[j * 32 + cw * 4 + lane] = flags ? 0.0f : v;
+            mid[j * 32 + cw * R + lane] = flags ? 0.0f : v;
             report(flags, p.error);
         }
     }
@@ -248,9 +253,10 @@ stream_gate_up_kernel(StreamParams p) {
 }
 
 // ---- down + router-weighted scatter-add -------------------------------------
-// Consumer warp cw owns rows 16cw .. 16cw+15 of the 128-row slab: lane l takes
-// rows 16cw + l/4 and 16cw + 8 + l/4 and blocks l%4, l%4+4, ...; two shuffles
-// finish each row, then out[token][row] += weight * y (red.global.add).
+// Consumer warp cw owns rows 8R*cw .. 8R*cw+8R-1 of the 128-row slab (R =
+// kDnLaneRows): lane l takes rows 8R*cw + l/4 + 8k (k < R) and blocks l%4,
+// l%4+4, ...; two shuffles finish each row, then out[token][row] += weight * y
+// (red.global.add).
 template <int N>
 __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, int I, int H, int row0,
                                           int lr0, int q, uint64_t *empty_bar, int lane, float *out, int *error) {
@@ -260,26 +266,37 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
     const uint16_t *ds = reinterpret_cast<const uint16_t *>(st + L.dsc);
     const int4 *mc = reinterpret_cast<const int4 *>(st + L.mcodes);
     const float2 *ms = reinterpret_cast<const float2 *>(st + L.msc);
+    constexpr int R = kDnLaneRows;
     int tok[N];
-    float w[N], acc[2][N];
+    float w[N], acc[R][N];
 #pragma unroll
-    for (int j = 0; j < N; ++j) { tok[j] = meta.tok[j]; w[j] = meta.w[j]; acc[0][j] = 0.0f; acc[1][j] = 0.0f; }
+    for (int j = 0; j < N; ++j) {
+        tok[j] = meta.tok[j];
+        w[j] = meta.w[j];
+#pragma unroll
+        for (int k = 0; k < R; ++k) acc[k][j] = 0.0f;
+    }
     for (int b = q; b < nb; b += 4) {
-        const uint4 w0 = dc[lr0 * nb + b], w1 = dc[(lr0 + 8) * nb + b];
-        const float d0 = h2f(ds[lr0 * nb + b]), d1 = h2f(ds[(lr0 + 8) * nb + b]);
+        uint4 wk[R];
+        float dk[R];
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            wk[k] = dc[(lr0 + 8 * k) * nb + b];
+            dk[k] = h2f(ds[(lr0 + 8 * k) * nb + b]);
+        }
 #pragma unroll
         for (int j = 0; j < N; ++j) {
             const int4 xlo = mc[j * (I / 16) + 2 * b], xhi = mc[j * (I / 16) + 2 * b + 1];
             const float2 sc = ms[j * nb + b];
             const float s8x8 = 8.0f * sc.y;
-            acc[0][j] = block_term(block_dot2(w0, xlo, xhi), d0, sc.x, s8x8, acc[0][j]);
-            acc[1][j] = block_term(block_dot2(w1, xlo, xhi), d1, sc.x, s8x8, acc[1][j]);
+#pragma unroll
+            for (int k = 0; k < R; ++k) acc[k][j] = block_term(block_dot2(wk[k], xlo, xhi), dk[k], sc.x, s8x8, acc[k][j]);
         }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar);   // stage fully read by this warp
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
+    for (int k = 0; k < R; ++k)
 #pragma unroll
         for (int j = 0; j < N; ++j) {
             float v = acc[k][j];
@@ -355,7 +372,7 @@ stream_down_kernel(StreamParams p) {
     }
 
     const int cw = warp - 1, q = lane & 3;
-    const int lr0 = cw * (kDnRows / kConsumerWarps) + (lane >> 2);
+    const int lr0 = cw * 8 * kDnLaneRows + (lane >> 2);
     int i = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++i) {
         const int s = i % p.stages;
