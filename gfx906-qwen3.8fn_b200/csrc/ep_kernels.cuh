@@ -10,13 +10,15 @@
 //   3. dispatch: one warp per (token, destination) stores the token's Q8_1
 //      row, tensor-core block constants and its (local expert, weight) list
 //      straight into the destination's receive buffer (peer stores); the
-//      last CTA publishes, per destination, the slot count and the epoch;
+//      last CTA publishes, per destination, the slot count and the epoch
+//      (for T <= 32 the routing launch does steps 2-3 itself: its quantising
+//      CTAs store every row into every rank at slot source * T_max + t);
 //   4. every rank waits for all P epochs, groups its received slots by local
 //      expert (the single-GPU grouping kernels over slot masks) and runs the
 //      expert kernels, accumulating each slot's weighted expert outputs into
 //      its local partial buffer;
-//   5. it publishes "done" to every peer; after all peers are done, each rank
-//      pulls, for each of its tokens, the partial rows from the destinations
+//   5. the combine launch publishes "done" to every peer; after all peers are
+//      done, each rank pulls, for each of its tokens, the partial rows from the destinations
 //      it used (peer loads, destinations in ascending order) and adds them
 //      into its residual.
 // Receive regions are fixed per source (slot = source * T_max + index), so no
@@ -445,6 +447,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterParams p) {
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
     __shared__ int ready;
     const int t = blockIdx.x;
+    grid_launch_dependents();   // the next layer's routing CTAs may become resident and wait
     // This rank's partial rows are final (the expert kernels before this launch
     // completed): CTA 0 publishes that to every peer first.
     if (t == 0 && threadIdx.x < p.world) {

@@ -313,8 +313,7 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
         }
         // block 0 routes; the others quantise x (one warp per 32-value block)
         const int qblocks = sr.xq.codes ? (T * (h->desc.hidden / 32) + 15) / 16 : 0;
-        route_small_kernel<<<1 + qblocks, 512, 0, s>>>(sr);
-        return cuda_status(cudaGetLastError(), "route_small_kernel");
+        return cuda_status(launch_overlapped(route_small_kernel, 1 + qblocks, 512, 0, s, sr), "route_small_kernel");
     }
     route_topk_kernel<<<chunks, kRouteThreads, 0, s>>>(rp);
     MOE_CUDA(cudaGetLastError());

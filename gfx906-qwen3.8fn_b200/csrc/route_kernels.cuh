@@ -462,6 +462,12 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
     __shared__ uint32_t smask[kRouterExperts];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, e = threadIdx.x;
     const int T = p.tokens, H = p.hidden;
+    // Launched with programmatic serialisation: the CTAs may be resident
+    // before the preceding kernel (which may still read this layer's tile list
+    // and activation buffers) has finished; wait for it.  No early trigger: expert
+    // CTAs made resident while routing runs measured slower than a launch at
+    // its end.
+    grid_dependency_wait();
     if (blockIdx.x > 0) {
         // blocks 1.. quantise x, one warp per 32-value block, alongside the routing block
         const int stride = (gridDim.x - 1) * 16, nb = H / 32;

@@ -322,6 +322,7 @@ stream_down_kernel(StreamParams p) {
     uint8_t *stages = smem + 128;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     init_ring(full, empty, p.stages);
+    grid_launch_dependents();   // the next layer's routing CTAs may take the SMs' spare room and wait
     const int total = *p.num_tiles * slabs;
 
     if (warp == 0) {
