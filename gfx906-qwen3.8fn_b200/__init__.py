@@ -149,14 +149,36 @@ def make_desc(hidden=HIDDEN, inter=INTER, experts=EXPERTS, top_k=TOP_K, has_shar
     return desc_t(hidden, inter, experts, top_k, has_shared, device, max_tokens)
 
 
-class MoeWeights:
+class _Owned:
+    """Owner of one library handle, released exactly once by close() or by the
+    garbage collector (also during interpreter shutdown, when module globals
+    may already be gone: the destroy entry point is bound at creation)."""
+
+    _destroy_name = ""
+    handle = None
+
+    def _own(self, h):
+        self._destroy = getattr(library(), self._destroy_name)
+        self.handle = h
+
+    def close(self):
+        h, self.handle = self.handle, None
+        if h:
+            self._destroy(h)
+
+    __del__ = close
+
+
+class MoeWeights(_Owned):
     """Device-resident Q4_0 experts of one layer (routed + shared)."""
+
+    _destroy_name = "moe_weights_destroy"
 
     def __init__(self, desc):
         self.desc = desc
         h = P()
         check(library().moe_weights_create(ctypes.byref(desc), ctypes.byref(h)))
-        self.handle = h
+        self._own(h)
 
     def synthesize(self, seed, layer=0, stream=None):
         check(library().moe_weights_synthesize(self.handle, seed, layer, _stream(stream)))
@@ -177,22 +199,18 @@ class MoeWeights:
                                                     _stream(stream)))
         return g, u, w
 
-    def close(self):
-        if getattr(self, "handle", None):
-            library().moe_weights_destroy(self.handle)
-            self.handle = None
-
-    __del__ = close
 
 
-class MoeLayer:
+class MoeLayer(_Owned):
     """Workspace of one routed-MoE FFN layer; `forward` is the whole hot path."""
+
+    _destroy_name = "moe_layer_destroy"
 
     def __init__(self, desc):
         self.desc = desc
         h = P()
         check(library().moe_layer_create(ctypes.byref(desc), ctypes.byref(h)))
-        self.handle = h
+        self._own(h)
 
     def forward(self, weights, x, logits, out, accumulate=True, stream=None):
         """out (+)= MoE(x).  x, out: fp32 cuda [T][H]; logits fp32 cuda [T][E]."""
@@ -229,12 +247,6 @@ class MoeLayer:
         check(library().moe_layer_read_flags(self.handle, ctypes.byref(f), int(clear), _stream(stream)))
         return f.value
 
-    def close(self):
-        if getattr(self, "handle", None):
-            library().moe_layer_destroy(self.handle)
-            self.handle = None
-
-    __del__ = close
 
 
 EP_HANDLE_BYTES = 64
@@ -249,21 +261,23 @@ class EpWeights(MoeWeights):
         self.rank, self.world = rank, world
         h = P()
         check(library().moe_ep_weights_create(ctypes.byref(desc), rank, world, ctypes.byref(h)))
-        self.handle = h
+        self._own(h)
 
 
-class EpLayer:
+class EpLayer(_Owned):
     """One rank of the expert-parallel layer (one process per GPU).
 
     Peer buffers are mapped with CUDA IPC; `connect(exchange)` takes a
     function that all-gathers one bytes object per rank (for example
     `exchange_handles` over a torch.distributed group)."""
 
+    _destroy_name = "moe_ep_destroy"
+
     def __init__(self, desc, rank, world):
         self.desc, self.rank, self.world = desc, rank, world
         h = P()
         check(library().moe_ep_create(ctypes.byref(desc), rank, world, ctypes.byref(h)))
-        self.handle = h
+        self._own(h)
 
     def ipc_handle(self):
         buf = ctypes.create_string_buffer(EP_HANDLE_BYTES)
@@ -290,12 +304,6 @@ class EpLayer:
         check(library().moe_ep_read_flags(self.handle, ctypes.byref(f), int(clear), _stream(stream)))
         return f.value
 
-    def close(self):
-        if getattr(self, "handle", None):
-            library().moe_ep_destroy(self.handle)
-            self.handle = None
-
-    __del__ = close
 
 
 def exchange_handles(handle, group=None):
@@ -350,16 +358,17 @@ def q4_linear(w_q4_0, rows, k, xq, columns, with_dots=False, stream=None):
     return (out, dots) if with_dots else out
 
 
-class RouteGroups:
+class RouteGroups(_Owned):
     """Host route grouping with the reference's contract (src/routes.hpp:28-65)."""
 
     CHUNK1024, LAYERWISE16384 = 0, 1
+    _destroy_name = "moe_route_groups_destroy"
 
     def __init__(self, token_capacity, bound=CHUNK1024):
         h = P()
         L = library()
         check(L.moe_route_groups_create(token_capacity, bound, ctypes.byref(h)), L.moe_route_groups_message)
-        self.handle = h
+        self._own(h)
         self.capacity = token_capacity
 
     def prepare(self, ids, weights, tokens):
@@ -394,22 +403,19 @@ class RouteGroups:
         start = int(c[:expert].sum())
         return a[start:start + int(c[expert])]
 
-    def close(self):
-        if getattr(self, "handle", None):
-            library().moe_route_groups_destroy(self.handle)
-            self.handle = None
-
-    __del__ = close
 
 
-class GpuExpert:
+class GpuExpert(_Owned):
     """Single resident expert (src/gpu_expert.hpp:7-21) on the sm_100a kernels."""
+
+    _destroy_name = "moe_expert_destroy"
 
     def __init__(self, gate, up, down, device=0, max_columns=8, hidden=HIDDEN, inter=INTER):
         h = P()
         check(library().moe_expert_create(_ptr(gate), _ptr(up), _ptr(down), hidden, inter, device, max_columns,
                                           ctypes.byref(h)))
-        self.handle, self.hidden, self.inter = h, hidden, inter
+        self._own(h)
+        self.hidden, self.inter = hidden, inter
 
     def check_quantization(self, x, expected_q8):
         import numpy as np
@@ -436,9 +442,3 @@ class GpuExpert:
         check(library().moe_expert_run(self.handle, _ptr(x), columns, _ptr(out), repeats, *map(ctypes.byref, t)))
         return out, dict(upload_ms=t[0].value, resident_ms=t[1].value, completed_wall_ms=t[2].value)
 
-    def close(self):
-        if getattr(self, "handle", None):
-            library().moe_expert_destroy(self.handle)
-            self.handle = None
-
-    __del__ = close

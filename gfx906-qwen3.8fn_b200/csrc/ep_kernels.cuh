@@ -287,9 +287,12 @@ struct EpSmallGroupParams {
     int max_tiles;
     int *error;
 };
-constexpr int kEpSmallSlots = 512;
+constexpr int kEpSmallSlots = 256;   // world <= 8 ranks x T_max <= 32
 __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams g) {
     __shared__ uint32_t smask[kEpSmallSlots / kChunk][kRouterExperts];
+    __shared__ int16_t sid[kEpSmallSlots * kEpSlotIds];   // received (local expert) lists, -1 = none
+    __shared__ float sw[kEpSmallSlots * kEpSlotIds];
+    __shared__ int scount[kEpMaxRanks];
     __shared__ int failed;
     const int e = threadIdx.x, lane = e & 31;
     const EpCtl *c = reinterpret_cast<const EpCtl *>(g.arena + g.L.ctl);
@@ -298,7 +301,8 @@ __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams 
         if (e < g.world) {
             const uint32_t want = *g.epoch;
             const long long t0 = clock64();
-            while (static_cast<uint32_t>(ld_acquire_sys64(&c->recv[e])) != want) {
+            uint64_t v;
+            while (static_cast<uint32_t>(v = ld_acquire_sys64(&c->recv[e])) != want) {
                 if (clock64() - t0 > (1ll << 31)) {
                     atomicOr(g.error, kFlagTimeout);
                     ok = false;
@@ -306,6 +310,7 @@ __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams 
                 }
                 __nanosleep(64);
             }
+            scount[e] = static_cast<int>(v >> 32);
         }
         ok = __all_sync(0xffffffffu, ok);
         if (e == 0) failed = !ok;
@@ -317,13 +322,17 @@ __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams 
         if (e == 0) *g.num_tiles = 0;
         return;
     }
+    // one pass over the received lists (independent loads), into shared memory
     const int32_t *ids = reinterpret_cast<const int32_t *>(g.arena + g.L.ids);
     const float *ws = reinterpret_cast<const float *>(g.arena + g.L.w);
     for (int i = e; i < g.slots * kEpSlotIds; i += blockDim.x) {
         const int slot = i / kEpSlotIds;
-        if (!ep_slot_valid(c, slot, g.t_max)) continue;
-        const int id = ids[i];
-        if (id >= 0 && id < kRouterExperts) atomicOr(&smask[slot / kChunk][id], 1u << (slot % kChunk));
+        const bool valid = slot % g.t_max < scount[slot / g.t_max];
+        const int id = valid ? ids[i] : -1;
+        const bool live = id >= 0 && id < kRouterExperts;
+        sid[i] = static_cast<int16_t>(live ? id : -1);
+        sw[i] = live ? ws[i] : 0.0f;
+        if (live) atomicOr(&smask[slot / kChunk][id], 1u << (slot % kChunk));
     }
     __syncthreads();
     int count = 0;
@@ -345,8 +354,8 @@ __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams 
             int r = 0;
 #pragma unroll
             for (int q = 0; q < kEpSlotIds; ++q)
-                if (ids[slot * kEpSlotIds + q] == e) r = q;
-            const float w = ws[slot * kEpSlotIds + r];
+                if (sid[slot * kEpSlotIds + q] == e) r = q;
+            const float w = sw[slot * kEpSlotIds + r];
             const int pair = off + pos;
             g.pair_token[pair] = slot;
             if (g.pair_rank) g.pair_rank[pair] = r;
@@ -443,8 +452,10 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterParams p) {
 // Combine: publish this rank's "partials final", wait until every peer has
 // published its own (bounded), then out[t] += sum over the token's destinations d (ascending) of the
 // partial row d holds for it, clearing that row for the next epoch.  One CTA
-// per token.
-__global__ void __launch_bounds__(256) ep_combine_kernel(EpParams p) {
+// per token, one float4 column per thread for H <= 4 * kEpCombineThreads, so
+// every peer load of the token is in flight at once (one NVLink round trip).
+constexpr int kEpCombineThreads = 512;
+__global__ void __launch_bounds__(kEpCombineThreads) ep_combine_kernel(EpParams p) {
     __shared__ int ready;
     const int t = blockIdx.x;
     grid_launch_dependents();   // the next layer's routing CTAs may become resident and wait

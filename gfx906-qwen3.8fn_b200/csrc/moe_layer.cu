@@ -1322,7 +1322,8 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
     if (const int st = launch_experts(&r, w, partial, r.tiles_max, s, nullptr, tc_tiles)) return st;
     // 5. the combine publishes "done", waits for every peer's, then pulls the partial rows
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
-    ep_combine_kernel<<<tokens, 256, 0, s>>>(p);
+    const int cthreads = std::min(kEpCombineThreads, std::max(32, (H / 4 + 31) / 32 * 32));
+    ep_combine_kernel<<<tokens, cthreads, 0, s>>>(p);
     return cuda_status(cudaGetLastError(), "ep_combine_kernel");
 }
 
