@@ -78,6 +78,40 @@ __device__ __forceinline__ float block_term(int dot, float d4, float d8, float s
     return fmaf(d4, fmaf(small_int_to_float(dot), d8, -s8x8), acc);
 }
 
+// Packed pairs of fp32 (Blackwell f32x2 arithmetic), low word = first element.
+__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t pkf2(float lo, float hi) { return pk2(__float_as_uint(lo), __float_as_uint(hi)); }
+__device__ __forceinline__ void upk2(uint64_t v, float &lo, float &hi) {
+    uint32_t a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+    lo = __uint_as_float(a);
+    hi = __uint_as_float(b);
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// block_term for two weight rows against the same activation block, as
+// packed f32x2 operations with the scalar form's per-element rounding (the
+// results are bit-identical to two block_term calls).
+__device__ __forceinline__ uint64_t block_term2(int dot0, int dot1, uint64_t d4, uint64_t d8, uint64_t neg_s8x8,
+                                                uint64_t acc) {
+    const uint64_t bias = pkf2(-12582912.0f, -12582912.0f);
+    const uint64_t f = add2(pk2(static_cast<uint32_t>(dot0 + 0x4b400000), static_cast<uint32_t>(dot1 + 0x4b400000)),
+                            bias);
+    return fma2(d4, fma2(f, d8, neg_s8x8), acc);
+}
+
 // Block dot as two independent dp4a chains.  High nibbles are masked in place
 // (byte values 16*q) and the chain is shifted once: each partial is a multiple
 // of 16 and |partial| <= 16*240*128 < 2^31, so the result equals block_dot.

@@ -283,7 +283,7 @@ struct EpSmallGroupParams {
     int32_t *pair_rank;
     float *pair_weight;
     TileRec *tiles;
-    int *num_tiles;
+    int *num_tiles;           // [0] tiles, [1] shared-expert tiles at the end of the list
     int max_tiles;
     int *error;
 };
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams 
     for (int k = 0; k < chunks; ++k) smask[k][e] = 0u;
     __syncthreads();
     if (failed) {
-        if (e == 0) *g.num_tiles = 0;
+        if (e == 0) { g.num_tiles[0] = 0; g.num_tiles[1] = 0; }
         return;
     }
     // one pass over the received lists (independent loads), into shared memory
@@ -397,7 +397,8 @@ __global__ void __launch_bounds__(512) ep_group_small_kernel(EpSmallGroupParams 
     if (e == 0) {
         int n = tiles_total + shared_tiles;
         if (n > g.max_tiles) { atomicOr(g.error, kFlagArithmetic); n = g.max_tiles; }
-        *g.num_tiles = n;
+        g.num_tiles[0] = n;
+        g.num_tiles[1] = max(0, n - tiles_total);
     }
     (void)lane;
 }

@@ -522,7 +522,7 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
         h->pair_weight = a.take<float>(h->pairs_max);
         h->tiles = a.take<TileRec>(h->tiles_max);
         h->tile_off = a.take<int32_t>(kRouterExperts);
-        h->num_tiles = a.take<int>(1);
+        h->num_tiles = a.take<int>(2);   // [0] work tiles, [1] shared-expert tiles at the end
         h->error = a.take<int>(1);
         tc_workspace_take(h->tc, a, T, H, I, T > kChunk);
         if (pass == 0) {
@@ -841,7 +841,7 @@ constexpr NoAllocLayout noalloc_layout() {
     L.pair_weight = at;  at = align256(at + sizeof(float) * kNoAllocMaxTokens * kTopK);
     L.tiles = at;        at = align256(at + sizeof(TileRec) * kNoAllocTiles);
     L.tile_off = at;     at = align256(at + sizeof(int32_t) * kRouterExperts);
-    L.num_tiles = at;    at = align256(at + sizeof(int));
+    L.num_tiles = at;    at = align256(at + 2 * sizeof(int));
     L.bytes = at;
     return L;
 }
@@ -1005,7 +1005,7 @@ void ep_take_rx(moe_ep_s *ep, Arena &a) {
     r.pair_weight = a.take<float>(pairs);
     r.tiles = a.take<TileRec>(ep->rx_tiles);
     r.tile_off = a.take<int32_t>(kRouterExperts);
-    r.num_tiles = a.take<int>(1);
+    r.num_tiles = a.take<int>(2);
     r.error = a.take<int>(1);
     r.tc.max_tiles = pairs / kTcM + kRouterExperts + 2 + ep->t_max / kTcM;
     r.tc.tiles = a.take<int4>(r.tc.max_tiles);

@@ -278,7 +278,7 @@ struct ScanParams {
     int32_t *tile_off;      // [512]: first tile of each routed expert
     int32_t *pair_token;    // shared-expert pairs (written by route_topk at tokens*10 + t,
     float *pair_weight;     // or here at offsets[512] + t when shared_w is given)
-    int *num_tiles;
+    int *num_tiles;         // [0] tiles, [1] how many of them (at the end) are shared-expert tiles
     int max_tiles;
     int *error;
     // Groups of at least tc_min pairs (0: never) go to the tensor-core path
@@ -362,7 +362,8 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
     if (e == 0) {
         int n = tiles_total + shared_tiles;
         if (n > p.max_tiles) { atomicOr(p.error, kFlagArithmetic); n = p.max_tiles; }
-        *p.num_tiles = n;
+        p.num_tiles[0] = n;
+        p.num_tiles[1] = max(0, n - tiles_total);
         if (p.tc_num) {
             int m = tc_total + shared_tc;
             if (m > p.tc_max) { atomicOr(p.error, kFlagArithmetic); m = p.tc_max; }
@@ -433,7 +434,10 @@ __global__ void identity_route_kernel(int tokens, int tile, TileRec *tiles, int 
             for (int j = r.n; j < tile; ++j) { r.tok[j] = 0; r.w[j] = 0.0f; }
         }
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) *num_tiles = (tokens + tile - 1) / tile;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        num_tiles[0] = (tokens + tile - 1) / tile;
+        num_tiles[1] = 0;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -453,7 +457,7 @@ struct SmallRouteParams {
     int32_t *offsets;       // [514]
     TileRec *tiles;
     int32_t *tile_off;
-    int *num_tiles;
+    int *num_tiles;         // [0] tiles, [1] how many of them (at the end) are shared-expert tiles
     int max_tiles;
 };
 
@@ -600,7 +604,8 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
     if (e == 0) {
         int n = tiles_total + shared_tiles;
         if (n > sp.max_tiles) { atomicOr(p.error, kFlagArithmetic); n = sp.max_tiles; }
-        *sp.num_tiles = n;
+        sp.num_tiles[0] = n;
+        sp.num_tiles[1] = max(0, n - tiles_total);
     }
 }
 

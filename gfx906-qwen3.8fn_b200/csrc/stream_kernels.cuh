@@ -35,7 +35,7 @@ struct StreamParams {
     ExpertLayout layout;
     Q8Planar x, mid;
     const TileRec *tiles;
-    const int *num_tiles;
+    const int *num_tiles;   // [0] tiles, [1] shared-expert tiles at the end of the list
     float *out;
     int *error;
     int stages;
@@ -71,6 +71,30 @@ struct DnStage {
     }
 };
 
+// Order of the work items.  CTA c takes positions c, c + G, c + 2G, ... (G =
+// gridDim.x), so with r = total % G the CTAs c >= r get one item fewer.  The
+// shared-expert items (the list's last S items, all tokens: the most dot
+// products per weight byte) are placed at positions r .. r+S-1, i.e. on those
+// CTAs, instead of on the CTAs that already have the extra item.  The map is a
+// bijection of [0, total) for any S.
+struct ItemOrder {
+    int total, heavy_at, heavy_n;
+    __device__ __forceinline__ int operator()(int pos) const {
+        if (pos < heavy_at) return pos;
+        if (pos < heavy_at + heavy_n) return total - heavy_n + (pos - heavy_at);
+        return pos - heavy_n;
+    }
+};
+
+__device__ __forceinline__ ItemOrder item_order(const int *num_tiles, int slabs) {
+    const int2 nt = *reinterpret_cast<const int2 *>(num_tiles);
+    ItemOrder o;
+    o.total = nt.x * slabs;
+    o.heavy_n = min(max(nt.y, 0), nt.x) * slabs;
+    o.heavy_at = min(o.total % static_cast<int>(gridDim.x), o.total - o.heavy_n);
+    return o;
+}
+
 __device__ __forceinline__ TileRec load_tile(const TileRec *t) {
     TileRec r;
     const int4 *s = reinterpret_cast<const int4 *>(t);
@@ -84,15 +108,17 @@ __device__ __forceinline__ TileRec load_tile(const TileRec *t) {
 // the byte count and enqueues the bulk copies of one item.
 template <class Issue>
 __device__ __forceinline__ void stream_producer(const StreamParams &p, uint8_t *stages, uint64_t *full,
-                                                uint64_t *empty, int total, int slabs, Issue issue) {
+                                                uint64_t *empty, const ItemOrder &order, int slabs, Issue issue) {
+    const int total = order.total;
     int i = 0;
-    int item = blockIdx.x;
+    int pos = blockIdx.x;
     TileRec next;
-    if (item < total) next = load_tile(p.tiles + item / slabs);
-    for (; item < total; item += gridDim.x, ++i) {
+    if (pos < total) next = load_tile(p.tiles + order(pos) / slabs);
+    for (; pos < total; pos += gridDim.x, ++i) {
+        const int item = order(pos);
         const TileRec rec = next;
-        const int following = item + gridDim.x;
-        if (following < total) next = load_tile(p.tiles + following / slabs);
+        const int following = pos + gridDim.x;
+        if (following < total) next = load_tile(p.tiles + order(following) / slabs);
         const int s = i % p.stages;
         if (i >= p.stages && !mbar_wait(&empty[s], ((i / p.stages) & 1) ^ 1, p.error)) break;
         uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
@@ -125,11 +151,12 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
     const uint16_t *gs = reinterpret_cast<const uint16_t *>(st + L.gsc);
     const uint16_t *us = reinterpret_cast<const uint16_t *>(st + L.usc);
     constexpr int R = kGuWarpRows;
-    float acc[2 * R][N];
+    // accumulators of rows (2q, 2q+1) packed as f32x2; rows 0..R-1 gate, R..2R-1 up
+    uint64_t acc2[R][N];
 #pragma unroll
-    for (int r = 0; r < 2 * R; ++r)
+    for (int q = 0; q < R; ++q)
 #pragma unroll
-        for (int j = 0; j < N; ++j) acc[r][j] = 0.0f;
+        for (int j = 0; j < N; ++j) acc2[q][j] = 0ull;
     for (int b = lane; b < nb; b += 32) {
         uint4 wc[2 * R];
         float d4[2 * R];
@@ -141,17 +168,28 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
             d4[r] = h2f(gs[blk]);
             d4[R + r] = h2f(us[blk]);
         }
+        uint64_t d4p[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) d4p[q] = pkf2(d4[2 * q], d4[2 * q + 1]);
 #pragma unroll
         for (int j = 0; j < N; ++j) {
             const int4 lo = __ldg(xr[j] + 2 * b), hi = __ldg(xr[j] + 2 * b + 1);
             const float2 sc = __ldg(sr[j] + b);
-            const float s8x8 = 8.0f * sc.y;
+            const float ns = -(8.0f * sc.y);
+            const uint64_t d8 = pkf2(sc.x, sc.x), nsp = pkf2(ns, ns);
 #pragma unroll
-            for (int r = 0; r < 2 * R; ++r) acc[r][j] = block_term(block_dot2(wc[r], lo, hi), d4[r], sc.x, s8x8, acc[r][j]);
+            for (int q = 0; q < R; ++q)
+                acc2[q][j] = block_term2(block_dot2(wc[2 * q], lo, hi), block_dot2(wc[2 * q + 1], lo, hi), d4p[q], d8,
+                                         nsp, acc2[q][j]);
         }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar);   // slab fully read by this warp
+    float acc[2 * R][N];
+#pragma unroll
+    for (int q = 0; q < R; ++q)
+#pragma unroll
+        for (int j = 0; j < N; ++j) upk2(acc2[q][j], acc[2 * q][j], acc[2 * q + 1][j]);
 #pragma unroll
     for (int r = 0; r < 2 * R; ++r)
 #pragma unroll
@@ -189,11 +227,11 @@ stream_gate_up_kernel(StreamParams p) {
     init_ring(full, empty, p.stages);
     grid_dependency_wait();     // tile list and x codes of the routing kernels
     grid_launch_dependents();   // the down kernel may take SMs as this grid's CTAs finish
-    const int total = *p.num_tiles * slabs;
+    const ItemOrder order = item_order(p.num_tiles, slabs);
 
     if (warp == 0) {
         if (lane != 0) return;
-        stream_producer(p, stages, full, empty, total, slabs,
+        stream_producer(p, stages, full, empty, order, slabs,
                         [&](int item, uint8_t *st, uint64_t *bar, const TileRec &rec) {
             const int slab = item % slabs;
             const uint8_t *ex = p.weights + static_cast<size_t>(rec.e) * p.layout.bytes;
@@ -210,7 +248,8 @@ stream_gate_up_kernel(StreamParams p) {
     const int cw = warp - 1;
     bool failed = false;
     int i = 0;
-    for (int item = blockIdx.x; item < total; item += gridDim.x, ++i) {
+    for (int pos = blockIdx.x; pos < order.total; pos += gridDim.x, ++i) {
+        const int item = order(pos);
         const TileRec rec = load_tile(p.tiles + item / slabs);
         const int n = rec.n < kGemvTile ? rec.n : kGemvTile;
         const int4 *xr[kGemvTile];
@@ -267,34 +306,44 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
     const int4 *mc = reinterpret_cast<const int4 *>(st + L.mcodes);
     const float2 *ms = reinterpret_cast<const float2 *>(st + L.msc);
     constexpr int R = kDnLaneRows;
+    static_assert(R % 2 == 0, "down rows are accumulated in f32x2 pairs");
     int tok[N];
-    float w[N], acc[R][N];
+    float w[N];
+    uint64_t acc2[R / 2][N];   // rows (lr0 + 16p, lr0 + 16p + 8) packed as f32x2
 #pragma unroll
     for (int j = 0; j < N; ++j) {
         tok[j] = meta.tok[j];
         w[j] = meta.w[j];
 #pragma unroll
-        for (int k = 0; k < R; ++k) acc[k][j] = 0.0f;
+        for (int k = 0; k < R / 2; ++k) acc2[k][j] = 0ull;
     }
     for (int b = q; b < nb; b += 4) {
         uint4 wk[R];
-        float dk[R];
+        uint64_t dk[R / 2];
 #pragma unroll
-        for (int k = 0; k < R; ++k) {
-            wk[k] = dc[(lr0 + 8 * k) * nb + b];
-            dk[k] = h2f(ds[(lr0 + 8 * k) * nb + b]);
-        }
+        for (int k = 0; k < R; ++k) wk[k] = dc[(lr0 + 8 * k) * nb + b];
+#pragma unroll
+        for (int k = 0; k < R / 2; ++k)
+            dk[k] = pkf2(h2f(ds[(lr0 + 16 * k) * nb + b]), h2f(ds[(lr0 + 16 * k + 8) * nb + b]));
 #pragma unroll
         for (int j = 0; j < N; ++j) {
             const int4 xlo = mc[j * (I / 16) + 2 * b], xhi = mc[j * (I / 16) + 2 * b + 1];
             const float2 sc = ms[j * nb + b];
-            const float s8x8 = 8.0f * sc.y;
+            const float ns = -(8.0f * sc.y);
+            const uint64_t d8 = pkf2(sc.x, sc.x), nsp = pkf2(ns, ns);
 #pragma unroll
-            for (int k = 0; k < R; ++k) acc[k][j] = block_term(block_dot2(wk[k], xlo, xhi), dk[k], sc.x, s8x8, acc[k][j]);
+            for (int k = 0; k < R / 2; ++k)
+                acc2[k][j] = block_term2(block_dot2(wk[2 * k], xlo, xhi), block_dot2(wk[2 * k + 1], xlo, xhi), dk[k],
+                                         d8, nsp, acc2[k][j]);
         }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar);   // stage fully read by this warp
+    float acc[R][N];
+#pragma unroll
+    for (int k = 0; k < R / 2; ++k)
+#pragma unroll
+        for (int j = 0; j < N; ++j) upk2(acc2[k][j], acc[2 * k][j], acc[2 * k + 1][j]);
 #pragma unroll
     for (int k = 0; k < R; ++k)
 #pragma unroll
@@ -323,7 +372,7 @@ stream_down_kernel(StreamParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     init_ring(full, empty, p.stages);
     grid_launch_dependents();   // the next layer's routing CTAs may take the SMs' spare room and wait
-    const int total = *p.num_tiles * slabs;
+    const ItemOrder order = item_order(p.num_tiles, slabs);
 
     if (warp == 0) {
         // Producer.  The tile list comes from the routing kernels, which
@@ -347,7 +396,8 @@ stream_down_kernel(StreamParams p) {
                 issue_mid(st, &full[k % p.stages], *reinterpret_cast<const TileRec *>(st));
             }
         };
-        for (int item = blockIdx.x; item < total; item += gridDim.x, ++i) {
+        for (int pos = blockIdx.x; pos < order.total; pos += gridDim.x, ++i) {
+            const int item = order(pos);
             const TileRec rec = load_tile(p.tiles + item / slabs);
             const int s = i % p.stages;
             if (i >= p.stages) {
@@ -375,7 +425,8 @@ stream_down_kernel(StreamParams p) {
     const int cw = warp - 1, q = lane & 3;
     const int lr0 = cw * 8 * kDnLaneRows + (lane >> 2);
     int i = 0;
-    for (int item = blockIdx.x; item < total; item += gridDim.x, ++i) {
+    for (int pos = blockIdx.x; pos < order.total; pos += gridDim.x, ++i) {
+        const int item = order(pos);
         const int s = i % p.stages;
         if (!mbar_wait(&full[s], (i / p.stages) & 1, p.error)) break;
         const uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;

@@ -165,29 +165,6 @@ __device__ __forceinline__ void unpack_centred(const uint4 w, uint4 &lo, uint4 &
     hi = make_uint4(c(w.x >> 4), c(w.y >> 4), c(w.z >> 4), c(w.w >> 4));
 }
 
-// Packed pairs of fp32 (Blackwell f32x2 arithmetic), low word = first element.
-__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-    return r;
-}
-__device__ __forceinline__ uint64_t pkf2(float lo, float hi) { return pk2(__float_as_uint(lo), __float_as_uint(hi)); }
-__device__ __forceinline__ void upk2(uint64_t v, float &lo, float &hi) {
-    uint32_t a, b;
-    asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
-    lo = __uint_as_float(a);
-    hi = __uint_as_float(b);
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
 // Two 16-bit two's-complement dots (low half first) -> the fp32 pair
 // (kTcUnbias + v): the bit pattern 0x4b400000 + (v + 2^15) is the float
 // 1.5*2^23 + 2^15 + v exactly for |v| < 2^15.
