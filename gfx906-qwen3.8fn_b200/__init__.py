@@ -24,6 +24,7 @@ LIB_PATH = os.path.join(HERE, "libqwen_moe_b200.so")
 MOE_OK, MOE_INVALID_ARGUMENT, MOE_NOT_SUPPORTED, MOE_CUDA_ERROR = 0, 1, 2, 3
 MOE_NUMERIC_ERROR, MOE_NCCL_ERROR, MOE_TIMEOUT, MOE_OUT_OF_MEMORY = 4, 5, 6, 7
 MOE_OUT_ACCUMULATE, MOE_OUT_OVERWRITE = 0, 1
+MOE_Q4_0, MOE_Q4_1 = 2, 3      # the reference's TensorType values (src/model.hpp:17-19)
 HIDDEN, INTER, EXPERTS, TOP_K = 2048, 512, 512, 10
 
 EXPORTED = [
@@ -38,6 +39,7 @@ EXPORTED = [
     "moe_route_groups_assignments", "moe_route_groups_counts", "moe_route_groups_message",
     "moe_route_noalloc", "moe_ep_weights_create", "moe_ep_create", "moe_ep_destroy", "moe_ep_ipc_handle",
     "moe_ep_open_peers", "moe_ep_forward", "moe_ep_read_flags",
+    "moe_weights_create_typed", "moe_ep_weights_create_typed", "moe_q4_1_linear", "moe_expert_create_typed",
 ]
 
 
@@ -102,6 +104,10 @@ def library(path=LIB_PATH):
         "moe_route_groups_counts": (I, [P, P]),
         "moe_route_groups_message": (ctypes.c_char_p, []),
         "moe_ep_weights_create": (I, [DESC_P, I, I, ctypes.POINTER(P)]),
+        "moe_ep_weights_create_typed": (I, [DESC_P, I, I, I, ctypes.POINTER(P)]),
+        "moe_weights_create_typed": (I, [DESC_P, I, ctypes.POINTER(P)]),
+        "moe_q4_1_linear": (I, [P, I, I, P, I, P, P, P]),
+        "moe_expert_create_typed": (I, [P, P, P, I, I, I, I, I, ctypes.POINTER(P)]),
         "moe_ep_create": (I, [DESC_P, I, I, ctypes.POINTER(P)]),
         "moe_ep_destroy": (I, [P]),
         "moe_ep_ipc_handle": (I, [P, P]),
@@ -174,10 +180,10 @@ class MoeWeights(_Owned):
 
     _destroy_name = "moe_weights_destroy"
 
-    def __init__(self, desc):
-        self.desc = desc
+    def __init__(self, desc, down_type=MOE_Q4_0):
+        self.desc, self.down_type = desc, down_type
         h = P()
-        check(library().moe_weights_create(ctypes.byref(desc), ctypes.byref(h)))
+        check(library().moe_weights_create_typed(ctypes.byref(desc), down_type, ctypes.byref(h)))
         self._own(h)
 
     def synthesize(self, seed, layer=0, stream=None):
@@ -193,8 +199,9 @@ class MoeWeights(_Owned):
     def download_expert(self, expert, stream=None):
         import numpy as np
         d = self.desc
-        n = d.hidden * d.inter // 32 * 18
-        g, u, w = (np.empty(n, np.uint8) for _ in range(3))
+        blocks = d.hidden * d.inter // 32
+        g, u = (np.empty(blocks * 18, np.uint8) for _ in range(2))
+        w = np.empty(blocks * (20 if self.down_type == MOE_Q4_1 else 18), np.uint8)
         check(library().moe_weights_download_expert(self.handle, expert, _ptr(g), _ptr(u), _ptr(w),
                                                     _stream(stream)))
         return g, u, w
@@ -256,11 +263,11 @@ class EpWeights(MoeWeights):
     """Expert shard of rank `rank` of `world`: routed experts
     [rank*512/world, (rank+1)*512/world) as local 0.., then the shared expert."""
 
-    def __init__(self, desc, rank, world):
-        self.desc = desc
+    def __init__(self, desc, rank, world, down_type=MOE_Q4_0):
+        self.desc, self.down_type = desc, down_type
         self.rank, self.world = rank, world
         h = P()
-        check(library().moe_ep_weights_create(ctypes.byref(desc), rank, world, ctypes.byref(h)))
+        check(library().moe_ep_weights_create_typed(ctypes.byref(desc), rank, world, down_type, ctypes.byref(h)))
         self._own(h)
 
 
@@ -358,6 +365,16 @@ def q4_linear(w_q4_0, rows, k, xq, columns, with_dots=False, stream=None):
     return (out, dots) if with_dots else out
 
 
+def q4_1_linear(w_q4_1, rows, k, xq, columns, with_dots=False, stream=None):
+    """Canonical Q4_1 (cuda uint8, 20-byte blocks) x canonical Q8_1 -> fp32 [columns][rows] (+ int32 dots)."""
+    import torch
+    out = torch.empty(columns, rows, device=xq.device)
+    dots = torch.empty(columns, rows, k // 32, dtype=torch.int32, device=xq.device) if with_dots else None
+    check(library().moe_q4_1_linear(_ptr(w_q4_1), rows, k, _ptr(xq), columns, _ptr(out), _ptr(dots),
+                                    _stream(stream)))
+    return (out, dots) if with_dots else out
+
+
 class RouteGroups(_Owned):
     """Host route grouping with the reference's contract (src/routes.hpp:28-65)."""
 
@@ -410,10 +427,10 @@ class GpuExpert(_Owned):
 
     _destroy_name = "moe_expert_destroy"
 
-    def __init__(self, gate, up, down, device=0, max_columns=8, hidden=HIDDEN, inter=INTER):
+    def __init__(self, gate, up, down, device=0, max_columns=8, hidden=HIDDEN, inter=INTER, down_type=MOE_Q4_0):
         h = P()
-        check(library().moe_expert_create(_ptr(gate), _ptr(up), _ptr(down), hidden, inter, device, max_columns,
-                                          ctypes.byref(h)))
+        check(library().moe_expert_create_typed(_ptr(gate), _ptr(up), _ptr(down), down_type, hidden, inter, device,
+                                                max_columns, ctypes.byref(h)))
         self._own(h)
         self.hidden, self.inter = hidden, inter
 

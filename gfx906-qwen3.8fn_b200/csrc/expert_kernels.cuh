@@ -2,23 +2,31 @@
 // expert kernels (decode-size groups), plus the synthetic generator and
 // layout repacks.
 //
-// Weight layout (one expert, planar; same byte count as canonical Q4_0):
+// Weight layout (one expert, planar; same byte count as the canonical blocks):
 //   gate codes [I][H/32][16] | up codes [I][H/32][16] | down codes [H][I/32][16]
 //   | gate scales [I][H/32] half | up scales | down scales [H][I/32] half
+//   [| down minima [H][I/32] half, when the down matrix is Q4_1]
 // Block (r, b) of a matrix is canonical block r*(K/32)+b: its 16 code bytes
-// and its half scale, split so code rows load as aligned 16-byte vectors
-// (the reference's optional planar Q4_0 layout, src/hip/expert.hip:147-159).
+// and its half scale (and minimum), split so code rows load as aligned
+// 16-byte vectors (the reference's optional planar layout,
+// src/hip/expert.hip:147-159).  Gate and up are Q4_0; down is Q4_0 or Q4_1
+// (the reference's layers 0-5 carry Q4_1 down matrices,
+// src/memory_main.hip:41-42).
 #pragma once
 #include "common.cuh"
 
 namespace qmoe {
 
+constexpr int kDownQ4_0 = 0;
+constexpr int kDownQ4_1 = 1;
+
 struct ExpertLayout {
-    size_t gate_codes, up_codes, down_codes, gate_scales, up_scales, down_scales, bytes;
+    size_t gate_codes, up_codes, down_codes, gate_scales, up_scales, down_scales, down_mins, bytes;
     int hidden, inter;
+    int down_type;   // kDownQ4_0 or kDownQ4_1
 };
 
-inline ExpertLayout make_layout(int H, int I) {
+inline ExpertLayout make_layout(int H, int I, int down_type = kDownQ4_0) {
     ExpertLayout L;
     const size_t codes = static_cast<size_t>(H) * I / 2, scales = static_cast<size_t>(H) * I / 16;
     L.gate_codes = 0;
@@ -27,10 +35,22 @@ inline ExpertLayout make_layout(int H, int I) {
     L.gate_scales = 3 * codes;
     L.up_scales = 3 * codes + scales;
     L.down_scales = 3 * codes + 2 * scales;
-    L.bytes = 3 * codes + 3 * scales;
+    L.down_mins = 3 * codes + 3 * scales;
+    L.bytes = 3 * codes + 3 * scales + (down_type == kDownQ4_1 ? scales : 0);
     L.hidden = H;
     L.inter = I;
+    L.down_type = down_type;
     return L;
+}
+
+// One Q4_1 block's contribution with the reference's contract
+// (src/quant.cpp:88-102, src/cpu_expert.cpp:194-205): the products d4*d8 and
+// m4*s8 (exact in fp32 for half operands) are rounded to half (RNE), then
+// acc + fma(dot, half(d4*d8), half(m4*s8)) -- inner FMA, separate add.
+__device__ __forceinline__ float block_term_q4_1(int dot, float d4, float m4, float d8, float s8, float acc) {
+    const float dd = __half2float(__float2half_rn(__fmul_rn(d4, d8)));
+    const float ms = __half2float(__float2half_rn(__fmul_rn(m4, s8)));
+    return __fadd_rn(acc, fmaf(small_int_to_float(dot), dd, ms));
 }
 
 // ---------------------------------------------------------------------------
@@ -106,6 +126,12 @@ synth_kernel(uint8_t *base, ExpertLayout L, int experts_total, uint64_t seed, ui
         }
         const uint16_t d = f2h(__fmul_rn(static_cast<float>(mx), 6.6073582e-08f));
         uint8_t *ex = base + static_cast<size_t>(e) * L.bytes;
+        if (m == 2 && L.down_type == kDownQ4_1) {
+            // Q4_1 down: minimum -8 d (0.5 + u/65536), u a 16-bit draw
+            const uint64_t r = mix64(b + (i << 6) + 34);
+            const float f = 0.5f + static_cast<float>(r & 0xffffu) * (1.0f / 65536.0f);
+            reinterpret_cast<uint16_t *>(ex + L.down_mins)[i] = f2h(__fmul_rn(-8.0f * h2f(d), f));
+        }
         const size_t code_off = m == 0 ? L.gate_codes : m == 1 ? L.up_codes : L.down_codes;
         const size_t scale_off = m == 0 ? L.gate_scales : m == 1 ? L.up_scales : L.down_scales;
         reinterpret_cast<uint4 *>(ex + code_off)[i] =
@@ -129,6 +155,27 @@ repack_kernel(uint8_t *canonical, uint8_t *codes, uint16_t *scales, size_t block
             c[0] = scales[i] & 0xff;
             c[1] = scales[i] >> 8;
             for (int j = 0; j < 16; ++j) c[2 + j] = codes[i * 16 + j];
+        }
+    }
+}
+
+// canonical 20-byte Q4_1 blocks (half d, half m, 16 code bytes) <-> planar
+// (codes, scales, minima).  dir 0: canonical -> planar, dir 1: back.
+__global__ void __launch_bounds__(256)
+repack_q4_1_kernel(uint8_t *canonical, uint8_t *codes, uint16_t *scales, uint16_t *mins, size_t blocks, int dir) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < blocks;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        uint8_t *c = canonical + i * 20;
+        if (dir == 0) {
+            scales[i] = static_cast<uint16_t>(c[0] | (c[1] << 8));
+            mins[i] = static_cast<uint16_t>(c[2] | (c[3] << 8));
+            for (int j = 0; j < 16; ++j) codes[i * 16 + j] = c[4 + j];
+        } else {
+            c[0] = scales[i] & 0xff;
+            c[1] = scales[i] >> 8;
+            c[2] = mins[i] & 0xff;
+            c[3] = mins[i] >> 8;
+            for (int j = 0; j < 16; ++j) c[4 + j] = codes[i * 16 + j];
         }
     }
 }
@@ -289,6 +336,8 @@ down_kernel(GroupParams p) {
         const uint8_t *ex = p.weights + static_cast<size_t>(e) * p.layout.bytes;
         const uint4 *dcodes = reinterpret_cast<const uint4 *>(ex + p.layout.down_codes);
         const uint16_t *dsc = reinterpret_cast<const uint16_t *>(ex + p.layout.down_scales);
+        const uint16_t *dmn = reinterpret_cast<const uint16_t *>(ex + p.layout.down_mins);
+        const bool q41 = p.layout.down_type == kDownQ4_1;
         const int row = ds * 64 + (threadIdx.x >> 2);
         float acc[NT];
 #pragma unroll
@@ -297,12 +346,15 @@ down_kernel(GroupParams p) {
             const size_t blk = static_cast<size_t>(row) * nbd + b;
             const uint4 wc = __ldg(dcodes + blk);
             const float d4 = h2f(__ldg(dsc + blk));
+            const float m4 = q41 ? h2f(__ldg(dmn + blk)) : 0.0f;
 #pragma unroll
             for (int j = 0; j < NT; ++j) {
                 if (j < n) {
                     const int4 xlo = sm[j * (I / 16) + 2 * b], xhi = sm[j * (I / 16) + 2 * b + 1];
                     const float2 sc = ss[j * nbd + b];
-                    acc[j] = block_term(block_dot(wc, xlo, xhi), d4, sc.x, 8.0f * sc.y, acc[j]);
+                    const int dot = block_dot(wc, xlo, xhi);
+                    acc[j] = q41 ? block_term_q4_1(dot, d4, m4, sc.x, sc.y, acc[j])
+                                 : block_term(dot, d4, sc.x, 8.0f * sc.y, acc[j]);
                 }
             }
         }
@@ -359,6 +411,50 @@ q4_linear_kernel(const uint8_t *canonical_w, const uint8_t *codes, const uint16_
             const float d8 = h2f(static_cast<uint16_t>(a[0] | (a[1] << 8)));
             const float s8 = h2f(static_cast<uint16_t>(a[2] | (a[3] << 8)));
             acc = block_term(dot, h2f(hd), d8, 8.0f * s8, acc);
+            if (dots) dots[(static_cast<size_t>(c) * rows + r) * nb + b] = dot;
+        }
+        out[static_cast<size_t>(c) * rows + r] = acc;
+    }
+}
+
+// Parity tap for Q4_1 weights: canonical 20-byte blocks [rows][K/32] against
+// canonical Q8_1 [columns][K/32]; the block terms of block_term_q4_1 summed
+// in ascending block order, optional per-block int32 dots.
+// Canonical weights when w is non-null, else the planar (codes, scales, mins).
+__global__ void __launch_bounds__(256)
+q4_1_linear_kernel(const uint8_t *w, const uint8_t *codes, const uint16_t *scales, const uint16_t *mins, int rows,
+                   int nb, const uint8_t *xq, int columns, float *out, int32_t *dots) {
+    const size_t total = static_cast<size_t>(rows) * columns;
+    for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+         g += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(g / rows), r = static_cast<int>(g % rows);
+        float acc = 0.0f;
+        for (int b = 0; b < nb; ++b) {
+            const size_t blk = static_cast<size_t>(r) * nb + b;
+            uint16_t hd, hm;
+            uint32_t wv[4];
+            if (w) {
+                const uint8_t *s = w + blk * 20;
+                hd = static_cast<uint16_t>(s[0] | (s[1] << 8));
+                hm = static_cast<uint16_t>(s[2] | (s[3] << 8));
+                for (int k = 0; k < 4; ++k)
+                    wv[k] = s[4 + 4 * k] | (s[5 + 4 * k] << 8) | (s[6 + 4 * k] << 16) |
+                            (static_cast<uint32_t>(s[7 + 4 * k]) << 24);
+            } else {
+                const uint4 c = reinterpret_cast<const uint4 *>(codes)[blk];
+                wv[0] = c.x; wv[1] = c.y; wv[2] = c.z; wv[3] = c.w;
+                hd = scales[blk];
+                hm = mins[blk];
+            }
+            const uint8_t *a = xq + (static_cast<size_t>(c) * nb + b) * 36;
+            int xv[8];
+            for (int k = 0; k < 8; ++k)
+                xv[k] = a[4 + 4 * k] | (a[5 + 4 * k] << 8) | (a[6 + 4 * k] << 16) | (static_cast<int>(a[7 + 4 * k]) << 24);
+            const int dot = block_dot(make_uint4(wv[0], wv[1], wv[2], wv[3]), make_int4(xv[0], xv[1], xv[2], xv[3]),
+                                      make_int4(xv[4], xv[5], xv[6], xv[7]));
+            const float d8 = h2f(static_cast<uint16_t>(a[0] | (a[1] << 8)));
+            const float s8 = h2f(static_cast<uint16_t>(a[2] | (a[3] << 8)));
+            acc = block_term_q4_1(dot, h2f(hd), h2f(hm), d8, s8, acc);
             if (dots) dots[(static_cast<size_t>(c) * rows + r) * nb + b] = dot;
         }
         out[static_cast<size_t>(c) * rows + r] = acc;

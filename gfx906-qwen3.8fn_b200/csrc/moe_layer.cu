@@ -332,7 +332,8 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     sp.num_tiles = h->num_tiles;
     sp.max_tiles = h->tiles_max;
     sp.error = h->error;
-    if (x) {   // forward: large groups go to the tensor-core kernels
+    if (x && (!w || w->layout.down_type == kDownQ4_0)) {   // forward: large groups go to the tensor-core kernels
+        // (Q4_1 down matrices run every group on the dp4a kernels)
         sp.tc_min = kTcMinGroup;
         sp.tc_tile = kTcM;
         sp.tc_max = h->tc.max_tiles;
@@ -364,7 +365,7 @@ extern "C" {
 
 const char *moe_last_error_message(void) { return g_message; }
 
-int moe_abi_version(void) { return (1 << 16) | 0; }
+int moe_abi_version(void) { return (1 << 16) | 1; }
 
 const char *moe_status_string(int status) {
     switch (status) {
@@ -387,15 +388,21 @@ size_t moe_weights_expert_bytes(const moe_layer_desc *desc) {
 
 // ---------------------------------------------------------------- weights --
 int moe_weights_create(const moe_layer_desc *desc, moe_weights_t *out) {
+    return moe_weights_create_typed(desc, MOE_Q4_0, out);
+}
+
+int moe_weights_create_typed(const moe_layer_desc *desc, int down_type, moe_weights_t *out) {
     if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
     *out = nullptr;
     if (const int st = validate_desc(desc)) return st;
+    if (down_type != MOE_Q4_0 && down_type != MOE_Q4_1)
+        return fail(MOE_NOT_SUPPORTED, "down matrices must be Q4_0 or Q4_1");
     DeviceGuard guard(desc->device);
     MOE_CUDA(guard.status);
     auto *w = new (std::nothrow) moe_weights_s();
     if (!w) return fail(MOE_OUT_OF_MEMORY, "host allocation");
     w->desc = *desc;
-    w->layout = make_layout(desc->hidden, desc->inter);
+    w->layout = make_layout(desc->hidden, desc->inter, down_type == MOE_Q4_1 ? kDownQ4_1 : kDownQ4_0);
     w->experts_total = desc->experts + desc->has_shared;
     cudaError_t e = cudaMalloc(&w->base, w->layout.bytes * w->experts_total);
     if (e == cudaSuccess) e = cudaMalloc(&w->gate_vec, sizeof(float) * desc->hidden);
@@ -429,15 +436,19 @@ int moe_weights_upload_expert(moe_weights_t w, int expert, const void *gate, con
     auto s = static_cast<cudaStream_t>(stream);
     const ExpertLayout &L = w->layout;
     const size_t blocks = static_cast<size_t>(L.hidden) * L.inter / 32;  // per matrix
-    const size_t bytes = blocks * 18;
     uint8_t *ex = w->base + static_cast<size_t>(expert) * L.bytes;
     const void *src[3] = {gate, up, down};
     const size_t codes[3] = {L.gate_codes, L.up_codes, L.down_codes};
     const size_t scales[3] = {L.gate_scales, L.up_scales, L.down_scales};
     for (int m = 0; m < 3; ++m) {
-        MOE_CUDA(cudaMemcpyAsync(w->staging, src[m], bytes, cudaMemcpyHostToDevice, s));
-        repack_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
-                                          blocks, 0);
+        const bool q41 = m == 2 && L.down_type == kDownQ4_1;
+        MOE_CUDA(cudaMemcpyAsync(w->staging, src[m], blocks * (q41 ? 20 : 18), cudaMemcpyHostToDevice, s));
+        if (q41)
+            repack_q4_1_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
+                                                   reinterpret_cast<uint16_t *>(ex + L.down_mins), blocks, 0);
+        else
+            repack_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
+                                              blocks, 0);
         MOE_CUDA(cudaGetLastError());
         MOE_CUDA(cudaStreamSynchronize(s));  // staging is reused by the next matrix
     }
@@ -457,10 +468,15 @@ int moe_weights_download_expert(moe_weights_t w, int expert, void *gate, void *u
     const size_t codes[3] = {L.gate_codes, L.up_codes, L.down_codes};
     const size_t scales[3] = {L.gate_scales, L.up_scales, L.down_scales};
     for (int m = 0; m < 3; ++m) {
-        repack_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
-                                          blocks, 1);
+        const bool q41 = m == 2 && L.down_type == kDownQ4_1;
+        if (q41)
+            repack_q4_1_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
+                                                   reinterpret_cast<uint16_t *>(ex + L.down_mins), blocks, 1);
+        else
+            repack_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
+                                              blocks, 1);
         MOE_CUDA(cudaGetLastError());
-        MOE_CUDA(cudaMemcpyAsync(dst[m], w->staging, blocks * 18, cudaMemcpyDeviceToHost, s));
+        MOE_CUDA(cudaMemcpyAsync(dst[m], w->staging, blocks * (q41 ? 20 : 18), cudaMemcpyDeviceToHost, s));
         MOE_CUDA(cudaStreamSynchronize(s));
     }
     return MOE_OK;
@@ -607,7 +623,8 @@ int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const f
     // Upper bound on tensor-core tiles: every group of >= kTcMinGroup pairs,
     // 128 pairs per tile (the device writes the exact count).
     const int pairs = tokens * (kTopK + 1);
-    const int tc_tiles = tokens > kChunk ? std::min(h->tc.max_tiles, pairs / kTcMinGroup + pairs / kTcM + 1) : 0;
+    const bool tc_ok = tokens > kChunk && w->layout.down_type == kDownQ4_0;
+    const int tc_tiles = tc_ok ? std::min(h->tc.max_tiles, pairs / kTcMinGroup + pairs / kTcM + 1) : 0;
     return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events, tc_tiles);
 }
 
@@ -641,6 +658,24 @@ int moe_q4_linear(const void *w, int rows, int k, const void *xq, int columns, f
         static_cast<const uint8_t *>(w), nullptr, nullptr, rows, static_cast<int>(nb),
         static_cast<const uint8_t *>(xq), columns, out, dots);
     return cuda_status(cudaGetLastError(), "q4_linear_kernel");
+}
+
+int moe_q4_1_linear(const void *w, int rows, int k, const void *xq, int columns, float *out, int32_t *dots,
+                    void *stream) {
+    if (rows <= 0 || rows > 65536 || k <= 0 || k > 16384 || k % 32 || columns <= 0 || columns > 65536)
+        return fail(MOE_INVALID_ARGUMENT, "bad linear shape");
+    if (!aligned(w, 2) || !aligned(xq, 4) || !aligned(out, 4) || (dots && !aligned(dots, 4)))
+        return fail(MOE_INVALID_ARGUMENT, "null or misaligned linear buffers");
+    const size_t nb = k / 32;
+    if (overlap(out, static_cast<size_t>(rows) * columns * 4, w, rows * nb * 20) ||
+        overlap(out, static_cast<size_t>(rows) * columns * 4, xq, columns * nb * 36))
+        return fail(MOE_INVALID_ARGUMENT, "output overlaps an input");
+    int device = 0;
+    MOE_CUDA(cudaGetDevice(&device));
+    q4_1_linear_kernel<<<sm_count(device) * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t *>(w), nullptr, nullptr, nullptr, rows, static_cast<int>(nb),
+        static_cast<const uint8_t *>(xq), columns, out, dots);
+    return cuda_status(cudaGetLastError(), "q4_1_linear_kernel");
 }
 
 // ------------------------------------------------- single-expert fixture --
@@ -692,8 +727,15 @@ int moe_expert_destroy(moe_expert_t e) {
 
 int moe_expert_create(const void *gate, const void *up, const void *down, int hidden, int inter, int device,
                       int max_columns, moe_expert_t *out) {
+    return moe_expert_create_typed(gate, up, down, MOE_Q4_0, hidden, inter, device, max_columns, out);
+}
+
+int moe_expert_create_typed(const void *gate, const void *up, const void *down, int down_type, int hidden, int inter,
+                            int device, int max_columns, moe_expert_t *out) {
     if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
     *out = nullptr;
+    if (down_type != MOE_Q4_0 && down_type != MOE_Q4_1)
+        return fail(MOE_NOT_SUPPORTED, "down matrices must be Q4_0 or Q4_1");
     if (max_columns <= 0 || max_columns > 1024) return fail(MOE_INVALID_ARGUMENT, "max_columns must be 1..1024");
     if (!gate || !up || !down) return fail(MOE_INVALID_ARGUMENT, "null expert weights");
     moe_layer_desc d{hidden, inter, kRouterExperts, kTopK, 0, device, max_columns};
@@ -708,7 +750,7 @@ int moe_expert_create(const void *gate, const void *up, const void *down, int hi
     auto *w = new (std::nothrow) moe_weights_s();
     if (!w) { delete e; return fail(MOE_OUT_OF_MEMORY, "host allocation"); }
     w->desc = d;
-    w->layout = make_layout(hidden, inter);
+    w->layout = make_layout(hidden, inter, down_type == MOE_Q4_1 ? kDownQ4_1 : kDownQ4_0);
     w->experts_total = 1;
     e->w = w;
     int st = cuda_status(cudaMalloc(&w->base, w->layout.bytes), "cudaMalloc");
@@ -768,8 +810,13 @@ int moe_expert_linear(moe_expert_t e, int down, int up, const void *input, int c
     const size_t so = down ? L.down_scales : up ? L.up_scales : L.gate_scales;
     MOE_CUDA(cudaMemcpyAsync(e->q8, input, static_cast<size_t>(columns) * (in / 32) * 36, cudaMemcpyHostToDevice,
                              e->stream));
-    q4_linear_kernel<<<e->h->sms * 8, 256, 0, e->stream>>>(nullptr, ex + co, reinterpret_cast<const uint16_t *>(ex + so),
-                                                           rows, in / 32, e->q8, columns, e->y, nullptr);
+    if (down && L.down_type == kDownQ4_1)
+        q4_1_linear_kernel<<<e->h->sms * 8, 256, 0, e->stream>>>(
+            nullptr, ex + co, reinterpret_cast<const uint16_t *>(ex + so),
+            reinterpret_cast<const uint16_t *>(ex + L.down_mins), rows, in / 32, e->q8, columns, e->y, nullptr);
+    else
+        q4_linear_kernel<<<e->h->sms * 8, 256, 0, e->stream>>>(nullptr, ex + co, reinterpret_cast<const uint16_t *>(ex + so),
+                                                               rows, in / 32, e->q8, columns, e->y, nullptr);
     MOE_CUDA(cudaGetLastError());
     MOE_CUDA(cudaMemcpyAsync(output, e->y, static_cast<size_t>(columns) * rows * 4, cudaMemcpyDeviceToHost, e->stream));
     MOE_CUDA(cudaStreamSynchronize(e->stream));
@@ -1058,9 +1105,15 @@ EpParams ep_params(moe_ep_s *ep, int tokens, float *out) {
 extern "C" {
 
 int moe_ep_weights_create(const moe_layer_desc *desc, int rank, int world, moe_weights_t *out) {
+    return moe_ep_weights_create_typed(desc, rank, world, MOE_Q4_0, out);
+}
+
+int moe_ep_weights_create_typed(const moe_layer_desc *desc, int rank, int world, int down_type, moe_weights_t *out) {
     if (!out) return fail(MOE_INVALID_ARGUMENT, "null output handle");
     *out = nullptr;
     if (const int st = validate_desc(desc)) return st;
+    if (down_type != MOE_Q4_0 && down_type != MOE_Q4_1)
+        return fail(MOE_NOT_SUPPORTED, "down matrices must be Q4_0 or Q4_1");
     if (!(world == 1 || world == 2 || world == 4 || world == 8) || rank < 0 || rank >= world)
         return fail(MOE_INVALID_ARGUMENT, "world must be 1, 2, 4 or 8 and 0 <= rank < world");
     DeviceGuard guard(desc->device);
@@ -1068,7 +1121,7 @@ int moe_ep_weights_create(const moe_layer_desc *desc, int rank, int world, moe_w
     auto *w = new (std::nothrow) moe_weights_s();
     if (!w) return fail(MOE_OUT_OF_MEMORY, "host allocation");
     w->desc = *desc;
-    w->layout = make_layout(desc->hidden, desc->inter);
+    w->layout = make_layout(desc->hidden, desc->inter, down_type == MOE_Q4_1 ? kDownQ4_1 : kDownQ4_0);
     w->expert_count = kRouterExperts / world;
     w->expert_first = rank * w->expert_count;
     w->experts_total = w->expert_count + desc->has_shared;
@@ -1303,7 +1356,7 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
         sp.shared_w = shared_w;
         sp.shared_token0 = ep->rank * ep->t_max;
         sp.shared_expert = ep->ecount;
-        if (ep->tc) {
+        if (ep->tc && w->layout.down_type == kDownQ4_0) {   // Q4_1 down: every group on the dp4a kernels
             sp.tc_min = kTcMinGroup;
             sp.tc_tile = kTcM;
             sp.tc_max = r.tc.max_tiles;
@@ -1318,7 +1371,8 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
         MOE_CUDA(cudaGetLastError());
     }
     // expert kernels over the received slots, partial rows accumulated locally
-    const int tc_tiles = ep->tc ? std::min(r.tc.max_tiles, ep->rx_pairs / kTcMinGroup + ep->rx_pairs / kTcM + 1) : 0;
+    const bool tc_ok = ep->tc && w->layout.down_type == kDownQ4_0;
+    const int tc_tiles = tc_ok ? std::min(r.tc.max_tiles, ep->rx_pairs / kTcMinGroup + ep->rx_pairs / kTcM + 1) : 0;
     if (const int st = launch_experts(&r, w, partial, r.tiles_max, s, nullptr, tc_tiles)) return st;
     // 5. the combine publishes "done", waits for every peer's, then pulls the partial rows
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));

@@ -57,14 +57,17 @@ struct GuStage {
     }
 };
 
+// The minima slice (Q4_1 down matrices) is reserved in every stage, so one
+// ring layout serves both down types.
 struct DnStage {
-    uint32_t meta, dcodes, dsc, mcodes, msc, bytes;
+    uint32_t meta, dcodes, dsc, dmin, mcodes, msc, bytes;
     __host__ __device__ DnStage(int I) {
         const uint32_t nb = I / 32;
         meta = 0;
         dcodes = 128;
         dsc = dcodes + kDnRows * nb * 16;
-        mcodes = dsc + kDnRows * nb * 2;
+        dmin = dsc + kDnRows * nb * 2;
+        mcodes = dmin + kDnRows * nb * 2;
         msc = mcodes + kGemvTile * I;
         bytes = msc + kGemvTile * nb * 8;
         bytes = (bytes + 127) & ~127u;
@@ -296,13 +299,14 @@ stream_gate_up_kernel(StreamParams p) {
 // kDnLaneRows): lane l takes rows 8R*cw + l/4 + 8k (k < R) and blocks l%4,
 // l%4+4, ...; two shuffles finish each row, then out[token][row] += weight * y
 // (red.global.add).
-template <int N>
+template <int N, bool Q41>
 __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, int I, int H, int row0,
                                           int lr0, int q, uint64_t *empty_bar, int lane, float *out, int *error) {
     const int nb = I / 32;
     const TileRec &meta = *reinterpret_cast<const TileRec *>(st);
     const uint4 *dc = reinterpret_cast<const uint4 *>(st + L.dcodes);
     const uint16_t *ds = reinterpret_cast<const uint16_t *>(st + L.dsc);
+    const uint16_t *dm = reinterpret_cast<const uint16_t *>(st + L.dmin);
     const int4 *mc = reinterpret_cast<const int4 *>(st + L.mcodes);
     const float2 *ms = reinterpret_cast<const float2 *>(st + L.msc);
     constexpr int R = kDnLaneRows;
@@ -317,33 +321,62 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
 #pragma unroll
         for (int k = 0; k < R / 2; ++k) acc2[k][j] = 0ull;
     }
-    for (int b = q; b < nb; b += 4) {
-        uint4 wk[R];
-        uint64_t dk[R / 2];
+    float acc[R][N];
+    if constexpr (Q41) {
+        // Q4_1: every (row, block) needs its own half-rounded products, so
+        // the terms stay scalar.
 #pragma unroll
-        for (int k = 0; k < R; ++k) wk[k] = dc[(lr0 + 8 * k) * nb + b];
+        for (int k = 0; k < R; ++k)
 #pragma unroll
-        for (int k = 0; k < R / 2; ++k)
-            dk[k] = pkf2(h2f(ds[(lr0 + 16 * k) * nb + b]), h2f(ds[(lr0 + 16 * k + 8) * nb + b]));
+            for (int j = 0; j < N; ++j) acc[k][j] = 0.0f;
+        for (int b = q; b < nb; b += 4) {
+            uint4 wk[R];
+            float d4[R], m4[R];
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-            const int4 xlo = mc[j * (I / 16) + 2 * b], xhi = mc[j * (I / 16) + 2 * b + 1];
-            const float2 sc = ms[j * nb + b];
-            const float ns = -(8.0f * sc.y);
-            const uint64_t d8 = pkf2(sc.x, sc.x), nsp = pkf2(ns, ns);
+            for (int k = 0; k < R; ++k) {
+                wk[k] = dc[(lr0 + 8 * k) * nb + b];
+                d4[k] = h2f(ds[(lr0 + 8 * k) * nb + b]);
+                m4[k] = h2f(dm[(lr0 + 8 * k) * nb + b]);
+            }
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                const int4 xlo = mc[j * (I / 16) + 2 * b], xhi = mc[j * (I / 16) + 2 * b + 1];
+                const float2 sc = ms[j * nb + b];
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    acc[k][j] = block_term_q4_1(block_dot2(wk[k], xlo, xhi), d4[k], m4[k], sc.x, sc.y, acc[k][j]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar);   // stage fully read by this warp
+    } else {
+        for (int b = q; b < nb; b += 4) {
+            uint4 wk[R];
+            uint64_t dk[R / 2];
+#pragma unroll
+            for (int k = 0; k < R; ++k) wk[k] = dc[(lr0 + 8 * k) * nb + b];
 #pragma unroll
             for (int k = 0; k < R / 2; ++k)
-                acc2[k][j] = block_term2(block_dot2(wk[2 * k], xlo, xhi), block_dot2(wk[2 * k + 1], xlo, xhi), dk[k],
-                                         d8, nsp, acc2[k][j]);
+                dk[k] = pkf2(h2f(ds[(lr0 + 16 * k) * nb + b]), h2f(ds[(lr0 + 16 * k + 8) * nb + b]));
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                const int4 xlo = mc[j * (I / 16) + 2 * b], xhi = mc[j * (I / 16) + 2 * b + 1];
+                const float2 sc = ms[j * nb + b];
+                const float ns = -(8.0f * sc.y);
+                const uint64_t d8 = pkf2(sc.x, sc.x), nsp = pkf2(ns, ns);
+#pragma unroll
+                for (int k = 0; k < R / 2; ++k)
+                    acc2[k][j] = block_term2(block_dot2(wk[2 * k], xlo, xhi), block_dot2(wk[2 * k + 1], xlo, xhi),
+                                             dk[k], d8, nsp, acc2[k][j]);
+            }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar);   // stage fully read by this warp
+#pragma unroll
+        for (int k = 0; k < R / 2; ++k)
+#pragma unroll
+            for (int j = 0; j < N; ++j) upk2(acc2[k][j], acc[2 * k][j], acc[2 * k + 1][j]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar);   // stage fully read by this warp
-    float acc[R][N];
-#pragma unroll
-    for (int k = 0; k < R / 2; ++k)
-#pragma unroll
-        for (int j = 0; j < N; ++j) upk2(acc2[k][j], acc[2 * k][j], acc[2 * k + 1][j]);
 #pragma unroll
     for (int k = 0; k < R; ++k)
 #pragma unroll
@@ -366,6 +399,7 @@ stream_down_kernel(StreamParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int H = p.layout.hidden, I = p.layout.inter, nb = I / 32, slabs = H / kDnRows;
     const DnStage L(I);
+    const bool q41 = p.layout.down_type == kDownQ4_1;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
     uint8_t *stages = smem + 128;
@@ -408,11 +442,14 @@ stream_down_kernel(StreamParams p) {
             *reinterpret_cast<TileRec *>(st) = rec;
             const int slab = item % slabs;
             const uint8_t *ex = p.weights + static_cast<size_t>(rec.e) * p.layout.bytes;
-            mbar_arrive_expect_tx(&full[s], code_bytes + sc_bytes + rec.n * (I + nb * 8));
+            mbar_arrive_expect_tx(&full[s], code_bytes + (q41 ? 2 : 1) * sc_bytes + rec.n * (I + nb * 8));
             bulk_g2s(st + L.dcodes, ex + p.layout.down_codes + static_cast<size_t>(slab) * code_bytes, code_bytes,
                      &full[s]);
             bulk_g2s(st + L.dsc, ex + p.layout.down_scales + static_cast<size_t>(slab) * sc_bytes, sc_bytes,
                      &full[s]);
+            if (q41)
+                bulk_g2s(st + L.dmin, ex + p.layout.down_mins + static_cast<size_t>(slab) * sc_bytes, sc_bytes,
+                         &full[s]);
             if (dep) issue_mid(st, &full[s], rec);
         }
         if (!dep) resolve();
@@ -432,11 +469,20 @@ stream_down_kernel(StreamParams p) {
         const uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
         const int n = reinterpret_cast<const TileRec *>(st)->n;
         const int row0 = (item % slabs) * kDnRows + lr0;
-        switch (n) {
-        case 1: down_item<1>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-        case 2: down_item<2>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-        case 3: down_item<3>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-        default: down_item<4>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+        if (q41) {
+            switch (n) {
+            case 1: down_item<1, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            case 2: down_item<2, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            case 3: down_item<3, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            default: down_item<4, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            }
+        } else {
+            switch (n) {
+            case 1: down_item<1, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            case 2: down_item<2, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            case 3: down_item<3, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            default: down_item<4, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            }
         }
     }
 }

@@ -19,9 +19,10 @@
  *    or unrepresentable arithmetic), as the reference's session ops do.
  *
  * Q4_0 blocks are the canonical 18-byte GGML layout (half d, 16 code bytes,
- * low nibble of byte j = element j, high nibble = element j+16); Q8_1 blocks
- * are the reference's 36-byte ABI (half d, half raw sum, 32 int8 codes),
- * src/quant.hpp:8-18.
+ * low nibble of byte j = element j, high nibble = element j+16); Q4_1 blocks
+ * the canonical 20-byte layout (half d, half m, the same 16 code bytes; value
+ * d*q + m); Q8_1 blocks are the reference's 36-byte ABI (half d, half raw
+ * sum, 32 int8 codes), src/quant.hpp:8-18.
  */
 #ifndef QWEN_MOE_B200_H
 #define QWEN_MOE_B200_H
@@ -69,6 +70,9 @@ typedef struct moe_layer_desc {
     int max_tokens;  /* capacity of one forward */
 } moe_layer_desc;
 
+/* Weight block types, numbered as the reference's TensorType (src/model.hpp:17-19). */
+enum moe_tensor_type { MOE_Q4_0 = 2, MOE_Q4_1 = 3 };
+
 typedef struct moe_layer_s *moe_layer_t;
 typedef struct moe_weights_s *moe_weights_t;
 
@@ -82,23 +86,35 @@ int moe_abi_version(void);
  * blocks), then gate/up/down half scales.  Byte count equals the canonical
  * Q4_0 size.  The shared expert is stored as expert index `experts`. */
 int moe_weights_create(const moe_layer_desc *desc, moe_weights_t *out);
+/* The same with the down matrices of type down_type (MOE_Q4_0 or MOE_Q4_1;
+ * gate and up are always Q4_0).  The reference's layers 0-5 carry Q4_1 down
+ * matrices (src/memory_main.hip:41-42): each block contributes
+ * dot*half(d4*d8) + half(m4*s8) (src/quant.cpp:88-102).  A Q4_1-down expert
+ * adds a half minimum per down block to the planar region (1,835,008 bytes
+ * at H=2048, I=512).  Forwards over such weights run every expert group on
+ * the dp4a kernels (no tensor-core path).  MOE_NOT_SUPPORTED for other types. */
+int moe_weights_create_typed(const moe_layer_desc *desc, int down_type, moe_weights_t *out);
 int moe_weights_destroy(moe_weights_t w);
 /* Upload one expert from canonical host Q4_0 bytes (repacked to the planar
  * layout on the device).  Replaces the reference's expert staging
  * (src/session.hip:957-1042): all experts stay resident.  expert == experts
- * uploads the shared expert.  gate/up: [I][H/32] blocks, down: [H][I/32]. */
+ * uploads the shared expert.  gate/up: [I][H/32] blocks, down: [H][I/32]
+ * blocks of the weights' down type (20-byte Q4_1 blocks for MOE_Q4_1). */
 int moe_weights_upload_expert(moe_weights_t w, int expert, const void *gate_q4_0,
                               const void *up_q4_0, const void *down_q4_0, void *stream);
 /* Shared expert scalar gate vector (fp32 [H]), the reference's
  * ffn_gate_inp_shexp (src/session.hip:1101, used at :1398-1402). */
 int moe_weights_upload_shared_gate(moe_weights_t w, const float *gate_vec_host, void *stream);
 /* Fill every expert (and the shared expert) with the seeded synthetic Q4_0
- * generator on the device (bit-identical to the oracle's generator). */
+ * generator on the device (bit-identical to the oracle's generator); Q4_1
+ * down matrices take the same codes and scales plus the minimum
+ * -8*d*(0.5 + u/65536) from one more 16-bit draw per block. */
 int moe_weights_synthesize(moe_weights_t w, uint64_t seed, uint32_t layer, void *stream);
-/* Copy one expert back as canonical Q4_0 bytes (host), for parity checks. */
+/* Copy one expert back as canonical bytes (host; down in the weights' down
+ * type), for parity checks. */
 int moe_weights_download_expert(moe_weights_t w, int expert, void *gate_q4_0, void *up_q4_0,
                                 void *down_q4_0, void *stream);
-/* Device address of expert e's planar region (for expert-parallel sharding). */
+/* Bytes of one expert's planar region with Q4_0 down matrices. */
 size_t moe_weights_expert_bytes(const moe_layer_desc *desc);
 
 /* ---- layer workspace and forward ----------------------------------------- */
@@ -172,6 +188,9 @@ enum { MOE_EP_HANDLE_BYTES = 64 };
  * 512/world.  Upload, synthesis (same bits as the global experts) and
  * download work as for moe_weights_t with local indices. */
 int moe_ep_weights_create(const moe_layer_desc *desc, int rank, int world, moe_weights_t *out);
+/* The same with down matrices of type down_type (see moe_weights_create_typed). */
+int moe_ep_weights_create_typed(const moe_layer_desc *desc, int rank, int world, int down_type,
+                                moe_weights_t *out);
 /* Workspace of one rank; desc->max_tokens is the per-rank token capacity. */
 int moe_ep_create(const moe_layer_desc *desc, int rank, int world, moe_ep_t *out);
 int moe_ep_destroy(moe_ep_t ep);
@@ -203,11 +222,23 @@ int moe_quantize_q8_1(const float *x_dev, int width, int columns, void *q8_dev, 
  * ([columns][rows][K/32]), the bit-exact parity tap. */
 int moe_q4_linear(const void *w_q4_0_dev, int rows, int k, const void *x_q8_dev, int columns,
                   float *out_dev, int32_t *dots_dev, void *stream);
+/* Q4_1 x Q8_1 linear on canonical 20-byte Q4_1 weights [rows][K/32]:
+ * out[c][r] = sum over ascending b of the block terms
+ * acc + fma(dot, half(d4*d8), half(m4*s8)) -- the contract of the
+ * reference's Q4_1 down projection (src/quant.cpp:88-102,
+ * src/hip/linear.hip:204-211, src/cpu_expert.cpp:194-205).  dots_dev as for
+ * moe_q4_linear (the uncentred sum of code*activation per block). */
+int moe_q4_1_linear(const void *w_q4_1_dev, int rows, int k, const void *x_q8_dev, int columns,
+                    float *out_dev, int32_t *dots_dev, void *stream);
 
 /* ---- single-expert fixture API (src/gpu_expert.hpp:7-21) ---------------- */
 typedef struct moe_expert_s *moe_expert_t;
 int moe_expert_create(const void *gate_q4_0, const void *up_q4_0, const void *down_q4_0,
                       int hidden, int inter, int device, int max_columns, moe_expert_t *out);
+/* GpuExpert with a down matrix of type down_type (MOE_Q4_0 or MOE_Q4_1), as
+ * the reference's native expert shapes use (Q4_0 gate/up, Q4_1 down). */
+int moe_expert_create_typed(const void *gate_q4_0, const void *up_q4_0, const void *down, int down_type,
+                            int hidden, int inter, int device, int max_columns, moe_expert_t *out);
 int moe_expert_destroy(moe_expert_t e);
 /* Host fp32 [n] -> compare the GPU Q8_1 bytes with `expected` (host Q8_1);
  * MOE_INVALID_ARGUMENT when the input is not representable, MOE_NUMERIC_ERROR

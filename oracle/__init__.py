@@ -34,6 +34,8 @@ ASSIGN_DTYPE = np.dtype([("token", "<i4"), ("rank", "<i4"), ("expert", "<i4"), (
 
 HIDDEN, INTER, EXPERTS, TOP_K = 2048, 512, 512, 10
 Q4_BLOCK = 18
+Q4_1_BLOCK = 20
+Q4_0, Q4_1 = 2, 3          # TensorType values of the reference (src/model.hpp:17-19)
 
 
 def build(force=False):
@@ -73,6 +75,11 @@ def lib():
             "o_matrix_serial": (None, [P, P, I, I, I, P]),
             "o_matrix_mmvq": (None, [P, P, I, I, I, P]),
             "o_expert_whole": (I, [P, P, P, I, I, P, I, P, P, P]),
+            "o_expert_whole_typed": (I, [P, P, P, I, I, I, P, I, P, P, P]),
+            "o_block_dots_q4_1": (None, [P, P, I, I, I, P]),
+            "o_matrix_serial_q4_1": (None, [P, P, I, I, I, P]),
+            "o_matrix_mmvq_q4_1": (None, [P, P, I, I, I, P]),
+            "o_synth_q4_1": (None, [U64, U32, U32, U32, SZ, P]),
             "o_route_exp": (F, [F]),
             "o_router_softmax": (I, [P, I, P]),
             "o_select_routes": (I, [P, I, P, P]),
@@ -82,6 +89,7 @@ def lib():
             "o_synth_base": (U64, [U64, U32, U32, U32]),
             "o_synth_q4_0": (None, [U64, U32, U32, U32, SZ, P]),
             "o_fixture_xorshift_q4_0": (None, [U32, SZ, P]),
+            "o_fixture_xorshift_q4_1": (None, [U32, SZ, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -113,6 +121,7 @@ def _load_ref(path):
         "ref_routes_assignments": (SZ, [P, P, SZ]),
         "ref_routes_counts": (None, [P, P]),
         "ref_expert_new": (P, [P, P, P, SZ, SZ, I, I]),
+        "ref_expert_new_typed": (P, [P, P, P, I, SZ, SZ, I, I]),
         "ref_expert_free": (None, [P]),
         "ref_run_cpu_expert": (I, [P, I, P, SZ, I, P, SZ]),
         "ref_allowed_physical_cpus": (I, [P, SZ, ctypes.POINTER(SZ)]),
@@ -162,17 +171,33 @@ def synth_q4_0(seed, layer, expert, matrix, rows, blocks):
     return out
 
 
-def synth_expert(seed, layer, expert, hidden=HIDDEN, inter=INTER):
-    """(gate, up, down) canonical bytes; gate/up [inter][hidden/32], down [hidden][inter/32]."""
+def synth_q4_1(seed, layer, expert, matrix, rows, blocks):
+    """Canonical Q4_1 bytes [rows*blocks*20] of one generated matrix."""
+    out = np.empty(rows * blocks * Q4_1_BLOCK, dtype=np.uint8)
+    lib().o_synth_q4_1(seed, layer, expert, matrix, rows * blocks, ptr(out))
+    return out
+
+
+def synth_expert(seed, layer, expert, hidden=HIDDEN, inter=INTER, down_type=Q4_0):
+    """(gate, up, down) canonical bytes; gate/up [inter][hidden/32] Q4_0, down
+    [hidden][inter/32] of down_type (Q4_0 or Q4_1)."""
+    down = (synth_q4_1 if down_type == Q4_1 else synth_q4_0)(seed, layer, expert, 2, hidden, inter // 32)
     return (synth_q4_0(seed, layer, expert, 0, inter, hidden // 32),
             synth_q4_0(seed, layer, expert, 1, inter, hidden // 32),
-            synth_q4_0(seed, layer, expert, 2, hidden, inter // 32))
+            down)
 
 
 def fixture_xorshift_q4_0(seed, rows, blocks):
     """The reference cpu_expert test's seeded Q4_0 matrix (tests/cpu_expert_test.cpp:227-246)."""
     out = np.empty(rows * blocks * Q4_BLOCK, dtype=np.uint8)
     lib().o_fixture_xorshift_q4_0(seed, rows * blocks, ptr(out))
+    return out
+
+
+def fixture_xorshift_q4_1(seed, rows, blocks):
+    """Q4_1 version of the reference cpu_expert test matrix (tests/cpu_expert_test.cpp:219-241)."""
+    out = np.empty(rows * blocks * Q4_1_BLOCK, dtype=np.uint8)
+    lib().o_fixture_xorshift_q4_1(seed, rows * blocks, ptr(out))
     return out
 
 
@@ -200,15 +225,35 @@ def block_dots(w, xq, rows, blocks):
     return out.reshape(cols, rows, blocks)
 
 
-def expert_whole(gate, up, down, xq, hidden=HIDDEN, inter=INTER):
+def _q4_1_call(fn, w, xq, rows, blocks, dtype):
+    xq = np.ascontiguousarray(xq)
+    cols = xq.size // blocks
+    out = np.empty(cols * rows * (blocks if dtype == np.int32 else 1), dtype=dtype)
+    getattr(lib(), fn)(ptr(w), ptr(xq), rows, blocks, cols, ptr(out))
+    return out.reshape((cols, rows, blocks) if dtype == np.int32 else (cols, rows))
+
+
+def block_dots_q4_1(w, xq, rows, blocks):
+    return _q4_1_call("o_block_dots_q4_1", w, xq, rows, blocks, np.int32)
+
+
+def matrix_serial_q4_1(w, xq, rows, blocks):
+    return _q4_1_call("o_matrix_serial_q4_1", w, xq, rows, blocks, np.float32)
+
+
+def matrix_mmvq_q4_1(w, xq, rows, blocks):
+    return _q4_1_call("o_matrix_mmvq_q4_1", w, xq, rows, blocks, np.float32)
+
+
+def expert_whole(gate, up, down, xq, hidden=HIDDEN, inter=INTER, down_type=Q4_0):
     """Unweighted expert output [columns][hidden] (reference CpuExpert 'whole' order)."""
     xq = np.ascontiguousarray(xq)
     cols = xq.size // (hidden // 32)
     out = np.empty(cols * hidden, dtype=np.float32)
     scratch = np.empty(cols * inter * 3, dtype=np.float32)
     mq = np.zeros(cols * inter // 32, dtype=Q8_DTYPE)
-    flags = lib().o_expert_whole(ptr(gate), ptr(up), ptr(down), hidden, inter, ptr(xq), cols,
-                                 ptr(out), ptr(scratch), ptr(mq))
+    flags = lib().o_expert_whole_typed(ptr(gate), ptr(up), ptr(down), down_type, hidden, inter, ptr(xq), cols,
+                                       ptr(out), ptr(scratch), ptr(mq))
     return out.reshape(cols, hidden), flags
 
 
@@ -244,10 +289,11 @@ def route_groups(ids, weights, experts=EXPERTS):
     return dict(counts=counts, offsets=offsets, token=tok, rank=rank, expert=exp, weight=wt)
 
 
-def moe_layer(x, logits, experts_fn, shared, gate_vec, tokens=None):
+def moe_layer(x, logits, experts_fn, shared, gate_vec, tokens=None, down_type=Q4_0):
     """Whole-layer oracle for the given tokens (default: all).
 
-    experts_fn(e) -> (gate, up, down) canonical bytes; shared = (gate, up, down).
+    experts_fn(e) -> (gate, up, down) canonical bytes; shared = (gate, up, down);
+    down matrices of down_type (Q4_0 or Q4_1).
     Returns (out [len(tokens)][H], ids, weights, flags).
     """
     x = np.ascontiguousarray(x, dtype=np.float32)
@@ -268,12 +314,12 @@ def moe_layer(x, logits, experts_fn, shared, gate_vec, tokens=None):
         if e not in cache:
             cache[e] = experts_fn(int(e))
         g, u, d = cache.pop(e)
-        y, f = expert_whole(g, u, d, xq[cols[:, 0]], H)
+        y, f = expert_whole(g, u, d, xq[cols[:, 0]], H, down_type=down_type)
         flags |= f
         contrib[cols[:, 0], cols[:, 1]] = y
     out = np.empty((n, H), np.float32)
     lib().o_routed_fold(ptr(contrib), ptr(np.ascontiguousarray(w)), n, H, ptr(out))
-    ys, f = expert_whole(shared[0], shared[1], shared[2], xq, H)
+    ys, f = expert_whole(shared[0], shared[1], shared[2], xq, H, down_type=down_type)
     flags |= f
     gv = np.ascontiguousarray(gate_vec, dtype=np.float32)
     lib().o_shared_add(ptr(sub_x), ptr(gv), ptr(ys), n, H, ptr(out))

@@ -25,8 +25,11 @@
 
 typedef struct { uint16_t d; uint16_t s; int8_t qs[32]; } o_q8_1;   /* src/quant.hpp:17 */
 typedef struct { uint16_t d; uint8_t qs[16]; } o_q4_0;               /* src/quant.hpp:8  */
+typedef struct { uint16_t d, m; uint8_t qs[16]; } o_q4_1;            /* src/quant.hpp:9  */
 _Static_assert(sizeof(o_q8_1) == 36, "Q8_1 ABI is 36 bytes");
 _Static_assert(sizeof(o_q4_0) == 18, "Q4_0 ABI is 18 bytes");
+_Static_assert(sizeof(o_q4_1) == 20, "Q4_1 ABI is 20 bytes");
+enum { O_Q4_0 = 2, O_Q4_1 = 3 };   /* TensorType values, src/model.hpp:17-19 */
 
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
@@ -197,6 +200,80 @@ O_EXPORT void o_matrix_mmvq(const uint8_t *w, const o_q8_1 *x, int rows, int blo
 }
 
 /* ---------------------------------------------------------------------------
+ * Q4_1 (20-byte blocks: half d, half m, 16 code bytes; value d*q + m).
+ * Block term: float(dot)*half(d4*d8) + half(m4*s8), both products rounded to
+ * half RNE (src/quant.cpp:88-102 scaled_dot<Q4_1>).
+ * ------------------------------------------------------------------------- */
+static inline float o_half_round(float v) { return o_half_to_float(o_float_to_half(v)); }
+
+/* Per-block int32 dots of a Q4_1 matrix (uncentred sum of code*activation). */
+O_EXPORT void o_block_dots_q4_1(const uint8_t *w, const o_q8_1 *x, int rows, int blocks, int columns,
+                                int32_t *dots) {
+    for (int c = 0; c < columns; ++c)
+        for (int r = 0; r < rows; ++r)
+            for (int b = 0; b < blocks; ++b) {
+                const uint8_t *blk = w + ((size_t)r * blocks + b) * 20;
+                dots[((size_t)c * rows + r) * blocks + b] = o_block_dot(blk + 4, x[(size_t)c * blocks + b].qs);
+            }
+}
+
+/* Serial product, src/quant.cpp:141-170 (matmul<false, Q4_1>): per block
+ * t = float(dot)*dd; t = t + ms; acc = acc + t (separately rounded). */
+O_EXPORT void o_matrix_serial_q4_1(const uint8_t *w, const o_q8_1 *x, int rows, int blocks, int columns,
+                                   float *out) {
+    for (int c = 0; c < columns; ++c)
+        for (int r = 0; r < rows; ++r) {
+            float acc = 0.0f;
+            for (int b = 0; b < blocks; ++b) {
+                const uint8_t *blk = w + ((size_t)r * blocks + b) * 20;
+                uint16_t hd, hm; memcpy(&hd, blk, 2); memcpy(&hm, blk + 2, 2);
+                const o_q8_1 *a = &x[(size_t)c * blocks + b];
+                const float dd = o_half_round(o_half_to_float(hd) * o_half_to_float(a->d));
+                const float ms = o_half_round(o_half_to_float(hm) * o_half_to_float(a->s));
+                const float t = (float)o_block_dot(blk + 4, a->qs) * dd;
+                acc = acc + (t + ms);
+            }
+            out[(size_t)c * rows + r] = acc;
+        }
+}
+
+/* MMVQ order for Q4_1, src/cpu_expert.cpp:156-213 (matrix_gpu_order<Q4_1>)
+ * and src/hip/linear.hip:197-211: lane 2*(b%64)+f accumulates
+ * acc + fma(float(dot_f), dd, ms*0.5) for fragment f (bytes 8f..8f+7, both
+ * nibbles); then the same 128 -> 64 merge and XOR butterfly as Q4_0. */
+O_EXPORT void o_matrix_mmvq_q4_1(const uint8_t *w, const o_q8_1 *x, int rows, int blocks, int columns,
+                                 float *out) {
+    for (int c = 0; c < columns; ++c)
+        for (int r = 0; r < rows; ++r) {
+            float lane[128];
+            for (int i = 0; i < 128; ++i) lane[i] = 0.0f;
+            for (int b = 0; b < blocks; ++b) {
+                const uint8_t *blk = w + ((size_t)r * blocks + b) * 20;
+                uint16_t hd, hm; memcpy(&hd, blk, 2); memcpy(&hm, blk + 2, 2);
+                const o_q8_1 *a = &x[(size_t)c * blocks + b];
+                const float dd = o_half_round(o_half_to_float(hd) * o_half_to_float(a->d));
+                const float ms = o_half_round(o_half_to_float(hm) * o_half_to_float(a->s));
+                for (int f = 0; f < 2; ++f) {
+                    int dot = 0;
+                    for (int j = 8 * f; j < 8 * f + 8; ++j) {
+                        dot += (int)(blk[4 + j] & 15u) * (int)a->qs[j];
+                        dot += (int)(blk[4 + j] >> 4) * (int)a->qs[j + 16];
+                    }
+                    float *acc = &lane[2 * (b % 64) + f];
+                    *acc = *acc + fmaf((float)dot, dd, ms * 0.5f);
+                }
+            }
+            for (int i = 0; i < 64; ++i) lane[i] = lane[i] + lane[i + 64];
+            for (int mask = 1; mask < 64; mask <<= 1) {
+                float next[64];
+                for (int i = 0; i < 64; ++i) next[i] = lane[i] + lane[i ^ mask];
+                memcpy(lane, next, sizeof(next));
+            }
+            out[(size_t)c * rows + r] = lane[0];
+        }
+}
+
+/* ---------------------------------------------------------------------------
  * Whole expert for `columns` tokens: gate/up in MMVQ order, host-libm SiLU
  * g/(1+expf(-g)) * u, requantise the middle, down in MMVQ order.
  * src/cpu_expert.cpp:216-272 (execute, whole stage), shape-generic.
@@ -205,9 +282,20 @@ O_EXPORT void o_matrix_mmvq(const uint8_t *w, const o_q8_1 *x, int rows, int blo
  * xq: [columns][hidden/32]; out: [columns][hidden]; scratch >= columns*(3*inter)
  * floats and mq >= columns*inter/32 blocks.
  * ------------------------------------------------------------------------- */
+O_EXPORT int o_expert_whole_typed(const uint8_t *gate, const uint8_t *up, const uint8_t *down, int down_type,
+                                  int hidden, int inter, const o_q8_1 *xq, int columns,
+                                  float *out, float *scratch, o_q8_1 *mq);
 O_EXPORT int o_expert_whole(const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                             int hidden, int inter, const o_q8_1 *xq, int columns,
                             float *out, float *scratch, o_q8_1 *mq) {
+    return o_expert_whole_typed(gate, up, down, O_Q4_0, hidden, inter, xq, columns, out, scratch, mq);
+}
+
+/* As o_expert_whole with a Q4_0 (2) or Q4_1 (3) down matrix
+ * (src/cpu_expert.cpp:216-228 picks matrix_gpu_order by the down type). */
+O_EXPORT int o_expert_whole_typed(const uint8_t *gate, const uint8_t *up, const uint8_t *down, int down_type,
+                                  int hidden, int inter, const o_q8_1 *xq, int columns,
+                                  float *out, float *scratch, o_q8_1 *mq) {
     float *g = scratch, *u = scratch + (size_t)columns * inter, *mid = u + (size_t)columns * inter;
     o_matrix_mmvq(gate, xq, inter, hidden / 32, columns, g);
     o_matrix_mmvq(up, xq, inter, hidden / 32, columns, u);
@@ -225,7 +313,8 @@ O_EXPORT int o_expert_whole(const uint8_t *gate, const uint8_t *up, const uint8_
         flags |= f;
     }
     flags |= o_quantize_q8_1(mid, (size_t)columns * inter, mq);
-    o_matrix_mmvq(down, mq, hidden, inter / 32, columns, out);
+    if (down_type == O_Q4_1) o_matrix_mmvq_q4_1(down, mq, hidden, inter / 32, columns, out);
+    else o_matrix_mmvq(down, mq, hidden, inter / 32, columns, out);
     return flags;
 }
 
@@ -469,6 +558,39 @@ O_EXPORT void o_synth_q4_0(uint64_t seed, uint32_t layer, uint32_t expert, uint3
     }
 }
 
+/* Q4_1 version of the generator (for Q4_1 down matrices): the same codes
+ * and scale d as o_synth_q4_0, plus the minimum m = half(-8*d*(0.5 + u/65536))
+ * with u the low 16 bits of draw 34 of the block. */
+O_EXPORT void o_synth_q4_1(uint64_t seed, uint32_t layer, uint32_t expert, uint32_t matrix,
+                           size_t nblocks, uint8_t *out) {
+    const uint64_t base = o_synth_base(seed, layer, expert, matrix);
+    uint8_t q40[18];
+    for (size_t i = 0; i < nblocks; ++i) {
+        /* one Q4_0 block of the same stream position */
+        const uint64_t c0 = o_mix64(base + (i << 6) + 0), c1 = o_mix64(base + (i << 6) + 1);
+        for (int j = 0; j < 8; ++j) {
+            q40[2 + j] = (uint8_t)(c0 >> (8 * j));
+            q40[10 + j] = (uint8_t)(c1 >> (8 * j));
+        }
+        uint32_t mx = 0;
+        for (int j = 2; j < 34; ++j) {
+            const uint64_t r = o_mix64(base + (i << 6) + (uint64_t)j);
+            const uint32_t s = (uint32_t)(r & 0xffffu) + (uint32_t)((r >> 16) & 0xffffu) +
+                               (uint32_t)((r >> 32) & 0xffffu) + (uint32_t)(r >> 48);
+            const uint32_t dev = s >= 131070u ? s - 131070u : 131070u - s;
+            mx = dev > mx ? dev : mx;
+        }
+        const uint16_t d = o_float_to_half((float)mx * 6.6073582e-08f);
+        const uint64_t r = o_mix64(base + (i << 6) + 34);
+        const float f = 0.5f + (float)(uint32_t)(r & 0xffffu) * (1.0f / 65536.0f);
+        const uint16_t m = o_float_to_half((-8.0f * o_half_to_float(d)) * f);
+        uint8_t *blk = out + i * 20;
+        memcpy(blk, &d, 2);
+        memcpy(blk + 2, &m, 2);
+        memcpy(blk + 4, q40 + 2, 16);
+    }
+}
+
 /* ---------------------------------------------------------------------------
  * The reference test fixture's Q4_0 weights (tests/cpu_expert_test.cpp:227-246):
  * block i has scale (2 + (i*7 + state) % 11)/2048, negated when
@@ -485,6 +607,25 @@ O_EXPORT void o_fixture_xorshift_q4_0(uint32_t seed, size_t nblocks, uint8_t *ou
             seed ^= seed >> 17;
             seed ^= seed << 5;
             out[i * 18 + 2 + j] = (uint8_t)(seed & 255u);
+        }
+    }
+}
+
+/* The same fixture for Q4_1 matrices (tests/cpu_expert_test.cpp:219-241):
+ * 20-byte blocks with the same scale and codes and the minimum
+ * half(-7.5 * scale) of the unsigned scale. */
+O_EXPORT void o_fixture_xorshift_q4_1(uint32_t seed, size_t nblocks, uint8_t *out) {
+    for (size_t i = 0; i < nblocks; ++i) {
+        const float scale = (float)(2 + (i * 7 + seed) % 11) / 2048.0f;
+        const uint16_t d = o_float_to_half((i + seed) % 3 == 0 ? -scale : scale);
+        const uint16_t m = o_float_to_half(-7.5f * scale);
+        memcpy(out + i * 20, &d, 2);
+        memcpy(out + i * 20 + 2, &m, 2);
+        for (int j = 0; j < 16; ++j) {
+            seed ^= seed << 13;
+            seed ^= seed >> 17;
+            seed ^= seed << 5;
+            out[i * 20 + 4 + j] = (uint8_t)(seed & 255u);
         }
     }
 }

@@ -107,6 +107,15 @@ void* ref_expert_new(const void* gate, const void* up, const void* down, std::si
                              view(2, inter, hidden, down, down_bytes));
     } catch (const std::exception& e) { remember(e); return nullptr; }
 }
+// down_type: the reference's TensorType value of the down matrix (2 Q4_0, 3 Q4_1).
+void* ref_expert_new_typed(const void* gate, const void* up, const void* down, int down_type,
+                           std::size_t gate_bytes, std::size_t down_bytes, int hidden, int inter) {
+    try {
+        return new CpuExpert(view(2, hidden, inter, gate, gate_bytes),
+                             view(2, hidden, inter, up, gate_bytes),
+                             view(down_type, inter, hidden, down, down_bytes));
+    } catch (const std::exception& e) { remember(e); return nullptr; }
+}
 void ref_expert_free(void* h) { delete static_cast<CpuExpert*>(h); }
 
 // CpuExpertStatus as int. inputs: `columns` pointers to Q8_1 spans of

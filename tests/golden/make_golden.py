@@ -16,7 +16,12 @@ Fixtures:
 * expert_2048.npz   -- seeded synthetic weights (the repository generator) at
   2048/512 with run_cpu_expert outputs of the shape-patched reference build;
 * routes.npz        -- RouteGroups::prepare on the reference test's fixture
-  patterns (tests/routes_test.cpp:89-112) for several token counts.
+  patterns (tests/routes_test.cpp:89-112) for several token counts;
+* expert_q4_1.npz   -- Q4_1 down matrices: the reference cpu_expert test's
+  Fixture(TensorType::Q4_1) at 2560/640 (tests/cpu_expert_test.cpp:219-261)
+  and the repository's seeded Q4_1 generator at 2048/512, each with the
+  reference run_cpu_expert 'whole' outputs, plus matmul_scalar outputs of a
+  generated Q4_1 matrix.
 """
 import ctypes
 import os
@@ -117,6 +122,56 @@ def expert_2048():
                 out=out.reshape(3, H))
 
 
+def _run_expert(R, g, u, d, down_type, H, I, cols):
+    h = R.ref_expert_new_typed(O.ptr(g), O.ptr(u), O.ptr(d), down_type, g.size, d.size, H, I)
+    assert h, R.ref_last_message()
+    ptrs = (ctypes.c_void_p * 3)(*[cols[c].ctypes.data for c in range(3)])
+    out = np.zeros(3 * H, np.float32)
+    assert R.ref_run_cpu_expert(h, 3, ptrs, H // 32, 0, O.ptr(out), out.size) == 0, R.ref_last_message()
+    R.ref_expert_free(h)
+    return out.reshape(3, H)
+
+
+def expert_q4_1():
+    out = {}
+    # reference fixture, native shape
+    RN = O.ref_native()
+    H, I = 2560, 640
+    gate = O.fixture_xorshift_q4_0(0x70af451, I, H // 32)
+    up = O.fixture_xorshift_q4_0(0xa5f726e, I, H // 32)
+    down = O.fixture_xorshift_q4_1(0x525a31, H, I // 32)
+    floats = (np.float32(0.7) * np.sin(np.arange(10240, dtype=np.float32) * np.float32(0.137)).astype(np.float32)
+              + np.float32(0.2) * np.cos(np.arange(10240, dtype=np.float32) * np.float32(0.071)).astype(np.float32))
+    floats = np.ascontiguousarray(floats, dtype=np.float32)
+    q = np.zeros(320, O.Q8_DTYPE)
+    assert RN.ref_quantize_q8(O.ptr(floats), floats.size, O.ptr(q)) == 0
+    cols = np.ascontiguousarray(np.stack([q[s:s + 80] for s in (0, 160, 80)]))
+    out["native_xq"] = cols.view(np.uint8).reshape(3, 80 * 36)
+    out["native_out"] = _run_expert(RN, gate, up, down, 3, H, I, cols)
+    # repository generator, 2048/512
+    R = O.ref()
+    H, I, seed = 2048, 512, 41
+    g, u, d = O.synth_expert(seed, 2, 33, down_type=O.Q4_1)
+    x = np.random.default_rng(9).standard_normal((3, H)).astype(np.float32)
+    q = np.zeros((3, H // 32), O.Q8_DTYPE)
+    for c in range(3):
+        assert R.ref_quantize_q8(O.ptr(x[c]), H, O.ptr(q[c])) == 0
+    out["seed"] = np.array([seed, 2, 33])
+    out["x"] = x
+    out["out"] = _run_expert(R, g, u, d, 3, H, I, q)
+    # matmul_scalar of one generated Q4_1 matrix (rows 2048, K 512)
+    w = O.synth_q4_1(5, 1, 2, 2, 2048, 16)
+    xm = np.random.default_rng(10).standard_normal((3, 512)).astype(np.float32)
+    qm = np.zeros((3, 16), O.Q8_DTYPE)
+    for c in range(3):
+        assert R.ref_quantize_q8(O.ptr(xm[c]), 512, O.ptr(qm[c])) == 0
+    mo = np.zeros(3 * 2048, np.float32)
+    assert R.ref_matmul(0, 3, 512, 2048, O.ptr(w), w.size, O.ptr(qm), qm.size, 3, O.ptr(mo), mo.size) == 0
+    out["matmul_x"] = xm
+    out["matmul_out"] = mo.reshape(3, 2048)
+    return out
+
+
 def route_fixture(tokens, pattern):
     # tests/routes_test.cpp:89-112
     repeated = [511, 0, 510, 1, 127, 255, 256, 257, 400, 41]
@@ -160,6 +215,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "expert_native.npz"), **expert_native())
     np.savez_compressed(os.path.join(HERE, "expert_2048.npz"), **expert_2048())
     np.savez_compressed(os.path.join(HERE, "routes.npz"), **routes())
+    np.savez_compressed(os.path.join(HERE, "expert_q4_1.npz"), **expert_q4_1())
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

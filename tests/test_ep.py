@@ -63,8 +63,9 @@ def test_handle_exchange_two_ranks_gloo():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("tokens,routing", [(8, "normal"), (100, "normal"), (300, "zipf")])
-def test_ep_world1_matches_forward(pkg, tokens, routing):
+@pytest.mark.parametrize("tokens,routing,down_type", [(8, "normal", 2), (100, "normal", 2), (300, "zipf", 2),
+                                                      (8, "normal", 3), (300, "zipf", 3)])
+def test_ep_world1_matches_forward(pkg, tokens, routing, down_type):
     import torch
     desc = pkg.make_desc(max_tokens=tokens)
     rng = np.random.default_rng(tokens)
@@ -77,12 +78,12 @@ def test_ep_world1_matches_forward(pkg, tokens, routing):
         lg = rng.standard_normal((tokens, 512)).astype(np.float32)
     logits = torch.from_numpy(lg).cuda()
     gate = (rng.standard_normal(2048) * 0.05).astype(np.float32)
-    full = pkg.MoeWeights(desc)
+    full = pkg.MoeWeights(desc, down_type)
     full.synthesize(3, 1)
     full.upload_shared_gate(gate)
     ref = torch.zeros(tokens, 2048, device="cuda")
     pkg.MoeLayer(desc).forward(full, x, logits, ref)
-    shard = pkg.EpWeights(desc, 0, 1)
+    shard = pkg.EpWeights(desc, 0, 1, down_type)
     shard.synthesize(3, 1)
     shard.upload_shared_gate(gate)
     ep = pkg.EpLayer(desc, 0, 1)

@@ -131,14 +131,14 @@ def test_route_bit_exact(pkg, O, torch, T, kind):
 
 # -------------------------------------------------------------------- layer --
 class LayerCase:
-    def __init__(self, pkg, O, torch, T, seed, logits_kind="normal", max_tokens=None):
-        self.pkg, self.O, self.T, self.seed = pkg, O, T, seed
+    def __init__(self, pkg, O, torch, T, seed, logits_kind="normal", max_tokens=None, down_type=2):
+        self.pkg, self.O, self.T, self.seed, self.down_type = pkg, O, T, seed, down_type
         rng = np.random.default_rng(seed)
         self.x = rng.standard_normal((T, H)).astype(np.float32)
         self.logits = zipf_logits(rng, T) if logits_kind == "zipf" else rng.standard_normal((T, E)).astype(np.float32)
         self.gate_vec = (rng.standard_normal(H) * 0.02).astype(np.float32)
         self.desc = pkg.make_desc(max_tokens=max_tokens or T)
-        self.weights = pkg.MoeWeights(self.desc)
+        self.weights = pkg.MoeWeights(self.desc, down_type)
         self.weights.synthesize(seed, 0)
         self.weights.upload_shared_gate(self.gate_vec)
         self.layer = pkg.MoeLayer(self.desc)
@@ -147,8 +147,10 @@ class LayerCase:
 
     def oracle(self, tokens=None):
         O, seed = self.O, self.seed
-        out, ids, w, flags = O.moe_layer(self.x, self.logits, lambda e: O.synth_expert(seed, 0, e),
-                                         O.synth_expert(seed, 0, 512), self.gate_vec, tokens)
+        dt = self.down_type
+        out, ids, w, flags = O.moe_layer(self.x, self.logits, lambda e: O.synth_expert(seed, 0, e, down_type=dt),
+                                         O.synth_expert(seed, 0, 512, down_type=dt), self.gate_vec, tokens,
+                                         down_type=dt)
         return out
 
 
@@ -248,3 +250,63 @@ def test_gpu_expert_api(pkg, O, torch):
     want, _ = O.expert_whole(g, u, d, xq)
     assert_close(y, want)
     assert timing["resident_ms"] > 0
+
+
+# ------------------------------------------------------------------- Q4_1 --
+# Q4_1 down matrices (the reference's layers 0-5): block term
+# acc + fma(dot, half(d4*d8), half(m4*s8)).
+@pytest.mark.parametrize("rows,k,cols", [(2048, 512, 5), (96, 64, 1)])
+def test_q4_1_linear_dots_bit_exact(pkg, O, torch, rows, k, cols):
+    rng = np.random.default_rng(rows + 3 * cols)
+    w = O.synth_q4_1(8, 1, rows % 5, 2, rows, k // 32)
+    xq, _ = O.quantize(rng.standard_normal((cols, k)).astype(np.float32))
+    out, dots = pkg.q4_1_linear(torch.from_numpy(w).cuda(), rows, k,
+                                torch.from_numpy(xq.view(np.uint8).reshape(cols, -1).copy()).cuda(), cols,
+                                with_dots=True)
+    assert np.array_equal(dots.cpu().numpy(), O.block_dots_q4_1(w, xq, rows, k // 32))
+    ref = O.matrix_serial_q4_1(w, xq, rows, k // 32)
+    assert np.all(np.abs(out.cpu().numpy() - ref) <= 2e-4 + 2e-5 * np.abs(ref))
+
+
+def test_q4_1_weights_generator_and_roundtrip(pkg, O, torch):
+    desc = pkg.make_desc(max_tokens=1)
+    w = pkg.MoeWeights(desc, pkg.MOE_Q4_1)
+    w.synthesize(99, 7)
+    torch.cuda.synchronize()
+    for e in (0, 300, 512):
+        for a, b in zip(w.download_expert(e), O.synth_expert(99, 7, e, down_type=O.Q4_1)):
+            assert np.array_equal(a, b), e
+    g, u, d = O.synth_expert(1, 1, 1, down_type=O.Q4_1)
+    w.upload_expert(3, g, u, d)
+    for a, b in zip(w.download_expert(3), (g, u, d)):
+        assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("T,kind", [(1, "normal"), (8, "normal"), (33, "normal"), (300, "zipf")])
+def test_q4_1_forward_matches_oracle(pkg, O, torch, T, kind):
+    """Decode sizes on the streaming kernels and prefill sizes (all groups on
+    the dp4a kernels: no tensor-core path for Q4_1 down)."""
+    c = LayerCase(pkg, O, torch, T, seed=500 + T, logits_kind=kind, down_type=pkg.MOE_Q4_1)
+    out = torch.zeros(T, H, device="cuda")
+    c.layer.forward(c.weights, c.xd, c.ld, out, accumulate=False)
+    torch.cuda.synchronize()
+    assert c.layer.read_flags() == 0
+    sample = None if T <= 33 else np.random.default_rng(1).choice(T, 12, replace=False)
+    got = out.cpu().numpy() if sample is None else out.cpu().numpy()[sample]
+    assert_close(got, c.oracle(sample))
+
+
+def test_q4_1_gpu_expert_api(pkg, O, torch):
+    """GpuExpert with the reference's native type mix (Q4_0 gate/up, Q4_1 down)."""
+    g, u, d = O.synth_expert(4, 0, 9, down_type=O.Q4_1)
+    ex = pkg.GpuExpert(g, u, d, max_columns=5, down_type=pkg.MOE_Q4_1)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((5, H)).astype(np.float32)
+    xq, _ = O.quantize(x)
+    mid, _ = O.quantize(rng.standard_normal((5, I)).astype(np.float32))
+    got = ex.linear(True, False, mid, 5)
+    ref = O.matrix_serial_q4_1(d, mid, H, I // 32)
+    assert np.all(np.abs(got - ref) <= 2e-4 + 2e-5 * np.abs(ref))
+    y, _ = ex.run(x, 5, repeats=2)
+    want, _ = O.expert_whole(g, u, d, xq, down_type=O.Q4_1)
+    assert_close(y, want)

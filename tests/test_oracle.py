@@ -251,3 +251,103 @@ def test_layer_oracle_composition(O):
         acc[t] += ys[0] / (1 + math.exp(-raw))
     rms = np.sqrt(np.mean(acc ** 2))
     assert np.max(np.abs(out - acc)) <= 1e-5 * rms
+
+
+# ------------------------------------------------------------------- Q4_1 --
+def _q4_1_rows(d, m, codes):
+    w = np.zeros((len(codes), 20), np.uint8)
+    for r, c in enumerate(codes):
+        w[r, 0:2] = np.array([d], np.uint16).view(np.uint8)
+        w[r, 2:4] = np.array([m], np.uint16).view(np.uint8)
+        w[r, 4:] = c
+    return w.ravel()
+
+
+def test_q4_1_literal_matrix_known_answer(O):
+    # tests/quant_test.cpp:575-603: Q4_1 (d 1, m 0.5) expected {-79, -207, -6145.5, -24577.5}
+    x = np.zeros(2, O.Q8_DTYPE)
+    x["d"] = 0x3c00
+    x[0]["s"], x[1]["s"] = 0x4000, 0xc200
+    x[0]["qs"] = [3] * 16 + [-4] * 16
+    x[1]["qs"] = [-128] * 32
+    w = _q4_1_rows(0x3c00, 0x3800, (0x21, 0x75))
+    want = [-79.0, -207.0, -6145.5, -24577.5]
+    assert O.matrix_serial_q4_1(w, x, 2, 1).ravel().tolist() == want
+    assert O.matrix_mmvq_q4_1(w, x, 2, 1).ravel().tolist() == want
+
+
+def test_q4_1_half_rounded_products(O):
+    # tests/quant_test.cpp:480-500: the products d4*d8 and m4*s8 are rounded to half
+    x = np.zeros(1, O.Q8_DTYPE)
+    x["d"], x["s"] = 0x3c01, 0x3c01
+    x[0]["qs"] = [127] * 32
+    w = _q4_1_rows(0x3c01, 0xbc01, (0xff,))
+    got = O.matrix_serial_q4_1(w, x, 1, 1).item()
+    h = O.lib().o_half_to_float
+    dd = np.float32(h(O.lib().o_float_to_half(np.float32(h(0x3c01)) * np.float32(h(0x3c01)))))
+    ms = np.float32(h(O.lib().o_float_to_half(np.float32(h(0xbc01)) * np.float32(h(0x3c01)))))
+    assert got == np.float32(np.float32(32 * 15 * 127) * dd) + ms
+    unrounded = float(32 * 15 * 127) * h(0x3c01) * h(0x3c01) + h(0xbc01) * h(0x3c01)
+    assert abs(unrounded - got) > 0.01
+    # 2^-14 * 2^-14 rounds to half zero; the offset m*s = 0.5 * 3 remains
+    x["d"], x["s"] = 0x0400, 0x4200
+    w = _q4_1_rows(0x0400, 0x3800, (0xff,))
+    assert O.matrix_serial_q4_1(w, x, 1, 1).item() == 1.5
+
+
+def test_q4_1_block_dots_and_serial_match_golden(O):
+    g = golden("expert_q4_1.npz")
+    w = O.synth_q4_1(5, 1, 2, 2, 2048, 16)
+    xq, _ = O.quantize(g["matmul_x"])
+    out = O.matrix_serial_q4_1(w, xq, 2048, 16)
+    assert np.array_equal(out.view(np.uint32), g["matmul_out"].view(np.uint32))
+    # uncentred block dots: the Q4_0 dot routine over the same code bytes
+    dots = O.block_dots_q4_1(w, xq, 2048, 16)
+    w0 = np.concatenate([np.zeros((2048 * 16, 2), np.uint8), w.reshape(-1, 20)[:, 4:]], axis=1).ravel()
+    assert np.array_equal(dots, O.block_dots(w0, xq, 2048, 16))
+
+
+def test_q4_1_serial_matches_reference(O):
+    R = _ref_or_skip(O)
+    rng = np.random.default_rng(12)
+    for rows, blocks in ((512, 64), (2048, 16), (7, 3)):
+        w = O.synth_q4_1(9, 0, 1, 2, rows, blocks)
+        xq, _ = O.quantize(rng.standard_normal((3, blocks * 32)).astype(np.float32))
+        a = O.matrix_serial_q4_1(w, xq, rows, blocks)
+        for avx2 in (0, 1):
+            out = np.zeros(3 * rows, np.float32)
+            assert R.ref_matmul(avx2, 3, blocks * 32, rows, O.ptr(w), w.size, O.ptr(xq), xq.size, 3, O.ptr(out),
+                                out.size) == 0
+            assert np.array_equal(a.ravel().view(np.uint32), out.view(np.uint32))
+
+
+def test_q4_1_expert_whole_matches_reference_fixtures(O):
+    g = golden("expert_q4_1.npz")
+    # the reference cpu_expert test's Fixture(TensorType::Q4_1) at 2560/640
+    H, I = 2560, 640
+    gate = O.fixture_xorshift_q4_0(0x70af451, I, H // 32)
+    up = O.fixture_xorshift_q4_0(0xa5f726e, I, H // 32)
+    down = O.fixture_xorshift_q4_1(0x525a31, H, I // 32)
+    xq = np.ascontiguousarray(g["native_xq"]).view(O.Q8_DTYPE).reshape(3, 80)
+    out, flags = O.expert_whole(gate, up, down, xq, H, I, down_type=O.Q4_1)
+    assert flags == 0
+    assert np.array_equal(out.view(np.uint32), g["native_out"].view(np.uint32))
+    # the repository's Q4_1 generator at 2048/512
+    seed, layer, expert = (int(v) for v in g["seed"])
+    gate, up, down = O.synth_expert(seed, layer, expert, down_type=O.Q4_1)
+    xq, _ = O.quantize(g["x"])
+    out, flags = O.expert_whole(gate, up, down, xq, down_type=O.Q4_1)
+    assert flags == 0
+    assert np.array_equal(out.view(np.uint32), g["out"].view(np.uint32))
+
+
+def test_q4_1_generator(O):
+    """Q4_1 down matrices share the Q4_0 generator's codes and scales; the
+    minimum lies in [-12 d, -4 d]."""
+    w1 = O.synth_q4_1(3, 4, 5, 2, 64, 16).reshape(-1, 20)
+    w0 = O.synth_q4_0(3, 4, 5, 2, 64, 16).reshape(-1, 18)
+    assert np.array_equal(w1[:, :2], w0[:, :2]) and np.array_equal(w1[:, 4:], w0[:, 2:])
+    h = O.lib().o_half_to_float
+    d = np.array([h(int(v)) for v in w1[:, :2].copy().view(np.uint16).ravel()])
+    m = np.array([h(int(v)) for v in w1[:, 2:4].copy().view(np.uint16).ravel()])
+    assert np.all(m <= -4 * d * (1 - 1e-3)) and np.all(m >= -12 * d * (1 + 1e-3))
