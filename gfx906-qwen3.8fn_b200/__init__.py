@@ -40,6 +40,7 @@ EXPORTED = [
     "moe_route_noalloc", "moe_ep_weights_create", "moe_ep_create", "moe_ep_destroy", "moe_ep_ipc_handle",
     "moe_ep_open_peers", "moe_ep_forward", "moe_ep_read_flags",
     "moe_weights_create_typed", "moe_ep_weights_create_typed", "moe_q4_1_linear", "moe_expert_create_typed",
+    "moe_forward_contributions",
 ]
 
 
@@ -107,6 +108,7 @@ def library(path=LIB_PATH):
         "moe_ep_weights_create_typed": (I, [DESC_P, I, I, I, ctypes.POINTER(P)]),
         "moe_weights_create_typed": (I, [DESC_P, I, ctypes.POINTER(P)]),
         "moe_q4_1_linear": (I, [P, I, I, P, I, P, P, P]),
+        "moe_forward_contributions": (I, [P, P, P, P, I, P, P, P, I, P]),
         "moe_expert_create_typed": (I, [P, P, P, I, I, I, I, I, ctypes.POINTER(P)]),
         "moe_ep_create": (I, [DESC_P, I, I, ctypes.POINTER(P)]),
         "moe_ep_destroy": (I, [P]),
@@ -225,6 +227,18 @@ class MoeLayer(_Owned):
         flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
         check(library().moe_forward(self.handle, weights.handle, _ptr(x), _ptr(logits), T, _ptr(out), flag,
                                     _stream(stream)))
+
+    def forward_contributions(self, weights, x, logits, out, accumulate=True, stream=None):
+        """Deterministic trace mode: out (+)= the reference-order fold of the per-(token, rank)
+        contributions.  Returns (contrib [T][10][H], shared [T][H] or None) as cuda tensors."""
+        import torch
+        T, H = x.shape
+        contrib = torch.empty(T, TOP_K, H, device=x.device)
+        shared = torch.empty(T, H, device=x.device) if self.desc.has_shared else None
+        flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
+        check(library().moe_forward_contributions(self.handle, weights.handle, _ptr(x), _ptr(logits), T,
+                                                  _ptr(contrib), _ptr(shared), _ptr(out), flag, _stream(stream)))
+        return contrib, shared
 
     def forward_profiled(self, weights, x, logits, out, events, accumulate=True, stream=None):
         """forward() recording torch.cuda.Event objects [before gate/up, before down, after down]."""

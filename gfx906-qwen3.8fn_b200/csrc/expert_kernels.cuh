@@ -180,6 +180,35 @@ repack_q4_1_kernel(uint8_t *canonical, uint8_t *codes, uint16_t *scales, uint16_
     }
 }
 
+// Where the rows of a down projection go.  Normally the router-weighted
+// scatter-add into the residual (red.global.add, sanitised).  In trace mode
+// (contrib non-null) the raw, unweighted row of pair (token, rank) is stored
+// at contrib[token][rank][H] -- the reference's moe_scatter layout
+// (src/hip/session_ops.hip:358-373) -- and the shared expert's row at
+// shared[token][H]; the fold kernel then applies the reference's rank-order
+// fold and sigmoid-gated shared add.
+struct DownSink {
+    float *out;
+    float *contrib = nullptr;
+    float *shared = nullptr;
+    const int32_t *pair_rank = nullptr;   // rank of each routed pair
+    int shared_expert = 0;                // expert index of the shared expert's tiles
+    __device__ __forceinline__ void put(int e, int p0, int tok, int j, int row, int H, float v, float w,
+                                        int *error) const {
+        if (contrib) {
+            float *dst = e == shared_expert ? shared + static_cast<size_t>(tok) * H
+                                            : contrib + (static_cast<size_t>(tok) * kTopK + pair_rank[p0 + j]) * H;
+            dst[row] = v;
+            return;
+        }
+        int flags = 0;
+        const float y = arithmetic(v, flags);
+        const float c = arithmetic(__fmul_rn(w, y), flags);
+        atomicAdd(out + static_cast<size_t>(tok) * H + row, c);
+        report(flags, error);
+    }
+};
+
 // ---------------------------------------------------------------------------
 // Shared parameters of the grouped expert kernels.
 struct GroupParams {
@@ -191,7 +220,7 @@ struct GroupParams {
     const int *num_tiles;
     const int32_t *pair_token;
     const float *pair_weight;
-    float *out;                 // [T][H]
+    DownSink sink;              // out [T][H] (or the trace-mode buffers)
     int *error;
 };
 
@@ -364,15 +393,47 @@ down_kernel(GroupParams p) {
             acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 2);
         }
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            if (j < n && (j & 3) == q) {
-                int flags = 0;
-                const float y = arithmetic(acc[j], flags);
-                const float c = arithmetic(__fmul_rn(swt[j], y), flags);
-                atomicAdd(p.out + static_cast<size_t>(stok[j]) * H + row, c);
-                report(flags, p.error);
-            }
+        for (int j = 0; j < NT; ++j)
+            if (j < n && (j & 3) == q) p.sink.put(e, p0, stok[j], j, row, H, acc[j], swt[j], p.error);
+    }
+}
+
+// Trace-mode fold over the stored contributions, element (t, c) per thread,
+// in the reference's order: routed_fold (src/hip/session_ops.hip:305-324,
+// ten separately rounded multiply/adds over ranks 0..9 from 0, zero on any
+// flag), then shared_sigmoid_add (:376-391, scale * shared added to that,
+// zero on any flag; the scale is the shared gate's sigmoid computed by the
+// routing kernel with the same operations), then out = value (overwrite)
+// or out + value.
+__global__ void __launch_bounds__(256)
+fold_kernel(const float *contrib, const float *weights, const float *shared, const float *shared_scale, int T, int H,
+            float *out, int overwrite, int *error) {
+    const size_t total = static_cast<size_t>(T) * H;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t t = i / H, c = i % H;
+        int flags = 0;
+        float value = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kTopK; ++r) {
+            const float x = operand(contrib[(t * kTopK + r) * H + c], flags);
+            const float scale = operand(weights[t * kTopK + r], flags);
+            const float contribution = arithmetic(__fmul_rn(scale, x), flags);
+            value = arithmetic(__fadd_rn(value, contribution), flags);
         }
+        value = flags ? 0.0f : value;
+        report(flags, error);
+        if (shared) {
+            int f2 = 0;
+            const float x = operand(shared[i], f2);
+            const float original = operand(value, f2);
+            const float scale = operand(shared_scale[t], f2);
+            const float contribution = arithmetic(__fmul_rn(scale, x), f2);
+            const float v = arithmetic(__fadd_rn(original, contribution), f2);
+            value = f2 ? 0.0f : v;
+            report(f2, error);
+        }
+        out[i] = overwrite ? value : __fadd_rn(out[i], value);
     }
 }
 

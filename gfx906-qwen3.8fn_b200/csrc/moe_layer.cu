@@ -188,7 +188,7 @@ GroupParams group_params(moe_layer_s *h, const moe_weights_s *w, float *out) {
     g.num_tiles = h->num_tiles;
     g.pair_token = h->pair_token;
     g.pair_weight = h->pair_weight;
-    g.out = out;
+    g.sink.out = out;
     g.error = h->error;
     return g;
 }
@@ -223,8 +223,11 @@ int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, 
 }
 
 int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_tiles, cudaStream_t s,
-                   void *const *events = nullptr, int tc_tiles = 0) {
+                   void *const *events = nullptr, int tc_tiles = 0, const DownSink *trace = nullptr) {
     const ExpertLayout &L = w->layout;
+    DownSink sink;
+    if (trace) sink = *trace;
+    sink.out = out;
     if (h->gu_stages) {
         StreamParams sp;
         sp.weights = w->base;
@@ -233,7 +236,7 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         sp.mid = h->mid;
         sp.tiles = h->tiles;
         sp.num_tiles = h->num_tiles;
-        sp.out = out;
+        sp.sink = sink;
         sp.error = h->error;
         const int gu_items = max_tiles * (L.inter / kGuRows), dn_items = max_tiles * (L.hidden / kDnRows);
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[0]), s));
@@ -259,6 +262,7 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         return MOE_OK;
     }
     GroupParams g = group_params(h, w, out);
+    g.sink = sink;
     const int slabs = L.inter / 32, dslabs = L.hidden / 64;
     const int gu_grid = std::max(1, std::min(max_tiles * slabs, h->sms * 8));
     const int dn_grid = std::max(1, std::min(max_tiles * dslabs, h->sms * 8));
@@ -281,7 +285,8 @@ int launch_quantize(const float *x, size_t blocks, Q8Planar out, uint8_t *canoni
 }
 
 int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const float *logits, int T,
-                 float *probs, cudaStream_t s, const EpParams *ep = nullptr, uint32_t *quant_done = nullptr) {
+                 float *probs, cudaStream_t s, const EpParams *ep = nullptr, uint32_t *quant_done = nullptr,
+                 bool allow_tc = true) {
     const int chunks = (T + kChunk - 1) / kChunk;
     RouteParams rp;
     rp.logits = logits;
@@ -332,7 +337,7 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     sp.num_tiles = h->num_tiles;
     sp.max_tiles = h->tiles_max;
     sp.error = h->error;
-    if (x && (!w || w->layout.down_type == kDownQ4_0)) {   // forward: large groups go to the tensor-core kernels
+    if (x && allow_tc && (!w || w->layout.down_type == kDownQ4_0)) {   // forward: large groups go to the tensor-core kernels
         // (Q4_1 down matrices run every group on the dp4a kernels)
         sp.tc_min = kTcMinGroup;
         sp.tc_tile = kTcM;
@@ -626,6 +631,54 @@ int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const f
     const bool tc_ok = tokens > kChunk && w->layout.down_type == kDownQ4_0;
     const int tc_tiles = tc_ok ? std::min(h->tc.max_tiles, pairs / kTcMinGroup + pairs / kTcM + 1) : 0;
     return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events, tc_tiles);
+}
+
+int moe_forward_contributions(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens,
+                              float *contrib, float *shared, float *out, int flags, void *stream) {
+    if (!h || !w) return fail(MOE_INVALID_ARGUMENT, "null layer or weights");
+    if (std::memcmp(&h->desc, &w->desc, offsetof(moe_layer_desc, device) + sizeof(int)) != 0)
+        return fail(MOE_INVALID_ARGUMENT, "layer and weights describe different shapes or devices");
+    if (tokens < 1 || tokens > h->desc.max_tokens) return fail(MOE_INVALID_ARGUMENT, "tokens outside 1..max_tokens");
+    if (flags != MOE_OUT_ACCUMULATE && flags != MOE_OUT_OVERWRITE) return fail(MOE_INVALID_ARGUMENT, "bad flags");
+    const int H = h->desc.hidden;
+    const size_t xbytes = static_cast<size_t>(tokens) * H * 4, lbytes = static_cast<size_t>(tokens) * kRouterExperts * 4;
+    const size_t cbytes = xbytes * kTopK;
+    if (!aligned(x, 16) || !aligned(logits, 16) || !aligned(out, 16) || !aligned(contrib, 16) ||
+        (h->desc.has_shared && !aligned(shared, 16)) || (!h->desc.has_shared && shared))
+        return fail(MOE_INVALID_ARGUMENT, "x, logits, out, contributions (and shared, exactly when the layer has a "
+                                          "shared expert) must be 16-byte aligned device pointers");
+    if (overlap(out, xbytes, logits, lbytes) || overlap(contrib, cbytes, x, xbytes) ||
+        overlap(contrib, cbytes, logits, lbytes) || overlap(contrib, cbytes, out, xbytes) ||
+        (shared && (overlap(shared, xbytes, x, xbytes) || overlap(shared, xbytes, logits, lbytes) ||
+                    overlap(shared, xbytes, out, xbytes) || overlap(shared, xbytes, contrib, cbytes))))
+        return fail(MOE_INVALID_ARGUMENT, "trace buffers overlap an input or out");
+    if (flags == MOE_OUT_OVERWRITE && overlap(out, xbytes, x, xbytes))
+        return fail(MOE_INVALID_ARGUMENT, "overwrite requires out disjoint from x (accumulate may alias exactly)");
+    if (flags == MOE_OUT_ACCUMULATE && overlap(out, xbytes, x, xbytes) && out != x)
+        return fail(MOE_INVALID_ARGUMENT, "out may alias x only exactly");
+    DeviceGuard guard(h->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    // every (token, rank) row is written by its pair; zero first so a token
+    // whose routing failed (flagged) still folds defined values
+    MOE_CUDA(cudaMemsetAsync(contrib, 0, cbytes, s));
+    if (shared) MOE_CUDA(cudaMemsetAsync(shared, 0, xbytes, s));
+    if (tokens > kChunk)
+        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s,
+                                           h->tc.x_tc))
+            return st;
+    if (const int st = launch_route(h, w, x, logits, tokens, nullptr, s, nullptr, nullptr, false)) return st;
+    DownSink trace;
+    trace.contrib = contrib;
+    trace.shared = shared;
+    trace.pair_rank = h->pair_rank;
+    trace.shared_expert = w->expert_count;
+    if (const int st = launch_experts(h, w, nullptr, tiles_bound(tokens, h->desc.has_shared), s, nullptr, 0, &trace))
+        return st;
+    fold_kernel<<<std::min<size_t>((xbytes / 4 + 255) / 256, static_cast<size_t>(h->sms) * 8), 256, 0, s>>>(
+        contrib, h->weights, shared, h->pair_weight + static_cast<size_t>(tokens) * kTopK, tokens, H, out,
+        flags == MOE_OUT_OVERWRITE, h->error);
+    return cuda_status(cudaGetLastError(), "fold_kernel");
 }
 
 int moe_quantize_q8_1(const float *x, int width, int columns, void *q8, int *error, void *stream) {

@@ -36,7 +36,7 @@ struct StreamParams {
     Q8Planar x, mid;
     const TileRec *tiles;
     const int *num_tiles;   // [0] tiles, [1] shared-expert tiles at the end of the list
-    float *out;
+    DownSink sink;          // down rows: weighted scatter-add into out, or trace-mode stores
     int *error;
     int stages;
     uint32_t stage_bytes;
@@ -301,9 +301,11 @@ stream_gate_up_kernel(StreamParams p) {
 // (red.global.add).
 template <int N, bool Q41>
 __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, int I, int H, int row0,
-                                          int lr0, int q, uint64_t *empty_bar, int lane, float *out, int *error) {
+                                          int lr0, int q, uint64_t *empty_bar, int lane, const DownSink &sink,
+                                          int *error) {
     const int nb = I / 32;
     const TileRec &meta = *reinterpret_cast<const TileRec *>(st);
+    const int me = meta.e, mp0 = meta.p0;   // read before the stage is released
     const uint4 *dc = reinterpret_cast<const uint4 *>(st + L.dcodes);
     const uint16_t *ds = reinterpret_cast<const uint16_t *>(st + L.dsc);
     const uint16_t *dm = reinterpret_cast<const uint16_t *>(st + L.dmin);
@@ -384,13 +386,7 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
             float v = acc[k][j];
             v += __shfl_xor_sync(0xffffffffu, v, 1);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
-            if ((j & 3) == q) {
-                int flags = 0;
-                const float y = arithmetic(v, flags);
-                const float c = arithmetic(__fmul_rn(w[j], y), flags);
-                atomicAdd(out + static_cast<size_t>(tok[j]) * H + row0 + 8 * k, c);
-                report(flags, error);
-            }
+            if ((j & 3) == q) sink.put(me, mp0, tok[j], j, row0 + 8 * k, H, v, w[j], error);
         }
 }
 
@@ -471,17 +467,17 @@ stream_down_kernel(StreamParams p) {
         const int row0 = (item % slabs) * kDnRows + lr0;
         if (q41) {
             switch (n) {
-            case 1: down_item<1, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-            case 2: down_item<2, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-            case 3: down_item<3, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-            default: down_item<4, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            case 1: down_item<1, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 2: down_item<2, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 3: down_item<3, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            default: down_item<4, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
             }
         } else {
             switch (n) {
-            case 1: down_item<1, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-            case 2: down_item<2, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-            case 3: down_item<3, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
-            default: down_item<4, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.out, p.error); break;
+            case 1: down_item<1, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 2: down_item<2, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 3: down_item<3, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            default: down_item<4, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
             }
         }
     }

@@ -139,6 +139,26 @@ int moe_forward(moe_layer_t h, moe_weights_t w, const float *x_dev, const float 
 int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x_dev, const float *logits_dev,
                          int tokens, float *out_dev, int flags, void *stream, void *const *events);
 
+/* Deterministic trace mode of moe_forward, for bitwise debugging against
+ * the reference's grouped path (moe_scatter + routed_fold +
+ * shared_sigmoid_add, src/hip/session_ops.hip:305-391, called from
+ * src/session.hip:1412-1556).  Every routed pair's unweighted down output is
+ * stored at contrib_dev[token][rank][H] (the reference's [T][10][H]
+ * contribution layout), the shared expert's at shared_dev[token][H] (NULL
+ * exactly when the layer has no shared expert); then, per element, the
+ * reference's operation order over those buffers: value = sum over ranks
+ * 0..9 of weight*contribution (ten separately rounded multiply/adds from 0;
+ * 0 on any non-finite operand), then value + sigmoid(gate)*shared (0 on any
+ * non-finite operand); out = value (MOE_OUT_OVERWRITE) or out + value
+ * (MOE_OUT_ACCUMULATE).  No atomics: bit-identical from run to run.  Every
+ * expert group runs on the dp4a kernels (no tensor-core path), so this is a
+ * debugging mode, not the fast path.  contrib_dev: T*10*H floats; shared_dev:
+ * T*H floats; both caller-owned, 16-byte aligned, disjoint from x, logits
+ * and out. */
+int moe_forward_contributions(moe_layer_t h, moe_weights_t w, const float *x_dev, const float *logits_dev,
+                              int tokens, float *contrib_dev, float *shared_dev, float *out_dev, int flags,
+                              void *stream);
+
 /* Routing only (parity tap for src/hip/session_ops.hip:401-434 router_softmax,
  * src/session.hip:666-687 select_routes and src/routes.cpp:59-115 grouping).
  * Outputs (device, any may be NULL): probs fp32 [T][experts], ids int32

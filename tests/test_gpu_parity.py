@@ -310,3 +310,49 @@ def test_q4_1_gpu_expert_api(pkg, O, torch):
     y, _ = ex.run(x, 5, repeats=2)
     want, _ = O.expert_whole(g, u, d, xq, down_type=O.Q4_1)
     assert_close(y, want)
+
+
+# -------------------------------------------------------------- trace mode --
+@pytest.mark.parametrize("T,kind,shared", [(8, "normal", True), (8, "normal", False), (100, "zipf", True)])
+def test_forward_contributions_trace_mode(pkg, O, torch, T, kind, shared):
+    """moe_forward_contributions: deterministic [T][10][H] contributions and the
+    reference's rank-order fold over them (src/hip/session_ops.hip:305-391)."""
+    seed = 900 + T
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    logits = zipf_logits(rng, T) if kind == "zipf" else rng.standard_normal((T, E)).astype(np.float32)
+    gate_vec = (rng.standard_normal(H) * 0.02).astype(np.float32)
+    desc = pkg.make_desc(max_tokens=T, has_shared=int(shared))
+    weights = pkg.MoeWeights(desc)
+    weights.synthesize(seed, 0)
+    if shared:
+        weights.upload_shared_gate(gate_vec)
+    layer = pkg.MoeLayer(desc)
+    xd, ld = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+    runs = []
+    for _ in range(2):
+        out = torch.zeros(T, H, device="cuda")
+        contrib, sh = layer.forward_contributions(weights, xd, ld, out, accumulate=False)
+        torch.cuda.synchronize()
+        runs.append((out.cpu().numpy(), contrib.cpu().numpy(), None if sh is None else sh.cpu().numpy()))
+    assert layer.read_flags() == 0
+    (out, contrib, sh), (out2, contrib2, sh2) = runs
+    assert np.array_equal(f32bits(out), f32bits(out2)) and np.array_equal(f32bits(contrib), f32bits(contrib2))
+    probs, _ = O.router_softmax(logits)
+    ids, w = O.select_routes(probs)
+    fold = np.empty((T, H), np.float32)
+    O.lib().o_routed_fold(O.ptr(np.ascontiguousarray(contrib)), O.ptr(w), T, H, O.ptr(fold))
+    if not shared:
+        assert np.array_equal(f32bits(out), f32bits(fold))   # the fold itself is the reference's, bit for bit
+    # each stored contribution is its expert's unweighted output for that token
+    xq, _ = O.quantize(x)
+    for t in range(min(T, 4)):
+        for r in range(10):
+            want, _ = O.expert_whole(*O.synth_expert(seed, 0, int(ids[t, r])), xq[t:t + 1])
+            assert_close(contrib[t, r][None], want)
+    if shared:
+        want, _ = O.expert_whole(*O.synth_expert(seed, 0, 512), xq[:min(T, 4)])
+        assert_close(sh[:min(T, 4)], want)
+        ref, _, _, _ = O.moe_layer(x, logits, lambda e: O.synth_expert(seed, 0, e), O.synth_expert(seed, 0, 512),
+                                   gate_vec, np.arange(min(T, 8)))
+        assert_close(out[:min(T, 8)], ref)
