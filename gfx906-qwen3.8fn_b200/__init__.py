@@ -40,7 +40,8 @@ EXPORTED = [
     "moe_route_noalloc", "moe_ep_weights_create", "moe_ep_create", "moe_ep_destroy", "moe_ep_ipc_handle",
     "moe_ep_open_peers", "moe_ep_forward", "moe_ep_read_flags",
     "moe_weights_create_typed", "moe_ep_weights_create_typed", "moe_q4_1_linear", "moe_expert_create_typed",
-    "moe_forward_contributions",
+    "moe_forward_contributions", "moe_weights_upload_router", "moe_forward_hidden", "moe_router_logits",
+    "moe_ep_forward_hidden",
 ]
 
 
@@ -109,6 +110,10 @@ def library(path=LIB_PATH):
         "moe_weights_create_typed": (I, [DESC_P, I, ctypes.POINTER(P)]),
         "moe_q4_1_linear": (I, [P, I, I, P, I, P, P, P]),
         "moe_forward_contributions": (I, [P, P, P, P, I, P, P, P, I, P]),
+        "moe_weights_upload_router": (I, [P, P, P]),
+        "moe_forward_hidden": (I, [P, P, P, I, P, I, P]),
+        "moe_router_logits": (I, [P, P, I, P, P]),
+        "moe_ep_forward_hidden": (I, [P, P, P, I, P, I, P]),
         "moe_expert_create_typed": (I, [P, P, P, I, I, I, I, I, ctypes.POINTER(P)]),
         "moe_ep_create": (I, [DESC_P, I, I, ctypes.POINTER(P)]),
         "moe_ep_destroy": (I, [P]),
@@ -198,6 +203,21 @@ class MoeWeights(_Owned):
     def upload_shared_gate(self, gate_vec, stream=None):
         check(library().moe_weights_upload_shared_gate(self.handle, _ptr(gate_vec), _stream(stream)))
 
+    def upload_router(self, router, stream=None):
+        """ffn_gate_inp as host fp32 [512][H]."""
+        import numpy as np
+        router = np.ascontiguousarray(router, dtype=np.float32)
+        if router.shape != (EXPERTS, self.desc.hidden):
+            raise ValueError("router matrix must be fp32 [512][hidden]")
+        check(library().moe_weights_upload_router(self.handle, _ptr(router), _stream(stream)))
+
+    def router_logits(self, x, stream=None):
+        """Router logits fp32 cuda [T][512] of x (cuda fp32 [T][H])."""
+        import torch
+        logits = torch.empty(x.shape[0], EXPERTS, device=x.device)
+        check(library().moe_router_logits(self.handle, _ptr(x), x.shape[0], _ptr(logits), _stream(stream)))
+        return logits
+
     def download_expert(self, expert, stream=None):
         import numpy as np
         d = self.desc
@@ -227,6 +247,12 @@ class MoeLayer(_Owned):
         flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
         check(library().moe_forward(self.handle, weights.handle, _ptr(x), _ptr(logits), T, _ptr(out), flag,
                                     _stream(stream)))
+
+    def forward_hidden(self, weights, x, out, accumulate=True, stream=None):
+        """out (+)= MoE(x) with the router logits computed on the device."""
+        flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
+        check(library().moe_forward_hidden(self.handle, weights.handle, _ptr(x), x.shape[0], _ptr(out), flag,
+                                           _stream(stream)))
 
     def forward_contributions(self, weights, x, logits, out, accumulate=True, stream=None):
         """Deterministic trace mode: out (+)= the reference-order fold of the per-(token, rank)
@@ -319,6 +345,11 @@ class EpLayer(_Owned):
         flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
         check(library().moe_ep_forward(self.handle, weights.handle, _ptr(x), _ptr(logits), T, _ptr(out), flag,
                                        _stream(stream)))
+
+    def forward_hidden(self, weights, x, out, accumulate=True, stream=None):
+        flag = MOE_OUT_ACCUMULATE if accumulate else MOE_OUT_OVERWRITE
+        check(library().moe_ep_forward_hidden(self.handle, weights.handle, _ptr(x), x.shape[0], _ptr(out), flag,
+                                              _stream(stream)))
 
     def read_flags(self, clear=True, stream=None):
         f = ctypes.c_int(0)

@@ -21,6 +21,7 @@
 #include "stream_kernels.cuh"
 #include "tc_kernels.cuh"
 #include "ep_kernels.cuh"
+#include "router_kernels.cuh"
 
 using namespace qmoe;
 
@@ -106,6 +107,7 @@ struct moe_weights_s {
     int expert_count = kRouterExperts;   // routed experts held; the shared expert follows
     uint8_t *base = nullptr; // experts_total * layout.bytes
     float *gate_vec = nullptr;
+    float *router = nullptr;     // ffn_gate_inp as fp32 [512][H] (zero until uploaded)
     uint8_t *staging = nullptr;  // canonical bytes of one expert (3 matrices)
 };
 
@@ -123,6 +125,7 @@ struct moe_layer_s {
     int *num_tiles;
     int *error;
     int gu_stages, dn_stages;   // shared-memory ring depth of the streaming kernels (0: not used)
+    float *logits = nullptr;    // [max_tokens][512] router logits of moe_forward_hidden
     TcWorkspace tc;
 };
 
@@ -409,12 +412,15 @@ int moe_weights_create_typed(const moe_layer_desc *desc, int down_type, moe_weig
     w->desc = *desc;
     w->layout = make_layout(desc->hidden, desc->inter, down_type == MOE_Q4_1 ? kDownQ4_1 : kDownQ4_0);
     w->experts_total = desc->experts + desc->has_shared;
+    const size_t rbytes = sizeof(float) * kRouterExperts * desc->hidden;
     cudaError_t e = cudaMalloc(&w->base, w->layout.bytes * w->experts_total);
     if (e == cudaSuccess) e = cudaMalloc(&w->gate_vec, sizeof(float) * desc->hidden);
+    if (e == cudaSuccess) e = cudaMalloc(&w->router, rbytes);
     if (e == cudaSuccess) e = cudaMalloc(&w->staging, w->layout.bytes / 16 * 18);
     if (e == cudaSuccess) e = cudaMemset(w->gate_vec, 0, sizeof(float) * desc->hidden);
+    if (e == cudaSuccess) e = cudaMemset(w->router, 0, rbytes);
     if (e != cudaSuccess) {
-        cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->staging);
+        cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->router); cudaFree(w->staging);
         delete w;
         return cuda_status(e, "moe_weights_create");
     }
@@ -427,6 +433,7 @@ int moe_weights_destroy(moe_weights_t w) {
     DeviceGuard guard(w->desc.device);
     cudaFree(w->base);
     cudaFree(w->gate_vec);
+    cudaFree(w->router);
     cudaFree(w->staging);
     delete w;
     return MOE_OK;
@@ -498,6 +505,18 @@ int moe_weights_upload_shared_gate(moe_weights_t w, const float *gate_vec, void 
     return MOE_OK;
 }
 
+int moe_weights_upload_router(moe_weights_t w, const float *router, void *stream) {
+    if (!w || !router) return fail(MOE_INVALID_ARGUMENT, "null router argument");
+    if (!w->router) return fail(MOE_NOT_SUPPORTED, "these weights hold no router matrix");
+    DeviceGuard guard(w->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    MOE_CUDA(cudaMemcpyAsync(w->router, router, sizeof(float) * kRouterExperts * w->desc.hidden,
+                             cudaMemcpyHostToDevice, s));
+    MOE_CUDA(cudaStreamSynchronize(s));
+    return MOE_OK;
+}
+
 int moe_weights_synthesize(moe_weights_t w, uint64_t seed, uint32_t layer, void *stream) {
     if (!w) return fail(MOE_INVALID_ARGUMENT, "null weights");
     DeviceGuard guard(w->desc.device);
@@ -534,6 +553,7 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
         h->mid.scales = a.take<float2>(static_cast<size_t>(h->pairs_max) * (I / 32));
         h->ids = a.take<int32_t>(static_cast<size_t>(T) * kTopK);
         h->weights = a.take<float>(static_cast<size_t>(T) * kTopK);
+        h->logits = a.take<float>(static_cast<size_t>(T) * kRouterExperts);
         h->masks = a.take<uint32_t>(static_cast<size_t>(h->chunks_max) * kRouterExperts);
         h->base = a.take<int32_t>(static_cast<size_t>(h->chunks_max) * kRouterExperts);
         h->counts = a.take<int32_t>(kRouterExperts);
@@ -631,6 +651,33 @@ int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const f
     const bool tc_ok = tokens > kChunk && w->layout.down_type == kDownQ4_0;
     const int tc_tiles = tc_ok ? std::min(h->tc.max_tiles, pairs / kTcMinGroup + pairs / kTcM + 1) : 0;
     return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events, tc_tiles);
+}
+
+int moe_router_logits(moe_weights_t w, const float *x, int tokens, float *logits, void *stream) {
+    if (!w || !w->router) return fail(MOE_INVALID_ARGUMENT, "null weights or no router matrix");
+    if (tokens < 1 || tokens > 65536) return fail(MOE_INVALID_ARGUMENT, "tokens must be 1..65536");
+    const int H = w->desc.hidden;
+    if (!aligned(x, 16) || !aligned(logits, 16) ||
+        overlap(logits, static_cast<size_t>(tokens) * kRouterExperts * 4, x, static_cast<size_t>(tokens) * H * 4))
+        return fail(MOE_INVALID_ARGUMENT, "x and logits must be disjoint 16-byte aligned device buffers");
+    DeviceGuard guard(w->desc.device);
+    MOE_CUDA(guard.status);
+    auto s = static_cast<cudaStream_t>(stream);
+    if (tokens <= kRouterGemvTokens)
+        router_gemv_kernel<<<kRouterExperts / kRouterGemvWarps, 32 * kRouterGemvWarps, 0, s>>>(x, w->router, logits,
+                                                                                              tokens, H);
+    else
+        router_gemm_kernel<<<dim3(kRouterExperts / kRouterTile, (tokens + kRouterTile - 1) / kRouterTile), 256, 0, s>>>(
+            x, w->router, logits, tokens, H);
+    return cuda_status(cudaGetLastError(), "router kernel");
+}
+
+int moe_forward_hidden(moe_layer_t h, moe_weights_t w, const float *x, int tokens, float *out, int flags,
+                       void *stream) {
+    if (!h || !w) return fail(MOE_INVALID_ARGUMENT, "null layer or weights");
+    if (tokens < 1 || tokens > h->desc.max_tokens) return fail(MOE_INVALID_ARGUMENT, "tokens outside 1..max_tokens");
+    if (const int st = moe_router_logits(w, x, tokens, h->logits, stream)) return st;
+    return moe_forward_profiled(h, w, x, h->logits, tokens, out, flags, stream, nullptr);
 }
 
 int moe_forward_contributions(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens,
@@ -1178,12 +1225,15 @@ int moe_ep_weights_create_typed(const moe_layer_desc *desc, int rank, int world,
     w->expert_count = kRouterExperts / world;
     w->expert_first = rank * w->expert_count;
     w->experts_total = w->expert_count + desc->has_shared;
+    const size_t rbytes = sizeof(float) * kRouterExperts * desc->hidden;
     cudaError_t e = cudaMalloc(&w->base, w->layout.bytes * w->experts_total);
     if (e == cudaSuccess) e = cudaMalloc(&w->gate_vec, sizeof(float) * desc->hidden);
+    if (e == cudaSuccess) e = cudaMalloc(&w->router, rbytes);
     if (e == cudaSuccess) e = cudaMalloc(&w->staging, w->layout.bytes / 16 * 18);
     if (e == cudaSuccess) e = cudaMemset(w->gate_vec, 0, sizeof(float) * desc->hidden);
+    if (e == cudaSuccess) e = cudaMemset(w->router, 0, rbytes);
     if (e != cudaSuccess) {
-        cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->staging);
+        cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->router); cudaFree(w->staging);
         delete w;
         return cuda_status(e, "moe_ep_weights_create");
     }
@@ -1432,6 +1482,14 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
     const int cthreads = std::min(kEpCombineThreads, std::max(32, (H / 4 + 31) / 32 * 32));
     ep_combine_kernel<<<tokens, cthreads, 0, s>>>(p);
     return cuda_status(cudaGetLastError(), "ep_combine_kernel");
+}
+
+int moe_ep_forward_hidden(moe_ep_t ep, moe_weights_t w, const float *x, int tokens, float *out, int flags,
+                          void *stream) {
+    if (!ep || !w) return fail(MOE_INVALID_ARGUMENT, "null expert-parallel layer or weights");
+    if (tokens < 1 || tokens > ep->desc.max_tokens) return fail(MOE_INVALID_ARGUMENT, "tokens outside 1..max_tokens");
+    if (const int st = moe_router_logits(w, x, tokens, ep->tx->logits, stream)) return st;
+    return moe_ep_forward(ep, w, x, ep->tx->logits, tokens, out, flags, stream);
 }
 
 int moe_ep_read_flags(moe_ep_t ep, int *flags, int clear, void *stream) {

@@ -105,6 +105,10 @@ int moe_weights_upload_expert(moe_weights_t w, int expert, const void *gate_q4_0
 /* Shared expert scalar gate vector (fp32 [H]), the reference's
  * ffn_gate_inp_shexp (src/session.hip:1101, used at :1398-1402). */
 int moe_weights_upload_shared_gate(moe_weights_t w, const float *gate_vec_host, void *stream);
+/* Router matrix ffn_gate_inp (src/session.hip:1097) as host fp32 [512][H]
+ * (row e = expert e's H weights, i.e. the GGUF tensor {H, 512} with H
+ * fastest), for moe_forward_hidden / moe_router_logits.  Zero until uploaded. */
+int moe_weights_upload_router(moe_weights_t w, const float *router_host, void *stream);
 /* Fill every expert (and the shared expert) with the seeded synthetic Q4_0
  * generator on the device (bit-identical to the oracle's generator); Q4_1
  * down matrices take the same codes and scales plus the minimum
@@ -131,6 +135,18 @@ int moe_layer_destroy(moe_layer_t h);
  * No host synchronisation: the call is capturable in a CUDA graph. */
 int moe_forward(moe_layer_t h, moe_weights_t w, const float *x_dev, const float *logits_dev,
                 int tokens, float *out_dev, int flags, void *stream);
+
+/* moe_forward from the hidden state: the router logits x * W_router^T are
+ * computed on the device (fp32, into the layer's workspace) and routed with
+ * no host round trip -- the reference's router.apply + router_softmax +
+ * probability D2H + host select_routes (src/session.hip:1420-1433) as one
+ * device sequence.  Requires moe_weights_upload_router. */
+int moe_forward_hidden(moe_layer_t h, moe_weights_t w, const float *x_dev, int tokens, float *out_dev,
+                       int flags, void *stream);
+/* Router logits tap: logits_dev fp32 [T][512] = x_dev [T][H] times the
+ * uploaded router matrix (fp32 products and sums on the CUDA cores; the
+ * reference uses a dense BLAS GEMM, so agreement is to fp32 rounding). */
+int moe_router_logits(moe_weights_t w, const float *x_dev, int tokens, float *logits_dev, void *stream);
 
 /* moe_forward with three caller-created CUDA events recorded on `stream`:
  * events[0] before the gate/up kernel, events[1] between gate/up and down,
@@ -225,6 +241,10 @@ int moe_ep_open_peers(moe_ep_t ep, const void *handles_host);
  * peers are open. */
 int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x_dev, const float *logits_dev, int tokens,
                    float *out_dev, int flags, void *stream);
+/* moe_ep_forward from the hidden state (router logits computed on the
+ * device from the shard weights' router matrix, as moe_forward_hidden). */
+int moe_ep_forward_hidden(moe_ep_t ep, moe_weights_t w, const float *x_dev, int tokens, float *out_dev,
+                          int flags, void *stream);
 /* Sticky flags of the rank (MOE_FLAG_TIMEOUT included); synchronises `stream`. */
 int moe_ep_read_flags(moe_ep_t ep, int *flags_host, int clear, void *stream);
 

@@ -356,3 +356,56 @@ def test_forward_contributions_trace_mode(pkg, O, torch, T, kind, shared):
         ref, _, _, _ = O.moe_layer(x, logits, lambda e: O.synth_expert(seed, 0, e), O.synth_expert(seed, 0, 512),
                                    gate_vec, np.arange(min(T, 8)))
         assert_close(out[:min(T, 8)], ref)
+
+
+# ------------------------------------------------------------- router GEMM --
+@pytest.mark.parametrize("T", [1, 8, 33, 300])
+def test_router_logits_fp32(pkg, O, torch, T):
+    """x * W_router^T on the device: fp32 sums of 2048 products, checked against
+    fp64 with an fp32 accumulation bound (the reference's BLAS order is unspecified)."""
+    rng = np.random.default_rng(40 + T)
+    W = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    desc = pkg.make_desc(max_tokens=T)
+    w = pkg.MoeWeights(desc)
+    w.upload_router(W)
+    got = w.router_logits(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = x.astype(np.float64) @ W.astype(np.float64).T
+    bound = 2e-5 * (np.abs(x).astype(np.float64) @ np.abs(W).astype(np.float64).T)
+    assert np.all(np.abs(got - ref) <= bound)
+
+
+@pytest.mark.parametrize("T", [8, 100])
+def test_forward_hidden_routes_device_logits(pkg, O, torch, T):
+    """moe_forward_hidden == moe_forward over the device logits, and those
+    logits route exactly as the oracle routes them."""
+    seed = 70 + T
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    gate_vec = (rng.standard_normal(H) * 0.02).astype(np.float32)
+    desc = pkg.make_desc(max_tokens=T)
+    w = pkg.MoeWeights(desc)
+    w.synthesize(seed, 0)
+    w.upload_shared_gate(gate_vec)
+    w.upload_router(W)
+    layer = pkg.MoeLayer(desc)
+    xd = torch.from_numpy(x).cuda()
+    out_h = torch.zeros(T, H, device="cuda")
+    layer.forward_hidden(w, xd, out_h, accumulate=False)
+    logits = w.router_logits(xd)
+    out_l = torch.zeros(T, H, device="cuda")
+    layer.forward(w, xd, logits, out_l, accumulate=False)
+    torch.cuda.synchronize()
+    assert layer.read_flags() == 0
+    lg = logits.cpu().numpy()
+    assert_close(out_h.cpu().numpy(), out_l.cpu().numpy())
+    r = layer.route(logits)
+    probs, _ = O.router_softmax(lg)
+    ids, wts = O.select_routes(probs)
+    assert np.array_equal(r["ids"].cpu().numpy(), ids)
+    assert np.array_equal(f32bits(r["weights"].cpu().numpy()), f32bits(wts))
+    sample = np.arange(min(T, 6))
+    ref, _, _, _ = O.moe_layer(x, lg, lambda e: O.synth_expert(seed, 0, e), O.synth_expert(seed, 0, 512), gate_vec,
+                               sample)
+    assert_close(out_h.cpu().numpy()[sample], ref)
