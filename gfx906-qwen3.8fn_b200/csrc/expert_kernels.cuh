@@ -182,7 +182,8 @@ repack_q4_1_kernel(uint8_t *canonical, uint8_t *codes, uint16_t *scales, uint16_
 
 // Where the rows of a down projection go.  Normally the router-weighted
 // scatter-add into the residual (red.global.add, sanitised).  In trace mode
-// (contrib non-null) the raw, unweighted row of pair (token, rank) is stored
+// (put<true>, a separate kernel instantiation so the normal epilogue carries
+// no branch) the raw, unweighted row of pair (token, rank) is stored
 // at contrib[token][rank][H] -- the reference's moe_scatter layout
 // (src/hip/session_ops.hip:358-373) -- and the shared expert's row at
 // shared[token][H]; the fold kernel then applies the reference's rank-order
@@ -193,9 +194,10 @@ struct DownSink {
     float *shared = nullptr;
     const int32_t *pair_rank = nullptr;   // rank of each routed pair
     int shared_expert = 0;                // expert index of the shared expert's tiles
+    template <bool Trace>
     __device__ __forceinline__ void put(int e, int p0, int tok, int j, int row, int H, float v, float w,
                                         int *error) const {
-        if (contrib) {
+        if constexpr (Trace) {
             float *dst = e == shared_expert ? shared + static_cast<size_t>(tok) * H
                                             : contrib + (static_cast<size_t>(tok) * kTopK + pair_rank[p0 + j]) * H;
             dst[row] = v;
@@ -332,7 +334,7 @@ gate_up_kernel(GroupParams p) {
 // t%4+4, ...; the four partial sums meet in two shuffles, then
 // out[token][row] += weight * y (red.global.add).  Replaces the reference's
 // scatter + rank fold (src/hip/session_ops.hip:292-324,358-373).
-template <int NT>
+template <int NT, bool Trace = false>
 __global__ void __launch_bounds__(kGemvThreads)
 down_kernel(GroupParams p) {
     const int H = p.layout.hidden, I = p.layout.inter;
@@ -394,7 +396,7 @@ down_kernel(GroupParams p) {
         }
 #pragma unroll
         for (int j = 0; j < NT; ++j)
-            if (j < n && (j & 3) == q) p.sink.put(e, p0, stok[j], j, row, H, acc[j], swt[j], p.error);
+            if (j < n && (j & 3) == q) p.sink.put<Trace>(e, p0, stok[j], j, row, H, acc[j], swt[j], p.error);
     }
 }
 

@@ -147,6 +147,8 @@ size_t stream_dn_smem(int I, int stages) { return 128 + size_t(stages) * DnStage
 int configure_kernels(moe_layer_s *h, int H, int I) {
     MOE_CUDA(cudaFuncSetAttribute(gate_up_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(gate_up_smem(H))));
+    MOE_CUDA(cudaFuncSetAttribute(down_kernel<kGemvTile, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(down_smem(I))));
     MOE_CUDA(cudaFuncSetAttribute(down_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(down_smem(I))));
     // The streaming kernels need at least two stages in shared memory.
@@ -156,7 +158,9 @@ int configure_kernels(moe_layer_s *h, int H, int I) {
     if (h->gu_stages) {
         MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(stream_gu_smem(H, h->gu_stages))));
-        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(stream_dn_smem(I, h->dn_stages))));
+        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(stream_dn_smem(I, h->dn_stages))));
     }
     return MOE_OK;
@@ -257,7 +261,8 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
         sp.stages = h->dn_stages;
         sp.stage_bytes = DnStage(L.inter).bytes;
-        MOE_CUDA(launch_overlapped(stream_down_kernel, std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
+        MOE_CUDA(launch_overlapped(trace ? stream_down_kernel<true> : stream_down_kernel<false>,
+                                   std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
                                    stream_dn_smem(L.inter, sp.stages), s, sp));
         if (tc_tiles)
             if (const int st = launch_tc(h, w, out, tc_tiles, true, s)) return st;
@@ -273,7 +278,8 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
     gate_up_kernel<kGemvTile><<<gu_grid, kGemvThreads, gate_up_smem(L.hidden), s>>>(g);
     MOE_CUDA(cudaGetLastError());
     if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
-    down_kernel<kGemvTile><<<dn_grid, kGemvThreads, down_smem(L.inter), s>>>(g);
+    if (trace) down_kernel<kGemvTile, true><<<dn_grid, kGemvThreads, down_smem(L.inter), s>>>(g);
+    else down_kernel<kGemvTile><<<dn_grid, kGemvThreads, down_smem(L.inter), s>>>(g);
     MOE_CUDA(cudaGetLastError());
     if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[2]), s));
     return MOE_OK;

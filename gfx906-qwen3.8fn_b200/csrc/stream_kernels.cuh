@@ -299,7 +299,7 @@ stream_gate_up_kernel(StreamParams p) {
 // kDnLaneRows): lane l takes rows 8R*cw + l/4 + 8k (k < R) and blocks l%4,
 // l%4+4, ...; two shuffles finish each row, then out[token][row] += weight * y
 // (red.global.add).
-template <int N, bool Q41>
+template <int N, bool Q41, bool Trace>
 __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, int I, int H, int row0,
                                           int lr0, int q, uint64_t *empty_bar, int lane, const DownSink &sink,
                                           int *error) {
@@ -386,10 +386,11 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
             float v = acc[k][j];
             v += __shfl_xor_sync(0xffffffffu, v, 1);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
-            if ((j & 3) == q) sink.put(me, mp0, tok[j], j, row0 + 8 * k, H, v, w[j], error);
+            if ((j & 3) == q) sink.put<Trace>(me, mp0, tok[j], j, row0 + 8 * k, H, v, w[j], error);
         }
 }
 
+template <bool Trace>
 __global__ void __launch_bounds__(kStreamThreads, 1)
 stream_down_kernel(StreamParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -467,17 +468,17 @@ stream_down_kernel(StreamParams p) {
         const int row0 = (item % slabs) * kDnRows + lr0;
         if (q41) {
             switch (n) {
-            case 1: down_item<1, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 2: down_item<2, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 3: down_item<3, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            default: down_item<4, true>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 1: down_item<1, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 2: down_item<2, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 3: down_item<3, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            default: down_item<4, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
             }
         } else {
             switch (n) {
-            case 1: down_item<1, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 2: down_item<2, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 3: down_item<3, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            default: down_item<4, false>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 1: down_item<1, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 2: down_item<2, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 3: down_item<3, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            default: down_item<4, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
             }
         }
     }
