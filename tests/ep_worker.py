@@ -10,14 +10,14 @@ import sys
 import numpy as np
 
 
-def _setup(rank, world, port, use_gpu):
+def _setup(rank, world, port, use_gpu, device=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
     dist.init_process_group("gloo", rank=rank, world_size=world)
     if use_gpu:
         import torch
-        torch.cuda.set_device(rank)
+        torch.cuda.set_device(rank if device is None else device)
     return dist
 
 
@@ -86,3 +86,51 @@ def forward_worker(rank, world, port, tokens, routing, queue):
         dist.destroy_process_group()
     except Exception as ex:
         queue.put((rank, "error", repr(ex), 0.0))
+
+
+def silent_peer_worker(rank, world, port, queue):
+    """Failure detection without a fault: both ranks live on GPU 0 and open each
+    other's buffers, but rank 1 never runs a forward.  Rank 0's bounded waits
+    (received slots, peers' "done") run out on flags nothing sets; the forward
+    must return with MOE_FLAG_TIMEOUT in the rank's flags and the context must
+    stay usable (a single-GPU forward afterwards is clean).  Rank 1 keeps its
+    buffers alive until rank 0 is done; no two kernels wait on one another."""
+    try:
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        import time
+        import torch
+        import __graft_entry__
+        pkg = __graft_entry__.load_package()
+        dist = _setup(rank, world, port, use_gpu=True, device=0)
+        desc = pkg.make_desc(max_tokens=8, device=0)
+        ep = pkg.EpLayer(desc, rank, world)
+        ep.connect(pkg.exchange_handles)
+        result = (rank, 0, 0.0, 0)
+        if rank == 0:
+            shard = pkg.EpWeights(desc, rank, world)
+            shard.synthesize(5, 0)
+            rng = np.random.default_rng(0)
+            x = torch.from_numpy(rng.standard_normal((8, 2048)).astype(np.float32)).cuda()
+            logits = torch.from_numpy(rng.standard_normal((8, 512)).astype(np.float32)).cuda()
+            out = torch.zeros(8, 2048, device="cuda")
+            t0 = time.time()
+            ep.forward(shard, x, logits, out)
+            flags = ep.read_flags()            # synchronises: the bounded waits have given up
+            waited = time.time() - t0
+            full = pkg.MoeWeights(desc)
+            full.synthesize(5, 0)
+            layer = pkg.MoeLayer(desc)
+            ref = torch.zeros(8, 2048, device="cuda")
+            layer.forward(full, x, logits, ref)
+            torch.cuda.synchronize()
+            result = (rank, flags, waited, layer.read_flags())
+            ep.close()                          # the importer unmaps first
+        dist.barrier()                          # rank 1 frees its buffers only after that
+        if rank != 0:
+            ep.close()
+        dist.barrier()
+        queue.put(result)
+        dist.destroy_process_group()
+    except Exception as ex:
+        queue.put((rank, "error", repr(ex), 0))

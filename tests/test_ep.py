@@ -111,3 +111,19 @@ def test_ep_two_ranks_match_single_gpu(tokens, routing):
         assert flags == 0, (rank, flags)
         for e in errs:
             assert e <= TOL_RMS * rms, (rank, e, rms)
+
+
+@pytest.mark.gpu
+def test_ep_silent_peer_times_out_with_flag(pkg):
+    """A peer that never publishes: the bounded device waits give up after ~1 s
+    each and report MOE_FLAG_TIMEOUT; nothing hangs and the context stays
+    usable.  Two processes on one GPU; only one of them launches kernels."""
+    import ep_worker
+    res = run_ranks(ep_worker.silent_peer_worker, 2, timeout=240)
+    rank0 = res[0]
+    assert rank0[1] != "error", rank0
+    _, flags, waited, after = rank0
+    assert flags & 4, flags          # MOE_FLAG_TIMEOUT
+    assert 0.5 < waited < 30.0, waited
+    assert after == 0
+    assert res[1][1] != "error", res[1]
