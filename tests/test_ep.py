@@ -127,3 +127,35 @@ def test_ep_silent_peer_times_out_with_flag(pkg):
     assert 0.5 < waited < 30.0, waited
     assert after == 0
     assert res[1][1] != "error", res[1]
+
+
+@pytest.mark.gpu
+def test_ep_world1_forward_hidden(pkg):
+    """moe_ep_forward_hidden (router logits on the device from the shard's router
+    matrix) equals the single-GPU moe_forward_hidden."""
+    import torch
+    T = 8
+    desc = pkg.make_desc(max_tokens=T)
+    rng = np.random.default_rng(77)
+    x = torch.from_numpy(rng.standard_normal((T, 2048)).astype(np.float32)).cuda()
+    router = (rng.standard_normal((512, 2048)) * 0.02).astype(np.float32)
+    gate = (rng.standard_normal(2048) * 0.05).astype(np.float32)
+    full = pkg.MoeWeights(desc)
+    full.synthesize(9, 2)
+    full.upload_shared_gate(gate)
+    full.upload_router(router)
+    ref = torch.zeros(T, 2048, device="cuda")
+    pkg.MoeLayer(desc).forward_hidden(full, x, ref, accumulate=False)
+    shard = pkg.EpWeights(desc, 0, 1)
+    shard.synthesize(9, 2)
+    shard.upload_shared_gate(gate)
+    shard.upload_router(router)
+    ep = pkg.EpLayer(desc, 0, 1)
+    ep.connect(lambda h: [h])
+    out = torch.zeros(T, 2048, device="cuda")
+    ep.forward_hidden(shard, x, out, accumulate=False)
+    torch.cuda.synchronize()
+    r = ref.cpu().numpy()
+    rms = np.sqrt(np.mean(r.astype(np.float64) ** 2))
+    assert np.abs(out.cpu().numpy() - r).max() <= TOL_RMS * rms
+    assert ep.read_flags() == 0
