@@ -3,9 +3,9 @@
 // work item's weights into a ring of shared-memory stages with cp.async.bulk
 // (completion counted on an mbarrier); warps 1..8 are consumers that run the
 // u4 x s8 dp4a dots out of shared memory and release each stage on an
-// "empty" mbarrier.  Up to two gate/up stages (72 KB each) or four down
-// stages (~40 KB each) are in flight per SM while a third is consumed, so HBM
-// latency is covered by bytes in flight rather than by resident warps.
+// "empty" mbarrier.  Three gate/up stages (72 KB each) or five down stages
+// (43 KB each, minima slice included) make the ring, so HBM latency is
+// covered by bytes in flight rather than by resident warps.
 //
 // Work is coarse per warp on purpose: a consumer lane handles 16 (gate/up)
 // or 8 (down) block-rows per stage, so the fixed per-stage work (reductions,
