@@ -117,3 +117,26 @@ def test_route_groups_all_experts_large_batch(pkg, O):
     a = rg.assignments()
     assert np.array_equal(a["token"], r["token"]) and np.array_equal(a["rank"], r["rank"])
     assert np.array_equal(rg.counts(), r["counts"])
+
+
+def test_new_entry_points_reject_before_any_device_call(pkg):
+    """Typed weights, the Q4_1 tap, trace mode, router and hidden-state entry
+    points validate their arguments before touching a device."""
+    L = pkg.library()
+    h = ctypes.c_void_p()
+    d = pkg.make_desc(max_tokens=8)
+    for bad_type in (0, 1, 8, 99):   # only Q4_0 (2) and Q4_1 (3) down matrices
+        assert L.moe_weights_create_typed(ctypes.byref(d), bad_type, ctypes.byref(h)) == pkg.MOE_NOT_SUPPORTED
+        assert L.moe_ep_weights_create_typed(ctypes.byref(d), 0, 1, bad_type, ctypes.byref(h)) == pkg.MOE_NOT_SUPPORTED
+        assert not h.value
+    assert L.moe_expert_create_typed(None, None, None, 9, 2048, 512, 0, 4, ctypes.byref(h)) in (
+        pkg.MOE_INVALID_ARGUMENT, pkg.MOE_NOT_SUPPORTED)
+    for rows, k, cols in ((0, 512, 1), (2048, 500, 1), (2048, 512, 0)):
+        assert L.moe_q4_1_linear(None, rows, k, None, cols, None, None, None) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_q4_1_linear(None, 2048, 512, None, 1, None, None, None) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_forward_contributions(None, None, None, None, 8, None, None, None, 0, None) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_router_logits(None, None, 8, None, None) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_forward_hidden(None, None, None, 8, None, 0, None) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_ep_forward_hidden(None, None, None, 8, None, 0, None) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_weights_upload_router(None, None, None) == pkg.MOE_INVALID_ARGUMENT
+    assert L.moe_abi_version() == (1 << 16) | 1
