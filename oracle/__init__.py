@@ -289,11 +289,13 @@ def route_groups(ids, weights, experts=EXPERTS):
     return dict(counts=counts, offsets=offsets, token=tok, rank=rank, expert=exp, weight=wt)
 
 
-def moe_layer(x, logits, experts_fn, shared, gate_vec, tokens=None, down_type=Q4_0):
+def moe_layer(x, logits, experts_fn, shared, gate_vec, tokens=None, down_type=Q4_0, threads=1):
     """Whole-layer oracle for the given tokens (default: all).
 
     experts_fn(e) -> (gate, up, down) canonical bytes; shared = (gate, up, down);
-    down matrices of down_type (Q4_0 or Q4_1).
+    down matrices of down_type (Q4_0 or Q4_1).  `threads` > 1 runs the experts
+    (and column ranges of the shared expert) on a thread pool: the C calls
+    release the GIL and every column's result is independent of the split.
     Returns (out [len(tokens)][H], ids, weights, flags).
     """
     x = np.ascontiguousarray(x, dtype=np.float32)
@@ -308,19 +310,39 @@ def moe_layer(x, logits, experts_fn, shared, gate_vec, tokens=None, down_type=Q4
     ids, w = select_routes(probs)
     n = len(tokens)
     contrib = np.zeros((n, TOP_K, H), np.float32)
-    cache = {}
-    for e in np.unique(ids):
+
+    def one(e):
         cols = np.argwhere(ids == e)
-        if e not in cache:
-            cache[e] = experts_fn(int(e))
-        g, u, d = cache.pop(e)
-        y, f = expert_whole(g, u, d, xq[cols[:, 0]], H, down_type=down_type)
+        g, u, d = experts_fn(int(e))
+        y, f = expert_whole(g, u, d, np.ascontiguousarray(xq[cols[:, 0]]), H, down_type=down_type)
+        return cols, y, f
+
+    experts = [int(e) for e in np.unique(ids)]
+    if threads > 1 and len(experts) > 1:
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            results = list(pool.map(one, experts))
+    else:
+        results = [one(e) for e in experts]
+    for cols, y, f in results:
         flags |= f
         contrib[cols[:, 0], cols[:, 1]] = y
     out = np.empty((n, H), np.float32)
     lib().o_routed_fold(ptr(contrib), ptr(np.ascontiguousarray(w)), n, H, ptr(out))
-    ys, f = expert_whole(shared[0], shared[1], shared[2], xq, H, down_type=down_type)
-    flags |= f
+    if threads > 1 and n >= 64:
+        from concurrent.futures import ThreadPoolExecutor
+        step = (n + threads - 1) // threads
+        parts = [(c, min(n, c + step)) for c in range(0, n, step)]
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            res = list(pool.map(lambda r: expert_whole(shared[0], shared[1], shared[2],
+                                                       np.ascontiguousarray(xq[r[0]:r[1]]), H,
+                                                       down_type=down_type), parts))
+        ys = np.concatenate([y for y, _ in res])
+        for _, f in res:
+            flags |= f
+    else:
+        ys, f = expert_whole(shared[0], shared[1], shared[2], xq, H, down_type=down_type)
+        flags |= f
     gv = np.ascontiguousarray(gate_vec, dtype=np.float32)
     lib().o_shared_add(ptr(sub_x), ptr(gv), ptr(ys), n, H, ptr(out))
     return out, ids, w, flags
