@@ -41,7 +41,7 @@ EXPORTED = [
     "moe_ep_open_peers", "moe_ep_forward", "moe_ep_read_flags",
     "moe_weights_create_typed", "moe_ep_weights_create_typed", "moe_q4_1_linear", "moe_expert_create_typed",
     "moe_forward_contributions", "moe_weights_upload_router", "moe_forward_hidden", "moe_router_logits",
-    "moe_ep_forward_hidden",
+    "moe_ep_forward_hidden", "moe_debug_block_dots",
 ]
 
 
@@ -121,6 +121,7 @@ def library(path=LIB_PATH):
         "moe_ep_open_peers": (I, [P, P]),
         "moe_ep_forward": (I, [P, P, P, P, I, P, I, P]),
         "moe_ep_read_flags": (I, [P, ctypes.POINTER(I), I, P]),
+        "moe_debug_block_dots": (I, [P, P, P, P, I, I, I, P, P, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -287,6 +288,26 @@ class MoeLayer(_Owned):
         check(library().moe_route(self.handle, _ptr(logits), T, _ptr(r["probs"]), _ptr(r["ids"]),
                                   _ptr(r["weights"]), _ptr(r["offsets"]), _ptr(r["token"]), _ptr(r["rank"]),
                                   _stream(stream)))
+        return r
+
+    def block_dots(self, weights, x, logits, expert, max_pairs, stream=None):
+        """Parity tap: forward (overwrite) recording expert `expert`'s per-block
+        int32 dots.  Returns dict of cuda tensors gate/up [P][I][H/32], down
+        [P][H][I/32], mid_codes [P][I], mid_ds [P][I/32] (half d | half s<<16)
+        and out [T][H]."""
+        import torch
+        T, H = x.shape
+        Ii = self.desc.inter
+        dev = x.device
+        r = dict(gate=torch.zeros(max_pairs, Ii, H // 32, dtype=torch.int32, device=dev),
+                 up=torch.zeros(max_pairs, Ii, H // 32, dtype=torch.int32, device=dev),
+                 down=torch.zeros(max_pairs, H, Ii // 32, dtype=torch.int32, device=dev),
+                 mid_codes=torch.zeros(max_pairs, Ii, dtype=torch.int8, device=dev),
+                 mid_ds=torch.zeros(max_pairs, Ii // 32, dtype=torch.int32, device=dev),
+                 out=torch.empty(T, H, device=dev))
+        check(library().moe_debug_block_dots(self.handle, weights.handle, _ptr(x), _ptr(logits), T, expert, max_pairs,
+                                             _ptr(r["gate"]), _ptr(r["up"]), _ptr(r["down"]), _ptr(r["mid_codes"]),
+                                             _ptr(r["mid_ds"]), _ptr(r["out"]), _stream(stream)))
         return r
 
     def read_flags(self, clear=True, stream=None):

@@ -20,7 +20,7 @@ struct EpCtl {
 
 // Byte offsets inside a rank's exported arena (identical on every rank).
 struct EpLayout {
-    size_t codes, scales, tc, ids, w, partial, ctl, bytes;
+    size_t codes, scales, ids, w, partial, ctl, bytes;
 };
 inline EpLayout make_ep_layout(int H, int slots) {
     EpLayout L;
@@ -29,7 +29,6 @@ inline EpLayout make_ep_layout(int H, int slots) {
     L.ctl = take(sizeof(EpCtl));
     L.codes = take(static_cast<size_t>(slots) * H);
     L.scales = take(static_cast<size_t>(slots) * (H / 32) * 8);
-    L.tc = take(static_cast<size_t>(slots) * (H / 32) * 8);
     L.ids = take(static_cast<size_t>(slots) * kEpSlotIds * 4);
     L.w = take(static_cast<size_t>(slots) * kEpSlotIds * 4);
     L.partial = take(static_cast<size_t>(slots) * H * 4);
@@ -49,7 +48,6 @@ struct EpParams {
     const float *weights;         // [T][10]
     const int8_t *xcodes;         // [T][H]
     const float2 *xscales;        // [T][H/32]
-    const float2 *xtc;            // [T][H/32]
     int32_t *pos;                 // [T][kEpMaxRanks] slot index in each destination
     uint8_t *dmask;               // [T] destination ranks
     int32_t *counts;              // [kEpMaxRanks] slots sent to each destination

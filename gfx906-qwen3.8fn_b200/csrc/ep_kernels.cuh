@@ -113,15 +113,10 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpParams p) {
         const uint4 *sc = reinterpret_cast<const uint4 *>(p.xcodes + static_cast<size_t>(t) * H);
         uint4 *dc = reinterpret_cast<uint4 *>(dst + p.L.codes + slot * H);
         for (int i = lane; i < H / 16; i += 32) dc[i] = sc[i];
-        // block scales and tensor-core constants: nb float2 each
+        // block scales: nb float2
         const uint4 *ss = reinterpret_cast<const uint4 *>(p.xscales + static_cast<size_t>(t) * nb);
         uint4 *ds = reinterpret_cast<uint4 *>(dst + p.L.scales + slot * nb * 8);
-        const uint4 *st = reinterpret_cast<const uint4 *>(p.xtc + static_cast<size_t>(t) * nb);
-        uint4 *dt = reinterpret_cast<uint4 *>(dst + p.L.tc + slot * nb * 8);
-        for (int i = lane; i < nb / 2; i += 32) {
-            ds[i] = ss[i];
-            dt[i] = st[i];
-        }
+        for (int i = lane; i < nb / 2; i += 32) ds[i] = ss[i];
         // (local expert, weight) list: the routed experts d owns (the shared
         // expert of the own tokens is added by the receiver's grouping)
         if (lane < kEpSlotIds) {
@@ -195,12 +190,7 @@ __global__ void __launch_bounds__(1024) ep_plan_dispatch_small_kernel(EpParams p
         for (int i = lane; i < H / 16; i += 32) dc[i] = sc[i];
         const uint4 *ss = reinterpret_cast<const uint4 *>(p.xscales + static_cast<size_t>(t) * nb);
         uint4 *ds = reinterpret_cast<uint4 *>(dst + p.L.scales + slot * nb * 8);
-        const uint4 *st = reinterpret_cast<const uint4 *>(p.xtc + static_cast<size_t>(t) * nb);
-        uint4 *dt = reinterpret_cast<uint4 *>(dst + p.L.tc + slot * nb * 8);
-        for (int i = lane; i < nb / 2; i += 32) {
-            ds[i] = ss[i];
-            dt[i] = st[i];
-        }
+        for (int i = lane; i < nb / 2; i += 32) ds[i] = ss[i];
         if (lane < kEpSlotIds) {
             int id = -1;
             float w = 0.0f;

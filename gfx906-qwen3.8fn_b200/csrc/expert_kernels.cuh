@@ -57,16 +57,12 @@ __device__ __forceinline__ float block_term_q4_1(int dot, float d4, float m4, fl
 // fp32 [rows][K] -> Q8_1.  One warp per 32-value block, lane = element.
 // Writes the planar form (codes/scales) and/or canonical 36-byte blocks.
 __global__ void __launch_bounds__(256)
-quantize_kernel(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error, float2 *tc) {
+quantize_kernel(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error) {
     const size_t warp_global = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const size_t stride = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
     for (size_t b = warp_global; b < blocks; b += stride) {
         const Q8Lane q = quantize_lane(x[b * 32 + lane]);
-        if (tc) {   // (d, 8*(sum(codes)*d - s)) for the tensor-core path's centred weights
-            const int csum = __reduce_add_sync(0xffffffffu, static_cast<int>(q.code));
-            if (lane == 0) tc[b] = make_float2(h2f(q.d), 8.0f * (static_cast<float>(csum) * h2f(q.d) - h2f(q.s)));
-        }
         if (out.codes) {
             out.codes[b * 32 + lane] = q.code;
             if (lane == 0) out.scales[b] = make_float2(h2f(q.d), h2f(q.s));
@@ -209,6 +205,18 @@ struct DownSink {
         atomicAdd(out + static_cast<size_t>(tok) * H + row, c);
         report(flags, error);
     }
+};
+
+// Records the per-block integer dots (and the middle Q8_1) of one expert's
+// pairs for bit-exact parity checks.  Only the Tap instantiations of the
+// streaming and tensor-core kernels write it (moe_debug_block_dots).
+struct TapSink {
+    int expert = -1;                 // expert index whose pairs are recorded
+    const int32_t *pair0 = nullptr;  // device: index of that expert's first pair
+    int max_pairs = 0;
+    int32_t *gate = nullptr, *up = nullptr, *down = nullptr;   // [pair][row][block]
+    int8_t *mid_codes = nullptr;     // [pair][I]
+    uint32_t *mid_ds = nullptr;      // [pair][I/32]: half d | half s << 16
 };
 
 // ---------------------------------------------------------------------------

@@ -20,6 +20,7 @@
 #include "route_kernels.cuh"
 #include "stream_kernels.cuh"
 #include "tc_kernels.cuh"
+#include "tcr_kernels.cuh"
 #include "ep_kernels.cuh"
 #include "router_kernels.cuh"
 
@@ -109,6 +110,9 @@ struct moe_weights_s {
     float *gate_vec = nullptr;
     float *router = nullptr;     // ffn_gate_inp as fp32 [512][H] (zero until uploaded)
     uint8_t *staging = nullptr;  // canonical bytes of one expert (3 matrices)
+    TcrMaps maps;                // tensor maps of the codes and scales (tensor-core path)
+    int raw_rowmajor = 0;        // codes maps are 3-D [expert][row][bytes] (4-D [expert][block][row][16] refused)
+    bool tc_ok = false;          // the tensor-core kernels can run on these weights
 };
 
 struct moe_layer_s {
@@ -156,12 +160,13 @@ int configure_kernels(moe_layer_s *h, int H, int I) {
     h->dn_stages = stream_stages(DnStage(I).bytes, 5);
     if (h->gu_stages < 2 || h->dn_stages < 2) h->gu_stages = h->dn_stages = 0;
     if (h->gu_stages) {
-        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(stream_gu_smem(H, h->gu_stages))));
-        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(stream_dn_smem(I, h->dn_stages))));
-        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(stream_dn_smem(I, h->dn_stages))));
+        const int gu = static_cast<int>(stream_gu_smem(H, h->gu_stages));
+        const int dn = static_cast<int>(stream_dn_smem(I, h->dn_stages));
+        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
+        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
+        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn));
+        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn));
+        MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn));
     }
     return MOE_OK;
 }
@@ -185,6 +190,82 @@ cudaError_t launch_overlapped(void (*kernel)(Args...), int grid, int block, size
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Tensor maps over every expert of a weights object for the TMA loads of the
+// tensor-core kernels: per matrix the code bytes as {16 bytes, row, block,
+// expert} (box 16 x 128 rows x 4 blocks: one stage lands block-major, each
+// block's 128 rows contiguous) -- or, where the driver refuses that stride
+// order, as {row bytes, row, expert} (box 64 bytes x 128 rows) -- and the
+// half scales as {block, row, expert} (box 8 blocks x 128 rows).  Weights
+// whose shape does not tile (rows not a multiple of 128, fewer than 8
+// blocks per row, Q4_1 down matrices) never use the tensor-core path.
+int build_maps(moe_weights_s *w) {
+    const ExpertLayout &L = w->layout;
+    w->tc_ok = false;
+    if (L.down_type != kDownQ4_0 || L.hidden % kRowsM || L.inter % (2 * kRowsM)) return MOE_OK;
+    const EncodeTiledFn enc = encode_tiled();
+    if (!enc) return fail(MOE_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
+    const size_t code_off[3] = {L.gate_codes, L.up_codes, L.down_codes};
+    const size_t sc_off[3] = {L.gate_scales, L.up_scales, L.down_scales};
+    const cuuint64_t rows[3] = {cuuint64_t(L.inter), cuuint64_t(L.inter), cuuint64_t(L.hidden)};
+    const cuuint64_t nbm[3] = {cuuint64_t(L.hidden / 32), cuuint64_t(L.hidden / 32), cuuint64_t(L.inter / 32)};
+    const cuuint64_t E = static_cast<cuuint64_t>(w->experts_total), EB = static_cast<cuuint64_t>(L.bytes);
+    const cuuint32_t one[4] = {1, 1, 1, 1};
+    int rowmajor = 0;
+    for (; rowmajor < 2; ++rowmajor) {
+        bool ok = true;
+        for (int m = 0; m < 3 && ok; ++m) {
+            CUresult r;
+            if (!rowmajor) {
+                const cuuint64_t dims[4] = {16, rows[m], nbm[m], E};
+                const cuuint64_t strides[3] = {nbm[m] * 16, 16, EB};
+                const cuuint32_t box[4] = {16, kRowsM, kRowsKB, 1};
+                r = enc(&w->maps.codes[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w->base + code_off[m], dims, strides, box,
+                        one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            } else {
+                const cuuint64_t dims[3] = {nbm[m] * 16, rows[m], E};
+                const cuuint64_t strides[2] = {nbm[m] * 16, EB};
+                const cuuint32_t box[3] = {kRowsKB * 16, kRowsM, 1};
+                r = enc(&w->maps.codes[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w->base + code_off[m], dims, strides, box,
+                        one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            }
+            ok = r == CUDA_SUCCESS;
+        }
+        if (ok) break;
+    }
+    if (rowmajor == 2) return fail(MOE_CUDA_ERROR, "cuTensorMapEncodeTiled refused the weight code maps");
+    for (int m = 0; m < 3; ++m) {
+        const cuuint64_t dims[3] = {nbm[m], rows[m], E};
+        const cuuint64_t strides[2] = {nbm[m] * 2, EB};
+        const cuuint32_t box[3] = {8, kRowsM, 1};
+        if (enc(&w->maps.scales[m], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, w->base + sc_off[m], dims, strides, box, one,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return fail(MOE_CUDA_ERROR, "cuTensorMapEncodeTiled refused the weight scale maps");
+    }
+    w->raw_rowmajor = rowmajor;
+    w->tc_ok = true;
+    return MOE_OK;
+}
+
 GroupParams group_params(moe_layer_s *h, const moe_weights_s *w, float *out) {
     GroupParams g;
     g.weights = w->base;
@@ -200,37 +281,53 @@ GroupParams group_params(moe_layer_s *h, const moe_weights_s *w, float *out) {
     return g;
 }
 
-// gate/up + down over the tile list already in the workspace.  `events`
-// (optional, three entries) are recorded around the two kernels.
-TcParams tc_params(moe_layer_s *h, const moe_weights_s *w, float *out, bool down) {
-    TcParams t;
-    t.weights = w->base;
-    t.layout = w->layout;
-    t.a_arr = down ? h->tc.a_dn : h->tc.a_gu;
-    t.sc_arr = down ? h->tc.sc_dn : h->tc.sc_gu;
+TcrParams tcr_params(moe_layer_s *h, const moe_weights_s *w, float *out, bool down, const TapSink *tap) {
+    TcrParams t;
+    t.maps = w->maps;
+    t.hidden = w->layout.hidden;
+    t.inter = w->layout.inter;
+    t.raw_rowmajor = w->raw_rowmajor;
+    t.b_arr = down ? h->tc.b_dn : h->tc.b_gu;
+    t.bsc_arr = down ? h->tc.sc_dn : h->tc.sc_gu;
     t.tiles = h->tc.tiles;
     t.num_tiles = h->tc.num_tiles;
     t.pair_token = h->pair_token;
     t.pair_weight = h->pair_weight;
-    t.mid_arr = h->tc.a_dn;
+    t.mid_arr = h->tc.b_dn;
     t.mid_sc_arr = h->tc.sc_dn;
     t.out = out;
     t.error = h->error;
+    if (tap) t.tap = *tap;
     return t;
 }
 
-// Large groups (tiles of up to 128 pairs) on the tcgen05 kernels.
-int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, bool down, cudaStream_t s) {
+// Tensor-core expert kernel over the tile list already in the workspace:
+// persistent, one CTA per SM at most.
+int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, bool down, cudaStream_t s,
+              const TapSink *tap) {
     const ExpertLayout &L = w->layout;
-    const int items = tc_tiles * (down ? L.hidden / kTcN : L.inter / (kTcN / 2));
+    const int items = tc_tiles * ((down ? L.hidden : L.inter) / kRowsM);
     const int grid = std::max(1, std::min(items, h->sms));
-    if (down) tc_expert_kernel<true><<<grid, kTcThreads, TcSmem::bytes, s>>>(tc_params(h, w, out, true));
-    else tc_expert_kernel<false><<<grid, kTcThreads, TcSmem::bytes, s>>>(tc_params(h, w, out, false));
-    return cuda_status(cudaGetLastError(), "tc_expert_kernel");
+    const TcrParams prm = tcr_params(h, w, out, down, tap);
+    cudaError_t e;
+    if (down)
+        e = launch_overlapped(tap ? tc_rows_kernel<true, true> : tc_rows_kernel<true, false>, grid, kRowsThreads,
+                              RowsStage<true>::smem, s, prm);
+    else
+        e = launch_overlapped(tap ? tc_rows_kernel<false, true> : tc_rows_kernel<false, false>, grid, kRowsThreads,
+                              RowsStage<false>::smem, s, prm);
+    return cuda_status(e, "tc_rows_kernel");
 }
 
+// gate/up + down over the tile lists already in the workspace: the streaming
+// dp4a kernels for the small tiles (`stream_groups`: decode sizes, Q4_1 down
+// matrices, trace mode) and the tensor-core kernels for `tc_tiles` (an upper
+// bound on the device-written count).  `events` (optional, three entries) are
+// recorded before the gate/up kernels, between gate/up and down, and after
+// down.  `tap` records one expert's per-block dots (parity taps).
 int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_tiles, cudaStream_t s,
-                   void *const *events = nullptr, int tc_tiles = 0, const DownSink *trace = nullptr) {
+                   void *const *events = nullptr, int tc_tiles = 0, const DownSink *trace = nullptr,
+                   bool stream_groups = true, const TapSink *tap = nullptr) {
     const ExpertLayout &L = w->layout;
     DownSink sink;
     if (trace) sink = *trace;
@@ -245,27 +342,34 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         sp.num_tiles = h->num_tiles;
         sp.sink = sink;
         sp.error = h->error;
+        if (tap) sp.tap = *tap;
         const int gu_items = max_tiles * (L.inter / kGuRows), dn_items = max_tiles * (L.hidden / kDnRows);
-        if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[0]), s));
-        sp.stages = h->gu_stages;
-        sp.stage_bytes = GuStage(L.hidden).bytes;
-        MOE_CUDA(launch_overlapped(stream_gate_up_kernel, std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
-                                   stream_gu_smem(L.hidden, sp.stages), s, sp));
         if (tc_tiles) {
-            tc_gather_kernel<<<dim3(std::min(tc_tiles, h->sms * 2), L.hidden / 256), kTcM, 0, s>>>(
-                h->tc.tiles, h->tc.num_tiles, h->pair_token, h->xq.codes, h->tc.x_tc, L.hidden, h->tc.a_gu,
-                h->tc.sc_gu);
+            tc_rows_gather_kernel<<<dim3(std::min(tc_tiles, h->sms * 2), L.hidden / 256), kRowsNP, 0, s>>>(
+                h->tc.tiles, h->tc.num_tiles, h->pair_token, h->xq, L.hidden, h->tc.b_gu, h->tc.sc_gu);
             MOE_CUDA(cudaGetLastError());
-            if (const int st = launch_tc(h, w, out, tc_tiles, false, s)) return st;
         }
-        if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
-        sp.stages = h->dn_stages;
-        sp.stage_bytes = DnStage(L.inter).bytes;
-        MOE_CUDA(launch_overlapped(trace ? stream_down_kernel<true> : stream_down_kernel<false>,
-                                   std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
-                                   stream_dn_smem(L.inter, sp.stages), s, sp));
+        if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[0]), s));
+        if (stream_groups) {
+            sp.stages = h->gu_stages;
+            sp.stage_bytes = GuStage(L.hidden).bytes;
+            MOE_CUDA(launch_overlapped(tap ? stream_gate_up_kernel<true> : stream_gate_up_kernel<false>,
+                                       std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
+                                       stream_gu_smem(L.hidden, sp.stages), s, sp));
+        }
         if (tc_tiles)
-            if (const int st = launch_tc(h, w, out, tc_tiles, true, s)) return st;
+            if (const int st = launch_tc(h, w, out, tc_tiles, false, s, tap)) return st;
+        if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[1]), s));
+        if (stream_groups) {
+            sp.stages = h->dn_stages;
+            sp.stage_bytes = DnStage(L.inter).bytes;
+            auto kernel = trace ? stream_down_kernel<true, false>
+                                : (tap ? stream_down_kernel<false, true> : stream_down_kernel<false, false>);
+            MOE_CUDA(launch_overlapped(kernel, std::max(1, std::min(dn_items, h->sms)), kStreamThreads,
+                                       stream_dn_smem(L.inter, sp.stages), s, sp));
+        }
+        if (tc_tiles)
+            if (const int st = launch_tc(h, w, out, tc_tiles, true, s, tap)) return st;
         if (events) MOE_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[2]), s));
         return MOE_OK;
     }
@@ -286,10 +390,10 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
 }
 
 int launch_quantize(const float *x, size_t blocks, Q8Planar out, uint8_t *canonical, int *error, int sms,
-                    cudaStream_t s, float2 *tc = nullptr) {
+                    cudaStream_t s) {
     const size_t warps = blocks;
     const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((warps + 7) / 8, size_t(sms) * 16)));
-    quantize_kernel<<<grid, 256, 0, s>>>(x, blocks, out, canonical, error, tc);
+    quantize_kernel<<<grid, 256, 0, s>>>(x, blocks, out, canonical, error);
     return cuda_status(cudaGetLastError(), "quantize_kernel");
 }
 
@@ -346,10 +450,10 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     sp.num_tiles = h->num_tiles;
     sp.max_tiles = h->tiles_max;
     sp.error = h->error;
-    if (x && allow_tc && (!w || w->layout.down_type == kDownQ4_0)) {   // forward: large groups go to the tensor-core kernels
+    if (x && allow_tc && w && w->tc_ok) {   // forward above decode size: the groups go to the tensor-core kernels
         // (Q4_1 down matrices run every group on the dp4a kernels)
-        sp.tc_min = kTcMinGroup;
-        sp.tc_tile = kTcM;
+        sp.tc_min = kRowsMinGroup;
+        sp.tc_tile = kTcTile;
         sp.tc_max = h->tc.max_tiles;
         sp.tc_tiles = h->tc.tiles;
         sp.tc_num = h->tc.num_tiles;
@@ -425,10 +529,11 @@ int moe_weights_create_typed(const moe_layer_desc *desc, int down_type, moe_weig
     if (e == cudaSuccess) e = cudaMalloc(&w->staging, w->layout.bytes / 16 * 18);
     if (e == cudaSuccess) e = cudaMemset(w->gate_vec, 0, sizeof(float) * desc->hidden);
     if (e == cudaSuccess) e = cudaMemset(w->router, 0, rbytes);
-    if (e != cudaSuccess) {
+    const int st = e != cudaSuccess ? cuda_status(e, "moe_weights_create") : build_maps(w);
+    if (st) {
         cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->router); cudaFree(w->staging);
         delete w;
-        return cuda_status(e, "moe_weights_create");
+        return st;
     }
     *out = w;
     return MOE_OK;
@@ -571,7 +676,7 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
         h->tile_off = a.take<int32_t>(kRouterExperts);
         h->num_tiles = a.take<int>(2);   // [0] work tiles, [1] shared-expert tiles at the end
         h->error = a.take<int>(1);
-        tc_workspace_take(h->tc, a, T, H, I, T > kChunk);
+        tc_workspace_take(h->tc, a, h->pairs_max, H, I, T > kChunk);
         if (pass == 0) {
             const size_t bytes = a.used + 256;
             const cudaError_t e = cudaMalloc(&a.base, bytes);
@@ -580,7 +685,7 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
         }
     }
     if (const int st = configure_kernels(h, H, I)) { cudaFree(h->arena.base); delete h; return st; }
-    if (const int st = tc_configure()) { cudaFree(h->arena.base); delete h; return st; }
+    if (const int st = tc_rows_configure()) { cudaFree(h->arena.base); delete h; return st; }
     *out = h;
     return MOE_OK;
 }
@@ -626,8 +731,11 @@ int moe_forward(moe_layer_t h, moe_weights_t w, const float *x, const float *log
     return moe_forward_profiled(h, w, x, logits, tokens, out, flags, stream, nullptr);
 }
 
-int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens,
-                         float *out, int flags, void *stream, void *const *events) {
+}  // extern "C"
+
+namespace {
+int forward_impl(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens, float *out,
+                 int flags, void *stream, void *const *events, const TapSink *tap) {
     if (!h || !w) return fail(MOE_INVALID_ARGUMENT, "null layer or weights");
     if (std::memcmp(&h->desc, &w->desc, offsetof(moe_layer_desc, device) + sizeof(int)) != 0)
         return fail(MOE_INVALID_ARGUMENT, "layer and weights describe different shapes or devices");
@@ -647,16 +755,53 @@ int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const f
     auto s = static_cast<cudaStream_t>(stream);
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
     if (tokens > kChunk)   // small batches quantise inside the fused routing kernel
-        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s,
-                                           h->tc.x_tc))
+        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s))
             return st;
     if (const int st = launch_route(h, w, x, logits, tokens, nullptr, s)) return st;
-    // Upper bound on tensor-core tiles: every group of >= kTcMinGroup pairs,
-    // 128 pairs per tile (the device writes the exact count).
-    const int pairs = tokens * (kTopK + 1);
-    const bool tc_ok = tokens > kChunk && w->layout.down_type == kDownQ4_0;
-    const int tc_tiles = tc_ok ? std::min(h->tc.max_tiles, pairs / kTcMinGroup + pairs / kTcM + 1) : 0;
-    return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events, tc_tiles);
+    // Above decode size every group runs on the tensor-core kernels (the
+    // device writes the tile count; this is its upper bound).
+    const bool tc = tokens > kChunk && w->tc_ok;
+    const int tc_tiles = tc ? tc_tiles_bound(tokens * (kTopK + 1)) : 0;
+    return launch_experts(h, w, out, tiles_bound(tokens, h->desc.has_shared), s, events, tc_tiles, nullptr, !tc, tap);
+}
+}  // namespace
+
+extern "C" {
+
+int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens,
+                         float *out, int flags, void *stream, void *const *events) {
+    return forward_impl(h, w, x, logits, tokens, out, flags, stream, events, nullptr);
+}
+
+int moe_debug_block_dots(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens, int expert,
+                         int max_pairs, int32_t *gate_dots, int32_t *up_dots, int32_t *down_dots, int8_t *mid_codes,
+                         uint32_t *mid_ds, float *out, void *stream) {
+    if (!h || !w) return fail(MOE_INVALID_ARGUMENT, "null layer or weights");
+    if (expert < 0 || expert > w->expert_count || (expert == w->expert_count && !h->desc.has_shared))
+        return fail(MOE_INVALID_ARGUMENT, "expert must be a routed expert index or the shared expert's");
+    if (max_pairs < 1 || max_pairs > h->desc.max_tokens)
+        return fail(MOE_INVALID_ARGUMENT, "max_pairs must be 1..max_tokens");
+    const int H = h->desc.hidden, I = h->desc.inter;
+    const size_t gbytes = static_cast<size_t>(max_pairs) * I * (H / 32) * 4;
+    const size_t dbytes = static_cast<size_t>(max_pairs) * H * (I / 32) * 4;
+    const void *outs[5] = {gate_dots, up_dots, down_dots, mid_codes, mid_ds};
+    const size_t sizes[5] = {gbytes, gbytes, dbytes, static_cast<size_t>(max_pairs) * I,
+                             static_cast<size_t>(max_pairs) * (I / 32) * 4};
+    for (int i = 0; i < 5; ++i) {
+        if (!aligned(outs[i], 4)) return fail(MOE_INVALID_ARGUMENT, "null or misaligned tap buffer");
+        for (int j = 0; j < i; ++j)
+            if (overlap(outs[i], sizes[i], outs[j], sizes[j])) return fail(MOE_INVALID_ARGUMENT, "tap buffers overlap");
+    }
+    TapSink tap;
+    tap.expert = expert;
+    tap.pair0 = h->offsets + expert;   // offsets[512] is the shared expert's first pair
+    tap.max_pairs = max_pairs;
+    tap.gate = gate_dots;
+    tap.up = up_dots;
+    tap.down = down_dots;
+    tap.mid_codes = mid_codes;
+    tap.mid_ds = mid_ds;
+    return forward_impl(h, w, x, logits, tokens, out, MOE_OUT_OVERWRITE, stream, nullptr, &tap);
 }
 
 int moe_router_logits(moe_weights_t w, const float *x, int tokens, float *logits, void *stream) {
@@ -717,8 +862,7 @@ int moe_forward_contributions(moe_layer_t h, moe_weights_t w, const float *x, co
     MOE_CUDA(cudaMemsetAsync(contrib, 0, cbytes, s));
     if (shared) MOE_CUDA(cudaMemsetAsync(shared, 0, xbytes, s));
     if (tokens > kChunk)
-        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s,
-                                           h->tc.x_tc))
+        if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, h->xq, nullptr, h->error, h->sms, s))
             return st;
     if (const int st = launch_route(h, w, x, logits, tokens, nullptr, s, nullptr, nullptr, false)) return st;
     DownSink trace;
@@ -862,6 +1006,7 @@ int moe_expert_create_typed(const void *gate, const void *up, const void *down, 
     int st = cuda_status(cudaMalloc(&w->base, w->layout.bytes), "cudaMalloc");
     if (!st) st = cuda_status(cudaMalloc(&w->gate_vec, sizeof(float) * hidden), "cudaMalloc");
     if (!st) st = cuda_status(cudaMalloc(&w->staging, w->layout.bytes / 16 * 18), "cudaMalloc");
+    if (!st) st = build_maps(w);
     if (!st) st = cuda_status(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream");
     if (!st) st = cuda_status(cudaEventCreate(&e->begin), "event");
     if (!st) st = cuda_status(cudaEventCreate(&e->end), "event");
@@ -1160,25 +1305,13 @@ void ep_take_rx(moe_ep_s *ep, Arena &a) {
     r.tile_off = a.take<int32_t>(kRouterExperts);
     r.num_tiles = a.take<int>(2);
     r.error = a.take<int>(1);
-    r.tc.max_tiles = pairs / kTcM + kRouterExperts + 2 + ep->t_max / kTcM;
-    r.tc.tiles = a.take<int4>(r.tc.max_tiles);
-    r.tc.num_tiles = a.take<int>(1);
-    r.tc.a_gu = r.tc.a_dn = nullptr;
-    r.tc.sc_gu = r.tc.sc_dn = nullptr;
-    if (ep->tc) {
-        const size_t bg = static_cast<size_t>(r.tc.max_tiles) * (H / 32), bd = static_cast<size_t>(r.tc.max_tiles) * (I / 32);
-        r.tc.a_gu = a.take<uint8_t>(bg * kTcM * 32);
-        r.tc.sc_gu = a.take<float2>(bg * kTcM);
-        r.tc.a_dn = a.take<uint8_t>(bd * kTcM * 32);
-        r.tc.sc_dn = a.take<float2>(bd * kTcM);
-    }
+    tc_workspace_take(r.tc, a, pairs, H, I, ep->tc);
     ep->pos = a.take<int32_t>(static_cast<size_t>(ep->t_max) * kEpMaxRanks);
     ep->dmask = a.take<uint8_t>(ep->t_max);
     ep->counts = a.take<int32_t>(kEpMaxRanks);
     ep->epoch = a.take<uint32_t>(1);
     ep->blocks_done = a.take<uint32_t>(1);
     ep->quant_done = a.take<uint32_t>(1);
-    (void)H;
 }
 
 EpParams ep_params(moe_ep_s *ep, int tokens, float *out) {
@@ -1195,7 +1328,6 @@ EpParams ep_params(moe_ep_s *ep, int tokens, float *out) {
     p.weights = ep->tx->weights;
     p.xcodes = ep->tx->xq.codes;
     p.xscales = ep->tx->xq.scales;
-    p.xtc = ep->tx->tc.x_tc;
     p.pos = ep->pos;
     p.dmask = ep->dmask;
     p.counts = ep->counts;
@@ -1238,10 +1370,11 @@ int moe_ep_weights_create_typed(const moe_layer_desc *desc, int rank, int world,
     if (e == cudaSuccess) e = cudaMalloc(&w->staging, w->layout.bytes / 16 * 18);
     if (e == cudaSuccess) e = cudaMemset(w->gate_vec, 0, sizeof(float) * desc->hidden);
     if (e == cudaSuccess) e = cudaMemset(w->router, 0, rbytes);
-    if (e != cudaSuccess) {
+    const int st = e != cudaSuccess ? cuda_status(e, "moe_ep_weights_create") : build_maps(w);
+    if (st) {
         cudaFree(w->base); cudaFree(w->gate_vec); cudaFree(w->router); cudaFree(w->staging);
         delete w;
-        return cuda_status(e, "moe_ep_weights_create");
+        return st;
     }
     *out = w;
     return MOE_OK;
@@ -1305,7 +1438,6 @@ int moe_ep_create(const moe_layer_desc *desc, int rank, int world, moe_ep_t *out
     r.tiles_max = ep->rx_tiles;
     r.xq.codes = reinterpret_cast<int8_t *>(ep->exported + ep->L.codes);
     r.xq.scales = reinterpret_cast<float2 *>(ep->exported + ep->L.scales);
-    r.tc.x_tc = reinterpret_cast<float2 *>(ep->exported + ep->L.tc);
     r.gu_stages = ep->tx->gu_stages;
     r.dn_stages = ep->tx->dn_stages;
     ep->peers.base[rank] = ep->exported;
@@ -1390,7 +1522,7 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
     // 1. own tokens: Q8_1 (+ tensor-core constants), routing, shared gate
     if (tokens > kChunk || ep->tc)
         if (const int st = launch_quantize(x, static_cast<size_t>(tokens) * H / 32, tx->xq, nullptr, tx->error,
-                                           tx->sms, s, tx->tc.x_tc))
+                                           tx->sms, s))
             return st;
     EpParams p = ep_params(ep, tokens, out);
     if (tokens <= kChunk && !ep->tc) {
@@ -1465,9 +1597,9 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
         sp.shared_w = shared_w;
         sp.shared_token0 = ep->rank * ep->t_max;
         sp.shared_expert = ep->ecount;
-        if (ep->tc && w->layout.down_type == kDownQ4_0) {   // Q4_1 down: every group on the dp4a kernels
-            sp.tc_min = kTcMinGroup;
-            sp.tc_tile = kTcM;
+        if (ep->tc && w->tc_ok) {   // Q4_1 down: every group on the dp4a kernels
+            sp.tc_min = kRowsMinGroup;
+            sp.tc_tile = kTcTile;
             sp.tc_max = r.tc.max_tiles;
             sp.tc_tiles = r.tc.tiles;
             sp.tc_num = r.tc.num_tiles;
@@ -1480,9 +1612,9 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
         MOE_CUDA(cudaGetLastError());
     }
     // expert kernels over the received slots, partial rows accumulated locally
-    const bool tc_ok = ep->tc && w->layout.down_type == kDownQ4_0;
-    const int tc_tiles = tc_ok ? std::min(r.tc.max_tiles, ep->rx_pairs / kTcMinGroup + ep->rx_pairs / kTcM + 1) : 0;
-    if (const int st = launch_experts(&r, w, partial, r.tiles_max, s, nullptr, tc_tiles)) return st;
+    const bool tc = ep->tc && w->tc_ok;
+    const int tc_tiles = tc ? r.tc.max_tiles : 0;
+    if (const int st = launch_experts(&r, w, partial, r.tiles_max, s, nullptr, tc_tiles, nullptr, !tc)) return st;
     // 5. the combine publishes "done", waits for every peer's, then pulls the partial rows
     if (flags == MOE_OUT_OVERWRITE) MOE_CUDA(cudaMemsetAsync(out, 0, xbytes, s));
     const int cthreads = std::min(kEpCombineThreads, std::max(32, (H / 4 + 31) / 32 * 32));

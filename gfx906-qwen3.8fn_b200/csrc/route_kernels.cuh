@@ -281,8 +281,8 @@ struct ScanParams {
     int *num_tiles;         // [0] tiles, [1] how many of them (at the end) are shared-expert tiles
     int max_tiles;
     int *error;
-    // Groups of at least tc_min pairs (0: never) go to the tensor-core path
-    // as tiles of up to tc_tile pairs: {expert, first pair, count, 0}.
+    // Groups of at least tc_min pairs (0: never) go to the tensor-core path,
+    // split evenly into ceil(n / tc_tile) tiles: {expert, first pair, count, 0}.
     int tc_min = 0, tc_tile = 128, tc_max = 0;
     int4 *tc_tiles = nullptr;
     int *tc_num = nullptr;
@@ -324,8 +324,10 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
         }
     }
     for (int i = 0; i < ntc; ++i)
-        if (tcoff + i < p.tc_max)
-            p.tc_tiles[tcoff + i] = make_int4(e, off + i * p.tc_tile, min(p.tc_tile, run - i * p.tc_tile), 0);
+        if (tcoff + i < p.tc_max) {
+            const int a = i * run / ntc, b = (i + 1) * run / ntc;
+            p.tc_tiles[tcoff + i] = make_int4(e, off + a, b - a, 0);
+        }
     int shared_tiles = 0, shared_tc = 0;
     // shared pair i: from route_topk at tokens*10 + i, or given directly
     const int shared_src = p.shared_w ? total : p.tokens * kTopK;
@@ -337,9 +339,10 @@ __global__ void __launch_bounds__(512) route_scan_kernel(ScanParams p) {
     if (p.has_shared && p.tc_min > 0 && p.tokens >= p.tc_min) {
         shared_tc = (p.tokens + p.tc_tile - 1) / p.tc_tile;
         for (int i = e; i < shared_tc; i += 512)
-            if (tc_total + i < p.tc_max)
-                p.tc_tiles[tc_total + i] = make_int4(p.shared_expert, total + i * p.tc_tile,
-                                                     min(p.tc_tile, p.tokens - i * p.tc_tile), 0);
+            if (tc_total + i < p.tc_max) {
+                const int a = i * p.tokens / shared_tc, b = (i + 1) * p.tokens / shared_tc;
+                p.tc_tiles[tc_total + i] = make_int4(p.shared_expert, total + a, b - a, 0);
+            }
     } else if (p.has_shared) {
         shared_tiles = (p.tokens + p.tile - 1) / p.tile;
         for (int i = e; i < shared_tiles; i += 512) {

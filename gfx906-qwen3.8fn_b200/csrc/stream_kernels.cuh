@@ -40,6 +40,18 @@ struct StreamParams {
     int *error;
     int stages;
     uint32_t stage_bytes;
+    TapSink tap;            // per-block dot tap (Tap instantiations only)
+};
+
+// Where a Tap instantiation stores the dots of one item of the tapped expert.
+struct ItemTap {
+    int32_t *dst0 = nullptr, *dst1 = nullptr;   // gate and up (or down) dot arrays, null when not tapped
+    int pl = 0;                                 // pair-local index of the item's first pair
+    int rows = 0, nb = 0, row0 = 0, max_pairs = 0;
+    __device__ __forceinline__ void put(int32_t *dst, int j, int row, int b, int dot) const {
+        const int q = pl + j;
+        if (q >= 0 && q < max_pairs) dst[(static_cast<size_t>(q) * rows + row0 + row) * nb + b] = dot;
+    }
 };
 
 // ---- stage layouts (meta, then codes, then half scales) --------------------
@@ -144,10 +156,10 @@ __device__ __forceinline__ void init_ring(uint64_t *full, uint64_t *empty, int s
 // ---- gate/up + SiLU*up + Q8_1 middle ---------------------------------------
 // Consumer warp cw owns gate rows and up rows R*cw .. R*cw+R-1 of the slab
 // (R = kGuWarpRows); lane l owns blocks l, l+32, ...
-template <int N>
+template <int N, bool Tap>
 __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_t *st, const GuStage &L,
                                              const int4 *const *xr, const float2 *const *sr, int cw, int lane,
-                                             uint64_t *empty_bar, float *mid) {
+                                             uint64_t *empty_bar, float *mid, const ItemTap &tap) {
     const int nb = p.layout.hidden / 32;
     const uint4 *gc = reinterpret_cast<const uint4 *>(st + L.gcodes);
     const uint4 *uc = reinterpret_cast<const uint4 *>(st + L.ucodes);
@@ -184,6 +196,12 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
             for (int q = 0; q < R; ++q)
                 acc2[q][j] = block_term2(block_dot2(wc[2 * q], lo, hi), block_dot2(wc[2 * q + 1], lo, hi), d4p[q], d8,
                                          nsp, acc2[q][j]);
+            if constexpr (Tap) {
+                if (tap.dst0)
+#pragma unroll
+                    for (int r = 0; r < 2 * R; ++r)
+                        tap.put(r < R ? tap.dst0 : tap.dst1, j, cw * R + (r % R), b, block_dot(wc[r], lo, hi));
+            }
         }
     }
     __syncwarp();
@@ -217,6 +235,7 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
     }
 }
 
+template <bool Tap>
 __global__ void __launch_bounds__(kStreamThreads, 1)
 stream_gate_up_kernel(StreamParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -251,6 +270,7 @@ stream_gate_up_kernel(StreamParams p) {
     const int cw = warp - 1;
     bool failed = false;
     int i = 0;
+    const int tap_base = (Tap && p.tap.expert >= 0) ? *p.tap.pair0 : 0;
     for (int pos = blockIdx.x; pos < order.total; pos += gridDim.x, ++i) {
         const int item = order(pos);
         const TileRec rec = load_tile(p.tiles + item / slabs);
@@ -270,13 +290,23 @@ stream_gate_up_kernel(StreamParams p) {
         const int s = i % p.stages;
         if (!failed && !mbar_wait(&full[s], (i / p.stages) & 1, p.error)) failed = true;
         float *mid = smid + (i & 1) * kGemvTile * 32;
+        ItemTap tap;
+        if (Tap && rec.e == p.tap.expert) {
+            tap.dst0 = p.tap.gate;
+            tap.dst1 = p.tap.up;
+            tap.pl = rec.p0 - tap_base;
+            tap.rows = I;
+            tap.nb = nb;
+            tap.row0 = (item % slabs) * kGuRows;
+            tap.max_pairs = p.tap.max_pairs;
+        }
         if (!failed) {
             const uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
             switch (n) {
-            case 1: gate_up_item<1>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
-            case 2: gate_up_item<2>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
-            case 3: gate_up_item<3>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
-            default: gate_up_item<4>(p, st, L, xr, sr, cw, lane, &empty[s], mid); break;
+            case 1: gate_up_item<1, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
+            case 2: gate_up_item<2, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
+            case 3: gate_up_item<3, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
+            default: gate_up_item<4, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
             }
         }
         named_barrier(1, kConsumerThreads);         // every consumer warp, even after a failed wait
@@ -290,6 +320,13 @@ stream_gate_up_kernel(StreamParams p) {
                 p.mid.scales[pair * slabs + slab] = make_float2(h2f(q.d), h2f(q.s));
                 report(q.flags, p.error);
             }
+            if constexpr (Tap) {
+                const int pl = rec.p0 + j - tap_base;
+                if (rec.e == p.tap.expert && pl >= 0 && pl < p.tap.max_pairs) {
+                    p.tap.mid_codes[static_cast<size_t>(pl) * I + slab * 32 + lane] = q.code;
+                    if (lane == 0) p.tap.mid_ds[static_cast<size_t>(pl) * slabs + slab] = q.d | (uint32_t(q.s) << 16);
+                }
+            }
         }
     }
 }
@@ -299,13 +336,22 @@ stream_gate_up_kernel(StreamParams p) {
 // kDnLaneRows): lane l takes rows 8R*cw + l/4 + 8k (k < R) and blocks l%4,
 // l%4+4, ...; two shuffles finish each row, then out[token][row] += weight * y
 // (red.global.add).
-template <int N, bool Q41, bool Trace>
+template <int N, bool Q41, bool Trace, bool Tap>
 __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, int I, int H, int row0,
                                           int lr0, int q, uint64_t *empty_bar, int lane, const DownSink &sink,
-                                          int *error) {
+                                          int *error, const TapSink &tsink, int tap_base) {
     const int nb = I / 32;
     const TileRec &meta = *reinterpret_cast<const TileRec *>(st);
     const int me = meta.e, mp0 = meta.p0;   // read before the stage is released
+    ItemTap tap;
+    if (Tap && me == tsink.expert) {
+        tap.dst0 = tsink.down;
+        tap.pl = mp0 - tap_base;
+        tap.rows = H;
+        tap.nb = I / 32;
+        tap.row0 = row0 - lr0;
+        tap.max_pairs = tsink.max_pairs;
+    }
     const uint4 *dc = reinterpret_cast<const uint4 *>(st + L.dcodes);
     const uint16_t *ds = reinterpret_cast<const uint16_t *>(st + L.dsc);
     const uint16_t *dm = reinterpret_cast<const uint16_t *>(st + L.dmin);
@@ -347,6 +393,11 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
 #pragma unroll
                 for (int k = 0; k < R; ++k)
                     acc[k][j] = block_term_q4_1(block_dot2(wk[k], xlo, xhi), d4[k], m4[k], sc.x, sc.y, acc[k][j]);
+                if constexpr (Tap) {
+                    if (tap.dst0)
+#pragma unroll
+                        for (int k = 0; k < R; ++k) tap.put(tap.dst0, j, lr0 + 8 * k, b, block_dot(wk[k], xlo, xhi));
+                }
             }
         }
         __syncwarp();
@@ -370,6 +421,11 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
                 for (int k = 0; k < R / 2; ++k)
                     acc2[k][j] = block_term2(block_dot2(wk[2 * k], xlo, xhi), block_dot2(wk[2 * k + 1], xlo, xhi),
                                              dk[k], d8, nsp, acc2[k][j]);
+                if constexpr (Tap) {
+                    if (tap.dst0)
+#pragma unroll
+                        for (int k = 0; k < R; ++k) tap.put(tap.dst0, j, lr0 + 8 * k, b, block_dot(wk[k], xlo, xhi));
+                }
             }
         }
         __syncwarp();
@@ -390,7 +446,7 @@ __device__ __forceinline__ void down_item(const uint8_t *st, const DnStage &L, i
         }
 }
 
-template <bool Trace>
+template <bool Trace, bool Tap>
 __global__ void __launch_bounds__(kStreamThreads, 1)
 stream_down_kernel(StreamParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -458,6 +514,7 @@ stream_down_kernel(StreamParams p) {
 
     const int cw = warp - 1, q = lane & 3;
     const int lr0 = cw * 8 * kDnLaneRows + (lane >> 2);
+    const int tap_base = (Tap && p.tap.expert >= 0) ? *p.tap.pair0 : 0;
     int i = 0;
     for (int pos = blockIdx.x; pos < order.total; pos += gridDim.x, ++i) {
         const int item = order(pos);
@@ -468,17 +525,41 @@ stream_down_kernel(StreamParams p) {
         const int row0 = (item % slabs) * kDnRows + lr0;
         if (q41) {
             switch (n) {
-            case 1: down_item<1, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 2: down_item<2, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 3: down_item<3, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            default: down_item<4, true, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 1:
+                down_item<1, true, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
+            case 2:
+                down_item<2, true, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
+            case 3:
+                down_item<3, true, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
+            default:
+                down_item<4, true, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
             }
         } else {
             switch (n) {
-            case 1: down_item<1, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 2: down_item<2, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            case 3: down_item<3, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
-            default: down_item<4, false, Trace>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error); break;
+            case 1:
+                down_item<1, false, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
+            case 2:
+                down_item<2, false, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
+            case 3:
+                down_item<3, false, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
+            default:
+                down_item<4, false, Trace, Tap>(st, L, I, H, row0, lr0, q, &empty[s], lane, p.sink, p.error,
+                                                            p.tap, tap_base);
+                break;
             }
         }
     }

@@ -30,7 +30,8 @@ struct RouteAssignment {
 };
 static_assert(sizeof(RouteAssignment) == 16);
 
-class RouteGroups {
+// Exported from libqwen_moe_b200.so (built with hidden default visibility).
+class __attribute__((visibility("default"))) RouteGroups {
 public:
     enum class Bound { chunk1024, layerwise16384 };
     explicit RouteGroups(int token_capacity, Bound bound = Bound::chunk1024);

@@ -255,6 +255,23 @@ int moe_ep_read_flags(moe_ep_t ep, int *flags_host, int clear, void *stream);
  * sticky bits in *error_dev (caller-zeroed). */
 int moe_quantize_q8_1(const float *x_dev, int width, int columns, void *q8_dev, int *error_dev,
                       void *stream);
+/* Per-block dot tap of the forward's own expert kernels (the parity tap
+ * moe_debug_block_dots; the reference checks its Session producer kernels
+ * against its CPU expert the same way, src/cpu_expert_shadow.hip:333-341).
+ * Runs moe_forward with MOE_OUT_OVERWRITE into out_dev, through the kernels a
+ * forward of this size uses (streaming dp4a kernels at decode sizes, the
+ * tensor-core kernels above), and records for the pairs of `expert` (0..511,
+ * or 512 for the shared expert), in the grouped pair order, numbered from the
+ * expert's first pair:
+ *   gate_dots, up_dots  int32 [max_pairs][I][H/32]  uncentred sum(q*x) per block,
+ *   down_dots           int32 [max_pairs][H][I/32]  against the middle Q8_1 the
+ *                                                  gate/up kernel produced,
+ *   mid_codes           int8  [max_pairs][I]        that middle's codes,
+ *   mid_ds              uint32 [max_pairs][I/32]    its half d | half s << 16.
+ * Pairs beyond max_pairs are not recorded. */
+int moe_debug_block_dots(moe_layer_t h, moe_weights_t w, const float *x_dev, const float *logits_dev, int tokens,
+                         int expert, int max_pairs, int32_t *gate_dots, int32_t *up_dots, int32_t *down_dots,
+                         int8_t *mid_codes, uint32_t *mid_ds, float *out_dev, void *stream);
 /* Q4_0 x Q8_1 linear: out[c][r] = sum_b d4*(dot*d8 - 8*s8) for canonical
  * Q4_0 weights [rows][K/32] and canonical Q8_1 input [columns][K/32].
  * Replaces launch_quantized_linear{,_short,_tiled} (src/hip/linear.hip:445-490).

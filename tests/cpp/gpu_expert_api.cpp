@@ -1,4 +1,5 @@
-// C++20 exercise of qmoe::GpuExpert (include/qmoe/gpu_expert.hpp) with the
+// C++20 exercise of qwen::GpuExpert (include/qwen/gpu_expert.hpp, a drop-in for the
+// reference's src/gpu_expert.hpp implemented by include/qmoe/gpu_expert.hpp) with the
 // reference GpuExpert's calls and error behaviour (src/gpu_expert.hpp,
 // src/hip/expert.hip:183-241).  Reads fixtures written by
 // tests/test_cpp_api.py into <dir>, writes the GPU results back there.
@@ -20,7 +21,7 @@
 #include <string>
 #include <vector>
 
-#include "qmoe/gpu_expert.hpp"
+#include "gpu_expert.hpp"   // include/qwen/: the reference's header name and namespace
 
 namespace {
 std::vector<std::byte> read_file(const std::string &path) {
@@ -64,21 +65,21 @@ int main(int argc, char **argv) {
     std::ifstream(dir + "/meta.txt") >> H >> I >> cols >> down_type;
     const auto gate = read_file(dir + "/gate.bin"), up = read_file(dir + "/up.bin"), down = read_file(dir + "/down.bin");
     const auto x = read_as<float>(dir + "/x.bin");
-    const auto xq = read_as<qmoe::Q8_1>(dir + "/xq.bin");
-    const auto mid = read_as<qmoe::Q8_1>(dir + "/mid.bin");
-    const auto dt = static_cast<qmoe::TensorType>(down_type);
-    const qmoe::QMatrix g{qmoe::TensorType::Q4_0, H, I, gate}, u{qmoe::TensorType::Q4_0, H, I, up}, d{dt, I, H, down};
+    const auto xq = read_as<qwen::Q8_1>(dir + "/xq.bin");
+    const auto mid = read_as<qwen::Q8_1>(dir + "/mid.bin");
+    const auto dt = static_cast<qwen::TensorType>(down_type);
+    const qwen::QMatrix g{qwen::TensorType::Q4_0, H, I, gate}, u{qwen::TensorType::Q4_0, H, I, up}, d{dt, I, H, down};
 
     // constructor checks: shape/type and byte size, before any device work
-    if (!throws<std::invalid_argument>([&] { qmoe::GpuExpert(g, u, g, 0, cols, true); }))
+    if (!throws<std::invalid_argument>([&] { qwen::GpuExpert(g, u, g, 0, cols, true); }))
         return fail("mismatched down shape accepted");
-    if (!throws<std::invalid_argument>([&] { qmoe::GpuExpert(g, u, d, 0, 0, true); }))
+    if (!throws<std::invalid_argument>([&] { qwen::GpuExpert(g, u, d, 0, 0, true); }))
         return fail("zero max_columns accepted");
-    const qmoe::QMatrix short_gate{qmoe::TensorType::Q4_0, H, I, std::span(gate).first(gate.size() - 1)};
-    if (!throws<std::invalid_argument>([&] { qmoe::GpuExpert(short_gate, u, d, 0, cols, true); }))
+    const qwen::QMatrix short_gate{qwen::TensorType::Q4_0, H, I, std::span(gate).first(gate.size() - 1)};
+    if (!throws<std::invalid_argument>([&] { qwen::GpuExpert(short_gate, u, d, 0, cols, true); }))
         return fail("short weight span accepted");
 
-    qmoe::GpuExpert expert(g, u, d, 0, cols, true);
+    qwen::GpuExpert expert(g, u, d, 0, cols, true);
     expert.check_quantization(x, xq);
     auto bad = xq;
     bad[0].qs[0] ^= 1;

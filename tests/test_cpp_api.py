@@ -1,6 +1,8 @@
-"""The C++20 host API headers (include/qmoe/*.hpp): qmoe::GpuExpert over the C
-ABI, exercised by tests/cpp/gpu_expert_api.cpp the way the reference's own
-GpuExpert is used (src/gpu_expert.hpp, src/hip/expert.hip:183-241).
+"""The C++20 host API headers at the reference's names (include/qwen/*.hpp, namespace
+qwen, over include/qmoe/*.hpp and the C ABI): qwen::GpuExpert exercised by
+tests/cpp/gpu_expert_api.cpp the way the reference's own GpuExpert is used
+(src/gpu_expert.hpp, src/hip/expert.hip:183-241), and qwen::RouteGroups by
+tests/cpp/routes_api.cpp (src/routes.hpp:18-65).
 
 CPU: the program compiles as C++20 and links against libqwen_moe_b200.so.
 GPU: it runs on oracle fixtures (Q4_0 and Q4_1 down) and its outputs match
@@ -17,12 +19,13 @@ PKG = os.path.join(ROOT, "gfx906-qwen3.8fn_b200")
 SRC = os.path.join(ROOT, "tests", "cpp", "gpu_expert_api.cpp")
 
 
-def build_program(out_dir):
+def build_program(out_dir, src=SRC, name="gpu_expert_api"):
     cxx = shutil.which("g++")
     if cxx is None:
         pytest.skip("no C++ compiler")
-    exe = os.path.join(out_dir, "gpu_expert_api")
-    cmd = [cxx, "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"), SRC,
+    exe = os.path.join(out_dir, name)
+    # include/qwen/ first, as a caller of the reference's headers would put it
+    cmd = [cxx, "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include", "qwen"), src,
            "-L", PKG, "-lqwen_moe_b200", f"-Wl,-rpath,{PKG}", "-o", exe]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
@@ -31,6 +34,14 @@ def build_program(out_dir):
 
 def test_gpu_expert_header_compiles_and_links(pkg, tmp_path):
     assert os.path.exists(build_program(str(tmp_path)))
+
+
+def test_route_groups_drop_in_header(pkg, tmp_path):
+    """qwen::RouteGroups through include/qwen/routes.hpp: grouping order, raw
+    weight bits, validation before mutation (host code, no GPU needed)."""
+    exe = build_program(str(tmp_path), os.path.join(ROOT, "tests", "cpp", "routes_api.cpp"), "routes_api")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and r.stdout.startswith("ok"), r.stdout + r.stderr
 
 
 @pytest.mark.gpu
