@@ -13,6 +13,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libqwen_moe_b200.so")
 SOURCES = ["moe_layer.cu", "route_groups.cpp"]
 HEADERS = ["common.cuh", "expert_kernels.cuh", "route_kernels.cuh", "stream_kernels.cuh", "ptx.cuh", "tc_kernels.cuh",
+           "tcr_kernels.cuh",
            "ep_kernels.cuh", "ep_common.cuh", "router_kernels.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
