@@ -45,11 +45,11 @@ DOWN_BYTES = 589824
 METRIC = "MoE-layer tokens/s (Q4_0 experts)"
 
 CONFIGS = {
-    1: dict(name="decode_T1", tokens=1, ubatches=1, layers=48, routing="normal"),
-    2: dict(name="decode_T8_ragged", tokens=8, ubatches=1, layers=48, routing="normal"),
-    3: dict(name="prefill_T4096_zipf1.1", tokens=4096, ubatches=1, layers=48, routing="zipf"),
-    4: dict(name="prefill_16384_ubatch1024_48layers", tokens=1024, ubatches=16, layers=48, routing="normal"),
-    5: dict(name="mixed_T32768", tokens=32768, ubatches=1, layers=8, routing="mixed"),
+    1: dict(name="decode_T1", tokens=1, ubatches=1, layers=48, routing="normal", steps=20),
+    2: dict(name="decode_T8_ragged", tokens=8, ubatches=1, layers=48, routing="normal", steps=20),
+    3: dict(name="prefill_T4096_zipf1.1", tokens=4096, ubatches=1, layers=48, routing="zipf", steps=10),
+    4: dict(name="prefill_16384_ubatch1024_48layers", tokens=1024, ubatches=16, layers=48, routing="normal", steps=5),
+    5: dict(name="mixed_T32768", tokens=32768, ubatches=1, layers=8, routing="mixed", steps=5),
 }
 
 
@@ -88,9 +88,9 @@ class ClockSampler:
     # NVML clocks-event reason bits, in NAMES order
     BITS = (0x8, 0x40, 0x20, 0x4)
 
-    def __init__(self, device):
+    def __init__(self, device, path=""):
         self.device = device
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_dev{device}.csv")
+        self.path = path
         self.thread = None
         self.rows = []
 
@@ -138,14 +138,14 @@ class ClockSampler:
             return None
         self.stop_evt.set()
         self.thread.join(timeout=5)
-        try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            with open(self.path, "w") as fh:
-                for sm, mx, pw, rs in self.rows:
-                    flags = ["Active" if rs & b else "Not Active" for b in self.BITS]
-                    fh.write(f"{self.device}, {sm}, {mx}, {pw:.2f}, 0x{rs:016x}, " + ", ".join(flags) + "\n")
-        except OSError:
-            pass
+        if self.path:
+            try:
+                with open(self.path, "w") as fh:
+                    for sm, mx, pw, rs in self.rows:
+                        flags = ["Active" if rs & b else "Not Active" for b in self.BITS]
+                        fh.write(f"{self.device}, {sm}, {mx}, {pw:.2f}, 0x{rs:016x}, " + ", ".join(flags) + "\n")
+            except OSError:
+                pass
         if not self.rows:
             return None
         reasons = sorted({n for _, _, _, rs in self.rows for n, b in zip(self.NAMES, self.BITS) if rs & b})
@@ -190,111 +190,171 @@ def expected_distinct(T, experts=E, k=K_TOP):
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_baseline(cfg, seed, budget_s=8.0):
-    """Reference CPU path (oracle/_ref CpuExpertPool, AVX2, pinned workers on all
-    physical cores) on one layer pass of the workload; restated routing/fold."""
+def cpu_pools(R, O):
+    """The reference's CpuExpertPool over every allowed physical core, split
+    into equal pools of at most 15 workers (its per-pool limit), workers pinned."""
     import ctypes
-    import oracle as O
-    R = O.ref()
-    if R is None:
-        return cpu_baseline_port(cfg, seed, budget_s)
-    T = min(cfg["tokens"], 8)
-    rng = np.random.default_rng(seed)
-    x = rng.standard_normal((T, H)).astype(np.float32)
-    logits = make_logits(rng, cfg, T)
-    gv = (rng.standard_normal(H) * 0.02).astype(np.float32)
-    probs, _ = O.router_softmax(logits)
-    ids, _ = O.select_routes(probs)
-    experts = sorted(set(int(e) for e in ids.ravel())) + [E]
-    wts = {e: O.synth_expert(seed, 0, e) for e in experts}
-    handles = {e: R.ref_expert_new(O.ptr(w[0]), O.ptr(w[1]), O.ptr(w[2]), w[0].size, w[2].size, H, I)
-               for e, w in wts.items()}
     cpus = np.zeros(4096, np.int32)
     n = ctypes.c_size_t(0)
     pin = R.ref_allowed_physical_cpus(O.ptr(cpus), cpus.size, ctypes.byref(n)) == 0 and n.value > 0
     ncores = n.value if pin else (os.cpu_count() or 1)
-    pools = []
-    start = 0
-    while start < ncores:
-        k = min(15, ncores - start)
+    npools = (ncores + 14) // 15
+    sizes = [ncores // npools + (1 if i < ncores % npools else 0) for i in range(npools)]
+    pools, start = [], 0
+    for k in sizes:
         p = R.ref_pool_new(k, 1 if pin else 0, O.ptr(cpus[start:start + k]) if pin else None, k if pin else 0)
         if not p:
-            break
-        pools.append(p)
+            raise RuntimeError("CpuExpertPool creation failed")
+        pools.append((p, k))
         start += k
-    ncores = sum(min(15, ncores - 15 * i) for i in range(len(pools)))
-    rg = R.ref_routes_new(max(T, 1), 0)
+    return pools, ncores
 
-    def one_pass():
-        xq, _ = O.quantize(x)
-        pr, _ = O.router_softmax(logits)
-        ids_, w_ = O.select_routes(pr)
-        assert R.ref_routes_prepare(rg, O.ptr(ids_), O.ptr(w_), ids_.size, T) == 0
-        a = np.zeros(ids_.size, O.ASSIGN_DTYPE)
-        R.ref_routes_assignments(rg, O.ptr(a), a.size)
-        contrib = np.zeros((T, K_TOP, H), np.float32)
-        shared = np.zeros((T, H), np.float32)
-        jobs = []
-        e_of = a["expert"]
-        for e in np.unique(e_of):
-            rows = a[e_of == e]
-            for c0 in range(0, len(rows), 3):
-                jobs.append((int(e), rows[c0:c0 + 3]))
-        for c0 in range(0, T, 3):
-            jobs.append((E, np.array([(t, K_TOP, E, 1.0) for t in range(c0, min(T, c0 + 3))], O.ASSIGN_DTYPE)))
-        outs = []
+
+class CpuReference:
+    """The reference's CPU expert path on one MoE-layer pass over
+    min(T, max_tokens) tokens: the reference's quantize_q8 order (restated),
+    router softmax and select_routes (restated), RouteGroups::prepare (the
+    reference's), whole CpuExpert jobs of <= 3 columns on the reference's
+    CpuExpertPool (AVX2, pinned workers on every allowed physical core), and the
+    rank-order fold and shared sigmoid add (restated).  Set up once; each
+    `one_pass()` is one timed unit."""
+
+    def __init__(self, cfg, seed, max_tokens=1024):
+        import ctypes
+        import oracle as O
+        R = O.ref()
+        if R is None:
+            raise RuntimeError("oracle/_ref was not built (the reference tree was absent at build time)")
+        self.O, self.R, self.ctypes = O, R, ctypes
+        T = self.T = min(cfg["tokens"], max_tokens)
+        rng = np.random.default_rng(seed)
+        self.x = rng.standard_normal((T, H)).astype(np.float32)
+        self.logits = make_logits(rng, cfg, T)
+        self.gv = (rng.standard_normal(H) * 0.02).astype(np.float32)
+        probs, _ = O.router_softmax(self.logits)
+        ids0, _ = O.select_routes(probs)
+        self.experts = sorted(set(int(e) for e in ids0.ravel())) + [E]
+        self.wts = {e: O.synth_expert(seed, 0, e) for e in self.experts}
+        self.handles = {e: R.ref_expert_new(O.ptr(w[0]), O.ptr(w[1]), O.ptr(w[2]), w[0].size, w[2].size, H, I)
+                        for e, w in self.wts.items()}
+        self.pools, _ = cpu_pools(R, O)
+        self.workers = sum(k for _, k in self.pools)
+        self.rg = R.ref_routes_new(max(T, 1), 0 if T <= 1024 else 1)
+        self.xq = np.zeros((T, H // 32), O.Q8_DTYPE)
+        self.row_bytes = (H // 32) * 36
+        self.out_all = np.zeros((T * (K_TOP + 1), H), np.float32)   # staging rows: routed pairs, then shared
+        self.ticket = ctypes.c_size_t(0)
+        self.njobs = 0
+
+    def run_jobs(self, jobs):
+        """Submit (expert, token rows, first output row) jobs round-robin over
+        the pools; a pool is drained only when its 30 tickets are in use, so
+        the other pools keep working meanwhile."""
+        R, ctypes = self.R, self.ctypes
+        used = [0] * len(self.pools)
         keep = []
-        qi = 0
-        while qi < len(jobs):
-            batch = []
-            for p in pools:
-                for _ in range(30):
-                    if qi >= len(jobs):
-                        break
-                    e, rows = jobs[qi]
-                    qi += 1
-                    cols = len(rows)
-                    inp = (ctypes.c_void_p * 3)(*[xq[int(r["token"])].ctypes.data for r in rows] + [None] * (3 - cols))
-                    out = np.zeros(cols * H, np.float32)
-                    ticket = ctypes.c_size_t(0)
-                    st = R.ref_pool_submit(p, handles[e], cols, inp, H // 32, 0, O.ptr(out), out.size, ctypes.byref(ticket))
-                    assert st == 0, st
-                    keep.append(inp)
-                    batch.append((rows, out))
-            for p in pools:
+        xq_base, out_base = self.xq.ctypes.data, self.out_all.ctypes.data
+        for i, (e, toks, row0) in enumerate(jobs):
+            pi = i % len(self.pools)
+            p, _ = self.pools[pi]
+            if used[pi] == 30:
                 assert R.ref_pool_drain(p) == 0
                 R.ref_pool_reset(p)
-            outs.extend(batch)
-        for rows, out in outs:
-            out = out.reshape(len(rows), H)
-            for r, y in zip(rows, out):
-                if int(r["rank"]) == K_TOP:
-                    shared[int(r["token"])] = y
-                else:
-                    contrib[int(r["token"]), int(r["rank"])] = y
+                used[pi] = 0
+            inp = (ctypes.c_void_p * 3)(*[xq_base + int(t) * self.row_bytes for t in toks] + [None] * (3 - len(toks)))
+            keep.append(inp)
+            st = R.ref_pool_submit(p, self.handles[e], len(toks), inp, H // 32, 0,
+                                   ctypes.c_void_p(out_base + row0 * H * 4), len(toks) * H, ctypes.byref(self.ticket))
+            assert st == 0, st
+            used[pi] += 1
+        for p, _ in self.pools:
+            assert R.ref_pool_drain(p) == 0
+            R.ref_pool_reset(p)
+
+    def one_pass(self):
+        O, R, T = self.O, self.R, self.T
+        O.lib().o_quantize_q8_1(O.ptr(self.x), self.x.size, O.ptr(self.xq))
+        pr, _ = O.router_softmax(self.logits)
+        ids_, w_ = O.select_routes(pr)
+        assert R.ref_routes_prepare(self.rg, O.ptr(ids_), O.ptr(w_), ids_.size, T) == 0
+        a = np.zeros(ids_.size, O.ASSIGN_DTYPE)
+        R.ref_routes_assignments(self.rg, O.ptr(a), a.size)
+        # one job per <= 3 consecutive pairs of a group; each job's output rows
+        # are contiguous staging rows, scattered to [token][rank] afterwards
+        jobs, staged, row = [], [], 0
+        e_of = a["expert"]
+        bounds = list(np.flatnonzero(np.r_[True, e_of[1:] != e_of[:-1]])) + [len(a)]
+        for g0, g1 in zip(bounds[:-1], bounds[1:]):
+            for c0 in range(g0, g1, 3):
+                chunk = a[c0:min(g1, c0 + 3)]
+                jobs.append((int(chunk[0]["expert"]), chunk["token"], row))
+                staged.append((row, chunk))
+                row += len(chunk)
+        shared0 = row
+        jobs += [(E, np.arange(c0, min(T, c0 + 3)), shared0 + c0) for c0 in range(0, T, 3)]
+        self.run_jobs(jobs)
+        contrib = np.empty((T, K_TOP, H), np.float32)
+        for r0, chunk in staged:
+            contrib[chunk["token"], chunk["rank"]] = self.out_all[r0:r0 + len(chunk)]
         res = np.empty((T, H), np.float32)
         O.lib().o_routed_fold(O.ptr(contrib), O.ptr(np.ascontiguousarray(w_)), T, H, O.ptr(res))
-        O.lib().o_shared_add(O.ptr(x), O.ptr(gv), O.ptr(shared), T, H, O.ptr(res))
+        O.lib().o_shared_add(O.ptr(self.x), O.ptr(self.gv),
+                             O.ptr(np.ascontiguousarray(self.out_all[shared0:shared0 + T])), T, H, O.ptr(res))
+        self.njobs = len(jobs)
         return res
 
-    one_pass()
+    def job_ms(self):
+        """One 3-column whole-expert job on one worker (the unit of the pass)."""
+        R, ctypes = self.R, self.ctypes
+        p1, _ = self.pools[0]
+        base = self.xq.ctypes.data
+        single = (ctypes.c_void_p * 3)(*[base + i * self.row_bytes if i < self.T else None for i in range(3)])
+        t1 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t1 < 0.3:
+            assert R.ref_pool_submit(p1, self.handles[self.experts[0]], min(3, self.T), single, H // 32, 0,
+                                     self.O.ptr(self.out_all), min(3, self.T) * H, ctypes.byref(self.ticket)) == 0
+            assert R.ref_pool_drain(p1) == 0
+            R.ref_pool_reset(p1)
+            reps += 1
+        return (time.perf_counter() - t1) / reps * 1e3
+
+    def describe(self, passes, pass_ms):
+        job = self.job_ms()
+        ideal = self.njobs / self.workers * job
+        return (f"{passes} passes of one MoE layer over T={self.T} tokens ({len(self.experts)} experts incl. shared, "
+                f"{self.njobs} whole-expert jobs of <= 3 columns) through the reference CpuExpertPool (AVX2, "
+                f"{len(self.pools)} pinned pool(s) of {'/'.join(str(k) for _, k in self.pools)} workers); routing "
+                f"and fold restated; {pass_ms:.1f} ms per pass vs {ideal:.1f} ms = jobs/workers x one 3-column job "
+                f"({job:.2f} ms)")
+
+    def close(self):
+        for p, _ in self.pools:
+            self.R.ref_pool_free(p)
+        for h in self.handles.values():
+            self.R.ref_expert_free(h)
+        self.R.ref_routes_free(self.rg)
+
+
+def cpu_baseline(cfg, seed, budget_s=8.0, max_tokens=1024):
+    """cpu_baseline record: CpuReference passes for about `budget_s` seconds."""
+    import oracle as O
+    if O.ref() is None:
+        return cpu_baseline_port(cfg, seed, budget_s)
+    ref = CpuReference(cfg, seed, max_tokens)
+    ref.one_pass()
     t0 = time.perf_counter()
     passes = 0
     while True:
-        one_pass()
+        ref.one_pass()
         passes += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = (time.perf_counter() - t0) / passes
-    for p in pools:
-        R.ref_pool_free(p)
-    for h in handles.values():
-        R.ref_expert_free(h)
-    R.ref_routes_free(rg)
-    return {"value": T / dt, "unit": "tokens/s", "cores": int(ncores), "kind": "reference",
-            "sample": f"{passes} passes of one MoE layer over T={T} tokens ({len(experts)} experts incl. shared) "
-                      f"through the reference CpuExpertPool (AVX2, {len(pools)} pool(s)); routing/fold restated; "
-                      f"{dt * 1e3:.2f} ms per pass"}
+    rec = {"value": ref.T / dt, "unit": "tokens/s", "cores": int(ref.workers), "kind": "reference",
+           "sample": ref.describe(passes, dt * 1e3)}
+    ref.close()
+    return rec
 
 
 def cpu_baseline_port(cfg, seed, budget_s=8.0):
@@ -378,7 +438,7 @@ def run_ours(args, cfg):
             graph.replay()
     torch.cuda.synchronize()
 
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(local, args.clocks_csv.replace("{rank}", str(rank)) if args.clocks_csv else "")
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
@@ -458,23 +518,24 @@ def run_ours(args, cfg):
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except Exception:
         pass
-    if T <= 32:
-        # decode: weight streaming, HBM-bound
-        peak = float(peaks.get("hbm_gbs", 6650.0))
-        roof = {"bound": "hbm", "kernel": "stream_gate_up_kernel", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9,
-                "peak": peak, "unit": "GB/s", "bytes_per_launch": gu_bytes,
-                "traffic": profile_traffic("stream_gate_up_decode_T8.md") if cfg["tokens"] == 8 else None,
-                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650 GB/s"}
-    else:
-        # prefill: int8 MACs of the gate/up contraction over all routed + shared pairs
-        ops = 2.0 * T * (K_TOP + 1) * (2 * I) * H
-        bf16 = float(peaks.get("bf16_tflops", 1590.0))
-        peak = 2.0 * bf16   # dense int8 rate = 2x dense bf16 rate on B200
-        roof = {"bound": "tensor", "kernel": "gate/up launch (tc_expert_kernel + stream_gate_up_kernel)",
-                "achieved": ops / (gu_ms * 1e-3) / 1e12, "peak": peak, "unit": "TOP/s (int8)",
-                "ops_per_launch": ops,
-                "traffic": profile_traffic("tc_expert_prefill_T4096_zipf.md") if cfg["tokens"] == 4096 else None,
-                "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops (of measured)" if peaks else "2 x fallback 1590"}
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    int8 = 2.0 * float(peaks.get("bf16_tflops", 1590.0))   # dense int8 rate = 2x dense bf16 rate on B200
+    src = "MEASURED_PEAKS.json (of measured)" if peaks else "profiling-recipe fallback"
+    ops = 2.0 * T * (K_TOP + 1) * (2 * I) * H          # int8 ops of the gate/up contraction, routed + shared
+    gbs, tops = gu_bytes / (gu_ms * 1e-3) / 1e9, ops / (gu_ms * 1e-3) / 1e12
+    # the binding roofline is the one with the longer ideal time for this launch
+    hbm_bound = gu_bytes / (hbm * 1e9) >= ops / (int8 * 1e12)
+    kernel = "stream_gate_up_kernel" if T <= 32 else "tc_rows_kernel<gate/up>"
+    traffic_file = {8: "stream_gate_up_decode_T8.md", 1024: "tc_rows_gate_up_T1024.md",
+                    4096: "tc_rows_gate_up_T4096_zipf.md"}.get(T)
+    roof = {"bound": "hbm" if hbm_bound else "tensor", "kernel": kernel,
+            "achieved": gbs if hbm_bound else tops, "peak": hbm if hbm_bound else int8,
+            "unit": "GB/s" if hbm_bound else "TOP/s (int8)",
+            "traffic": profile_traffic(traffic_file) if traffic_file else None,
+            "bytes_per_launch": gu_bytes, "ops_per_launch": ops,
+            "achieved_gbs": gbs, "achieved_int8_tops": tops, "int8_frac": tops / int8, "hbm_frac": gbs / hbm,
+            "peak_source": f"{src}: hbm_gbs {hbm:.0f} GB/s; int8 = 2 x bf16_tflops = {int8:.0f} TOP/s"}
+    peak = roof["peak"]
     roof["frac"] = roof["achieved"] / peak
     roof["launch_ms"] = gu_ms
     roof["down_launch_ms"] = dn_ms
@@ -493,9 +554,9 @@ def run_ours(args, cfg):
         "e2e": {"value": tokens_per_step / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms},
         "roofline": roof,
-        # per layer: fused routing + 2 streaming GEMVs (T <= 32); else quantise + 4 routing
-        # kernels + streaming and tensor-core gate/up and down
-        "gpu_launches": args.steps * U * L * (3 if T <= 32 else 9),
+        # per layer: fused routing + 2 streaming kernels (T <= 32); else quantise, 4 routing
+        # kernels, operand gather, tensor-core gate/up and down
+        "gpu_launches": args.steps * U * L * (3 if T <= 32 else 8),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -568,30 +629,39 @@ def ep_result(args, cfg, world, rank, ms, e2e_ms, h2d, d2h, clk, lg_host, T, U, 
 
 
 def run_reference(args, cfg):
+    """The reference's own CPU expert path (oracle/_ref: the reference's
+    RouteGroups and CpuExpertPool on every allowed physical core) on the same
+    workload, metric and unit: each step is one MoE-layer pass over the
+    config's first min(T, 1024) tokens.  Under torchrun only rank 0 runs."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    total = 0.0
-    line = None
+    import oracle as O
+    if O.ref() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference's CPU code) was not built"}),
+              flush=True)
+        return
+    ref = CpuReference(cfg, args.seed)
     for _ in range(args.warmup):
-        cpu_baseline(cfg, args.seed, budget_s=0.5)
+        ref.one_pass()
     t0 = time.perf_counter()
-    vals = []
     for _ in range(args.steps):
-        b = cpu_baseline(cfg, args.seed, budget_s=2.0)
-        vals.append(b["value"])
-        line = b
+        ref.one_pass()
     total = time.perf_counter() - t0
-    value = float(np.mean(vals))
-    T = min(cfg["tokens"], 8)
+    ms = total / args.steps * 1e3
+    value = ref.T / (ms * 1e-3)
+    base = {"value": value, "unit": "tokens/s", "cores": int(ref.workers), "kind": "reference",
+            "sample": ref.describe(args.steps, ms)}
+    ref.close()
     print(json.dumps({
         "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / value, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0xq8_1->int32,fp32", "data": "synthetic",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0xq8_1->int32,fp32",
+        "data": "synthetic (seeded Q4_0 weights, x~N(0,1), router logits per BASELINE config)",
         "config": {"workload": cfg["name"], "tokens_per_ubatch": cfg["tokens"], "layers_per_step": 1,
-                   "sampled_tokens": T},
-        "cpu_baseline": {k: line[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                   "sampled_tokens": ref.T},
+        "cpu_baseline": base,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": total,
     }), flush=True)
@@ -600,15 +670,18 @@ def run_reference(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=0, help="timed steps (default per config)")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
     ap.add_argument("--layers", type=int, default=0, help="layers per step (default per config)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clocks-csv", default="", help="also write the sampled SM clocks to this csv file")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
+    if args.steps <= 0:
+        args.steps = cfg["steps"]
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

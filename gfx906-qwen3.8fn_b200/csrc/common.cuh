@@ -127,6 +127,52 @@ __device__ __forceinline__ int block_dot2(const uint4 w, const int4 xlo, const i
     return a + (b >> 4);
 }
 
+// The two 16-element fragment dots of one block in the reference's MMVQ
+// order (src/cpu_expert.cpp:156-213): fragment 0 = elements 0..7 and
+// 16..23 (code bytes 0..7), fragment 1 = elements 8..15 and 24..31 (bytes
+// 8..15).  Uncentred u4 x s8, exact in int32; f0 + f1 == block_dot.
+__device__ __forceinline__ void frag_dots(const uint4 w, const int4 xlo, const int4 xhi, int &f0, int &f1) {
+    f0 = dp4a_us(w.x & 0x0f0f0f0fu, xlo.x, 0);
+    f0 = dp4a_us(w.y & 0x0f0f0f0fu, xlo.y, f0);
+    f0 = dp4a_us((w.x >> 4) & 0x0f0f0f0fu, xhi.x, f0);
+    f0 = dp4a_us((w.y >> 4) & 0x0f0f0f0fu, xhi.y, f0);
+    f1 = dp4a_us(w.z & 0x0f0f0f0fu, xlo.z, 0);
+    f1 = dp4a_us(w.w & 0x0f0f0f0fu, xlo.w, f1);
+    f1 = dp4a_us((w.z >> 4) & 0x0f0f0f0fu, xhi.z, f1);
+    f1 = dp4a_us((w.w >> 4) & 0x0f0f0f0fu, xhi.w, f1);
+}
+
+// The reference's Q4_0 x Q8_1 reduction order (MMVQ: src/hip/linear.hip:197-281,
+// restated on the CPU by matrix_gpu_order, src/cpu_expert.cpp:156-213): block b
+// fragment f accumulates into lane 2*(b % 64) + f as
+//   lane = fma(d4, fma(float(dot_f), d8, -4*s8), lane)   (lanes start at +0),
+// then lane[i] += lane[i + 64] for i < 64, then an XOR butterfly with masks
+// 1, 2, ..., 32 over the 64 lanes.  With lane pairs (beta, beta + 32) of
+// blocks packed as (fragment 0, fragment 1) f32x2 accumulators a0 (blocks
+// b % 64 == beta) and a1 (b % 64 == beta + 32), the value of the first two
+// levels is this leaf; the remaining levels are an ascending butterfly over
+// beta (warp_tree_sum when lane = beta).
+__device__ __forceinline__ uint64_t mmvq_term2(uint64_t dots, uint64_t d4, uint64_t d8, uint64_t m4, uint64_t acc) {
+    return fma2(d4, fma2(dots, d8, m4), acc);
+}
+__device__ __forceinline__ float mmvq_leaf(uint64_t a0, uint64_t a1) {
+    float x0, y0, x1, y1;
+    upk2(a0, x0, y0);
+    upk2(a1, x1, y1);
+    return __fadd_rn(__fadd_rn(x0, x1), __fadd_rn(y0, y1));
+}
+__device__ __forceinline__ float warp_tree_sum(float v) {
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+
+// exp rounded to nearest float: the double-precision exponential rounded
+// once.  The reference's CPU SiLU uses the C library's expf; in the range the
+// gate values take this differs from it in under 0.1 % of inputs, by one ulp,
+// which moves the Q8_1 middle code in about 4 of 10^6 of those cases.
+__device__ __forceinline__ float exp_rn(float x) { return __double2float_rn(exp(static_cast<double>(x))); }
+
 __device__ __forceinline__ void report(int flags, int *error) {
     if (flags) atomicOr(error, flags);
 }

@@ -209,16 +209,17 @@ EncodeTiledFn encode_tiled() {
 
 // Tensor maps over every expert of a weights object for the TMA loads of the
 // tensor-core kernels: per matrix the code bytes as {16 bytes, row, block,
-// expert} (box 16 x 128 rows x 4 blocks: one stage lands block-major, each
-// block's 128 rows contiguous) -- or, where the driver refuses that stride
-// order, as {row bytes, row, expert} (box 64 bytes x 128 rows) -- and the
-// half scales as {block, row, expert} (box 8 blocks x 128 rows).  Weights
-// whose shape does not tile (rows not a multiple of 128, fewer than 8
-// blocks per row, Q4_1 down matrices) never use the tensor-core path.
+// expert} (box 16 x 128 rows x 2 blocks for gate/up, 4 for down: a copy lands
+// block-major, each block's 128 rows contiguous) -- or, where the driver
+// refuses that stride order, as {row bytes, row, expert} (box 32 or 64 bytes x
+// 128 rows) -- and the half scales as {block, row, expert} (box 8 blocks x
+// 128 rows).  Weights of other shapes (the gate/up stage order is that of 64
+// blocks, H = 2048; I a multiple of 256) or with Q4_1 down matrices run every
+// group on the streaming kernels instead.
 int build_maps(moe_weights_s *w) {
     const ExpertLayout &L = w->layout;
     w->tc_ok = false;
-    if (L.down_type != kDownQ4_0 || L.hidden % kRowsM || L.inter % (2 * kRowsM)) return MOE_OK;
+    if (L.down_type != kDownQ4_0 || L.hidden != kRowsHidden || L.inter % (2 * kRowsM)) return MOE_OK;
     const EncodeTiledFn enc = encode_tiled();
     if (!enc) return fail(MOE_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
     const size_t code_off[3] = {L.gate_codes, L.up_codes, L.down_codes};
@@ -235,14 +236,14 @@ int build_maps(moe_weights_s *w) {
             if (!rowmajor) {
                 const cuuint64_t dims[4] = {16, rows[m], nbm[m], E};
                 const cuuint64_t strides[3] = {nbm[m] * 16, 16, EB};
-                const cuuint32_t box[4] = {16, kRowsM, kRowsKB, 1};
+                const cuuint32_t box[4] = {16, kRowsM, cuuint32_t(m == 2 ? 4 : 2), 1};
                 r = enc(&w->maps.codes[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w->base + code_off[m], dims, strides, box,
                         one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             } else {
                 const cuuint64_t dims[3] = {nbm[m] * 16, rows[m], E};
                 const cuuint64_t strides[2] = {nbm[m] * 16, EB};
-                const cuuint32_t box[3] = {kRowsKB * 16, kRowsM, 1};
+                const cuuint32_t box[3] = {cuuint32_t(m == 2 ? 64 : 32), kRowsM, 1};
                 r = enc(&w->maps.codes[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w->base + code_off[m], dims, strides, box,
                         one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -345,7 +346,7 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         if (tap) sp.tap = *tap;
         const int gu_items = max_tiles * (L.inter / kGuRows), dn_items = max_tiles * (L.hidden / kDnRows);
         if (tc_tiles) {
-            tc_rows_gather_kernel<<<dim3(std::min(tc_tiles, h->sms * 2), L.hidden / 256), kRowsNP, 0, s>>>(
+            tc_rows_gather_kernel<<<dim3(std::min(tc_tiles, h->sms * 8), L.hidden / 256), 2 * kTcTile, 0, s>>>(
                 h->tc.tiles, h->tc.num_tiles, h->pair_token, h->xq, L.hidden, h->tc.b_gu, h->tc.sc_gu);
             MOE_CUDA(cudaGetLastError());
         }

@@ -166,55 +166,46 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
     const uint16_t *gs = reinterpret_cast<const uint16_t *>(st + L.gsc);
     const uint16_t *us = reinterpret_cast<const uint16_t *>(st + L.usc);
     constexpr int R = kGuWarpRows;
-    // accumulators of rows (2q, 2q+1) packed as f32x2; rows 0..R-1 gate, R..2R-1 up
-    uint64_t acc2[R][N];
+    // Every (row, pair) value in the reference's MMVQ reduction order, so the
+    // middle Q8_1 is bit-identical to the reference CPU expert's.  Lane l takes
+    // the blocks b % 64 in {l, l + 32}: a0 accumulates b % 64 == l, a1 b % 64 ==
+    // l + 32, each as (fragment 0, fragment 1); rows 0..R-1 gate, R..2R-1 up.
+    float acc[2 * R][N];
 #pragma unroll
-    for (int q = 0; q < R; ++q)
+    for (int j = 0; j < N; ++j) {
+        uint64_t a0[2 * R], a1[2 * R];
 #pragma unroll
-        for (int j = 0; j < N; ++j) acc2[q][j] = 0ull;
-    for (int b = lane; b < nb; b += 32) {
-        uint4 wc[2 * R];
-        float d4[2 * R];
+        for (int r = 0; r < 2 * R; ++r) a0[r] = a1[r] = 0ull;
+        for (int b0 = lane; b0 < nb; b0 += 64) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int blk = (cw * R + r) * nb + b;
-            wc[r] = gc[blk];
-            wc[R + r] = uc[blk];
-            d4[r] = h2f(gs[blk]);
-            d4[R + r] = h2f(us[blk]);
-        }
-        uint64_t d4p[R];
+            for (int half = 0; half < 2; ++half) {
+                const int b = b0 + 32 * half;
+                if (b >= nb) break;
+                const int4 lo = __ldg(xr[j] + 2 * b), hi = __ldg(xr[j] + 2 * b + 1);
+                const float2 sc = __ldg(sr[j] + b);
+                const float m4 = -(4.0f * sc.y);
+                const uint64_t d8 = pkf2(sc.x, sc.x), m4p = pkf2(m4, m4);
 #pragma unroll
-        for (int q = 0; q < R; ++q) d4p[q] = pkf2(d4[2 * q], d4[2 * q + 1]);
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-            const int4 lo = __ldg(xr[j] + 2 * b), hi = __ldg(xr[j] + 2 * b + 1);
-            const float2 sc = __ldg(sr[j] + b);
-            const float ns = -(8.0f * sc.y);
-            const uint64_t d8 = pkf2(sc.x, sc.x), nsp = pkf2(ns, ns);
-#pragma unroll
-            for (int q = 0; q < R; ++q)
-                acc2[q][j] = block_term2(block_dot2(wc[2 * q], lo, hi), block_dot2(wc[2 * q + 1], lo, hi), d4p[q], d8,
-                                         nsp, acc2[q][j]);
-            if constexpr (Tap) {
-                if (tap.dst0)
-#pragma unroll
-                    for (int r = 0; r < 2 * R; ++r)
-                        tap.put(r < R ? tap.dst0 : tap.dst1, j, cw * R + (r % R), b, block_dot(wc[r], lo, hi));
+                for (int r = 0; r < 2 * R; ++r) {
+                    const int blk = (cw * R + (r % R)) * nb + b;
+                    const uint4 w = r < R ? gc[blk] : uc[blk];
+                    const float d4 = h2f(r < R ? gs[blk] : us[blk]);
+                    int f0, f1;
+                    frag_dots(w, lo, hi, f0, f1);
+                    const uint64_t dots = pkf2(small_int_to_float(f0), small_int_to_float(f1));
+                    if (half) a1[r] = mmvq_term2(dots, pkf2(d4, d4), d8, m4p, a1[r]);
+                    else a0[r] = mmvq_term2(dots, pkf2(d4, d4), d8, m4p, a0[r]);
+                    if constexpr (Tap) {
+                        if (tap.dst0) tap.put(r < R ? tap.dst0 : tap.dst1, j, cw * R + (r % R), b, f0 + f1);
+                    }
+                }
             }
         }
+#pragma unroll
+        for (int r = 0; r < 2 * R; ++r) acc[r][j] = warp_tree_sum(mmvq_leaf(a0[r], a1[r]));
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar);   // slab fully read by this warp
-    float acc[2 * R][N];
-#pragma unroll
-    for (int q = 0; q < R; ++q)
-#pragma unroll
-        for (int j = 0; j < N; ++j) upk2(acc2[q][j], acc[2 * q][j], acc[2 * q + 1][j]);
-#pragma unroll
-    for (int r = 0; r < 2 * R; ++r)
-#pragma unroll
-        for (int j = 0; j < N; ++j) acc[r][j] = warp_sum(acc[r][j]);
     // SiLU(gate) * up with the reference's sanitisation (session_ops.hip:250-262):
     // lane r < R finishes row R*cw + r.
     if (lane < R) {
@@ -227,7 +218,7 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
             int flags = 0;
             g = operand(g, flags);
             u = operand(u, flags);
-            const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), flags);
+            const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))), flags);
             const float v = arithmetic(__fmul_rn(act, u), flags);
             mid[j * 32 + cw * R + lane] = flags ? 0.0f : v;
             report(flags, p.error);

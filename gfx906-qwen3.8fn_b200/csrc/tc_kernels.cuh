@@ -60,13 +60,27 @@ __host__ __device__ __forceinline__ uint32_t tile_off(int row, int half) {
 }
 
 // ---- workspace ---------------------------------------------------------------
-constexpr int kTcTile = 64;   // pairs per tensor-core tile at most (the MMA's N)
+constexpr int kTcTile = 16;   // pairs per tensor-core tile (gate/up MMA N = 2 x 16 fragment rows)
+
+// Arranged operand slots of one tile (filled by the gather kernel for gate/up
+// and by the gate/up epilogue for down), K = H or I:
+//   gate/up codes: per block, 2 * kTcTile rows of 32 bytes (pair p: row 2p =
+//     fragment 0 elements, row 2p + 1 = fragment 1 elements, the other
+//     fragment's bytes zero) in the K-major core-matrix layout, blocks in the
+//     kernel's stage order (tc_gu_pos);
+//   down codes: per block, kTcTile rows of 32 bytes, blocks in order;
+//   constants: per block, (d8[kTcTile], m[kTcTile]) fp32 with m = -4*s8 for
+//     gate/up (per fragment) and -8*s8 for down (whole block).
+__host__ __device__ constexpr size_t tc_gu_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile * 32; }
+__host__ __device__ constexpr size_t tc_dn_slot(int K) { return static_cast<size_t>(K / 32) * kTcTile * 32; }
+__host__ __device__ constexpr size_t tc_sc_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile; }
+// Position of gate/up block b (of 64) in the stage order: stage k holds blocks
+// 2k, 2k+1, 2k+32, 2k+33.
+__host__ __device__ constexpr int tc_gu_pos(int b) { return 4 * ((b & 31) >> 1) + 2 * (b >> 5) + (b & 1); }
 
 // Tensor-core path of one layer workspace: the tile list ({expert, first pair,
-// count, 0}, groups split evenly into tiles of <= kTcTile pairs) and the
-// pre-arranged operand slots of every tile (see rows_b_slot / rows_sc_slot):
-// gate/up activations gathered from the quantised x, and the middle Q8_1 the
-// gate/up epilogue writes for the down pass.
+// count, 0}: each group in tiles of kTcTile pairs, the last one partial) and
+// the arranged operand slots of every tile.
 struct TcWorkspace {
     int4 *tiles;
     int *num_tiles;
@@ -88,10 +102,10 @@ inline void tc_workspace_take(TcWorkspace &w, ArenaT &a, int pairs, int H, int I
     w.sc_gu = w.sc_dn = nullptr;
     if (tc_used) {
         const size_t t = static_cast<size_t>(w.max_tiles);
-        w.b_gu = a.template take<uint8_t>(t * kTcTile * 32 * (H / 32));
-        w.sc_gu = a.template take<float>(t * kTcTile * 2 * (H / 32));
-        w.b_dn = a.template take<uint8_t>(t * kTcTile * 32 * (I / 32));
-        w.sc_dn = a.template take<float>(t * kTcTile * 2 * (I / 32));
+        w.b_gu = a.template take<uint8_t>(t * tc_gu_slot(H));
+        w.sc_gu = a.template take<float>(t * tc_sc_slot(H));
+        w.b_dn = a.template take<uint8_t>(t * tc_dn_slot(I));
+        w.sc_dn = a.template take<float>(t * tc_sc_slot(I));
     }
 }
 

@@ -1,40 +1,43 @@
 // tcr_kernels.cuh -- tcgen05 (kind::i8) grouped expert GEMMs with the weight
-// rows on the TMEM lanes (prefill and every batch above decode size).
+// rows on the TMEM lanes (every batch above decode size).
 //
-// One work item = (expert group tile of <= 64 pairs, slab of 128 weight rows).
-// The MMA is D[128 rows][Np pairs] = A . B^T, K = 32 per instruction = one
-// quantisation block, so every MMA result is one per-block integer dot:
+// One work item = (tile of <= 16 pairs of one expert's group, slab of 128
+// weight rows).  The MMA is D[128 rows][N] = A . B^T, K = 32 per instruction
+// = one quantisation block:
 //   A = the slab's Q4_0 codes unpacked to unsigned bytes (0..15, u8),
-//   B = the tile's Q8_1 activation codes (s8), Np = 16 * ceil(n / 16).
-// A u8 x s8 product gives the reference's uncentred dot sum(q * x) directly
-// (src/quant.cpp:48-55), |dot| <= 15 * 127 * 32 < 2^16.
+//   B = the tile's Q8_1 activation codes (s8).
+// A u8 x s8 product is the reference's uncentred dot sum(q * x)
+// (src/quant.cpp:48-55) with |dot| < 2^16.
 //
 // Exact conversion: every TMEM accumulator is preloaded with the bit pattern
-// of 1.5 * 2^23 (0x4b400000) and each MMA accumulates onto it, so the int32
-// result bits are 0x4b400000 + dot, which read as fp32 is exactly
-// 1.5 * 2^23 + dot (|dot| < 2^22 keeps the exponent).  One f32x2 subtraction
-// per two columns recovers the dot as an exact fp32; the reader then stores
-// the pattern back.  Per element the epilogue is
-//   acc += d4 * (dot * d8 - 8 * s8)
-// as two packed FMAs (d4 per lane = weight row, d8 and -8*s8 per column).
+// of 1.5 * 2^23 (0x4b400000) and each MMA accumulates onto it, so the result
+// bits read as fp32 are exactly 1.5 * 2^23 + dot; one subtraction recovers the
+// dot.  The reader stores the pattern back before releasing the region.
 //
-// Gate/up items hold 128 middle rows: two MMAs per block, gate into columns
-// [0, Np) and up into [64, 64 + Np) of the block's TMEM region, so the thread
-// of lane r owns gate row r and up row r of every pair.  The item end runs
-// SiLU(gate) * up and the Q8_1 requantisation of each 32-row middle block --
-// one warp holds exactly one block per pair column (lane = element), which is
-// the reference's XOR-butterfly sum order -- and writes the middle codes in
-// the down pass's operand layout.  Down items hold 128 output rows and end in
-// a router-weighted red.add into the residual (lane = row: coalesced).
+// Gate/up (the values the middle Q8_1 is quantised from) follow the
+// reference's MMVQ order bit for bit (common.cuh: mmvq_term2 / mmvq_leaf), so
+// the middle equals the reference CPU expert's: B holds two rows per pair,
+// one per 16-element fragment (the other fragment's bytes zero), so the MMA
+// (N = 32) gives both fragment dots; blocks b and b + 32 land in one TMEM
+// region and form the tree's leaves; a pipeline stage carries blocks 2k,
+// 2k+1, 2k+32, 2k+33 (one level-2 node of the tree), and the 16 nodes of an
+// item are summed as a binary tree with a four-slot stack in registers.  Each
+// epilogue thread owns one weight row (its TMEM lane) of gate and of up for
+// 8 pairs; the item end runs SiLU(gate) * up and the Q8_1 of each 32-row
+// middle block (one warp = one block per pair: lane = element, the
+// reference's butterfly order) and writes the down pass's operand.
+//
+// Down (its output is never requantised) uses whole-block dots and
+// acc += d4 * (dot * d8 - 8 * s8) per block in fp32, then a router-weighted
+// red.add into the residual (lane = output row: coalesced).
 //
 // Warp roles (12 warps):
 //   warp 0      TMEM allocation; lane 0 issues the TMA copies: raw weight
-//               codes and scales through 4-D/3-D tensor maps, the tile's
-//               pre-arranged activation operand as 1-D bulk copies;
-//   warp 1      lane 0 issues the MMAs (one elected thread);
+//               codes and scales through tensor maps, the tile's pre-arranged
+//               activation operand as 1-D bulk copies;
+//   warp 1      lane 0 issues the MMAs;
 //   warps 2-3   unpack raw Q4_0 codes shared -> shared into the MMA layout;
-//   warps 4-11  epilogue: two per TMEM lane quarter, each owning half of the
-//               tile's columns.
+//   warps 4-11  epilogue: two per TMEM lane quarter, 8 pairs each.
 // Every barrier wait is bounded (ptx.cuh); a wait that gives up sets the
 // timeout flag and the role leaves its loop.
 #pragma once
@@ -48,13 +51,14 @@
 namespace qmoe {
 
 constexpr int kRowsM = 128;            // weight rows per MMA (TMEM lanes)
-constexpr int kRowsNP = kTcTile;       // pairs per tile at most (MMA N)
 constexpr int kRowsKB = 4;             // quantisation blocks per pipeline stage
+constexpr int kRowsCW = kTcTile / 2;   // pairs per epilogue warp
 constexpr int kRowsUnpackWarps = 2;
 constexpr int kRowsEpiWarps = 8;
 constexpr int kRowsWarps = 2 + kRowsUnpackWarps + kRowsEpiWarps;
 constexpr int kRowsThreads = 32 * kRowsWarps;
 constexpr int kRowsMinGroup = 1;       // batches above decode size: every group on this path
+constexpr int kRowsHidden = 2048;      // the gate/up stage order pairs blocks b and b + 32 of 64
 constexpr uint32_t kMagicBits = 0x4b400000u;
 constexpr float kMagicF = 12582912.0f; // 1.5 * 2^23
 
@@ -67,9 +71,9 @@ struct alignas(64) TcrMaps {
 struct TcrParams {
     TcrMaps maps;
     int hidden, inter;
-    int raw_rowmajor;          // codes staged [row][block] (3-D map) instead of [block][row]
-    const uint8_t *b_arr;      // arranged activation operand, one slot per tile
-    const float *bsc_arr;      // arranged (d8, -8*s8) per (tile, block, pair)
+    int raw_rowmajor;          // codes staged [row][block] (3-D maps) instead of [block][row]
+    const uint8_t *b_arr;      // arranged activation operand (tc_gu_slot / tc_dn_slot per tile)
+    const float *bsc_arr;      // arranged per-pair constants (tc_sc_slot per tile)
     const int4 *tiles;         // {expert, first pair, count, 0}
     const int *num_tiles;
     const int32_t *pair_token;
@@ -81,31 +85,29 @@ struct TcrParams {
     TapSink tap;
 };
 
-// Arranged operand slots: tile t, block b holds Np rows of 32 code bytes in
-// the K-major core-matrix layout at t * slot + b * Np * 32, and the per-pair
-// constants d8[Np] then m8[Np] at t * sc_slot + b * 2 * Np floats.
-__host__ __device__ constexpr size_t rows_b_slot(int K) { return static_cast<size_t>(kRowsNP) * 32 * (K / 32); }
-__host__ __device__ constexpr size_t rows_sc_slot(int K) { return static_cast<size_t>(kRowsNP) * 2 * (K / 32); }
-
 template <bool Down>
 struct RowsStage {
-    static constexpr int M = Down ? 1 : 2;                                   // matrices per item
-    static constexpr uint32_t codes = 0;                                     // M x 4 blocks x 128 rows x 16 B
-    static constexpr uint32_t scales = codes + M * kRowsKB * kRowsM * 16;    // M x [128][8] half
-    static constexpr uint32_t b = scales + M * kRowsM * 8 * 2;               // [4][Np][32]
-    static constexpr uint32_t bsc = b + kRowsKB * kRowsNP * 32;              // [4][2][Np] fp32
-    static constexpr uint32_t raw_bytes = bsc + kRowsKB * 2 * kRowsNP * 4;
-    static constexpr uint32_t a_bytes = M * kRowsKB * kRowsM * 32;           // unpacked A tiles
-    static constexpr int raw_stages = Down ? 6 : 4;
+    static constexpr int M = Down ? 1 : 2;                                    // matrices per item
+    static constexpr int wins = Down ? 1 : 2;                                 // 8-block scale windows per stage
+    static constexpr int brows = Down ? kTcTile : 2 * kTcTile;                // B rows per block
+    static constexpr int bpc = Down ? 4 : 2;                                  // blocks per code copy
+    static constexpr uint32_t codes = 0;                                      // M x 4 blocks x 128 rows x 16 B
+    static constexpr uint32_t scales = codes + M * kRowsKB * kRowsM * 16;     // M x wins x [128][8] half
+    static constexpr uint32_t b = scales + M * wins * kRowsM * 16;            // [4][brows][32]
+    static constexpr uint32_t bsc = b + kRowsKB * brows * 32;                 // [4][2][kTcTile] fp32
+    static constexpr uint32_t raw_bytes = (bsc + kRowsKB * 2 * kTcTile * 4 + 1023) / 1024 * 1024;
+    static constexpr uint32_t a_bytes = M * kRowsKB * kRowsM * 32;            // unpacked A tiles
+    static constexpr int raw_stages = Down ? 8 : 4;
     static constexpr int a_stages = Down ? 4 : 3;
     static constexpr uint32_t raw_off = 1024;
     static constexpr uint32_t a_off = raw_off + raw_stages * raw_bytes;
     static constexpr uint32_t smem = a_off + a_stages * a_bytes;
-    static constexpr int reg_cols = Down ? 64 : 128;                         // TMEM columns per block
+    static constexpr int reg_cols = Down ? 64 : 128;   // TMEM columns per region (down: 1 block, gate/up: 2)
     static constexpr int regions = 512 / reg_cols;
+    static constexpr int regions_per_stage = Down ? 4 : 2;
 };
 static_assert(RowsStage<false>::smem <= 227 * 1024 && RowsStage<true>::smem <= 227 * 1024, "fits one CTA");
-static_assert(RowsStage<false>::raw_bytes % 1024 == 0 && RowsStage<true>::raw_bytes % 1024 == 0, "aligned");
+static_assert(RowsStage<false>::regions <= 8 && RowsStage<true>::regions <= 8, "barrier arrays hold 8");
 
 // ---- PTX -------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
@@ -160,7 +162,7 @@ __host__ __device__ constexpr uint32_t rows_idesc(int m, int n) {
 // Sequence counters of the epilogue across items.
 struct RowsSeq {
     int g = 0;          // pipeline stage sequence (raw and A rings advance together)
-    uint32_t k = 0;     // block sequence (TMEM regions)
+    uint32_t k = 0;     // TMEM region sequence
 };
 
 // 4 packed code bytes of lanes 4w..4w+3 in lane 4w (other lanes: don't care).
@@ -171,70 +173,224 @@ __device__ __forceinline__ uint32_t pack_lane_bytes(int8_t code) {
     return v;
 }
 
-// ---- epilogue of one item, CW columns per warp and matrix -----------------
-template <bool Down, bool Tap, int CW>
-__device__ __forceinline__ bool rows_epilogue_item(const TcrParams &p, uint8_t *smem, uint64_t *raw_full,
-                                                   uint64_t *raw_empty, uint64_t *tm_full, uint64_t *tm_empty,
-                                                   uint32_t tq, RowsSeq &sq, int item, int4 td, int lane, int quarter,
-                                                   int chunk) {
-    using St = RowsStage<Down>;
-    constexpr int M = St::M;
-    constexpr int R = St::regions;
-    const int H = p.hidden, I = p.inter;
-    const int K = Down ? I : H, nb = K / 32, ksteps = nb / kRowsKB;
-    const int rows_total = Down ? H : I, slabs = rows_total / kRowsM;
-    const int slab = item % slabs, tile = item / slabs;
-    const int e = td.x, p0 = td.y, n = td.z, np = 2 * CW;
-    const int col0 = chunk * CW;
-    const int row = slab * kRowsM + quarter * 32 + lane;   // weight row (gate/up: middle row) of this lane
-    uint64_t acc[M][CW / 2];
+// Read this warp's columns of one TMEM region (Cols per matrix at `off[m]`),
+// then store the preload pattern back and release the region.
+template <int M, int Cols>
+__device__ __forceinline__ void region_take(uint32_t taddr, const int (&off)[M], uint32_t (&v)[M][Cols],
+                                            uint64_t *empty_bar, int lane) {
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
-        for (int j = 0; j < CW / 2; ++j) acc[m][j] = 0ull;
+        for (int j = 0; j < Cols; j += 8) tmem_ld8(taddr + off[m] + j, &v[m][j]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int j = 0; j < Cols; j += 8) tie8(&v[m][j]);
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int j = 0; j < Cols; j += 8) tmem_st8_magic(taddr + off[m] + j);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+}
+
+// ---- gate/up epilogue of one item (exact MMVQ order) -----------------------
+template <bool Tap>
+__device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *smem, uint64_t *raw_full,
+                                                 uint64_t *raw_empty, uint64_t *tm_full, uint64_t *tm_empty,
+                                                 uint32_t tq, RowsSeq &sq, int item, int4 td, int lane, int quarter,
+                                                 int chunk) {
+    using St = RowsStage<false>;
+    constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile;
+    const int I = p.inter;
+    const int nb = kRowsHidden / 32, slabs = I / kRowsM;
+    const int slab = item % slabs, tile = item / slabs;
+    const int e = td.x, p0 = td.y, n = td.z;
+    const int pc0 = chunk * CW;                               // this warp's first pair
+    const int lrow = quarter * 32 + lane;                     // row within the slab
+    const int row = slab * kRowsM + lrow;                     // middle row of this lane
+    const uint64_t unbias = pkf2(-kMagicF, -kMagicF), zero2 = 0ull;
+    // binary-tree stack over the 16 level-2 nodes (s3 ends as the total)
+    float s0[2][CW], s1[2][CW], s2[2][CW], s3[2][CW], la[2][CW];
+    int tap_base = 0;
+    if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
+
+    for (int ks = 0; ks < nb / kRowsKB; ++ks, ++sq.g) {
+        const int s = sq.g % St::raw_stages;
+        const uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
+        if (!mbar_wait(&raw_full[s], (sq.g / St::raw_stages) & 1, p.error)) return false;
+#pragma unroll
+        for (int h = 0; h < 2; ++h, ++sq.k) {   // region h: blocks 2k+h (columns +0) and 2k+32+h (+32)
+            const int r = static_cast<int>(sq.k % R);
+            if (!mbar_wait(&tm_full[r], (sq.k / R) & 1, p.error)) return false;
+            tc_fence_after();
+            const uint32_t tr = tq + r * St::reg_cols + 2 * pc0;
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                uint32_t v[2][2 * CW];
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+#pragma unroll
+                    for (int j = 0; j < 2 * CW; j += 8) tmem_ld8(tr + m * 64 + q * 32 + j, &v[q][j]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+#pragma unroll
+                    for (int j = 0; j < 2 * CW; j += 8) tie8(&v[q][j]);
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+#pragma unroll
+                    for (int j = 0; j < 2 * CW; j += 8) tmem_st8_magic(tr + m * 64 + q * 32 + j);
+                // scales: window 0 holds blocks 2k, 2k+1, window 1 blocks 2k+32, 2k+33
+                const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales + m * 2 * kRowsM * 16);
+                const int col = (2 * ks) % 8 + h;
+                const float d4a = h2f(sc[lrow * 8 + col]), d4b = h2f(sc[kRowsM * 8 + lrow * 8 + col]);
+                const uint64_t d4ap = pkf2(d4a, d4a), d4bp = pkf2(d4b, d4b);
+                // pair constants of block 2k+h (stage slot h) and 2k+32+h (slot 2+h)
+                const float *ca = reinterpret_cast<const float *>(st + St::bsc) + h * 2 * NP + pc0;
+                const float *cb = reinterpret_cast<const float *>(st + St::bsc) + (2 + h) * 2 * NP + pc0;
+#pragma unroll
+                for (int j4 = 0; j4 < CW / 4; ++j4) {
+                    const float4 d8a = *reinterpret_cast<const float4 *>(ca + 4 * j4);
+                    const float4 m4a = *reinterpret_cast<const float4 *>(ca + NP + 4 * j4);
+                    const float4 d8b = *reinterpret_cast<const float4 *>(cb + 4 * j4);
+                    const float4 m4b = *reinterpret_cast<const float4 *>(cb + NP + 4 * j4);
+                    const float da[4] = {d8a.x, d8a.y, d8a.z, d8a.w}, ma[4] = {m4a.x, m4a.y, m4a.z, m4a.w};
+                    const float db[4] = {d8b.x, d8b.y, d8b.z, d8b.w}, mb[4] = {m4b.x, m4b.y, m4b.z, m4b.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int j = 4 * j4 + q;
+                        // (fragment 0, fragment 1) dots of blocks 2k+h and 2k+32+h
+                        const uint64_t ta = add2(pk2(v[0][2 * j], v[0][2 * j + 1]), unbias);
+                        const uint64_t tb = add2(pk2(v[1][2 * j], v[1][2 * j + 1]), unbias);
+                        const uint64_t a0 = mmvq_term2(ta, d4ap, pkf2(da[q], da[q]), pkf2(ma[q], ma[q]), zero2);
+                        const uint64_t a1 = mmvq_term2(tb, d4bp, pkf2(db[q], db[q]), pkf2(mb[q], mb[q]), zero2);
+                        const float leaf = mmvq_leaf(a0, a1);
+                        if (h == 0) {
+                            la[m][j] = leaf;
+                        } else {
+                            // node k = L(2k) + L(2k+1), pushed into the binary tree over k = 0..15
+                            float x = __fadd_rn(la[m][j], leaf);
+                            if (ks & 1) {
+                                x = __fadd_rn(s0[m][j], x);
+                                if (ks & 2) {
+                                    x = __fadd_rn(s1[m][j], x);
+                                    if (ks & 4) {
+                                        x = __fadd_rn(s2[m][j], x);
+                                        s3[m][j] = (ks & 8) ? __fadd_rn(s3[m][j], x) : x;
+                                    } else {
+                                        s2[m][j] = x;
+                                    }
+                                } else {
+                                    s1[m][j] = x;
+                                }
+                            } else {
+                                s0[m][j] = x;
+                            }
+                        }
+                        if constexpr (Tap) {
+                            const int pl = p0 + pc0 + j - tap_base;
+                            if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs) {
+                                float x0, y0, x1, y1;
+                                upk2(ta, x0, y0);
+                                upk2(tb, x1, y1);
+                                int32_t *dst = m == 0 ? p.tap.gate : p.tap.up;
+                                const size_t base = (static_cast<size_t>(pl) * I + row) * nb;
+                                dst[base + 2 * ks + h] = static_cast<int32_t>(x0) + static_cast<int32_t>(y0);
+                                dst[base + 2 * ks + 32 + h] = static_cast<int32_t>(x1) + static_cast<int32_t>(y1);
+                            }
+                        }
+                    }
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tm_empty[r]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[s]);   // done with the stage's scales and constants
+    }
+
+    // SiLU(gate) * up, then Q8_1 of the 32-row middle block held by this warp
+    int flags = 0;
+    const int jb = slab * (kRowsM / 32) + quarter;   // middle block index
+    const int nbI = I / 32;
+    uint8_t *mslot = p.mid_arr + static_cast<size_t>(tile) * tc_dn_slot(I) + static_cast<size_t>(jb) * NP * 32;
+    float *msc = p.mid_sc_arr + static_cast<size_t>(tile) * tc_sc_slot(I) + static_cast<size_t>(jb) * 2 * NP;
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+        const int c = pc0 + j;
+        Q8Lane q{0, 0, 0, 0};
+        if (c < n) {   // padded pairs get zero codes and constants
+            int f = 0;
+            const float gv = operand(s3[0][j], f), uv = operand(s3[1][j], f);
+            const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, exp_rn(-gv))), f);
+            const float val = arithmetic(__fmul_rn(act, uv), f);
+            q = quantize_lane(f ? 0.0f : val);
+            flags |= f | q.flags;
+        }
+        const uint32_t word = pack_lane_bytes(q.code);
+        if ((lane & 3) == 0) *reinterpret_cast<uint32_t *>(mslot + tile_off(c, lane >> 4) + (lane & 15)) = word;
+        if (lane == 0) {
+            msc[c] = h2f(q.d);
+            msc[NP + c] = -(8.0f * h2f(q.s));
+        }
+        if constexpr (Tap) {
+            const int pl = p0 + c - tap_base;
+            if (e == p.tap.expert && c < n && pl >= 0 && pl < p.tap.max_pairs) {
+                p.tap.mid_codes[static_cast<size_t>(pl) * I + row] = q.code;
+                if (lane == 0) p.tap.mid_ds[static_cast<size_t>(pl) * nbI + jb] = q.d | (uint32_t(q.s) << 16);
+            }
+        }
+    }
+    flags = __reduce_or_sync(0xffffffffu, flags);
+    if (lane == 0) report(flags, p.error);
+    return true;
+}
+
+// ---- down epilogue of one item ---------------------------------------------
+template <bool Tap>
+__device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *smem, uint64_t *raw_full,
+                                                 uint64_t *raw_empty, uint64_t *tm_full, uint64_t *tm_empty,
+                                                 uint32_t tq, RowsSeq &sq, int item, int4 td, int lane, int quarter,
+                                                 int chunk) {
+    using St = RowsStage<true>;
+    constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile;
+    const int H = p.hidden, I = p.inter;
+    const int nb = I / 32, slabs = H / kRowsM;
+    const int slab = item % slabs;
+    const int e = td.x, p0 = td.y, n = td.z;
+    const int pc0 = chunk * CW;
+    const int lrow = quarter * 32 + lane;
+    const int row = slab * kRowsM + lrow;                     // output row of this lane
+    uint64_t acc[CW / 2];
+#pragma unroll
+    for (int j = 0; j < CW / 2; ++j) acc[j] = 0ull;
     const uint64_t unbias = pkf2(-kMagicF, -kMagicF);
     int tap_base = 0;
     if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
 
-    for (int ks = 0; ks < ksteps; ++ks, ++sq.g) {
+    for (int ks = 0; ks < nb / kRowsKB; ++ks, ++sq.g) {
         const int s = sq.g % St::raw_stages;
         const uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
-        // acquire the TMA writes of this stage's scales (the phase is complete or about to be)
         if (!mbar_wait(&raw_full[s], (sq.g / St::raw_stages) & 1, p.error)) return false;
 #pragma unroll 1
         for (int kb = 0; kb < kRowsKB; ++kb, ++sq.k) {
             const int r = static_cast<int>(sq.k % R);
             if (!mbar_wait(&tm_full[r], (sq.k / R) & 1, p.error)) return false;
             tc_fence_after();
-            uint32_t v[M][CW];
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-#pragma unroll
-                for (int j = 0; j < CW; j += 8) tmem_ld8(tq + r * St::reg_cols + m * 64 + col0 + j, &v[m][j]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-#pragma unroll
-                for (int j = 0; j < CW; j += 8) tie8(&v[m][j]);
-            // give the region back: preload pattern into the columns just read
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-#pragma unroll
-                for (int j = 0; j < CW; j += 8) tmem_st8_magic(tq + r * St::reg_cols + m * 64 + col0 + j);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tm_empty[r]);
-            // weight scale of this lane's row (both matrices), pair constants per column
-            uint64_t d4p[M];
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales + m * kRowsM * 16);
-                const float d4 = h2f(sc[(quarter * 32 + lane) * 8 + (ks & 1) * 4 + kb]);
-                d4p[m] = pkf2(d4, d4);
-            }
-            const float *d8p = reinterpret_cast<const float *>(st + St::bsc) + kb * 2 * np + col0;
-            const float *m8p = d8p + np;
+            uint32_t v[1][CW];
+            const int off[1] = {pc0};
+            region_take<1, CW>(tq + r * St::reg_cols, off, v, &tm_empty[r], lane);
+            const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales);
+            const float d4 = h2f(sc[lrow * 8 + (ks & 1) * 4 + kb]);
+            const uint64_t d4p = pkf2(d4, d4);
+            const float *d8p = reinterpret_cast<const float *>(st + St::bsc) + kb * 2 * NP + pc0;
+            const float *m8p = d8p + NP;
 #pragma unroll
             for (int j4 = 0; j4 < CW / 4; ++j4) {
                 const float4 d8q = *reinterpret_cast<const float4 *>(d8p + 4 * j4);
@@ -244,91 +400,44 @@ __device__ __forceinline__ bool rows_epilogue_item(const TcrParams &p, uint8_t *
                     const uint64_t d8 = h ? pkf2(d8q.z, d8q.w) : pkf2(d8q.x, d8q.y);
                     const uint64_t m8 = h ? pkf2(m8q.z, m8q.w) : pkf2(m8q.x, m8q.y);
                     const int j = 4 * j4 + 2 * h;
-#pragma unroll
-                    for (int m = 0; m < M; ++m) {
-                        const uint64_t t = add2(pk2(v[m][j], v[m][j + 1]), unbias);   // exact dots
-                        acc[m][j / 2] = fma2(d4p[m], fma2(t, d8, m8), acc[m][j / 2]);
-                    }
+                    const uint64_t t = add2(pk2(v[0][j], v[0][j + 1]), unbias);   // exact dots
+                    acc[j / 2] = fma2(d4p, fma2(t, d8, m8), acc[j / 2]);
                 }
             }
             if constexpr (Tap) {
                 if (e == p.tap.expert) {
-                    const int b = ks * kRowsKB + kb;
 #pragma unroll
-                    for (int m = 0; m < M; ++m) {
-                        int32_t *dst = Down ? p.tap.down : (m == 0 ? p.tap.gate : p.tap.up);
-#pragma unroll
-                        for (int j = 0; j < CW; ++j) {
-                            const int pl = p0 + col0 + j - tap_base;
-                            if (col0 + j < n && pl >= 0 && pl < p.tap.max_pairs)
-                                dst[(static_cast<size_t>(pl) * rows_total + row) * nb + b] =
-                                    static_cast<int32_t>(__uint_as_float(v[m][j]) - kMagicF);
-                        }
+                    for (int j = 0; j < CW; ++j) {
+                        const int pl = p0 + pc0 + j - tap_base;
+                        if (pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs)
+                            p.tap.down[(static_cast<size_t>(pl) * H + row) * nb + ks * kRowsKB + kb] =
+                                static_cast<int32_t>(__uint_as_float(v[0][j]) - kMagicF);
                     }
                 }
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[s]);   // done with the stage's scales
+        if (lane == 0) mbar_arrive(&raw_empty[s]);
     }
-
-    float a[M][CW];
+    // router-weighted scatter-add of the 128-row slab into the residual
+    float a[CW];
 #pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int j = 0; j < CW / 2; ++j) upk2(acc[m][j], a[m][2 * j], a[m][2 * j + 1]);
+    for (int j = 0; j < CW / 2; ++j) upk2(acc[j], a[2 * j], a[2 * j + 1]);
     int flags = 0;
-    if constexpr (!Down) {
-        // SiLU(gate) * up, then Q8_1 of the 32-row middle block held by this warp
-        const int jb = slab * (kRowsM / 32) + quarter;   // middle block index
-        const int nbI = I / 32;
-        uint8_t *mslot = p.mid_arr + static_cast<size_t>(tile) * rows_b_slot(I) + static_cast<size_t>(jb) * np * 32;
-        float *msc = p.mid_sc_arr + static_cast<size_t>(tile) * rows_sc_slot(I) + static_cast<size_t>(jb) * 2 * np;
+    int tok_l = 0;
+    float w_l = 0.0f;
+    if (lane < CW && pc0 + lane < n) {
+        tok_l = __ldg(p.pair_token + p0 + pc0 + lane);
+        w_l = __ldg(p.pair_weight + p0 + pc0 + lane);
+    }
 #pragma unroll
-        for (int j = 0; j < CW; ++j) {
-            const int c = col0 + j;
-            Q8Lane q{0, 0, 0, 0};
-            if (c < n) {
-                int f = 0;
-                const float gv = operand(a[0][j], f), uv = operand(a[1][j], f);
-                const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), f);
-                const float val = arithmetic(__fmul_rn(act, uv), f);
-                q = quantize_lane(f ? 0.0f : val);
-                flags |= f | q.flags;
-            }
-            // padded columns (c >= n) get zero codes and constants
-            const uint32_t word = pack_lane_bytes(q.code);
-            if ((lane & 3) == 0)
-                *reinterpret_cast<uint32_t *>(mslot + tile_off(c, lane >> 4) + (lane & 15)) = word;
-            if (lane == 0) {
-                msc[c] = h2f(q.d);
-                msc[np + c] = -(8.0f * h2f(q.s));
-            }
-            if constexpr (Tap) {
-                const int pl = p0 + c - tap_base;
-                if (e == p.tap.expert && c < n && pl >= 0 && pl < p.tap.max_pairs) {
-                    p.tap.mid_codes[static_cast<size_t>(pl) * I + row] = q.code;
-                    if (lane == 0) p.tap.mid_ds[static_cast<size_t>(pl) * nbI + jb] = q.d | (uint32_t(q.s) << 16);
-                }
-            }
-        }
-    } else {
-        // router-weighted scatter-add of the 128-row slab into the residual
-        int tok_l = 0;
-        float w_l = 0.0f;
-        if (lane < CW && col0 + lane < n) {
-            tok_l = __ldg(p.pair_token + p0 + col0 + lane);
-            w_l = __ldg(p.pair_weight + p0 + col0 + lane);
-        }
-#pragma unroll
-        for (int j = 0; j < CW; ++j) {
-            const int tok = __shfl_sync(0xffffffffu, tok_l, j);
-            const float w = __shfl_sync(0xffffffffu, w_l, j);
-            if (col0 + j >= n) break;
-            const float y = arithmetic(a[0][j], flags);
-            const float cv = arithmetic(__fmul_rn(w, y), flags);
-            atomicAdd(p.out + static_cast<size_t>(tok) * H + row, cv);
-        }
+    for (int j = 0; j < CW; ++j) {
+        const int tok = __shfl_sync(0xffffffffu, tok_l, j);
+        const float w = __shfl_sync(0xffffffffu, w_l, j);
+        if (pc0 + j >= n) break;
+        const float y = arithmetic(a[j], flags);
+        const float cv = arithmetic(__fmul_rn(w, y), flags);
+        atomicAdd(p.out + static_cast<size_t>(tok) * H + row, cv);
     }
     flags = __reduce_or_sync(0xffffffffu, flags);
     if (lane == 0) report(flags, p.error);
@@ -390,35 +499,40 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                 tma_prefetch_map(&p.maps.codes[Down ? 2 : m]);
                 tma_prefetch_map(&p.maps.scales[Down ? 2 : m]);
             }
+            constexpr uint32_t bbytes = kRowsKB * St::brows * 32, sbytes = kRowsKB * 2 * kTcTile * 4;
+            const size_t bslot = Down ? tc_dn_slot(K) : tc_gu_slot(K), sslot = tc_sc_slot(K);
             int g = 0;
             bool failed = false;
             for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
                 const int tile = item / slabs, slab = item % slabs;
-                const int4 td = p.tiles[tile];
-                const int np = (td.z + 15) & ~15;
-                const uint32_t bbytes = kRowsKB * np * 32, sbytes = kRowsKB * np * 8;
+                const int e = p.tiles[tile].x;
                 for (int ks = 0; ks < ksteps; ++ks, ++g) {
                     const int s = g % RS;
                     if (g >= RS && !mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, p.error)) { failed = true; break; }
                     uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
-                    mbar_arrive_expect_tx(&raw_full[s], M * (kRowsKB * kRowsM * 16 + kRowsM * 16) + bbytes + sbytes);
+                    mbar_arrive_expect_tx(&raw_full[s],
+                                          M * (kRowsKB * kRowsM * 16 + St::wins * kRowsM * 16) + bbytes + sbytes);
                     for (int m = 0; m < M; ++m) {
                         const int mat = Down ? 2 : m;
-                        if (p.raw_rowmajor)
-                            tma_load_3d(st + St::codes + m * kRowsKB * kRowsM * 16, &p.maps.codes[mat],
-                                        ks * kRowsKB * 16, slab * kRowsM, td.x, &raw_full[s]);
-                        else
-                            tma_load_4d(st + St::codes + m * kRowsKB * kRowsM * 16, &p.maps.codes[mat], 0,
-                                        slab * kRowsM, ks * kRowsKB, td.x, &raw_full[s]);
-                        tma_load_3d(st + St::scales + m * kRowsM * 16, &p.maps.scales[mat], (ks * kRowsKB) & ~7,
-                                    slab * kRowsM, td.x, &raw_full[s]);
+                        // code copies: down blocks 4ks..4ks+3 at once; gate/up blocks (2ks, 2ks+1), then (+32, +33)
+                        for (int c = 0; c < kRowsKB / St::bpc; ++c) {
+                            const int b0 = Down ? kRowsKB * ks : 2 * ks + 32 * c;
+                            uint8_t *dst = st + St::codes + (m * kRowsKB + c * St::bpc) * kRowsM * 16;
+                            if (p.raw_rowmajor)
+                                tma_load_3d(dst, &p.maps.codes[mat], b0 * 16, slab * kRowsM, e, &raw_full[s]);
+                            else
+                                tma_load_4d(dst, &p.maps.codes[mat], 0, slab * kRowsM, b0, e, &raw_full[s]);
+                        }
+                        for (int w = 0; w < St::wins; ++w) {
+                            const int b0 = Down ? kRowsKB * ks : 2 * ks + 32 * w;
+                            tma_load_3d(st + St::scales + (m * St::wins + w) * kRowsM * 16, &p.maps.scales[mat],
+                                        b0 & ~7, slab * kRowsM, e, &raw_full[s]);
+                        }
                     }
-                    bulk_g2s(st + St::b,
-                             p.b_arr + static_cast<size_t>(tile) * rows_b_slot(K) + static_cast<size_t>(ks) * bbytes,
+                    bulk_g2s(st + St::b, p.b_arr + static_cast<size_t>(tile) * bslot + static_cast<size_t>(ks) * bbytes,
                              bbytes, &raw_full[s]);
                     bulk_g2s(st + St::bsc,
-                             p.bsc_arr + static_cast<size_t>(tile) * rows_sc_slot(K) +
-                                 static_cast<size_t>(ks) * kRowsKB * 2 * np,
+                             p.bsc_arr + static_cast<size_t>(tile) * sslot + static_cast<size_t>(ks) * kRowsKB * 2 * kTcTile,
                              sbytes, &raw_full[s]);
                 }
             }
@@ -428,13 +542,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
+            const uint32_t idesc = rows_idesc(kRowsM, St::brows);
             int g = 0;
             uint32_t kseq = 0;
             bool failed = false;
             for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
-                const int4 td = p.tiles[item / slabs];
-                const int np = (td.z + 15) & ~15;
-                const uint32_t idesc = rows_idesc(kRowsM, np);
                 for (int ks = 0; ks < ksteps && !failed; ++ks, ++g) {
                     const int sr = g % RS, sa = g % AS;
                     if (!mbar_wait(&a_full[sa], (g / AS) & 1, p.error) ||
@@ -445,15 +557,27 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                     tc_fence_after();
                     const uint32_t a_st = smem_u32(smem + St::a_off + sa * St::a_bytes);
                     const uint32_t b_st = smem_u32(smem + St::raw_off + sr * St::raw_bytes + St::b);
-                    for (int kb = 0; kb < kRowsKB; ++kb, ++kseq) {
+                    for (int h = 0; h < St::regions_per_stage; ++h, ++kseq) {
                         const int r = static_cast<int>(kseq % R);
                         if (!mbar_wait(&tm_empty[r], (kseq / R) & 1, p.error)) { failed = true; break; }
                         tc_fence_after();
-                        const uint64_t bd = smem_desc(b_st + kb * np * 32, 128, 256);
+                        if (Down) {
+                            // block h of the stage into the region's columns [0, 16)
+                            const uint64_t ad = smem_desc(a_st + h * kRowsM * 32, 128, 256);
+                            const uint64_t bd = smem_desc(b_st + h * St::brows * 32, 128, 256);
+                            mma_i8(tmem + r * St::reg_cols, ad, bd, idesc, 1u);
+                        } else {
+                            // stage slots h (block 2k+h) and 2+h (block 2k+32+h): columns [0,32) and [32,64)
+                            // of gate, +64 for up
 #pragma unroll
-                        for (int m = 0; m < M; ++m) {
-                            const uint64_t ad = smem_desc(a_st + (m * kRowsKB + kb) * kRowsM * 32, 128, 256);
-                            mma_i8(tmem + r * St::reg_cols + m * 64, ad, bd, idesc, 1u);
+                            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                                for (int q = 0; q < 2; ++q) {
+                                    const int slot = h + 2 * q;
+                                    const uint64_t ad = smem_desc(a_st + (m * kRowsKB + slot) * kRowsM * 32, 128, 256);
+                                    const uint64_t bd = smem_desc(b_st + slot * St::brows * 32, 128, 256);
+                                    mma_i8(tmem + r * St::reg_cols + m * 64 + q * 32, ad, bd, idesc, 1u);
+                                }
                         }
                         mma_commit(&tm_full[r]);
                     }
@@ -469,6 +593,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
         // ---------------- unpack: raw nibbles -> u8 K-major core matrices ----------------
         const int ut = threadIdx.x - 64;
         constexpr int kUnits = M * kRowsKB * kRowsM;
+        constexpr int copies = kRowsKB / St::bpc;
         int g = 0;
         bool failed = false;
         for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
@@ -484,8 +609,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
 #pragma unroll 4
                 for (int u = ut; u < kUnits; u += 32 * kRowsUnpackWarps) {
                     const int m = u / (kRowsKB * kRowsM), kb = (u / kRowsM) % kRowsKB, row = u % kRowsM;
-                    const int src =
-                        p.raw_rowmajor ? (m * kRowsM + row) * kRowsKB + kb : (m * kRowsKB + kb) * kRowsM + row;
+                    const int src = p.raw_rowmajor
+                                        ? ((m * copies + kb / St::bpc) * kRowsM + row) * St::bpc + kb % St::bpc
+                                        : (m * kRowsKB + kb) * kRowsM + row;
                     const uint4 w = reinterpret_cast<const uint4 *>(raw)[src];
                     const uint4 lo = make_uint4(w.x & 0x0f0f0f0fu, w.y & 0x0f0f0f0fu, w.z & 0x0f0f0f0fu,
                                                 w.w & 0x0f0f0f0fu);
@@ -518,26 +644,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
         RowsSeq sq;
         for (int item = blockIdx.x; item < total; item += gridDim.x) {
             const int4 td = p.tiles[item / slabs];
-            const int cw = ((td.z + 15) & ~15) / 2;
-            bool ok;
-            switch (cw) {
-            case 8:
-                ok = rows_epilogue_item<Down, Tap, 8>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item, td,
-                                                      lane, quarter, chunk);
-                break;
-            case 16:
-                ok = rows_epilogue_item<Down, Tap, 16>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item,
-                                                       td, lane, quarter, chunk);
-                break;
-            case 24:
-                ok = rows_epilogue_item<Down, Tap, 24>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item,
-                                                       td, lane, quarter, chunk);
-                break;
-            default:
-                ok = rows_epilogue_item<Down, Tap, 32>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item,
-                                                       td, lane, quarter, chunk);
-                break;
-            }
+            const bool ok = Down ? dn_epilogue_item<Tap>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item,
+                                                         td, lane, quarter, chunk)
+                                 : gu_epilogue_item<Tap>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item,
+                                                         td, lane, quarter, chunk);
             if (!ok) break;
         }
     }
@@ -550,24 +660,29 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
     }
 }
 
-// Gate/up B operand of every tile: row r < n of tile t is the Q8_1 codes of
-// token pair_token[p0 + r] and its constants (d8, -8*s8); rows n..Np-1 are
-// zero.  CTA (t, g): 64 threads (rows) x blocks 8g..8g+7.
-__global__ void __launch_bounds__(kRowsNP) tc_rows_gather_kernel(const int4 *tiles, const int *num_tiles,
-                                                                 const int32_t *pair_token, Q8Planar xq, int H,
-                                                                 uint8_t *b_arr, float *bsc_arr) {
-    const int nb = H / 32, row = threadIdx.x, b0 = blockIdx.y * 8;
+// Gate/up B operand of every tile: for pair r < n of tile t (token
+// pair_token[p0 + r]), row 2r = its Q8_1 codes of fragment 0 (elements 0..7
+// and 16..23, the rest zero) and row 2r + 1 those of fragment 1, blocks in
+// stage order, and the constants (d8, -4*s8); pairs n..15 are zero.
+// CTA (t, g): 32 threads (fragment rows) x blocks 8g..8g+7.
+__global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 *tiles, const int *num_tiles,
+                                                                     const int32_t *pair_token, Q8Planar xq, int H,
+                                                                     uint8_t *b_arr, float *bsc_arr) {
+    const int nb = H / 32, frow = threadIdx.x, pr = frow >> 1, frag = frow & 1, b0 = blockIdx.y * 8;
     for (int t = blockIdx.x; t < *num_tiles; t += gridDim.x) {
         const int4 td = tiles[t];
-        const int np = (td.z + 15) & ~15;
-        if (row >= np) continue;
         uint4 v[16];
         float2 c[8];
-        if (row < td.z) {
-            const int token = pair_token[td.y + row];
+        if (pr < td.z) {
+            const int token = pair_token[td.y + pr];
             const uint4 *src = reinterpret_cast<const uint4 *>(xq.codes + static_cast<size_t>(token) * H) + 2 * b0;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = src[i];
+            for (int i = 0; i < 16; ++i) {
+                v[i] = src[i];
+                // keep this row's fragment: bytes 0..7 of each 16-byte half (fragment 0) or 8..15 (fragment 1)
+                if (frag) v[i].x = v[i].y = 0u;
+                else v[i].z = v[i].w = 0u;
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) c[i] = xq.scales[static_cast<size_t>(token) * nb + b0 + i];
         } else {
@@ -576,16 +691,18 @@ __global__ void __launch_bounds__(kRowsNP) tc_rows_gather_kernel(const int4 *til
 #pragma unroll
             for (int i = 0; i < 8; ++i) c[i] = make_float2(0.0f, 0.0f);
         }
-        uint8_t *slot = b_arr + static_cast<size_t>(t) * rows_b_slot(H);
-        float *ss = bsc_arr + static_cast<size_t>(t) * rows_sc_slot(H);
+        uint8_t *slot = b_arr + static_cast<size_t>(t) * tc_gu_slot(H);
+        float *ss = bsc_arr + static_cast<size_t>(t) * tc_sc_slot(H);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int b = b0 + i;
-            uint8_t *dst = slot + static_cast<size_t>(b) * np * 32;
-            *reinterpret_cast<uint4 *>(dst + tile_off(row, 0)) = v[2 * i];
-            *reinterpret_cast<uint4 *>(dst + tile_off(row, 1)) = v[2 * i + 1];
-            ss[b * 2 * np + row] = c[i].x;
-            ss[b * 2 * np + np + row] = -(8.0f * c[i].y);
+            const int pos = tc_gu_pos(b0 + i);
+            uint8_t *dst = slot + static_cast<size_t>(pos) * 2 * kTcTile * 32;
+            *reinterpret_cast<uint4 *>(dst + tile_off(frow, 0)) = v[2 * i];
+            *reinterpret_cast<uint4 *>(dst + tile_off(frow, 1)) = v[2 * i + 1];
+            if (!frag) {
+                ss[pos * 2 * kTcTile + pr] = c[i].x;
+                ss[pos * 2 * kTcTile + kTcTile + pr] = -(4.0f * c[i].y);
+            }
         }
     }
 }
