@@ -25,6 +25,7 @@ def _inputs():
     paths = [os.path.join(CSRC, s) for s in SOURCES + HEADERS]
     paths.append(os.path.join(HERE, "..", "include", "qwen_moe_b200.h"))
     paths.append(os.path.join(HERE, "..", "include", "qmoe", "routes.hpp"))
+    paths.append(os.path.join(CSRC, "expf_table.c"))
     paths.append(os.path.abspath(__file__))
     return paths
 
@@ -36,17 +37,41 @@ def stale():
     return any(os.path.getmtime(p) > t for p in _inputs() if os.path.exists(p))
 
 
+def expf_table_object(build_dir):
+    """Object file holding the C library's expf corrections (csrc/expf_table.c):
+    generated once by running that program, embedded with .incbin."""
+    table = os.path.join(build_dir, "expf_table.bin")
+    gen = os.path.join(build_dir, "expf_table")
+    src = os.path.join(CSRC, "expf_table.c")
+    if not os.path.exists(table) or os.path.getmtime(table) < os.path.getmtime(src):
+        subprocess.run(["gcc", "-O2", src, "-o", gen, "-lm"], check=True)
+        subprocess.run([gen, table + ".tmp"], check=True, stdout=subprocess.DEVNULL)
+        os.replace(table + ".tmp", table)
+    asm = os.path.join(build_dir, "expf_table.S")
+    with open(asm, "w") as f:
+        f.write('\t.section .rodata\n\t.balign 16\n'
+                '\t.globl qmoe_expf_table_begin\n\t.hidden qmoe_expf_table_begin\nqmoe_expf_table_begin:\n'
+                f'\t.incbin "{table}"\n'
+                '\t.globl qmoe_expf_table_end\n\t.hidden qmoe_expf_table_end\nqmoe_expf_table_end:\n'
+                '\t.section .note.GNU-stack,"",@progbits\n')
+    obj = os.path.join(build_dir, "expf_table.o")
+    subprocess.run(["gcc", "-c", asm, "-o", obj], check=True)
+    return obj
+
+
 def build(force=False, ptxas_verbose=False):
     if not force and not stale():
         return LIB
     objs = []
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
-    os.makedirs(os.path.join(HERE, "_build"), exist_ok=True)
+    build_dir = os.path.join(HERE, "_build")
+    os.makedirs(build_dir, exist_ok=True)
     for src in SOURCES:
-        obj = os.path.join(HERE, "_build", os.path.splitext(src)[0] + ".o")
+        obj = os.path.join(build_dir, os.path.splitext(src)[0] + ".o")
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", os.path.join(CSRC, src), "-o", obj]
         subprocess.run(cmd, check=True)
         objs.append(obj)
+    objs.append(expf_table_object(build_dir))
     tmp = LIB + ".tmp"
     subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-ldl", "-lrt", "-lpthread"],
                    check=True)

@@ -167,11 +167,35 @@ __device__ __forceinline__ float warp_tree_sum(float v) {
     return v;
 }
 
-// exp rounded to nearest float: the double-precision exponential rounded
-// once.  The reference's CPU SiLU uses the C library's expf; in the range the
-// gate values take this differs from it in under 0.1 % of inputs, by one ulp,
-// which moves the Q8_1 middle code in about 4 of 10^6 of those cases.
-__device__ __forceinline__ float exp_rn(float x) { return __double2float_rn(exp(static_cast<double>(x))); }
+// The C library's expf, bit for bit: the reference's CPU SiLU computes
+// g / (1 + expf(-g)) (src/cpu_expert.cpp:248-259), and a middle Q8_1 that is
+// to equal the reference's byte for byte needs the same exp.  The device
+// takes the double-precision exponential rounded once to float and corrects
+// the inputs where the C library's expf rounds differently (0.008 % of the
+// floats in [-104, 89], listed at build time by csrc/expf_table.c), looked up
+// in a hash table of (x bits, expf bits) with linear probing; empty slots hold
+// key 0xffffffff (a NaN pattern, never a key).  The table is filled once per
+// device before any kernel of this library runs (expf_table_upload).
+constexpr int kExpfSlotsLog2 = 19;
+constexpr uint32_t kExpfEmpty = 0xffffffffu;
+constexpr int kExpfMaxProbe = 64;
+static __device__ uint2 g_expf_fix[1u << kExpfSlotsLog2];
+
+__host__ __device__ __forceinline__ uint32_t expf_fix_slot(uint32_t key) {
+    return (key * 2654435761u) >> (32 - kExpfSlotsLog2);
+}
+__device__ __forceinline__ float expf_ref(float x) {
+    const float y = __double2float_rn(exp(static_cast<double>(x)));
+    const uint32_t k = __float_as_uint(x);
+    uint32_t h = expf_fix_slot(k);
+    for (int i = 0; i < kExpfMaxProbe; ++i) {
+        const uint2 e = g_expf_fix[h];
+        if (e.x == k) return __uint_as_float(e.y);
+        if (e.x == kExpfEmpty) break;
+        h = (h + 1) & ((1u << kExpfSlotsLog2) - 1);
+    }
+    return y;
+}
 
 __device__ __forceinline__ void report(int flags, int *error) {
     if (flags) atomicOr(error, flags);

@@ -317,7 +317,7 @@ gate_up_kernel(GroupParams p) {
                     int flags = 0;
                     g = operand(g, flags);
                     u = operand(u, flags);
-                    const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))), flags);
+                    const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf_ref(-g))), flags);
                     const float v = arithmetic(__fmul_rn(act, u), flags);
                     smid[j * 32 + warp * 4 + lane] = flags ? 0.0f : v;
                     report(flags, p.error);

@@ -14,6 +14,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <vector>
 
 #include "common.cuh"
 #include "expert_kernels.cuh"
@@ -91,6 +92,43 @@ struct Arena {
         return p;
     }
 };
+
+// The C library's expf corrections embedded by the build (csrc/expf_table.c):
+// little-endian uint32 pairs (x bits, expf(x) bits).
+extern "C" const unsigned char qmoe_expf_table_begin[], qmoe_expf_table_end[];
+
+constexpr int kExpfDevices = 64;
+std::mutex g_expf_mutex;
+bool g_expf_loaded[kExpfDevices] = {};
+
+// Fill the current device's g_expf_fix hash table (once per device).
+int expf_table_upload() {
+    int device = 0;
+    MOE_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kExpfDevices) return fail(MOE_NOT_SUPPORTED, "device ordinal above 63");
+    std::lock_guard<std::mutex> lock(g_expf_mutex);
+    if (g_expf_loaded[device]) return MOE_OK;
+    static std::vector<uint2> table;
+    if (table.empty()) {
+        const size_t n = static_cast<size_t>(qmoe_expf_table_end - qmoe_expf_table_begin) / 8;
+        std::vector<uint2> t(size_t(1) << kExpfSlotsLog2, make_uint2(kExpfEmpty, 0u));
+        for (size_t i = 0; i < n; ++i) {
+            uint32_t kv[2];
+            std::memcpy(kv, qmoe_expf_table_begin + 8 * i, 8);
+            uint32_t h = expf_fix_slot(kv[0]);
+            int probe = 0;
+            while (t[h].x != kExpfEmpty) {
+                h = (h + 1) & ((1u << kExpfSlotsLog2) - 1);
+                if (++probe >= kExpfMaxProbe) return fail(MOE_CUDA_ERROR, "expf correction table: probe chain too long");
+            }
+            t[h] = make_uint2(kv[0], kv[1]);
+        }
+        table.swap(t);
+    }
+    MOE_CUDA(cudaMemcpyToSymbol(g_expf_fix, table.data(), table.size() * sizeof(uint2)));
+    g_expf_loaded[device] = true;
+    return MOE_OK;
+}
 
 int sm_count(int device) {
     int n = 0;
@@ -646,6 +684,7 @@ int moe_layer_create(const moe_layer_desc *desc, moe_layer_t *out) {
     if (const int st = validate_desc(desc)) return st;
     DeviceGuard guard(desc->device);
     MOE_CUDA(guard.status);
+    if (const int st = expf_table_upload()) return st;
     auto *h = new (std::nothrow) moe_layer_s();
     if (!h) return fail(MOE_OUT_OF_MEMORY, "host allocation");
     h->desc = *desc;

@@ -218,7 +218,7 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
             int flags = 0;
             g = operand(g, flags);
             u = operand(u, flags);
-            const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, exp_rn(-g))), flags);
+            const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf_ref(-g))), flags);
             const float v = arithmetic(__fmul_rn(act, u), flags);
             mid[j * 32 + cw * R + lane] = flags ? 0.0f : v;
             report(flags, p.error);

@@ -328,7 +328,7 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
         if (c < n) {   // padded pairs get zero codes and constants
             int f = 0;
             const float gv = operand(s3[0][j], f), uv = operand(s3[1][j], f);
-            const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, exp_rn(-gv))), f);
+            const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, expf_ref(-gv))), f);
             const float val = arithmetic(__fmul_rn(act, uv), f);
             q = quantize_lane(f ? 0.0f : val);
             flags |= f | q.flags;
