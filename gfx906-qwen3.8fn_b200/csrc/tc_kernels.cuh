@@ -69,11 +69,13 @@ constexpr int kTcTile = 16;   // pairs per tensor-core tile (gate/up MMA N = 2 x
 //     fragment's bytes zero) in the K-major core-matrix layout, blocks in the
 //     kernel's stage order (tc_gu_pos);
 //   down codes: per block, kTcTile rows of 32 bytes, blocks in order;
-//   constants: per block, (d8[kTcTile], m[kTcTile]) fp32 with m = -4*s8 for
-//     gate/up (per fragment) and -8*s8 for down (whole block).
+//   gate/up constants: per block, (d8, d8)[kTcTile] then (m4, m4)[kTcTile] fp32
+//     with m4 = -4*s8 (per fragment), each duplicated to load as an f32x2;
+//   down constants: per block, d8[kTcTile] then m8[kTcTile], m8 = -8*s8.
 __host__ __device__ constexpr size_t tc_gu_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile * 32; }
 __host__ __device__ constexpr size_t tc_dn_slot(int K) { return static_cast<size_t>(K / 32) * kTcTile * 32; }
-__host__ __device__ constexpr size_t tc_sc_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile; }
+__host__ __device__ constexpr size_t tc_gu_sc_slot(int K) { return static_cast<size_t>(K / 32) * 4 * kTcTile; }
+__host__ __device__ constexpr size_t tc_dn_sc_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile; }
 // Position of gate/up block b (of 64) in the stage order: stage k holds blocks
 // 2k, 2k+1, 2k+32, 2k+33.
 __host__ __device__ constexpr int tc_gu_pos(int b) { return 4 * ((b & 31) >> 1) + 2 * (b >> 5) + (b & 1); }
@@ -103,9 +105,9 @@ inline void tc_workspace_take(TcWorkspace &w, ArenaT &a, int pairs, int H, int I
     if (tc_used) {
         const size_t t = static_cast<size_t>(w.max_tiles);
         w.b_gu = a.template take<uint8_t>(t * tc_gu_slot(H));
-        w.sc_gu = a.template take<float>(t * tc_sc_slot(H));
+        w.sc_gu = a.template take<float>(t * tc_gu_sc_slot(H));
         w.b_dn = a.template take<uint8_t>(t * tc_dn_slot(I));
-        w.sc_dn = a.template take<float>(t * tc_sc_slot(I));
+        w.sc_dn = a.template take<float>(t * tc_dn_sc_slot(I));
     }
 }
 

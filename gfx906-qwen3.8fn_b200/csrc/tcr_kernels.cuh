@@ -73,7 +73,7 @@ struct TcrParams {
     int hidden, inter;
     int raw_rowmajor;          // codes staged [row][block] (3-D maps) instead of [block][row]
     const uint8_t *b_arr;      // arranged activation operand (tc_gu_slot / tc_dn_slot per tile)
-    const float *bsc_arr;      // arranged per-pair constants (tc_sc_slot per tile)
+    const float *bsc_arr;      // arranged per-pair constants (tc_gu_sc_slot / tc_dn_sc_slot per tile)
     const int4 *tiles;         // {expert, first pair, count, 0}
     const int *num_tiles;
     const int32_t *pair_token;
@@ -94,8 +94,9 @@ struct RowsStage {
     static constexpr uint32_t codes = 0;                                      // M x 4 blocks x 128 rows x 16 B
     static constexpr uint32_t scales = codes + M * kRowsKB * kRowsM * 16;     // M x wins x [128][8] half
     static constexpr uint32_t b = scales + M * wins * kRowsM * 16;            // [4][brows][32]
-    static constexpr uint32_t bsc = b + kRowsKB * brows * 32;                 // [4][2][kTcTile] fp32
-    static constexpr uint32_t raw_bytes = (bsc + kRowsKB * 2 * kTcTile * 4 + 1023) / 1024 * 1024;
+    static constexpr uint32_t bsc = b + kRowsKB * brows * 32;                 // [4][cwords][kTcTile] fp32
+    static constexpr int cwords = Down ? 2 : 4;                               // constants per pair and block
+    static constexpr uint32_t raw_bytes = (bsc + kRowsKB * cwords * kTcTile * 4 + 1023) / 1024 * 1024;
     static constexpr uint32_t a_bytes = M * kRowsKB * kRowsM * 32;            // unpacked A tiles
     static constexpr int raw_stages = Down ? 8 : 4;
     static constexpr int a_stages = Down ? 4 : 3;
@@ -197,24 +198,45 @@ __device__ __forceinline__ void region_take(uint32_t taddr, const int (&off)[M],
     if (lane == 0) mbar_arrive(empty_bar);
 }
 
+// SiLU(gate) * up of one middle value (the reference's sanitisation,
+// src/hip/session_ops.hip:250-262) and the Q8_1 of the 32-value block the
+// warp holds (lane = element).  Out of line: the item end calls it per pair.
+struct MidQ {
+    Q8Lane q;
+    int flags;
+};
+__device__ __noinline__ MidQ silu_q8(float g, float u) {
+    int f = 0;
+    const float gv = operand(g, f), uv = operand(u, f);
+    const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, expf_ref(-gv))), f);
+    const float val = arithmetic(__fmul_rn(act, uv), f);
+    MidQ r;
+    r.q = quantize_lane(f ? 0.0f : val);
+    r.flags = f | r.q.flags;
+    return r;
+}
+
 // ---- gate/up epilogue of one item (exact MMVQ order) -----------------------
+// Pairs are handled two at a time (u = unit of pairs pc0 + 2u, pc0 + 2u + 1)
+// as packed f32x2 values; units without a real pair are skipped.
 template <bool Tap>
 __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *smem, uint64_t *raw_full,
                                                  uint64_t *raw_empty, uint64_t *tm_full, uint64_t *tm_empty,
                                                  uint32_t tq, RowsSeq &sq, int item, int4 td, int lane, int quarter,
                                                  int chunk) {
     using St = RowsStage<false>;
-    constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile;
+    constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile, U = CW / 2;
     const int I = p.inter;
     const int nb = kRowsHidden / 32, slabs = I / kRowsM;
     const int slab = item % slabs, tile = item / slabs;
     const int e = td.x, p0 = td.y, n = td.z;
     const int pc0 = chunk * CW;                               // this warp's first pair
+    const int units = min(U, max(0, (n - pc0 + 1) / 2));      // units holding a real pair
     const int lrow = quarter * 32 + lane;                     // row within the slab
     const int row = slab * kRowsM + lrow;                     // middle row of this lane
     const uint64_t unbias = pkf2(-kMagicF, -kMagicF), zero2 = 0ull;
-    // binary-tree stack over the 16 level-2 nodes (s3 ends as the total)
-    float s0[2][CW], s1[2][CW], s2[2][CW], s3[2][CW], la[2][CW];
+    // binary-tree stack over the 16 level-2 nodes, per matrix and unit (s3 ends as the total)
+    uint64_t s0[2][U], s1[2][U], s2[2][U], s3[2][U];
     int tap_base = 0;
     if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
 
@@ -222,12 +244,16 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
         const int s = sq.g % St::raw_stages;
         const uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
         if (!mbar_wait(&raw_full[s], (sq.g / St::raw_stages) & 1, p.error)) return false;
-#pragma unroll
+        uint64_t la[2][U], node[2][U];
+#pragma unroll 1
         for (int h = 0; h < 2; ++h, ++sq.k) {   // region h: blocks 2k+h (columns +0) and 2k+32+h (+32)
             const int r = static_cast<int>(sq.k % R);
             if (!mbar_wait(&tm_full[r], (sq.k / R) & 1, p.error)) return false;
             tc_fence_after();
             const uint32_t tr = tq + r * St::reg_cols + 2 * pc0;
+            // duplicated pair constants (d8, d8) and (-4 s8, -4 s8) of block 2k+h (slot h) and 2k+32+h (slot 2+h)
+            const uint64_t *ka = reinterpret_cast<const uint64_t *>(st + St::bsc) + h * 2 * NP + pc0;
+            const uint64_t *kb = reinterpret_cast<const uint64_t *>(st + St::bsc) + (2 + h) * 2 * NP + pc0;
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
                 uint32_t v[2][2 * CW];
@@ -249,48 +275,21 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
                 const int col = (2 * ks) % 8 + h;
                 const float d4a = h2f(sc[lrow * 8 + col]), d4b = h2f(sc[kRowsM * 8 + lrow * 8 + col]);
                 const uint64_t d4ap = pkf2(d4a, d4a), d4bp = pkf2(d4b, d4b);
-                // pair constants of block 2k+h (stage slot h) and 2k+32+h (slot 2+h)
-                const float *ca = reinterpret_cast<const float *>(st + St::bsc) + h * 2 * NP + pc0;
-                const float *cb = reinterpret_cast<const float *>(st + St::bsc) + (2 + h) * 2 * NP + pc0;
 #pragma unroll
-                for (int j4 = 0; j4 < CW / 4; ++j4) {
-                    const float4 d8a = *reinterpret_cast<const float4 *>(ca + 4 * j4);
-                    const float4 m4a = *reinterpret_cast<const float4 *>(ca + NP + 4 * j4);
-                    const float4 d8b = *reinterpret_cast<const float4 *>(cb + 4 * j4);
-                    const float4 m4b = *reinterpret_cast<const float4 *>(cb + NP + 4 * j4);
-                    const float da[4] = {d8a.x, d8a.y, d8a.z, d8a.w}, ma[4] = {m4a.x, m4a.y, m4a.z, m4a.w};
-                    const float db[4] = {d8b.x, d8b.y, d8b.z, d8b.w}, mb[4] = {m4b.x, m4b.y, m4b.z, m4b.w};
+                for (int u = 0; u < U; ++u) {
+                    if (u >= units) break;
+                    float leaf[2];
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int j = 4 * j4 + q;
-                        // (fragment 0, fragment 1) dots of blocks 2k+h and 2k+32+h
+                    for (int jj = 0; jj < 2; ++jj) {
+                        const int j = 2 * u + jj;
+                        // (fragment 0, fragment 1) dots of blocks 2k+h and 2k+32+h, exact
                         const uint64_t ta = add2(pk2(v[0][2 * j], v[0][2 * j + 1]), unbias);
                         const uint64_t tb = add2(pk2(v[1][2 * j], v[1][2 * j + 1]), unbias);
-                        const uint64_t a0 = mmvq_term2(ta, d4ap, pkf2(da[q], da[q]), pkf2(ma[q], ma[q]), zero2);
-                        const uint64_t a1 = mmvq_term2(tb, d4bp, pkf2(db[q], db[q]), pkf2(mb[q], mb[q]), zero2);
-                        const float leaf = mmvq_leaf(a0, a1);
-                        if (h == 0) {
-                            la[m][j] = leaf;
-                        } else {
-                            // node k = L(2k) + L(2k+1), pushed into the binary tree over k = 0..15
-                            float x = __fadd_rn(la[m][j], leaf);
-                            if (ks & 1) {
-                                x = __fadd_rn(s0[m][j], x);
-                                if (ks & 2) {
-                                    x = __fadd_rn(s1[m][j], x);
-                                    if (ks & 4) {
-                                        x = __fadd_rn(s2[m][j], x);
-                                        s3[m][j] = (ks & 8) ? __fadd_rn(s3[m][j], x) : x;
-                                    } else {
-                                        s2[m][j] = x;
-                                    }
-                                } else {
-                                    s1[m][j] = x;
-                                }
-                            } else {
-                                s0[m][j] = x;
-                            }
-                        }
+                        const uint64_t a0 = mmvq_term2(ta, d4ap, ka[j], ka[NP + j], zero2);
+                        const uint64_t a1 = mmvq_term2(tb, d4bp, kb[j], kb[NP + j], zero2);
+                        float sx, sy;
+                        upk2(add2(a0, a1), sx, sy);   // lanes i and i + 64 of both fragments
+                        leaf[jj] = __fadd_rn(sx, sy);  // the fragments' lanes (XOR 1)
                         if constexpr (Tap) {
                             const int pl = p0 + pc0 + j - tap_base;
                             if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs) {
@@ -304,6 +303,9 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
                             }
                         }
                     }
+                    const uint64_t l2 = pkf2(leaf[0], leaf[1]);
+                    if (h == 0) la[m][u] = l2;
+                    else node[m][u] = add2(la[m][u], l2);   // node k = L(2k) + L(2k+1)
                 }
             }
             tmem_wait_st();
@@ -313,6 +315,31 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[s]);   // done with the stage's scales and constants
+        // push node k into the binary tree over k = 0..15 (one warp-uniform branch nest)
+        if (!(ks & 1)) {
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int u = 0; u < U; ++u) s0[m][u] = node[m][u];
+        } else if (!(ks & 2)) {
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int u = 0; u < U; ++u) s1[m][u] = add2(s0[m][u], node[m][u]);
+        } else if (!(ks & 4)) {
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int u = 0; u < U; ++u) s2[m][u] = add2(s1[m][u], add2(s0[m][u], node[m][u]));
+        } else {
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const uint64_t x = add2(s2[m][u], add2(s1[m][u], add2(s0[m][u], node[m][u])));
+                    s3[m][u] = (ks & 8) ? add2(s3[m][u], x) : x;
+                }
+        }
     }
 
     // SiLU(gate) * up, then Q8_1 of the 32-row middle block held by this warp
@@ -320,30 +347,29 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
     const int jb = slab * (kRowsM / 32) + quarter;   // middle block index
     const int nbI = I / 32;
     uint8_t *mslot = p.mid_arr + static_cast<size_t>(tile) * tc_dn_slot(I) + static_cast<size_t>(jb) * NP * 32;
-    float *msc = p.mid_sc_arr + static_cast<size_t>(tile) * tc_sc_slot(I) + static_cast<size_t>(jb) * 2 * NP;
+    float *msc = p.mid_sc_arr + static_cast<size_t>(tile) * tc_dn_sc_slot(I) + static_cast<size_t>(jb) * 2 * NP;
 #pragma unroll
     for (int j = 0; j < CW; ++j) {
         const int c = pc0 + j;
-        Q8Lane q{0, 0, 0, 0};
+        MidQ r{{0, 0, 0, 0}, 0};
         if (c < n) {   // padded pairs get zero codes and constants
-            int f = 0;
-            const float gv = operand(s3[0][j], f), uv = operand(s3[1][j], f);
-            const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, expf_ref(-gv))), f);
-            const float val = arithmetic(__fmul_rn(act, uv), f);
-            q = quantize_lane(f ? 0.0f : val);
-            flags |= f | q.flags;
+            float g0, g1, u0, u1;
+            upk2(s3[0][j / 2], g0, g1);
+            upk2(s3[1][j / 2], u0, u1);
+            r = silu_q8((j & 1) ? g1 : g0, (j & 1) ? u1 : u0);
+            flags |= r.flags;
         }
-        const uint32_t word = pack_lane_bytes(q.code);
+        const uint32_t word = pack_lane_bytes(r.q.code);
         if ((lane & 3) == 0) *reinterpret_cast<uint32_t *>(mslot + tile_off(c, lane >> 4) + (lane & 15)) = word;
         if (lane == 0) {
-            msc[c] = h2f(q.d);
-            msc[NP + c] = -(8.0f * h2f(q.s));
+            msc[c] = h2f(r.q.d);
+            msc[NP + c] = -(8.0f * h2f(r.q.s));
         }
         if constexpr (Tap) {
             const int pl = p0 + c - tap_base;
             if (e == p.tap.expert && c < n && pl >= 0 && pl < p.tap.max_pairs) {
-                p.tap.mid_codes[static_cast<size_t>(pl) * I + row] = q.code;
-                if (lane == 0) p.tap.mid_ds[static_cast<size_t>(pl) * nbI + jb] = q.d | (uint32_t(q.s) << 16);
+                p.tap.mid_codes[static_cast<size_t>(pl) * I + row] = r.q.code;
+                if (lane == 0) p.tap.mid_ds[static_cast<size_t>(pl) * nbI + jb] = r.q.d | (uint32_t(r.q.s) << 16);
             }
         }
     }
@@ -499,8 +525,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                 tma_prefetch_map(&p.maps.codes[Down ? 2 : m]);
                 tma_prefetch_map(&p.maps.scales[Down ? 2 : m]);
             }
-            constexpr uint32_t bbytes = kRowsKB * St::brows * 32, sbytes = kRowsKB * 2 * kTcTile * 4;
-            const size_t bslot = Down ? tc_dn_slot(K) : tc_gu_slot(K), sslot = tc_sc_slot(K);
+            constexpr uint32_t bbytes = kRowsKB * St::brows * 32, sbytes = kRowsKB * St::cwords * kTcTile * 4;
+            const size_t bslot = Down ? tc_dn_slot(K) : tc_gu_slot(K);
+            const size_t sslot = Down ? tc_dn_sc_slot(K) : tc_gu_sc_slot(K);
             int g = 0;
             bool failed = false;
             for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
@@ -532,7 +559,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                     bulk_g2s(st + St::b, p.b_arr + static_cast<size_t>(tile) * bslot + static_cast<size_t>(ks) * bbytes,
                              bbytes, &raw_full[s]);
                     bulk_g2s(st + St::bsc,
-                             p.bsc_arr + static_cast<size_t>(tile) * sslot + static_cast<size_t>(ks) * kRowsKB * 2 * kTcTile,
+                             p.bsc_arr + static_cast<size_t>(tile) * sslot +
+                                 static_cast<size_t>(ks) * kRowsKB * St::cwords * kTcTile,
                              sbytes, &raw_full[s]);
                 }
             }
@@ -663,7 +691,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
 // Gate/up B operand of every tile: for pair r < n of tile t (token
 // pair_token[p0 + r]), row 2r = its Q8_1 codes of fragment 0 (elements 0..7
 // and 16..23, the rest zero) and row 2r + 1 those of fragment 1, blocks in
-// stage order, and the constants (d8, -4*s8); pairs n..15 are zero.
+// stage order, and the constants (d8, d8) and (-4*s8, -4*s8) (duplicated so
+// they load as f32x2 operands); pairs n..15 are zero.
 // CTA (t, g): 32 threads (fragment rows) x blocks 8g..8g+7.
 __global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 *tiles, const int *num_tiles,
                                                                      const int32_t *pair_token, Q8Planar xq, int H,
@@ -692,17 +721,16 @@ __global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 
             for (int i = 0; i < 8; ++i) c[i] = make_float2(0.0f, 0.0f);
         }
         uint8_t *slot = b_arr + static_cast<size_t>(t) * tc_gu_slot(H);
-        float *ss = bsc_arr + static_cast<size_t>(t) * tc_sc_slot(H);
+        float *ss = bsc_arr + static_cast<size_t>(t) * tc_gu_sc_slot(H);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int pos = tc_gu_pos(b0 + i);
             uint8_t *dst = slot + static_cast<size_t>(pos) * 2 * kTcTile * 32;
             *reinterpret_cast<uint4 *>(dst + tile_off(frow, 0)) = v[2 * i];
             *reinterpret_cast<uint4 *>(dst + tile_off(frow, 1)) = v[2 * i + 1];
-            if (!frag) {
-                ss[pos * 2 * kTcTile + pr] = c[i].x;
-                ss[pos * 2 * kTcTile + kTcTile + pr] = -(4.0f * c[i].y);
-            }
+            // (d8, d8) and (-4 s8, -4 s8): each fragment-row thread writes one copy
+            ss[pos * 4 * kTcTile + 2 * pr + frag] = c[i].x;
+            ss[pos * 4 * kTcTile + 2 * kTcTile + 2 * pr + frag] = -(4.0f * c[i].y);
         }
     }
 }
