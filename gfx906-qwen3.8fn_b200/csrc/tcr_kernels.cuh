@@ -9,10 +9,11 @@
 // A u8 x s8 product is the reference's uncentred dot sum(q * x)
 // (src/quant.cpp:48-55) with |dot| < 2^16.
 //
-// Exact conversion: every TMEM accumulator is preloaded with the bit pattern
-// of 1.5 * 2^23 (0x4b400000) and each MMA accumulates onto it, so the result
-// bits read as fp32 are exactly 1.5 * 2^23 + dot; one subtraction recovers the
-// dot.  The reader stores the pattern back before releasing the region.
+// Exact conversion: each TMEM column range is written by one MMA (no
+// accumulation), so it holds the int32 dot; adding it to the bit pattern of
+// 1.5 * 2^23 and subtracting 1.5 * 2^23 in fp32 gives the dot as an exact
+// float (|dot| < 2^22) -- an integer add and half an f32x2 subtraction per
+// value instead of the quarter-rate int-to-float conversion.
 //
 // Gate/up (the values the middle Q8_1 is quantised from) follow the
 // reference's MMVQ order bit for bit (common.cuh: mmvq_term2 / mmvq_leaf), so
@@ -23,7 +24,7 @@
 // 2k+1, 2k+32, 2k+33 (one level-2 node of the tree), and the 16 nodes of an
 // item are summed as a binary tree with a four-slot stack in registers.  Each
 // epilogue thread owns one weight row (its TMEM lane) of gate and of up for
-// 8 pairs; the item end runs SiLU(gate) * up and the Q8_1 of each 32-row
+// 4 pairs; the item end runs SiLU(gate) * up and the Q8_1 of each 32-row
 // middle block (one warp = one block per pair: lane = element, the
 // reference's butterfly order) and writes the down pass's operand.
 //
@@ -37,7 +38,7 @@
 //               activation operand as 1-D bulk copies;
 //   warp 1      lane 0 issues the MMAs;
 //   warps 2-3   unpack raw Q4_0 codes shared -> shared into the MMA layout;
-//   warps 4-11  epilogue: two per TMEM lane quarter, 8 pairs each.
+//   warps 4-19  epilogue: four per TMEM lane quarter, 4 pairs each.
 // Every barrier wait is bounded (ptx.cuh); a wait that gives up sets the
 // timeout flag and the role leaves its loop.
 #pragma once
@@ -52,14 +53,14 @@ namespace qmoe {
 
 constexpr int kRowsM = 128;            // weight rows per MMA (TMEM lanes)
 constexpr int kRowsKB = 4;             // quantisation blocks per pipeline stage
-constexpr int kRowsCW = kTcTile / 2;   // pairs per epilogue warp
+constexpr int kRowsCW = kTcTile / 4;   // pairs per epilogue warp (four warps per TMEM lane quarter)
 constexpr int kRowsUnpackWarps = 2;
-constexpr int kRowsEpiWarps = 8;
+constexpr int kRowsEpiWarps = 16;
 constexpr int kRowsWarps = 2 + kRowsUnpackWarps + kRowsEpiWarps;
 constexpr int kRowsThreads = 32 * kRowsWarps;
 constexpr int kRowsMinGroup = 1;       // batches above decode size: every group on this path
 constexpr int kRowsHidden = 2048;      // the gate/up stage order pairs blocks b and b + 32 of 64
-constexpr uint32_t kMagicBits = 0x4b400000u;
+constexpr int kMagicBits = 0x4b400000;  // bit pattern of 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f; // 1.5 * 2^23
 
 // Tensor maps over one weights object (all experts), built on the host.
@@ -137,13 +138,27 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t *r) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                  : "r"(taddr));
 }
-// Store the preload pattern into 8 consecutive columns.
-__device__ __forceinline__ void tmem_st8_magic(uint32_t taddr) {
-    const uint32_t m = kMagicBits;
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(m)
-                 : "memory");
+// 4 consecutive TMEM columns of this warp's lane quarter.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t *r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tie4(uint32_t *r) {
+    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]) : : "memory");
+}
+// Two int32 dots as an exact f32x2 (|dot| < 2^22).
+__device__ __forceinline__ uint64_t dots2(uint32_t a, uint32_t b) {
+    return add2(pk2(a + static_cast<uint32_t>(kMagicBits), b + static_cast<uint32_t>(kMagicBits)),
+                pkf2(-kMagicF, -kMagicF));
+}
+// Release a TMEM region read by this warp (its loads have completed).
+__device__ __forceinline__ void region_release(uint64_t *empty_bar, int lane) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+}
+
 // Tie 8 registers to a point after the TMEM load wait, so no use of them is
 // scheduled before it.
 __device__ __forceinline__ void tie8(uint32_t *r) {
@@ -172,30 +187,6 @@ __device__ __forceinline__ uint32_t pack_lane_bytes(int8_t code) {
     v |= __shfl_down_sync(0xffffffffu, v, 1) << 8;
     v |= __shfl_down_sync(0xffffffffu, v, 2) << 16;
     return v;
-}
-
-// Read this warp's columns of one TMEM region (Cols per matrix at `off[m]`),
-// then store the preload pattern back and release the region.
-template <int M, int Cols>
-__device__ __forceinline__ void region_take(uint32_t taddr, const int (&off)[M], uint32_t (&v)[M][Cols],
-                                            uint64_t *empty_bar, int lane) {
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int j = 0; j < Cols; j += 8) tmem_ld8(taddr + off[m] + j, &v[m][j]);
-    tmem_wait_ld();
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int j = 0; j < Cols; j += 8) tie8(&v[m][j]);
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int j = 0; j < Cols; j += 8) tmem_st8_magic(taddr + off[m] + j);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar);
 }
 
 // SiLU(gate) * up of one middle value (the reference's sanitisation,
@@ -234,7 +225,7 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
     const int units = min(U, max(0, (n - pc0 + 1) / 2));      // units holding a real pair
     const int lrow = quarter * 32 + lane;                     // row within the slab
     const int row = slab * kRowsM + lrow;                     // middle row of this lane
-    const uint64_t unbias = pkf2(-kMagicF, -kMagicF), zero2 = 0ull;
+    const uint64_t zero2 = 0ull;
     // binary-tree stack over the 16 level-2 nodes, per matrix and unit (s3 ends as the total)
     uint64_t s0[2][U], s1[2][U], s2[2][U], s3[2][U];
     int tap_base = 0;
@@ -256,20 +247,13 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
             const uint64_t *kb = reinterpret_cast<const uint64_t *>(st + St::bsc) + (2 + h) * 2 * NP + pc0;
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
+                static_assert(2 * CW == 8, "one x8 load per matrix and block");
                 uint32_t v[2][2 * CW];
 #pragma unroll
-                for (int q = 0; q < 2; ++q)
-#pragma unroll
-                    for (int j = 0; j < 2 * CW; j += 8) tmem_ld8(tr + m * 64 + q * 32 + j, &v[q][j]);
+                for (int q = 0; q < 2; ++q) tmem_ld8(tr + m * 64 + q * 32, v[q]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int q = 0; q < 2; ++q)
-#pragma unroll
-                    for (int j = 0; j < 2 * CW; j += 8) tie8(&v[q][j]);
-#pragma unroll
-                for (int q = 0; q < 2; ++q)
-#pragma unroll
-                    for (int j = 0; j < 2 * CW; j += 8) tmem_st8_magic(tr + m * 64 + q * 32 + j);
+                for (int q = 0; q < 2; ++q) tie8(v[q]);
                 // scales: window 0 holds blocks 2k, 2k+1, window 1 blocks 2k+32, 2k+33
                 const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales + m * 2 * kRowsM * 16);
                 const int col = (2 * ks) % 8 + h;
@@ -283,8 +267,8 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
                     for (int jj = 0; jj < 2; ++jj) {
                         const int j = 2 * u + jj;
                         // (fragment 0, fragment 1) dots of blocks 2k+h and 2k+32+h, exact
-                        const uint64_t ta = add2(pk2(v[0][2 * j], v[0][2 * j + 1]), unbias);
-                        const uint64_t tb = add2(pk2(v[1][2 * j], v[1][2 * j + 1]), unbias);
+                        const uint64_t ta = dots2(v[0][2 * j], v[0][2 * j + 1]);
+                        const uint64_t tb = dots2(v[1][2 * j], v[1][2 * j + 1]);
                         const uint64_t a0 = mmvq_term2(ta, d4ap, ka[j], ka[NP + j], zero2);
                         const uint64_t a1 = mmvq_term2(tb, d4bp, kb[j], kb[NP + j], zero2);
                         float sx, sy;
@@ -308,10 +292,7 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
                     else node[m][u] = add2(la[m][u], l2);   // node k = L(2k) + L(2k+1)
                 }
             }
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tm_empty[r]);
+            region_release(&tm_empty[r], lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[s]);   // done with the stage's scales and constants
@@ -396,7 +377,6 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
     uint64_t acc[CW / 2];
 #pragma unroll
     for (int j = 0; j < CW / 2; ++j) acc[j] = 0ull;
-    const uint64_t unbias = pkf2(-kMagicF, -kMagicF);
     int tap_base = 0;
     if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
 
@@ -409,9 +389,12 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
             const int r = static_cast<int>(sq.k % R);
             if (!mbar_wait(&tm_full[r], (sq.k / R) & 1, p.error)) return false;
             tc_fence_after();
+            static_assert(CW == 4, "one x4 load per block");
             uint32_t v[1][CW];
-            const int off[1] = {pc0};
-            region_take<1, CW>(tq + r * St::reg_cols, off, v, &tm_empty[r], lane);
+            tmem_ld4(tq + r * St::reg_cols + pc0, v[0]);
+            tmem_wait_ld();
+            tie4(v[0]);
+            region_release(&tm_empty[r], lane);
             const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales);
             const float d4 = h2f(sc[lrow * 8 + (ks & 1) * 4 + kb]);
             const uint64_t d4p = pkf2(d4, d4);
@@ -426,7 +409,7 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
                     const uint64_t d8 = h ? pkf2(d8q.z, d8q.w) : pkf2(d8q.x, d8q.y);
                     const uint64_t m8 = h ? pkf2(m8q.z, m8q.w) : pkf2(m8q.x, m8q.y);
                     const int j = 4 * j4 + 2 * h;
-                    const uint64_t t = add2(pk2(v[0][j], v[0][j + 1]), unbias);   // exact dots
+                    const uint64_t t = dots2(v[0][j], v[0][j + 1]);   // exact dots
                     acc[j / 2] = fma2(d4p, fma2(t, d8, m8), acc[j / 2]);
                 }
             }
@@ -437,7 +420,7 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
                         const int pl = p0 + pc0 + j - tap_base;
                         if (pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs)
                             p.tap.down[(static_cast<size_t>(pl) * H + row) * nb + ks * kRowsKB + kb] =
-                                static_cast<int32_t>(__uint_as_float(v[0][j]) - kMagicF);
+                                static_cast<int32_t>(v[0][j]);
                     }
                 }
             }
@@ -593,7 +576,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                             // block h of the stage into the region's columns [0, 16)
                             const uint64_t ad = smem_desc(a_st + h * kRowsM * 32, 128, 256);
                             const uint64_t bd = smem_desc(b_st + h * St::brows * 32, 128, 256);
-                            mma_i8(tmem + r * St::reg_cols, ad, bd, idesc, 1u);
+                            mma_i8(tmem + r * St::reg_cols, ad, bd, idesc, 0u);
                         } else {
                             // stage slots h (block 2k+h) and 2+h (block 2k+32+h): columns [0,32) and [32,64)
                             // of gate, +64 for up
@@ -604,7 +587,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                                     const int slot = h + 2 * q;
                                     const uint64_t ad = smem_desc(a_st + (m * kRowsKB + slot) * kRowsM * 32, 128, 256);
                                     const uint64_t bd = smem_desc(b_st + slot * St::brows * 32, 128, 256);
-                                    mma_i8(tmem + r * St::reg_cols + m * 64 + q * 32, ad, bd, idesc, 1u);
+                                    mma_i8(tmem + r * St::reg_cols + m * 64 + q * 32, ad, bd, idesc, 0u);
                                 }
                         }
                         mma_commit(&tm_full[r]);
@@ -622,6 +605,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
         const int ut = threadIdx.x - 64;
         constexpr int kUnits = M * kRowsKB * kRowsM;
         constexpr int copies = kRowsKB / St::bpc;
+        static_assert(kUnits % (32 * kRowsUnpackWarps) == 0, "whole unpack rounds");
+        const bool rowmajor = p.raw_rowmajor != 0;
         int g = 0;
         bool failed = false;
         for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
@@ -634,12 +619,12 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                 }
                 const uint8_t *raw = smem + St::raw_off + sr * St::raw_bytes + St::codes;
                 uint8_t *a = smem + St::a_off + sa * St::a_bytes;
-#pragma unroll 4
-                for (int u = ut; u < kUnits; u += 32 * kRowsUnpackWarps) {
+#pragma unroll
+                for (int i = 0; i < kUnits / (32 * kRowsUnpackWarps); ++i) {
+                    const int u = ut + i * 32 * kRowsUnpackWarps;
                     const int m = u / (kRowsKB * kRowsM), kb = (u / kRowsM) % kRowsKB, row = u % kRowsM;
-                    const int src = p.raw_rowmajor
-                                        ? ((m * copies + kb / St::bpc) * kRowsM + row) * St::bpc + kb % St::bpc
-                                        : (m * kRowsKB + kb) * kRowsM + row;
+                    const int src = rowmajor ? ((m * copies + kb / St::bpc) * kRowsM + row) * St::bpc + kb % St::bpc
+                                             : (m * kRowsKB + kb) * kRowsM + row;
                     const uint4 w = reinterpret_cast<const uint4 *>(raw)[src];
                     const uint4 lo = make_uint4(w.x & 0x0f0f0f0fu, w.y & 0x0f0f0f0fu, w.z & 0x0f0f0f0fu,
                                                 w.w & 0x0f0f0f0fu);
@@ -659,15 +644,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
         }
     } else {
         // ---------------- epilogue ----------------
-        const int ew = warp - 2 - kRowsUnpackWarps;   // 0..7
-        const int quarter = warp & 3, chunk = ew >> 2;
+        const int ew = warp - 2 - kRowsUnpackWarps;   // 0..15
+        const int quarter = warp & 3, chunk = ew >> 2;    // TMEM lane quarter, pair chunk of kRowsCW
         const uint32_t tq = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-        // preload every column of this warp's half of its lane quarter
-        for (int c = chunk * 256; c < chunk * 256 + 256; c += 8) tmem_st8_magic(tq + c);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
+        if (lane == 0)   // every region starts free
             for (int r = 0; r < R; ++r) mbar_arrive(&tm_empty[r]);
         RowsSeq sq;
         for (int item = blockIdx.x; item < total; item += gridDim.x) {
