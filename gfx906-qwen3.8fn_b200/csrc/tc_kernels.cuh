@@ -64,17 +64,17 @@ constexpr int kTcTile = 16;   // pairs per tensor-core tile (gate/up MMA N = 2 x
 
 // Arranged operand slots of one tile (filled by the gather kernel for gate/up
 // and by the gate/up epilogue for down), K = H or I:
-//   gate/up codes: per block, 2 * kTcTile rows of 32 bytes (pair p: row 2p =
-//     fragment 0 elements, row 2p + 1 = fragment 1 elements, the other
+//   gate/up codes: per block, 2 * kTcTile rows of 32 bytes (pair p: row p =
+//     fragment 0 elements, row kTcTile + p = fragment 1 elements, the other
 //     fragment's bytes zero) in the K-major core-matrix layout, blocks in the
 //     kernel's stage order (tc_gu_pos);
 //   down codes: per block, kTcTile rows of 32 bytes, blocks in order;
-//   gate/up constants: per block, (d8, d8)[kTcTile] then (m4, m4)[kTcTile] fp32
-//     with m4 = -4*s8 (per fragment), each duplicated to load as an f32x2;
+//   gate/up constants: per block, d8[kTcTile] then m4[kTcTile] fp32 with
+//     m4 = -4*s8 (per fragment);
 //   down constants: per block, d8[kTcTile] then m8[kTcTile], m8 = -8*s8.
 __host__ __device__ constexpr size_t tc_gu_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile * 32; }
 __host__ __device__ constexpr size_t tc_dn_slot(int K) { return static_cast<size_t>(K / 32) * kTcTile * 32; }
-__host__ __device__ constexpr size_t tc_gu_sc_slot(int K) { return static_cast<size_t>(K / 32) * 4 * kTcTile; }
+__host__ __device__ constexpr size_t tc_gu_sc_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile; }
 __host__ __device__ constexpr size_t tc_dn_sc_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile; }
 // Position of gate/up block b (of 64) in the stage order: stage k holds blocks
 // 2k, 2k+1, 2k+32, 2k+33.

@@ -18,8 +18,10 @@
 // Gate/up (the values the middle Q8_1 is quantised from) follow the
 // reference's MMVQ order bit for bit (common.cuh: mmvq_term2 / mmvq_leaf), so
 // the middle equals the reference CPU expert's: B holds two rows per pair,
-// one per 16-element fragment (the other fragment's bytes zero), so the MMA
-// (N = 32) gives both fragment dots; blocks b and b + 32 land in one TMEM
+// one per 16-element fragment (the other fragment's bytes zero): rows 0..15
+// fragment 0 of pairs 0..15, rows 16..31 fragment 1, so the MMA (N = 32) gives
+// both fragment dots with adjacent columns = adjacent pairs, and the fp32
+// arithmetic runs as f32x2 over pairs; blocks b and b + 32 land in one TMEM
 // region and form the tree's leaves; a pipeline stage carries blocks 2k,
 // 2k+1, 2k+32, 2k+33 (one level-2 node of the tree), and the 16 nodes of an
 // item are summed as a binary tree with a four-slot stack in registers.  Each
@@ -96,7 +98,7 @@ struct RowsStage {
     static constexpr uint32_t scales = codes + M * kRowsKB * kRowsM * 16;     // M x wins x [128][8] half
     static constexpr uint32_t b = scales + M * wins * kRowsM * 16;            // [4][brows][32]
     static constexpr uint32_t bsc = b + kRowsKB * brows * 32;                 // [4][cwords][kTcTile] fp32
-    static constexpr int cwords = Down ? 2 : 4;                               // constants per pair and block
+    static constexpr int cwords = 2;                                          // constants per pair and block
     static constexpr uint32_t raw_bytes = (bsc + kRowsKB * cwords * kTcTile * 4 + 1023) / 1024 * 1024;
     static constexpr uint32_t a_bytes = M * kRowsKB * kRowsM * 32;            // unpacked A tiles
     static constexpr int raw_stages = Down ? 8 : 4;
@@ -191,12 +193,12 @@ __device__ __forceinline__ uint32_t pack_lane_bytes(int8_t code) {
 
 // SiLU(gate) * up of one middle value (the reference's sanitisation,
 // src/hip/session_ops.hip:250-262) and the Q8_1 of the 32-value block the
-// warp holds (lane = element).  Out of line: the item end calls it per pair.
+// warp holds (lane = element).
 struct MidQ {
     Q8Lane q;
     int flags;
 };
-__device__ __noinline__ MidQ silu_q8(float g, float u) {
+__device__ __forceinline__ MidQ silu_q8(float g, float u) {
     int f = 0;
     const float gv = operand(g, f), uv = operand(u, f);
     const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, expf_ref(-gv))), f);
@@ -208,8 +210,8 @@ __device__ __noinline__ MidQ silu_q8(float g, float u) {
 }
 
 // ---- gate/up epilogue of one item (exact MMVQ order) -----------------------
-// Pairs are handled two at a time (u = unit of pairs pc0 + 2u, pc0 + 2u + 1)
-// as packed f32x2 values; units without a real pair are skipped.
+// Pairs are handled two at a time (unit u = pairs pc0 + 2u, pc0 + 2u + 1) as
+// packed f32x2 values; units without a real pair are skipped.
 template <bool Tap>
 __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *smem, uint64_t *raw_full,
                                                  uint64_t *raw_empty, uint64_t *tm_full, uint64_t *tm_empty,
@@ -241,19 +243,26 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
             const int r = static_cast<int>(sq.k % R);
             if (!mbar_wait(&tm_full[r], (sq.k / R) & 1, p.error)) return false;
             tc_fence_after();
-            const uint32_t tr = tq + r * St::reg_cols + 2 * pc0;
-            // duplicated pair constants (d8, d8) and (-4 s8, -4 s8) of block 2k+h (slot h) and 2k+32+h (slot 2+h)
-            const uint64_t *ka = reinterpret_cast<const uint64_t *>(st + St::bsc) + h * 2 * NP + pc0;
-            const uint64_t *kb = reinterpret_cast<const uint64_t *>(st + St::bsc) + (2 + h) * 2 * NP + pc0;
+            const uint32_t tr = tq + r * St::reg_cols + pc0;
+            // pair constants d8 and -4 s8 of block 2k+h (slot h) and 2k+32+h (slot 2+h)
+            const uint64_t *ka = reinterpret_cast<const uint64_t *>(
+                reinterpret_cast<const float *>(st + St::bsc) + h * 2 * NP + pc0);
+            const uint64_t *kb = reinterpret_cast<const uint64_t *>(
+                reinterpret_cast<const float *>(st + St::bsc) + (2 + h) * 2 * NP + pc0);
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
-                static_assert(2 * CW == 8, "one x8 load per matrix and block");
-                uint32_t v[2][2 * CW];
+                // [block a / b][fragment] x this warp's CW pairs
+                static_assert(CW == 4, "one x4 load per matrix, block and fragment");
+                uint32_t v[2][2][CW];
 #pragma unroll
-                for (int q = 0; q < 2; ++q) tmem_ld8(tr + m * 64 + q * 32, v[q]);
+                for (int q = 0; q < 2; ++q)
+#pragma unroll
+                    for (int f = 0; f < 2; ++f) tmem_ld4(tr + m * 64 + q * 32 + f * NP, v[q][f]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int q = 0; q < 2; ++q) tie8(v[q]);
+                for (int q = 0; q < 2; ++q)
+#pragma unroll
+                    for (int f = 0; f < 2; ++f) tie4(v[q][f]);
                 // scales: window 0 holds blocks 2k, 2k+1, window 1 blocks 2k+32, 2k+33
                 const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales + m * 2 * kRowsM * 16);
                 const int col = (2 * ks) % 8 + h;
@@ -262,34 +271,37 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     if (u >= units) break;
-                    float leaf[2];
+                    const uint64_t d8a = ka[u], m4a = ka[NP / 2 + u], d8b = kb[u], m4b = kb[NP / 2 + u];
+                    // exact fragment dots of the unit's two pairs: block a (2k+h) and b (2k+32+h)
+                    const uint64_t ta0 = dots2(v[0][0][2 * u], v[0][0][2 * u + 1]);
+                    const uint64_t ta1 = dots2(v[0][1][2 * u], v[0][1][2 * u + 1]);
+                    const uint64_t tb0 = dots2(v[1][0][2 * u], v[1][0][2 * u + 1]);
+                    const uint64_t tb1 = dots2(v[1][1][2 * u], v[1][1][2 * u + 1]);
+                    // MMVQ lanes 2b+f (terms of block a) and 2b+f+64 (block b), summed, then the fragments
+                    const uint64_t leaf =
+                        add2(add2(mmvq_term2(ta0, d4ap, d8a, m4a, zero2), mmvq_term2(tb0, d4bp, d8b, m4b, zero2)),
+                             add2(mmvq_term2(ta1, d4ap, d8a, m4a, zero2), mmvq_term2(tb1, d4bp, d8b, m4b, zero2)));
+                    if (h == 0) la[m][u] = leaf;
+                    else node[m][u] = add2(la[m][u], leaf);   // node k = L(2k) + L(2k+1)
+                    if constexpr (Tap) {
+                        float a0, a1, c0, c1, b0, b1, e0, e1;
+                        upk2(ta0, a0, a1);
+                        upk2(ta1, c0, c1);
+                        upk2(tb0, b0, b1);
+                        upk2(tb1, e0, e1);
+                        const float da[2] = {a0 + c0, a1 + c1}, db[2] = {b0 + e0, b1 + e1};
 #pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        const int j = 2 * u + jj;
-                        // (fragment 0, fragment 1) dots of blocks 2k+h and 2k+32+h, exact
-                        const uint64_t ta = dots2(v[0][2 * j], v[0][2 * j + 1]);
-                        const uint64_t tb = dots2(v[1][2 * j], v[1][2 * j + 1]);
-                        const uint64_t a0 = mmvq_term2(ta, d4ap, ka[j], ka[NP + j], zero2);
-                        const uint64_t a1 = mmvq_term2(tb, d4bp, kb[j], kb[NP + j], zero2);
-                        float sx, sy;
-                        upk2(add2(a0, a1), sx, sy);   // lanes i and i + 64 of both fragments
-                        leaf[jj] = __fadd_rn(sx, sy);  // the fragments' lanes (XOR 1)
-                        if constexpr (Tap) {
+                        for (int jj = 0; jj < 2; ++jj) {
+                            const int j = 2 * u + jj;
                             const int pl = p0 + pc0 + j - tap_base;
                             if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs) {
-                                float x0, y0, x1, y1;
-                                upk2(ta, x0, y0);
-                                upk2(tb, x1, y1);
                                 int32_t *dst = m == 0 ? p.tap.gate : p.tap.up;
                                 const size_t base = (static_cast<size_t>(pl) * I + row) * nb;
-                                dst[base + 2 * ks + h] = static_cast<int32_t>(x0) + static_cast<int32_t>(y0);
-                                dst[base + 2 * ks + 32 + h] = static_cast<int32_t>(x1) + static_cast<int32_t>(y1);
+                                dst[base + 2 * ks + h] = static_cast<int32_t>(da[jj]);
+                                dst[base + 2 * ks + 32 + h] = static_cast<int32_t>(db[jj]);
                             }
                         }
                     }
-                    const uint64_t l2 = pkf2(leaf[0], leaf[1]);
-                    if (h == 0) la[m][u] = l2;
-                    else node[m][u] = add2(la[m][u], l2);   // node k = L(2k) + L(2k+1)
                 }
             }
             region_release(&tm_empty[r], lane);
@@ -669,10 +681,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
 }
 
 // Gate/up B operand of every tile: for pair r < n of tile t (token
-// pair_token[p0 + r]), row 2r = its Q8_1 codes of fragment 0 (elements 0..7
-// and 16..23, the rest zero) and row 2r + 1 those of fragment 1, blocks in
-// stage order, and the constants (d8, d8) and (-4*s8, -4*s8) (duplicated so
-// they load as f32x2 operands); pairs n..15 are zero.
+// pair_token[p0 + r]), row r = its Q8_1 codes of fragment 0 (elements 0..7
+// and 16..23, the rest zero) and row 16 + r those of fragment 1, blocks in
+// stage order, and the constants d8[16] then -4*s8[16]; pairs n..15 are zero.
 // CTA (t, g): 32 threads (fragment rows) x blocks 8g..8g+7.
 __global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 *tiles, const int *num_tiles,
                                                                      const int32_t *pair_token, Q8Planar xq, int H,
@@ -706,11 +717,12 @@ __global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 
         for (int i = 0; i < 8; ++i) {
             const int pos = tc_gu_pos(b0 + i);
             uint8_t *dst = slot + static_cast<size_t>(pos) * 2 * kTcTile * 32;
-            *reinterpret_cast<uint4 *>(dst + tile_off(frow, 0)) = v[2 * i];
-            *reinterpret_cast<uint4 *>(dst + tile_off(frow, 1)) = v[2 * i + 1];
-            // (d8, d8) and (-4 s8, -4 s8): each fragment-row thread writes one copy
-            ss[pos * 4 * kTcTile + 2 * pr + frag] = c[i].x;
-            ss[pos * 4 * kTcTile + 2 * kTcTile + 2 * pr + frag] = -(4.0f * c[i].y);
+            *reinterpret_cast<uint4 *>(dst + tile_off(frag * kTcTile + pr, 0)) = v[2 * i];
+            *reinterpret_cast<uint4 *>(dst + tile_off(frag * kTcTile + pr, 1)) = v[2 * i + 1];
+            if (!frag) {
+                ss[pos * 2 * kTcTile + pr] = c[i].x;
+                ss[pos * 2 * kTcTile + kTcTile + pr] = -(4.0f * c[i].y);
+            }
         }
     }
 }
