@@ -106,9 +106,11 @@ struct RowsStage {
     static constexpr uint32_t raw_off = 1024;
     static constexpr uint32_t a_off = raw_off + raw_stages * raw_bytes;
     static constexpr uint32_t smem = a_off + a_stages * a_bytes;
-    static constexpr int reg_cols = Down ? 64 : 128;   // TMEM columns per region (down: 1 block, gate/up: 2)
+    // TMEM columns per region: down 4 blocks x 16 pairs (one stage), gate/up
+    // 2 blocks x 2 matrices x 32 fragment columns (half a stage)
+    static constexpr int reg_cols = Down ? 64 : 128;
     static constexpr int regions = 512 / reg_cols;
-    static constexpr int regions_per_stage = Down ? 4 : 2;
+    static constexpr int regions_per_stage = Down ? 1 : 2;
 };
 static_assert(RowsStage<false>::smem <= 227 * 1024 && RowsStage<true>::smem <= 227 * 1024, "fits one CTA");
 static_assert(RowsStage<false>::regions <= 8 && RowsStage<true>::regions <= 8, "barrier arrays hold 8");
@@ -396,34 +398,29 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
         const int s = sq.g % St::raw_stages;
         const uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
         if (!mbar_wait(&raw_full[s], (sq.g / St::raw_stages) & 1, p.error)) return false;
-#pragma unroll 1
-        for (int kb = 0; kb < kRowsKB; ++kb, ++sq.k) {
-            const int r = static_cast<int>(sq.k % R);
-            if (!mbar_wait(&tm_full[r], (sq.k / R) & 1, p.error)) return false;
-            tc_fence_after();
-            static_assert(CW == 4, "one x4 load per block");
-            uint32_t v[1][CW];
-            tmem_ld4(tq + r * St::reg_cols + pc0, v[0]);
-            tmem_wait_ld();
-            tie4(v[0]);
-            region_release(&tm_empty[r], lane);
-            const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales);
+        const int r = static_cast<int>(sq.k % R);
+        ++sq.k;
+        if (!mbar_wait(&tm_full[r], ((sq.k - 1) / R) & 1, p.error)) return false;
+        tc_fence_after();
+        static_assert(CW == 4, "one x4 load per block");
+        uint32_t v[kRowsKB][CW];
+#pragma unroll
+        for (int kb = 0; kb < kRowsKB; ++kb) tmem_ld4(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int kb = 0; kb < kRowsKB; ++kb) tie4(v[kb]);
+        region_release(&tm_empty[r], lane);
+        const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales);
+#pragma unroll
+        for (int kb = 0; kb < kRowsKB; ++kb) {
             const float d4 = h2f(sc[lrow * 8 + (ks & 1) * 4 + kb]);
             const uint64_t d4p = pkf2(d4, d4);
-            const float *d8p = reinterpret_cast<const float *>(st + St::bsc) + kb * 2 * NP + pc0;
-            const float *m8p = d8p + NP;
+            const uint64_t *d8p = reinterpret_cast<const uint64_t *>(
+                reinterpret_cast<const float *>(st + St::bsc) + kb * 2 * NP + pc0);
 #pragma unroll
-            for (int j4 = 0; j4 < CW / 4; ++j4) {
-                const float4 d8q = *reinterpret_cast<const float4 *>(d8p + 4 * j4);
-                const float4 m8q = *reinterpret_cast<const float4 *>(m8p + 4 * j4);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint64_t d8 = h ? pkf2(d8q.z, d8q.w) : pkf2(d8q.x, d8q.y);
-                    const uint64_t m8 = h ? pkf2(m8q.z, m8q.w) : pkf2(m8q.x, m8q.y);
-                    const int j = 4 * j4 + 2 * h;
-                    const uint64_t t = dots2(v[0][j], v[0][j + 1]);   // exact dots
-                    acc[j / 2] = fma2(d4p, fma2(t, d8, m8), acc[j / 2]);
-                }
+            for (int u = 0; u < CW / 2; ++u) {
+                const uint64_t t = dots2(v[kb][2 * u], v[kb][2 * u + 1]);   // exact dots
+                acc[u] = fma2(d4p, fma2(t, d8p[u], d8p[NP / 2 + u]), acc[u]);
             }
             if constexpr (Tap) {
                 if (e == p.tap.expert) {
@@ -432,7 +429,7 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
                         const int pl = p0 + pc0 + j - tap_base;
                         if (pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs)
                             p.tap.down[(static_cast<size_t>(pl) * H + row) * nb + ks * kRowsKB + kb] =
-                                static_cast<int32_t>(v[0][j]);
+                                static_cast<int32_t>(v[kb][j]);
                     }
                 }
             }
@@ -585,10 +582,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                         if (!mbar_wait(&tm_empty[r], (kseq / R) & 1, p.error)) { failed = true; break; }
                         tc_fence_after();
                         if (Down) {
-                            // block h of the stage into the region's columns [0, 16)
-                            const uint64_t ad = smem_desc(a_st + h * kRowsM * 32, 128, 256);
-                            const uint64_t bd = smem_desc(b_st + h * St::brows * 32, 128, 256);
-                            mma_i8(tmem + r * St::reg_cols, ad, bd, idesc, 0u);
+                            // the stage's 4 blocks into the region's columns [16 kb, 16 kb + 16)
+#pragma unroll
+                            for (int kb = 0; kb < kRowsKB; ++kb) {
+                                const uint64_t ad = smem_desc(a_st + kb * kRowsM * 32, 128, 256);
+                                const uint64_t bd = smem_desc(b_st + kb * St::brows * 32, 128, 256);
+                                mma_i8(tmem + r * St::reg_cols + kb * kTcTile, ad, bd, idesc, 0u);
+                            }
                         } else {
                             // stage slots h (block 2k+h) and 2+h (block 2k+32+h): columns [0,32) and [32,64)
                             // of gate, +64 for up
