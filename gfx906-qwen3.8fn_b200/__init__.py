@@ -397,6 +397,13 @@ def route_noalloc(logits, error=None, stream=None):
     limited to 1024 tokens.  Returns dict ids/weights/offsets/token/rank and
     the error tensor."""
     import torch
+    # the C entry point cannot see the tensor: check what it relies on
+    if logits.dim() != 2 or logits.shape[1] != EXPERTS:
+        raise ValueError("logits must be [tokens][512]")
+    if logits.dtype != torch.float32 or not logits.is_contiguous():
+        raise ValueError("logits must be contiguous float32")
+    if logits.device.type != "cuda" or logits.device.index != torch.cuda.current_device():
+        raise ValueError("logits must be on the current CUDA device (the static scratch is per device)")
     T = logits.shape[0]
     dev = logits.device
     r = dict(ids=torch.empty(T, TOP_K, dtype=torch.int32, device=dev), weights=torch.empty(T, TOP_K, device=dev),

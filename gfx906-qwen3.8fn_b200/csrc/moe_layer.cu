@@ -148,6 +148,7 @@ struct moe_weights_s {
     float *gate_vec = nullptr;
     float *router = nullptr;     // ffn_gate_inp as fp32 [512][H] (zero until uploaded)
     uint8_t *staging = nullptr;  // canonical bytes of one expert (3 matrices)
+    cudaEvent_t staged = nullptr;  // recorded after the last repack that read `staging`
     TcrMaps maps;                // tensor maps of the codes and scales (tensor-core path)
     int raw_rowmajor = 0;        // codes maps are 3-D [expert][row][bytes] (4-D [expert][block][row][16] refused)
     bool tc_ok = false;          // the tensor-core kernels can run on these weights
@@ -585,6 +586,7 @@ int moe_weights_destroy(moe_weights_t w) {
     cudaFree(w->gate_vec);
     cudaFree(w->router);
     cudaFree(w->staging);
+    if (w->staged) cudaEventDestroy(w->staged);
     delete w;
     return MOE_OK;
 }
@@ -602,18 +604,26 @@ int moe_weights_upload_expert(moe_weights_t w, int expert, const void *gate, con
     const void *src[3] = {gate, up, down};
     const size_t codes[3] = {L.gate_codes, L.up_codes, L.down_codes};
     const size_t scales[3] = {L.gate_scales, L.up_scales, L.down_scales};
+    // The staging buffer holds all three matrices; a previous upload (on any
+    // stream) must have finished reading it before these copies overwrite it.
+    if (!w->staged) MOE_CUDA(cudaEventCreateWithFlags(&w->staged, cudaEventDisableTiming));
+    else MOE_CUDA(cudaStreamWaitEvent(s, w->staged, 0));
+    size_t off = 0;
     for (int m = 0; m < 3; ++m) {
         const bool q41 = m == 2 && L.down_type == kDownQ4_1;
-        MOE_CUDA(cudaMemcpyAsync(w->staging, src[m], blocks * (q41 ? 20 : 18), cudaMemcpyHostToDevice, s));
+        const size_t bytes = blocks * (q41 ? 20 : 18);
+        MOE_CUDA(cudaMemcpyAsync(w->staging + off, src[m], bytes, cudaMemcpyHostToDevice, s));
         if (q41)
-            repack_q4_1_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
+            repack_q4_1_kernel<<<256, 256, 0, s>>>(w->staging + off, ex + codes[m],
+                                                   reinterpret_cast<uint16_t *>(ex + scales[m]),
                                                    reinterpret_cast<uint16_t *>(ex + L.down_mins), blocks, 0);
         else
-            repack_kernel<<<256, 256, 0, s>>>(w->staging, ex + codes[m], reinterpret_cast<uint16_t *>(ex + scales[m]),
-                                              blocks, 0);
+            repack_kernel<<<256, 256, 0, s>>>(w->staging + off, ex + codes[m],
+                                              reinterpret_cast<uint16_t *>(ex + scales[m]), blocks, 0);
         MOE_CUDA(cudaGetLastError());
-        MOE_CUDA(cudaStreamSynchronize(s));  // staging is reused by the next matrix
+        off += bytes;
     }
+    MOE_CUDA(cudaEventRecord(w->staged, s));
     return MOE_OK;
 }
 
@@ -629,6 +639,7 @@ int moe_weights_download_expert(moe_weights_t w, int expert, void *gate, void *u
     void *dst[3] = {gate, up, down};
     const size_t codes[3] = {L.gate_codes, L.up_codes, L.down_codes};
     const size_t scales[3] = {L.gate_scales, L.up_scales, L.down_scales};
+    if (w->staged) MOE_CUDA(cudaStreamWaitEvent(s, w->staged, 0));   // uploads done with the staging buffer
     for (int m = 0; m < 3; ++m) {
         const bool q41 = m == 2 && L.down_type == kDownQ4_1;
         if (q41)
@@ -1058,6 +1069,7 @@ int moe_expert_create_typed(const void *gate, const void *up, const void *down, 
     if (!st) {
         const auto t0 = std::chrono::steady_clock::now();
         st = moe_weights_upload_expert(w, 0, gate, up, down, e->stream);
+        if (!st) st = cuda_status(cudaStreamSynchronize(e->stream), "upload");   // the reference times the finished upload
         e->upload_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     }
     if (st) { moe_expert_destroy(e); return st; }

@@ -99,7 +99,12 @@ int moe_weights_destroy(moe_weights_t w);
  * layout on the device).  Replaces the reference's expert staging
  * (src/session.hip:957-1042): all experts stay resident.  expert == experts
  * uploads the shared expert.  gate/up: [I][H/32] blocks, down: [H][I/32]
- * blocks of the weights' down type (20-byte Q4_1 blocks for MOE_Q4_1). */
+ * blocks of the weights' down type (20-byte Q4_1 blocks for MOE_Q4_1).
+ * Asynchronous on `stream` like cudaMemcpyAsync: the copies and repacks are
+ * enqueued and the call returns without synchronising (pageable sources are
+ * read before it returns, pinned ones when the stream reaches the copy);
+ * consecutive uploads into one weights object are ordered by an event on its
+ * staging buffer, whatever streams they use. */
 int moe_weights_upload_expert(moe_weights_t w, int expert, const void *gate_q4_0,
                               const void *up_q4_0, const void *down_q4_0, void *stream);
 /* Shared expert scalar gate vector (fp32 [H]), the reference's
@@ -194,8 +199,10 @@ int moe_route(moe_layer_t h, const float *logits_dev, int tokens, float *probs_d
  * library until the process exits, which limits tokens to 1..1024 (larger
  * counts return MOE_INVALID_ARGUMENT).  The first call on a device resolves
  * that array's address on the current device (cudaGetSymbolAddress); make
- * that first call before any stream capture.  Every call shares the array:
- * calls whose GPU work overlaps (other streams, other threads) race. */
+ * that first call before any stream capture.  The address is kept per
+ * device ordinal for the life of the process, so resetting a device
+ * (cudaDeviceReset) after that first call is not supported.  Every call shares
+ * the array: calls whose GPU work overlaps (other streams, other threads) race. */
 int moe_route_noalloc(const float *logits_dev, int tokens, int32_t *ids_dev, float *weights_dev,
                       int32_t *offsets_dev, int32_t *token_dev, int32_t *rank_dev, int *error_dev,
                       void *stream);

@@ -1,8 +1,9 @@
 #!/usr/bin/env python3
 """Build the reference's own CPU path into oracle/_ref/ (test infrastructure).
 
-Compiles, directly from the reference sources where they lie (default
-/root/reference, or --ref DIR / $QWEN_REF_DIR), with g++ and no build system:
+Compiles, directly from the reference sources where they lie (--ref DIR, else
+$QWEN_REF_DIR, else a checkout named "reference" beside this repository), with
+g++ and no build system:
 
 * oracle/_ref/bin/{routes,quant,cpu_expert}_test -- the reference's own CPU tests,
   run by --run-tests as the pin of the reference build itself;
@@ -108,9 +109,17 @@ def build(ref, run_tests):
                 raise SystemExit(f"reference {name}_test failed")
 
 
+def default_ref_tree():
+    """$QWEN_REF_DIR, else the reference checkout beside this repository."""
+    env = os.environ.get("QWEN_REF_DIR")
+    if env:
+        return env
+    return os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--ref", default=os.environ.get("QWEN_REF_DIR", "/root/reference"))
+    ap.add_argument("--ref", default=default_ref_tree())
     ap.add_argument("--run-tests", action="store_true", help="also build and run the reference's CPU tests")
     args = ap.parse_args()
     if not os.path.isdir(args.ref):
