@@ -1693,6 +1693,12 @@ int moe_ep_read_flags(moe_ep_t ep, int *flags, int clear, void *stream) {
     if (clear) MOE_CUDA(cudaMemsetAsync(ep->rx.error, 0, sizeof(int), s));
     MOE_CUDA(cudaStreamSynchronize(s));
     *flags = a | b;
+    // A timed-out wait leaves the quantising CTAs' completion count as it was
+    // (late CTAs may have added to it); the stream is idle now, so rewind it.
+    if (*flags & MOE_FLAG_TIMEOUT) {
+        MOE_CUDA(cudaMemsetAsync(ep->quant_done, 0, sizeof(uint32_t), s));
+        MOE_CUDA(cudaStreamSynchronize(s));
+    }
     return MOE_OK;
 }
 

@@ -540,11 +540,15 @@ __global__ void __launch_bounds__(512) route_small_kernel(SmallRouteParams sp) {
         // every quantising CTA has stored its rows (and fenced them system-wide)
         if (e == 0) {
             const long long t0 = clock64();
+            bool all_in = true;
             while (ld_acquire_gpu_u32(sp.quant_done) != gridDim.x - 1) {
-                if (clock64() - t0 > (1ll << 31)) { atomicOr(p.error, kFlagTimeout); break; }
+                if (clock64() - t0 > (1ll << 31)) { atomicOr(p.error, kFlagTimeout); all_in = false; break; }
                 __nanosleep(32);
             }
-            *sp.quant_done = 0u;
+            // Rewind for the next call only after a complete count: after a
+            // timeout late CTAs may still add to it, so it is left for the host
+            // to clear once the stream is idle (moe_ep_read_flags).
+            if (all_in) *sp.quant_done = 0u;
         }
         __syncthreads();
         if (e < ep.world) ep_publish(ep, e, static_cast<uint32_t>(T), *ep.epoch);

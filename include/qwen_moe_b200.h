@@ -252,7 +252,9 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x_dev, const float
  * device from the shard weights' router matrix, as moe_forward_hidden). */
 int moe_ep_forward_hidden(moe_ep_t ep, moe_weights_t w, const float *x_dev, int tokens, float *out_dev,
                           int flags, void *stream);
-/* Sticky flags of the rank (MOE_FLAG_TIMEOUT included); synchronises `stream`. */
+/* Sticky flags of the rank (MOE_FLAG_TIMEOUT included); synchronises `stream`.
+ * After a reported timeout it also rewinds the rank's internal completion
+ * counters, so the next forward starts clean. */
 int moe_ep_read_flags(moe_ep_t ep, int *flags_host, int clear, void *stream);
 
 /* ---- kernels exposed for parity taps ------------------------------------- */
