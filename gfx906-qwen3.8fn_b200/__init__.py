@@ -22,7 +22,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libqwen_moe_b200.so")
 
 MOE_OK, MOE_INVALID_ARGUMENT, MOE_NOT_SUPPORTED, MOE_CUDA_ERROR = 0, 1, 2, 3
-MOE_NUMERIC_ERROR, MOE_NCCL_ERROR, MOE_TIMEOUT, MOE_OUT_OF_MEMORY = 4, 5, 6, 7
+MOE_NUMERIC_ERROR, MOE_TIMEOUT, MOE_OUT_OF_MEMORY = 4, 6, 7
 MOE_OUT_ACCUMULATE, MOE_OUT_OVERWRITE = 0, 1
 MOE_Q4_0, MOE_Q4_1 = 2, 3      # the reference's TensorType values (src/model.hpp:17-19)
 HIDDEN, INTER, EXPERTS, TOP_K = 2048, 512, 512, 10

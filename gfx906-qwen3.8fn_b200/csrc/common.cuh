@@ -173,28 +173,61 @@ __device__ __forceinline__ float warp_tree_sum(float v) {
 // takes the double-precision exponential rounded once to float and corrects
 // the inputs where the C library's expf rounds differently (0.008 % of the
 // floats in [-104, 89], listed at build time by csrc/expf_table.c), looked up
-// in a hash table of (x bits, expf bits) with linear probing; empty slots hold
-// key 0xffffffff (a NaN pattern, never a key).  The table is filled once per
-// device before any kernel of this library runs (expf_table_upload).
-constexpr int kExpfSlotsLog2 = 19;
+// in a hash table of (x bits, expf bits) pairs in buckets of four (one
+// 32-byte sector per bucket), probing bucket after bucket; empty entries
+// hold key 0xffffffff (a NaN pattern, never a key).  With 2^18 buckets for
+// ~170 k corrections a lookup reads one bucket in all but ~0.5 % of cases.
+// The table is filled once per device before any kernel of this library
+// runs (expf_table_upload).
+constexpr int kExpfBucketsLog2 = 18;
+constexpr int kExpfBucket = 4;                         // entries per bucket
 constexpr uint32_t kExpfEmpty = 0xffffffffu;
-constexpr int kExpfMaxProbe = 64;
-static __device__ uint2 g_expf_fix[1u << kExpfSlotsLog2];
+constexpr int kExpfMaxProbe = 64;                      // buckets
+static __device__ uint4 g_expf_fix[(1u << kExpfBucketsLog2) * kExpfBucket / 2];   // 2 entries per uint4
 
-__host__ __device__ __forceinline__ uint32_t expf_fix_slot(uint32_t key) {
-    return (key * 2654435761u) >> (32 - kExpfSlotsLog2);
+__host__ __device__ __forceinline__ uint32_t expf_fix_bucket(uint32_t key) {
+    return (key * 2654435761u) >> (32 - kExpfBucketsLog2);
+}
+// Look key up in bucket b (entries e0 = {k0, v0, k1, v1}, e1 = {k2, v2, k3, v3}):
+// 1 found (value in *v), 0 absent (the bucket has an empty entry), -1 the
+// bucket is full without it (continue with the next bucket).
+__device__ __forceinline__ int expf_fix_match(uint4 e0, uint4 e1, uint32_t key, uint32_t *v) {
+    if (e0.x == key) { *v = e0.y; return 1; }
+    if (e0.z == key) { *v = e0.w; return 1; }
+    if (e1.x == key) { *v = e1.y; return 1; }
+    if (e1.z == key) { *v = e1.w; return 1; }
+    return (e0.x == kExpfEmpty || e0.z == kExpfEmpty || e1.x == kExpfEmpty || e1.z == kExpfEmpty) ? 0 : -1;
+}
+// N exponentials at once: the N first-bucket loads are in flight together.
+template <int N>
+__device__ __forceinline__ void expf_ref_n(const float (&x)[N], float (&y)[N]) {
+    uint32_t k[N], b[N];
+    uint4 e0[N], e1[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        k[j] = __float_as_uint(x[j]);
+        b[j] = expf_fix_bucket(k[j]);
+        e0[j] = g_expf_fix[2 * b[j]];
+        e1[j] = g_expf_fix[2 * b[j] + 1];
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) y[j] = __double2float_rn(exp(static_cast<double>(x[j])));
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        uint32_t v = 0;
+        int r = expf_fix_match(e0[j], e1[j], k[j], &v);
+        for (int i = 1; r < 0 && i < kExpfMaxProbe; ++i) {   // rare: the first bucket is full
+            const uint32_t bb = (b[j] + i) & ((1u << kExpfBucketsLog2) - 1);
+            r = expf_fix_match(g_expf_fix[2 * bb], g_expf_fix[2 * bb + 1], k[j], &v);
+        }
+        if (r > 0) y[j] = __uint_as_float(v);
+    }
 }
 __device__ __forceinline__ float expf_ref(float x) {
-    const float y = __double2float_rn(exp(static_cast<double>(x)));
-    const uint32_t k = __float_as_uint(x);
-    uint32_t h = expf_fix_slot(k);
-    for (int i = 0; i < kExpfMaxProbe; ++i) {
-        const uint2 e = g_expf_fix[h];
-        if (e.x == k) return __uint_as_float(e.y);
-        if (e.x == kExpfEmpty) break;
-        h = (h + 1) & ((1u << kExpfSlotsLog2) - 1);
-    }
-    return y;
+    const float xs[1] = {x};
+    float ys[1];
+    expf_ref_n<1>(xs, ys);
+    return ys[0];
 }
 
 __device__ __forceinline__ void report(int flags, int *error) {

@@ -108,24 +108,32 @@ int expf_table_upload() {
     if (device < 0 || device >= kExpfDevices) return fail(MOE_NOT_SUPPORTED, "device ordinal above 63");
     std::lock_guard<std::mutex> lock(g_expf_mutex);
     if (g_expf_loaded[device]) return MOE_OK;
-    static std::vector<uint2> table;
+    static std::vector<uint4> table;   // kExpfBucket / 2 uint4 per bucket
     if (table.empty()) {
         const size_t n = static_cast<size_t>(qmoe_expf_table_end - qmoe_expf_table_begin) / 8;
-        std::vector<uint2> t(size_t(1) << kExpfSlotsLog2, make_uint2(kExpfEmpty, 0u));
+        constexpr uint32_t nbk = 1u << kExpfBucketsLog2;
+        std::vector<uint32_t> t(static_cast<size_t>(nbk) * kExpfBucket * 2, kExpfEmpty);   // (key, value) entries
         for (size_t i = 0; i < n; ++i) {
             uint32_t kv[2];
             std::memcpy(kv, qmoe_expf_table_begin + 8 * i, 8);
-            uint32_t h = expf_fix_slot(kv[0]);
-            int probe = 0;
-            while (t[h].x != kExpfEmpty) {
-                h = (h + 1) & ((1u << kExpfSlotsLog2) - 1);
-                if (++probe >= kExpfMaxProbe) return fail(MOE_CUDA_ERROR, "expf correction table: probe chain too long");
-            }
-            t[h] = make_uint2(kv[0], kv[1]);
+            uint32_t b = expf_fix_bucket(kv[0]);
+            bool placed = false;
+            for (int probe = 0; probe < kExpfMaxProbe && !placed; ++probe, b = (b + 1) & (nbk - 1))
+                for (int j = 0; j < kExpfBucket && !placed; ++j) {
+                    uint32_t *entry = &t[(static_cast<size_t>(b) * kExpfBucket + j) * 2];
+                    if (entry[0] == kExpfEmpty) {
+                        entry[0] = kv[0];
+                        entry[1] = kv[1];
+                        placed = true;
+                    }
+                }
+            if (!placed) return fail(MOE_CUDA_ERROR, "expf correction table: probe chain too long");
         }
-        table.swap(t);
+        std::vector<uint4> packed(t.size() / 4);
+        std::memcpy(packed.data(), t.data(), t.size() * sizeof(uint32_t));
+        table.swap(packed);
     }
-    MOE_CUDA(cudaMemcpyToSymbol(g_expf_fix, table.data(), table.size() * sizeof(uint2)));
+    MOE_CUDA(cudaMemcpyToSymbol(g_expf_fix, table.data(), table.size() * sizeof(uint4)));
     g_expf_loaded[device] = true;
     return MOE_OK;
 }
@@ -532,7 +540,6 @@ const char *moe_status_string(int status) {
     case MOE_NOT_SUPPORTED: return "not_supported";
     case MOE_CUDA_ERROR: return "cuda_error";
     case MOE_NUMERIC_ERROR: return "numeric_error";
-    case MOE_NCCL_ERROR: return "nccl_error";
     case MOE_TIMEOUT: return "timeout";
     case MOE_OUT_OF_MEMORY: return "out_of_memory";
     default: return "unknown";

@@ -64,10 +64,10 @@ constexpr int kTcTile = 16;   // pairs per tensor-core tile (gate/up MMA N = 2 x
 
 // Arranged operand slots of one tile (filled by the gather kernel for gate/up
 // and by the gate/up epilogue for down), K = H or I:
-//   gate/up codes: per block, 2 * kTcTile rows of 32 bytes (pair p: row p =
-//     fragment 0 elements, row kTcTile + p = fragment 1 elements, the other
-//     fragment's bytes zero) in the K-major core-matrix layout, blocks in the
-//     kernel's stage order (tc_gu_pos);
+//   gate/up codes: per block, 2 * kTcTile rows of 32 bytes (one per pair and
+//     16-element fragment, the other fragment's bytes zero; row order
+//     tc_gu_brow in tcr_kernels.cuh) in the K-major core-matrix layout, blocks
+//     in the kernel's stage order (tc_gu_pos);
 //   down codes: per block, kTcTile rows of 32 bytes, blocks in order;
 //   gate/up constants: per block, d8[kTcTile] then m4[kTcTile] fp32 with
 //     m4 = -4*s8 (per fragment);

@@ -9,32 +9,34 @@
 // A u8 x s8 product is the reference's uncentred dot sum(q * x)
 // (src/quant.cpp:48-55) with |dot| < 2^16.
 //
-// Exact conversion: each TMEM column range is written by one MMA (no
-// accumulation), so it holds the int32 dot; adding it to the bit pattern of
-// 1.5 * 2^23 and subtracting 1.5 * 2^23 in fp32 gives the dot as an exact
-// float (|dot| < 2^22) -- an integer add and half an f32x2 subtraction per
-// value instead of the quarter-rate int-to-float conversion.
+// Exact conversion: before the integer MMAs of a TMEM region, one bf16 MMA
+// (kind::f16, A = 1 at k = 0, B = 1.5 * 2^23 at k = 0, f32 accumulator)
+// writes the bit pattern of 1.5 * 2^23 into every column of the region; the
+// integer MMAs then accumulate (s32) onto it, so each column holds
+// 0x4B400000 + dot, i.e. the float 1.5 * 2^23 + dot exactly (|dot| < 2^22),
+// and one f32x2 subtraction per two values gives the dots as exact floats --
+// no integer instruction and no quarter-rate conversion on the CUDA cores.
 //
 // Gate/up (the values the middle Q8_1 is quantised from) follow the
-// reference's MMVQ order bit for bit (common.cuh: mmvq_term2 / mmvq_leaf), so
-// the middle equals the reference CPU expert's: B holds two rows per pair,
-// one per 16-element fragment (the other fragment's bytes zero): rows 0..15
-// fragment 0 of pairs 0..15, rows 16..31 fragment 1, so the MMA (N = 32) gives
-// both fragment dots with adjacent columns = adjacent pairs, and the fp32
-// arithmetic runs as f32x2 over pairs; blocks b and b + 32 land in one TMEM
-// region and form the tree's leaves; a pipeline stage carries blocks 2k,
-// 2k+1, 2k+32, 2k+33 (one level-2 node of the tree), and the 16 nodes of an
-// item are summed as a binary tree with a four-slot stack in registers.  Each
-// epilogue thread owns one weight row (its TMEM lane) of gate and of up for
-// 4 pairs; the item end runs SiLU(gate) * up and the Q8_1 of each 32-row
-// middle block (one warp = one block per pair: lane = element, the
-// reference's butterfly order) and writes the down pass's operand.
+// reference's MMVQ order bit for bit (common.cuh: mmvq_term2), so the middle
+// equals the reference CPU expert's: B holds two rows per pair, one per
+// 16-element fragment (the other fragment's bytes zero), chunk-major
+// (tc_gu_brow: the 8 rows of pairs 4c..4c+3 adjacent), so the MMA (N = 32)
+// gives every epilogue warp its 4 pairs x 2 fragments as 8 adjacent columns
+// and the fp32 arithmetic runs as f32x2 over pairs; blocks b and b + 32 land
+// in one TMEM region and form the tree's leaves; a pipeline stage carries
+// blocks 2k, 2k+1, 2k+32, 2k+33 (one level-2 node of the tree), and the 16
+// nodes of an item are summed as a binary tree with a four-slot stack in
+// registers.  Each epilogue thread owns one weight row (its TMEM lane) of gate
+// and of up for 4 pairs; the item end runs SiLU(gate) * up and the Q8_1 of
+// each 32-row middle block (one warp = one block per pair: lane = element,
+// the reference's butterfly order) and writes the down pass's operand.
 //
 // Down (its output is never requantised) uses whole-block dots and
 // acc += d4 * (dot * d8 - 8 * s8) per block in fp32, then a router-weighted
 // red.add into the residual (lane = output row: coalesced).
 //
-// Warp roles (12 warps):
+// Warp roles (20 warps):
 //   warp 0      TMEM allocation; lane 0 issues the TMA copies: raw weight
 //               codes and scales through tensor maps, the tile's pre-arranged
 //               activation operand as 1-D bulk copies;
@@ -62,8 +64,12 @@ constexpr int kRowsWarps = 2 + kRowsUnpackWarps + kRowsEpiWarps;
 constexpr int kRowsThreads = 32 * kRowsWarps;
 constexpr int kRowsMinGroup = 1;       // batches above decode size: every group on this path
 constexpr int kRowsHidden = 2048;      // the gate/up stage order pairs blocks b and b + 32 of 64
-constexpr int kMagicBits = 0x4b400000;  // bit pattern of 1.5 * 2^23
-constexpr float kMagicF = 12582912.0f; // 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f; // 1.5 * 2^23 (bits 0x4B400000)
+constexpr uint32_t kBf16One = 0x3f80u, kBf16Magic = 0x4b40u;   // bf16 1.0 and 1.5 * 2^23
+
+// B row of (pair p, fragment f) in a gate/up block: chunk-major, the 8 rows
+// of pairs 4c..4c+3 adjacent (fragment 0 then 1).
+__host__ __device__ constexpr int tc_gu_brow(int p, int f) { return (p >> 2) * 8 + f * 4 + (p & 3); }
 
 // Tensor maps over one weights object (all experts), built on the host.
 struct alignas(64) TcrMaps {
@@ -88,32 +94,56 @@ struct TcrParams {
     TapSink tap;
 };
 
+constexpr int kRowsBarSlots = 16;   // entries per barrier array
+
+// Shared-memory rings of one CTA.  Each feeds its own consumers, so every
+// ring is released as soon as they are done with it:
+//   codes  the slab's raw Q4_0 codes of one stage (4 blocks x 128 rows x
+//          16 B of one matrix), read by the unpack warps;
+//   side   the tile's arranged activation operand (B, read by the MMAs) and
+//          per-pair constants (read by the epilogue) of one stage;
+//   scale  the weight rows' half scales of a stage group (gate/up: blocks
+//          8j..8j+7 and 32+8j..32+8j+7 of one matrix = 4 stages; down: blocks
+//          8j..8j+7 = 2 stages), read by the epilogue;
+//   A      the unpacked A operand of one stage (u8, K-major core matrices).
 template <bool Down>
 struct RowsStage {
-    static constexpr int M = Down ? 1 : 2;                                    // matrices per item
-    static constexpr int wins = Down ? 1 : 2;                                 // 8-block scale windows per stage
+    static constexpr int M = Down ? 1 : 2;                                    // matrices per item (one per stage)
+    static constexpr int wins = Down ? 1 : 2;                                 // 8-block scale windows per group
+    static constexpr int spw = Down ? 2 : 4;                                  // stages per scale group
     static constexpr int brows = Down ? kTcTile : 2 * kTcTile;                // B rows per block
     static constexpr int bpc = Down ? 4 : 2;                                  // blocks per code copy
-    static constexpr uint32_t codes = 0;                                      // M x 4 blocks x 128 rows x 16 B
-    static constexpr uint32_t scales = codes + M * kRowsKB * kRowsM * 16;     // M x wins x [128][8] half
-    static constexpr uint32_t b = scales + M * wins * kRowsM * 16;            // [4][brows][32]
-    static constexpr uint32_t bsc = b + kRowsKB * brows * 32;                 // [4][cwords][kTcTile] fp32
     static constexpr int cwords = 2;                                          // constants per pair and block
-    static constexpr uint32_t raw_bytes = (bsc + kRowsKB * cwords * kTcTile * 4 + 1023) / 1024 * 1024;
-    static constexpr uint32_t a_bytes = M * kRowsKB * kRowsM * 32;            // unpacked A tiles
-    static constexpr int raw_stages = Down ? 8 : 4;
-    static constexpr int a_stages = Down ? 4 : 3;
-    static constexpr uint32_t raw_off = 1024;
-    static constexpr uint32_t a_off = raw_off + raw_stages * raw_bytes;
-    static constexpr uint32_t smem = a_off + a_stages * a_bytes;
-    // TMEM columns per region: down 4 blocks x 16 pairs (one stage), gate/up
-    // 2 blocks x 2 matrices x 32 fragment columns (half a stage)
-    static constexpr int reg_cols = Down ? 64 : 128;
+    static constexpr uint32_t codes_bytes = kRowsKB * kRowsM * 16;
+    static constexpr uint32_t b = 0;                                          // side: [4][brows][32]
+    static constexpr uint32_t bsc = b + kRowsKB * brows * 32;                 // side: [4][cwords][kTcTile] fp32
+    static constexpr uint32_t side_bytes = bsc + kRowsKB * cwords * kTcTile * 4;
+    static constexpr uint32_t sc_bytes = wins * kRowsM * 16;                  // [wins][128][8] half
+    static constexpr uint32_t a_bytes = kRowsKB * kRowsM * 32;                // unpacked A tiles
+    static constexpr int code_stages = 8;                // powers of two: cheap slot and phase arithmetic
+    static constexpr int side_stages = 8;
+    static constexpr int sc_stages = 4;
+    static constexpr int a_stages = 4;
+    static constexpr uint32_t codes_off = 2048;
+    static constexpr uint32_t side_off = codes_off + code_stages * codes_bytes;
+    static constexpr uint32_t sc_off = (side_off + side_stages * side_bytes + 1023) / 1024 * 1024;
+    static constexpr uint32_t a_off = sc_off + sc_stages * sc_bytes;
+    static constexpr uint32_t magic_off = a_off + a_stages * a_bytes;        // bf16 A [128][16], B [128][16]
+    static constexpr uint32_t smem = magic_off + 2 * kRowsM * 32;
+    // TMEM columns per region = one stage: 4 blocks x brows (down 16 pairs,
+    // gate/up 16 pairs x 2 fragments)
+    static constexpr int reg_cols = kRowsKB * brows;
     static constexpr int regions = 512 / reg_cols;
-    static constexpr int regions_per_stage = Down ? 1 : 2;
+    static_assert(side_bytes % 128 == 0 && sc_bytes % 1024 == 0 && codes_bytes % 1024 == 0, "ring alignment");
+    static_assert((side_off % 1024) == 0 && (sc_off % 1024) == 0 && (a_off % 1024) == 0, "ring alignment");
 };
+// Polls of the TMA producer without progress (each followed by a ~64 ns
+// sleep) before it declares the consumers stopped: well above any real stall.
+constexpr uint32_t kProducerIdleLimit = 1u << 25;
 static_assert(RowsStage<false>::smem <= 227 * 1024 && RowsStage<true>::smem <= 227 * 1024, "fits one CTA");
-static_assert(RowsStage<false>::regions <= 8 && RowsStage<true>::regions <= 8, "barrier arrays hold 8");
+static_assert(RowsStage<true>::code_stages <= kRowsBarSlots && RowsStage<true>::side_stages <= kRowsBarSlots &&
+                  RowsStage<true>::regions <= kRowsBarSlots && RowsStage<false>::regions <= kRowsBarSlots,
+              "barrier arrays");
 
 // ---- PTX -------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
@@ -151,11 +181,12 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t *r) {
 __device__ __forceinline__ void tie4(uint32_t *r) {
     asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]) : : "memory");
 }
-// Two int32 dots as an exact f32x2 (|dot| < 2^22).
-__device__ __forceinline__ uint64_t dots2(uint32_t a, uint32_t b) {
-    return add2(pk2(a + static_cast<uint32_t>(kMagicBits), b + static_cast<uint32_t>(kMagicBits)),
-                pkf2(-kMagicF, -kMagicF));
+// Two TMEM words 0x4B400000 + dot as the exact f32x2 of the dots (|dot| < 2^22).
+__device__ __forceinline__ uint64_t from_magic2(uint32_t a, uint32_t b) {
+    return add2(pk2(a, b), pkf2(-kMagicF, -kMagicF));
 }
+__device__ __forceinline__ float lo_half(uint32_t w) { return h2f(static_cast<uint16_t>(w & 0xffffu)); }
+__device__ __forceinline__ float hi_half(uint32_t w) { return h2f(static_cast<uint16_t>(w >> 16)); }
 // Release a TMEM region read by this warp (its loads have completed).
 __device__ __forceinline__ void region_release(uint64_t *empty_bar, int lane) {
     tc_fence_before();
@@ -178,12 +209,82 @@ __host__ __device__ constexpr uint32_t rows_idesc(int m, int n) {
     return (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
 }
+// Instruction descriptor: kind::f16, A and B bf16, D f32, both K-major.
+__host__ __device__ constexpr uint32_t magic_idesc(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+// D[tmem] = A[smem] . B[smem]^T, kind::f16 (bf16 operands, f32 accumulator), issued by one thread.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(0u)
+        : "memory");
+}
 
 // Sequence counters of the epilogue across items.
 struct RowsSeq {
     int g = 0;          // pipeline stage sequence (raw and A rings advance together)
     uint32_t k = 0;     // TMEM region sequence
 };
+
+// Barriers of one CTA (shared memory), one full/empty pair per ring slot, as
+// fixed offsets from one base (one register, not one per array).
+struct RowsBars {
+    uint64_t *base;
+    __device__ uint64_t *code_full(int i) const { return base + 0 * kRowsBarSlots + i; }
+    __device__ uint64_t *code_empty(int i) const { return base + 1 * kRowsBarSlots + i; }
+    __device__ uint64_t *side_full(int i) const { return base + 2 * kRowsBarSlots + i; }
+    __device__ uint64_t *side_empty(int i) const { return base + 3 * kRowsBarSlots + i; }
+    __device__ uint64_t *sc_full(int i) const { return base + 4 * kRowsBarSlots + i; }
+    __device__ uint64_t *sc_empty(int i) const { return base + 5 * kRowsBarSlots + i; }
+    __device__ uint64_t *a_full(int i) const { return base + 6 * kRowsBarSlots + i; }
+    __device__ uint64_t *a_empty(int i) const { return base + 7 * kRowsBarSlots + i; }
+    __device__ uint64_t *tm_full(int i) const { return base + 8 * kRowsBarSlots + i; }
+    __device__ uint64_t *tm_empty(int i) const { return base + 9 * kRowsBarSlots + i; }
+    __device__ uint64_t *fin() const { return base + 10 * kRowsBarSlots; }
+};
+
+// Unpack stage g's raw Q4_0 codes (shared) into unsigned bytes in the K-major
+// core-matrix layout of its A slot (shared), split over the unpack warps'
+// threads (ut = 0 .. 32 * kRowsUnpackWarps - 1); each warp then arrives on
+// the A slot's full barrier and the code slot's empty barrier.  False when a
+// wait gave up.
+template <bool Down>
+__device__ __forceinline__ bool rows_unpack(uint8_t *smem, const RowsBars &b, int g, int ut, bool rowmajor, int lane,
+                                            int *error) {
+    using St = RowsStage<Down>;
+    constexpr int kThreads = 32 * kRowsUnpackWarps;
+    const int sr = g % St::code_stages, sa = g % St::a_stages;
+    if (!mbar_wait(b.code_full(sr), (g / St::code_stages) & 1, error)) return false;
+    if (g >= St::a_stages && !mbar_wait(b.a_empty(sa), ((g / St::a_stages) & 1) ^ 1, error)) return false;
+    const uint8_t *raw = smem + St::codes_off + sr * St::codes_bytes;
+    uint8_t *a = smem + St::a_off + sa * St::a_bytes;
+    constexpr int kUnits = kRowsKB * kRowsM;
+    static_assert(kUnits % kThreads == 0, "whole unpack rounds");
+#pragma unroll
+    for (int i = 0; i < kUnits / kThreads; ++i) {
+        const int u = ut + i * kThreads;
+        const int kb = u / kRowsM, row = u % kRowsM;
+        const int src = rowmajor ? ((kb / St::bpc) * kRowsM + row) * St::bpc + kb % St::bpc : kb * kRowsM + row;
+        const uint4 w = reinterpret_cast<const uint4 *>(raw)[src];
+        const uint4 lo = make_uint4(w.x & 0x0f0f0f0fu, w.y & 0x0f0f0f0fu, w.z & 0x0f0f0f0fu, w.w & 0x0f0f0f0fu);
+        const uint4 hi = make_uint4((w.x >> 4) & 0x0f0f0f0fu, (w.y >> 4) & 0x0f0f0f0fu, (w.z >> 4) & 0x0f0f0f0fu,
+                                    (w.w >> 4) & 0x0f0f0f0fu);
+        uint8_t *dst = a + kb * kRowsM * 32;
+        *reinterpret_cast<uint4 *>(dst + tile_off(row, 0)) = lo;
+        *reinterpret_cast<uint4 *>(dst + tile_off(row, 1)) = hi;
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(b.a_full(sa));
+        mbar_arrive(b.code_empty(sr));
+    }
+    return true;
+}
 
 // 4 packed code bytes of lanes 4w..4w+3 in lane 4w (other lanes: don't care).
 __device__ __forceinline__ uint32_t pack_lane_bytes(int8_t code) {
@@ -193,34 +294,23 @@ __device__ __forceinline__ uint32_t pack_lane_bytes(int8_t code) {
     return v;
 }
 
-// SiLU(gate) * up of one middle value (the reference's sanitisation,
-// src/hip/session_ops.hip:250-262) and the Q8_1 of the 32-value block the
-// warp holds (lane = element).
+// Q8_1 lane of one middle value and the sticky flags raised for it.
 struct MidQ {
     Q8Lane q;
     int flags;
 };
-__device__ __forceinline__ MidQ silu_q8(float g, float u) {
-    int f = 0;
-    const float gv = operand(g, f), uv = operand(u, f);
-    const float act = arithmetic(__fdiv_rn(gv, __fadd_rn(1.0f, expf_ref(-gv))), f);
-    const float val = arithmetic(__fmul_rn(act, uv), f);
-    MidQ r;
-    r.q = quantize_lane(f ? 0.0f : val);
-    r.flags = f | r.q.flags;
-    return r;
-}
 
 // ---- gate/up epilogue of one item (exact MMVQ order) -----------------------
 // Pairs are handled two at a time (unit u = pairs pc0 + 2u, pc0 + 2u + 1) as
 // packed f32x2 values; units without a real pair are skipped.
 template <bool Tap>
-__device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *smem, uint64_t *raw_full,
-                                                 uint64_t *raw_empty, uint64_t *tm_full, uint64_t *tm_empty,
-                                                 uint32_t tq, RowsSeq &sq, int item, int4 td, int lane, int quarter,
-                                                 int chunk) {
+__device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *smem, const RowsBars &bars,
+                                                 uint32_t tq, RowsSeq &sq, int item, int4 td,
+                                                 int lane, int quarter, int chunk) {
     using St = RowsStage<false>;
     constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile, U = CW / 2;
+    constexpr int kNodes = kRowsHidden / 32 / kRowsKB;        // 16 stages (level-2 nodes) per matrix
+    static_assert(CW == 4 && U == 2, "one x8 load per block: 4 pairs x 2 fragments");
     const int I = p.inter;
     const int nb = kRowsHidden / 32, slabs = I / kRowsM;
     const int slab = item % slabs, tile = item / slabs;
@@ -230,110 +320,108 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
     const int lrow = quarter * 32 + lane;                     // row within the slab
     const int row = slab * kRowsM + lrow;                     // middle row of this lane
     const uint64_t zero2 = 0ull;
-    // binary-tree stack over the 16 level-2 nodes, per matrix and unit (s3 ends as the total)
-    uint64_t s0[2][U], s1[2][U], s2[2][U], s3[2][U];
+    // binary-tree stack over the 16 level-2 nodes of the current matrix, per unit (s3 ends as the
+    // total); the gate totals wait in gt while the up pass runs
+    uint64_t s0[U], s1[U], s2[U], s3[U], gt[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) s3[u] = gt[u] = 0ull;   // units without a real pair stay 0
     int tap_base = 0;
     if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
 
-    for (int ks = 0; ks < nb / kRowsKB; ++ks, ++sq.g) {
-        const int s = sq.g % St::raw_stages;
-        const uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
-        if (!mbar_wait(&raw_full[s], (sq.g / St::raw_stages) & 1, p.error)) return false;
-        uint64_t la[2][U], node[2][U];
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h, ++sq.k) {   // region h: blocks 2k+h (columns +0) and 2k+32+h (+32)
-            const int r = static_cast<int>(sq.k % R);
-            if (!mbar_wait(&tm_full[r], (sq.k / R) & 1, p.error)) return false;
-            tc_fence_after();
-            const uint32_t tr = tq + r * St::reg_cols + pc0;
-            // pair constants d8 and -4 s8 of block 2k+h (slot h) and 2k+32+h (slot 2+h)
+    for (int ks = 0; ks < 2 * kNodes; ++ks, ++sq.g, ++sq.k) {
+        const int m = ks / kNodes, kk = ks % kNodes;          // matrix (gate, up), node within it
+        const int s = sq.g % St::side_stages;
+        const uint8_t *st = smem + St::side_off + s * St::side_bytes;
+        if (!mbar_wait(bars.side_full(s), (sq.g / St::side_stages) & 1, p.error)) return false;
+        const int q = sq.g / St::spw, qs = q % St::sc_stages;   // scale group (its windows stay for spw stages)
+        if (kk % St::spw == 0 && !mbar_wait(bars.sc_full(qs), (q / St::sc_stages) & 1, p.error)) return false;
+        // d4 of this row: window 0 holds blocks 2kk, 2kk+1 at columns c0, c0+1, window 1 blocks 2kk+32, 2kk+33
+        const uint8_t *d4row = smem + St::sc_off + qs * St::sc_bytes + lrow * 16 + ((2 * kk) % 8) * 2;
+        const int r = static_cast<int>(sq.k % R);
+        if (!mbar_wait(bars.tm_full(r), (sq.k / R) & 1, p.error)) return false;
+        tc_fence_after();
+        const uint32_t tr = tq + r * St::reg_cols + chunk * 8;
+        uint64_t node[U], la[U];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {   // leaf h: block 2kk+h (slot h) and 2kk+32+h (slot 2+h)
+            // columns: fragment 0 of the 4 pairs, then fragment 1
+            uint32_t va[8], vb[8];
+            tmem_ld8(tr + h * 32, va);
+            tmem_ld8(tr + (2 + h) * 32, vb);
+            tmem_wait_ld();
+            tie8(va);
+            tie8(vb);
+            if (h == 1) region_release(bars.tm_empty(r), lane);
+            // pair constants d8 and m4 = -4 s8 of block 2kk+h (slot h) and 2kk+32+h (slot 2+h), as pair units
             const uint64_t *ka = reinterpret_cast<const uint64_t *>(
                 reinterpret_cast<const float *>(st + St::bsc) + h * 2 * NP + pc0);
             const uint64_t *kb = reinterpret_cast<const uint64_t *>(
                 reinterpret_cast<const float *>(st + St::bsc) + (2 + h) * 2 * NP + pc0);
+            const float d4a = h2f(*reinterpret_cast<const uint16_t *>(d4row + 2 * h));
+            const float d4b = h2f(*reinterpret_cast<const uint16_t *>(d4row + kRowsM * 16 + 2 * h));
+            const uint64_t d4ap = pkf2(d4a, d4a), d4bp = pkf2(d4b, d4b);
 #pragma unroll
-            for (int m = 0; m < 2; ++m) {
-                // [block a / b][fragment] x this warp's CW pairs
-                static_assert(CW == 4, "one x4 load per matrix, block and fragment");
-                uint32_t v[2][2][CW];
+            for (int u = 0; u < U; ++u) {
+                if (u >= units) break;
+                // exact fragment dots of the unit's two pairs: block a (2kk+h) and b (2kk+32+h)
+                const uint64_t ta0 = from_magic2(va[2 * u], va[2 * u + 1]);
+                const uint64_t ta1 = from_magic2(va[4 + 2 * u], va[5 + 2 * u]);
+                const uint64_t tb0 = from_magic2(vb[2 * u], vb[2 * u + 1]);
+                const uint64_t tb1 = from_magic2(vb[4 + 2 * u], vb[5 + 2 * u]);
+                const uint64_t d8a = ka[u], m4a = ka[NP / 2 + u], d8b = kb[u], m4b = kb[NP / 2 + u];
+                // MMVQ lanes 2b+f (terms of block a) and 2b+f+64 (block b), summed, then the fragments
+                const uint64_t leaf = add2(add2(mmvq_term2(ta0, d4ap, d8a, m4a, zero2),
+                                                mmvq_term2(tb0, d4bp, d8b, m4b, zero2)),
+                                           add2(mmvq_term2(ta1, d4ap, d8a, m4a, zero2),
+                                                mmvq_term2(tb1, d4bp, d8b, m4b, zero2)));
+                if (h == 0) la[u] = leaf;
+                else node[u] = add2(la[u], leaf);   // node kk = L(2kk) + L(2kk+1)
+                if constexpr (Tap) {
+                    float a0, a1, c0, c1, b0, b1, e0, e1;
+                    upk2(ta0, a0, a1);
+                    upk2(ta1, c0, c1);
+                    upk2(tb0, b0, b1);
+                    upk2(tb1, e0, e1);
+                    const float da[2] = {a0 + c0, a1 + c1}, db[2] = {b0 + e0, b1 + e1};
 #pragma unroll
-                for (int q = 0; q < 2; ++q)
-#pragma unroll
-                    for (int f = 0; f < 2; ++f) tmem_ld4(tr + m * 64 + q * 32 + f * NP, v[q][f]);
-                tmem_wait_ld();
-#pragma unroll
-                for (int q = 0; q < 2; ++q)
-#pragma unroll
-                    for (int f = 0; f < 2; ++f) tie4(v[q][f]);
-                // scales: window 0 holds blocks 2k, 2k+1, window 1 blocks 2k+32, 2k+33
-                const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales + m * 2 * kRowsM * 16);
-                const int col = (2 * ks) % 8 + h;
-                const float d4a = h2f(sc[lrow * 8 + col]), d4b = h2f(sc[kRowsM * 8 + lrow * 8 + col]);
-                const uint64_t d4ap = pkf2(d4a, d4a), d4bp = pkf2(d4b, d4b);
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    if (u >= units) break;
-                    const uint64_t d8a = ka[u], m4a = ka[NP / 2 + u], d8b = kb[u], m4b = kb[NP / 2 + u];
-                    // exact fragment dots of the unit's two pairs: block a (2k+h) and b (2k+32+h)
-                    const uint64_t ta0 = dots2(v[0][0][2 * u], v[0][0][2 * u + 1]);
-                    const uint64_t ta1 = dots2(v[0][1][2 * u], v[0][1][2 * u + 1]);
-                    const uint64_t tb0 = dots2(v[1][0][2 * u], v[1][0][2 * u + 1]);
-                    const uint64_t tb1 = dots2(v[1][1][2 * u], v[1][1][2 * u + 1]);
-                    // MMVQ lanes 2b+f (terms of block a) and 2b+f+64 (block b), summed, then the fragments
-                    const uint64_t leaf =
-                        add2(add2(mmvq_term2(ta0, d4ap, d8a, m4a, zero2), mmvq_term2(tb0, d4bp, d8b, m4b, zero2)),
-                             add2(mmvq_term2(ta1, d4ap, d8a, m4a, zero2), mmvq_term2(tb1, d4bp, d8b, m4b, zero2)));
-                    if (h == 0) la[m][u] = leaf;
-                    else node[m][u] = add2(la[m][u], leaf);   // node k = L(2k) + L(2k+1)
-                    if constexpr (Tap) {
-                        float a0, a1, c0, c1, b0, b1, e0, e1;
-                        upk2(ta0, a0, a1);
-                        upk2(ta1, c0, c1);
-                        upk2(tb0, b0, b1);
-                        upk2(tb1, e0, e1);
-                        const float da[2] = {a0 + c0, a1 + c1}, db[2] = {b0 + e0, b1 + e1};
-#pragma unroll
-                        for (int jj = 0; jj < 2; ++jj) {
-                            const int j = 2 * u + jj;
-                            const int pl = p0 + pc0 + j - tap_base;
-                            if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs) {
-                                int32_t *dst = m == 0 ? p.tap.gate : p.tap.up;
-                                const size_t base = (static_cast<size_t>(pl) * I + row) * nb;
-                                dst[base + 2 * ks + h] = static_cast<int32_t>(da[jj]);
-                                dst[base + 2 * ks + 32 + h] = static_cast<int32_t>(db[jj]);
-                            }
+                    for (int jj = 0; jj < 2; ++jj) {
+                        const int j = 2 * u + jj;
+                        const int pl = p0 + pc0 + j - tap_base;
+                        if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs) {
+                            int32_t *dst = m == 0 ? p.tap.gate : p.tap.up;
+                            const size_t base = (static_cast<size_t>(pl) * I + row) * nb;
+                            dst[base + 2 * kk + h] = static_cast<int32_t>(da[jj]);
+                            dst[base + 2 * kk + 32 + h] = static_cast<int32_t>(db[jj]);
                         }
                     }
                 }
             }
-            region_release(&tm_empty[r], lane);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[s]);   // done with the stage's scales and constants
-        // push node k into the binary tree over k = 0..15 (one warp-uniform branch nest)
-        if (!(ks & 1)) {
+        if (lane == 0) {   // done with the stage's constants (and, at a group's end, its scale windows)
+            mbar_arrive(bars.side_empty(s));
+            if (kk % St::spw == St::spw - 1) mbar_arrive(bars.sc_empty(qs));
+        }
+        // push node kk into the binary tree over kk = 0..15 (one warp-uniform branch nest)
+        if (!(kk & 1)) {
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
+            for (int u = 0; u < U; ++u) s0[u] = node[u];
+        } else if (!(kk & 2)) {
 #pragma unroll
-                for (int u = 0; u < U; ++u) s0[m][u] = node[m][u];
-        } else if (!(ks & 2)) {
+            for (int u = 0; u < U; ++u) s1[u] = add2(s0[u], node[u]);
+        } else if (!(kk & 4)) {
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-                for (int u = 0; u < U; ++u) s1[m][u] = add2(s0[m][u], node[m][u]);
-        } else if (!(ks & 4)) {
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-                for (int u = 0; u < U; ++u) s2[m][u] = add2(s1[m][u], add2(s0[m][u], node[m][u]));
+            for (int u = 0; u < U; ++u) s2[u] = add2(s1[u], add2(s0[u], node[u]));
         } else {
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
+            for (int u = 0; u < U; ++u) {
+                const uint64_t x = add2(s2[u], add2(s1[u], add2(s0[u], node[u])));
+                s3[u] = (kk & 8) ? add2(s3[u], x) : x;
+            }
+            if (ks == kNodes - 1) {
 #pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const uint64_t x = add2(s2[m][u], add2(s1[m][u], add2(s0[m][u], node[m][u])));
-                    s3[m][u] = (ks & 8) ? add2(s3[m][u], x) : x;
-                }
+                for (int u = 0; u < U; ++u) gt[u] = s3[u];
+            }
         }
     }
 
@@ -343,15 +431,39 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
     const int nbI = I / 32;
     uint8_t *mslot = p.mid_arr + static_cast<size_t>(tile) * tc_dn_slot(I) + static_cast<size_t>(jb) * NP * 32;
     float *msc = p.mid_sc_arr + static_cast<size_t>(tile) * tc_dn_sc_slot(I) + static_cast<size_t>(jb) * 2 * NP;
+    // the reference's sanitisation (src/hip/session_ops.hip:250-262); the 4 exponentials together
+    float gv[CW], uv[CW], ng[CW], ex[CW];
+    int fj[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+        float g0, g1, u0, u1;
+        upk2(gt[j / 2], g0, g1);
+        upk2(s3[j / 2], u0, u1);
+        fj[j] = 0;
+        gv[j] = operand((j & 1) ? g1 : g0, fj[j]);
+        uv[j] = operand((j & 1) ? u1 : u0, fj[j]);
+        ng[j] = -gv[j];
+    }
+    {   // two at a time: the loads of a pair of lookups overlap, the register peak stays low
+        const float n0[2] = {ng[0], ng[1]}, n1[2] = {ng[2], ng[3]};
+        float x0[2], x1[2];
+        expf_ref_n<2>(n0, x0);
+        expf_ref_n<2>(n1, x1);
+        ex[0] = x0[0];
+        ex[1] = x0[1];
+        ex[2] = x1[0];
+        ex[3] = x1[1];
+    }
 #pragma unroll
     for (int j = 0; j < CW; ++j) {
         const int c = pc0 + j;
         MidQ r{{0, 0, 0, 0}, 0};
         if (c < n) {   // padded pairs get zero codes and constants
-            float g0, g1, u0, u1;
-            upk2(s3[0][j / 2], g0, g1);
-            upk2(s3[1][j / 2], u0, u1);
-            r = silu_q8((j & 1) ? g1 : g0, (j & 1) ? u1 : u0);
+            int f = fj[j];
+            const float act = arithmetic(__fdiv_rn(gv[j], __fadd_rn(1.0f, ex[j])), f);
+            const float val = arithmetic(__fmul_rn(act, uv[j]), f);
+            r.q = quantize_lane(f ? 0.0f : val);
+            r.flags = f | r.q.flags;
             flags |= r.flags;
         }
         const uint32_t word = pack_lane_bytes(r.q.code);
@@ -375,12 +487,12 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
 
 // ---- down epilogue of one item ---------------------------------------------
 template <bool Tap>
-__device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *smem, uint64_t *raw_full,
-                                                 uint64_t *raw_empty, uint64_t *tm_full, uint64_t *tm_empty,
-                                                 uint32_t tq, RowsSeq &sq, int item, int4 td, int lane, int quarter,
-                                                 int chunk) {
+__device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *smem, const RowsBars &bars,
+                                                 uint32_t tq, RowsSeq &sq, int item, int4 td,
+                                                 int lane, int quarter, int chunk) {
     using St = RowsStage<true>;
     constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile;
+    static_assert(CW == 4, "one x4 load per block");
     const int H = p.hidden, I = p.inter;
     const int nb = I / 32, slabs = H / kRowsM;
     const int slab = item % slabs;
@@ -395,47 +507,59 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
     if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
 
     for (int ks = 0; ks < nb / kRowsKB; ++ks, ++sq.g) {
-        const int s = sq.g % St::raw_stages;
-        const uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
-        if (!mbar_wait(&raw_full[s], (sq.g / St::raw_stages) & 1, p.error)) return false;
+        const int s = sq.g % St::side_stages;
+        const uint8_t *st = smem + St::side_off + s * St::side_bytes;
+        if (!mbar_wait(bars.side_full(s), (sq.g / St::side_stages) & 1, p.error)) return false;
+        const int q = sq.g / St::spw, qs = q % St::sc_stages;
+        if (ks % St::spw == 0 && !mbar_wait(bars.sc_full(qs), (q / St::sc_stages) & 1, p.error)) return false;
+        // d4 of blocks 4ks..4ks+3: columns (ks & 1) * 4 .. + 3 of the 8-block window
+        const uint2 d4q =
+            *reinterpret_cast<const uint2 *>(smem + St::sc_off + qs * St::sc_bytes + lrow * 16 + (ks & 1) * 8);
         const int r = static_cast<int>(sq.k % R);
         ++sq.k;
-        if (!mbar_wait(&tm_full[r], ((sq.k - 1) / R) & 1, p.error)) return false;
+        if (!mbar_wait(bars.tm_full(r), ((sq.k - 1) / R) & 1, p.error)) return false;
         tc_fence_after();
-        static_assert(CW == 4, "one x4 load per block");
         uint32_t v[kRowsKB][CW];
 #pragma unroll
         for (int kb = 0; kb < kRowsKB; ++kb) tmem_ld4(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
         tmem_wait_ld();
 #pragma unroll
         for (int kb = 0; kb < kRowsKB; ++kb) tie4(v[kb]);
-        region_release(&tm_empty[r], lane);
-        const uint16_t *sc = reinterpret_cast<const uint16_t *>(st + St::scales);
+        region_release(bars.tm_empty(r), lane);
+        const float *cb = reinterpret_cast<const float *>(st + St::bsc);
 #pragma unroll
         for (int kb = 0; kb < kRowsKB; ++kb) {
-            const float d4 = h2f(sc[lrow * 8 + (ks & 1) * 4 + kb]);
+            const uint32_t hw = (kb < 2) ? d4q.x : d4q.y;
+            const float d4 = (kb & 1) ? hi_half(hw) : lo_half(hw);
             const uint64_t d4p = pkf2(d4, d4);
-            const uint64_t *d8p = reinterpret_cast<const uint64_t *>(
-                reinterpret_cast<const float *>(st + St::bsc) + kb * 2 * NP + pc0);
+            const uint4 d8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + pc0);
+            const uint4 m8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + NP + pc0);
+            const uint64_t d8p[2] = {pk2(d8.x, d8.y), pk2(d8.z, d8.w)};
+            const uint64_t m8p[2] = {pk2(m8.x, m8.y), pk2(m8.z, m8.w)};
 #pragma unroll
             for (int u = 0; u < CW / 2; ++u) {
-                const uint64_t t = dots2(v[kb][2 * u], v[kb][2 * u + 1]);   // exact dots
-                acc[u] = fma2(d4p, fma2(t, d8p[u], d8p[NP / 2 + u]), acc[u]);
-            }
-            if constexpr (Tap) {
-                if (e == p.tap.expert) {
+                const uint64_t t = from_magic2(v[kb][2 * u], v[kb][2 * u + 1]);   // exact dots
+                acc[u] = fma2(d4p, fma2(t, d8p[u], m8p[u]), acc[u]);
+                if constexpr (Tap) {
+                    float t0, t1;
+                    upk2(t, t0, t1);
+                    const float tt[2] = {t0, t1};
 #pragma unroll
-                    for (int j = 0; j < CW; ++j) {
+                    for (int jj = 0; jj < 2; ++jj) {
+                        const int j = 2 * u + jj;
                         const int pl = p0 + pc0 + j - tap_base;
-                        if (pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs)
+                        if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs)
                             p.tap.down[(static_cast<size_t>(pl) * H + row) * nb + ks * kRowsKB + kb] =
-                                static_cast<int32_t>(v[kb][j]);
+                                static_cast<int32_t>(tt[jj]);
                     }
                 }
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[s]);
+        if (lane == 0) {
+            mbar_arrive(bars.side_empty(s));
+            if (ks % St::spw == St::spw - 1) mbar_arrive(bars.sc_empty(qs));
+        }
     }
     // router-weighted scatter-add of the 128-row slab into the residual
     float a[CW];
@@ -466,38 +590,49 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
 template <bool Down, bool Tap>
 __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_constant__ TcrParams p) {
     using St = RowsStage<Down>;
-    constexpr int M = St::M;
-    constexpr int RS = St::raw_stages, AS = St::a_stages, R = St::regions;
+    constexpr int CS = St::code_stages, SS = St::side_stages, QS = St::sc_stages, AS = St::a_stages;
+    constexpr int R = St::regions;
     extern __shared__ __align__(128) uint8_t smem[];
     const int H = p.hidden, I = p.inter;
-    const int K = Down ? I : H, nb = K / 32, ksteps = nb / kRowsKB;
+    const int K = Down ? I : H, nb = K / 32, nodes = nb / kRowsKB;
+    const int ksteps = Down ? nodes : 2 * nodes;     // gate/up: the gate pass, then the up pass
     const int slabs = (Down ? H : I) / kRowsM;
-    uint64_t *raw_full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *raw_empty = raw_full + 8;
-    uint64_t *a_full = raw_empty + 8;
-    uint64_t *a_empty = a_full + 8;
-    uint64_t *tm_full = a_empty + 8;
-    uint64_t *tm_empty = tm_full + 8;
-    uint64_t *fin = tm_empty + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 512);
+    RowsBars bars{reinterpret_cast<uint64_t *>(smem)};
+    uint64_t *fin = bars.fin();
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 1536);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < RS; ++s) {
-            mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], kRowsUnpackWarps + kRowsEpiWarps + 1);
+        for (int s = 0; s < CS; ++s) {
+            mbar_init(bars.code_full(s), 1);
+            mbar_init(bars.code_empty(s), kRowsUnpackWarps);
+        }
+        for (int s = 0; s < SS; ++s) {
+            mbar_init(bars.side_full(s), 1);
+            mbar_init(bars.side_empty(s), kRowsEpiWarps + 1);   // + the MMAs' commit (B operand)
+        }
+        for (int s = 0; s < QS; ++s) {
+            mbar_init(bars.sc_full(s), 1);
+            mbar_init(bars.sc_empty(s), kRowsEpiWarps);
         }
         for (int s = 0; s < AS; ++s) {
-            mbar_init(&a_full[s], kRowsUnpackWarps);
-            mbar_init(&a_empty[s], 1);
+            mbar_init(bars.a_full(s), kRowsUnpackWarps);
+            mbar_init(bars.a_empty(s), 1);
         }
         for (int r = 0; r < R; ++r) {
-            mbar_init(&tm_full[r], 1);
-            mbar_init(&tm_empty[r], kRowsEpiWarps);
+            mbar_init(bars.tm_full(r), 1);
+            mbar_init(bars.tm_empty(r), kRowsEpiWarps);
         }
         mbar_init(fin, 1);
         mbar_fence_init();
     }
+    // bf16 operands of the conversion-offset MMA: A row r = (1, 0, ..., 0), B row n = (1.5 * 2^23, 0, ..., 0)
+    for (int c = threadIdx.x; c < 4 * kRowsM; c += blockDim.x) {
+        const int which = c / (2 * kRowsM), rest = c % (2 * kRowsM), row = rest >> 1, half = rest & 1;
+        const uint4 v = make_uint4(half ? 0u : (which ? kBf16Magic : kBf16One), 0u, 0u, 0u);
+        *reinterpret_cast<uint4 *>(smem + St::magic_off + which * kRowsM * 32 + tile_off(row, half)) = v;
+    }
+    fence_proxy_async();
     if (warp == 0) {
         tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
@@ -512,100 +647,150 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
+        // One thread feeds the code ring and the side/scale rings
+        // independently: it polls (without blocking) for the next free slot of
+        // each and issues whichever copy can go, so the codes (released by the
+        // unpack) run ahead of the side data (released by the epilogue) and
+        // neither ring's consumers hold the other back.  Side copies never pass
+        // the code copies of the same stage.
         if (lane == 0) {
-            for (int m = 0; m < M; ++m) {
+            for (int m = 0; m < St::M; ++m) {
                 tma_prefetch_map(&p.maps.codes[Down ? 2 : m]);
                 tma_prefetch_map(&p.maps.scales[Down ? 2 : m]);
             }
             constexpr uint32_t bbytes = kRowsKB * St::brows * 32, sbytes = kRowsKB * St::cwords * kTcTile * 4;
             const size_t bslot = Down ? tc_dn_slot(K) : tc_gu_slot(K);
             const size_t sslot = Down ? tc_dn_sc_slot(K) : tc_gu_sc_slot(K);
-            int g = 0;
-            bool failed = false;
-            for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
-                const int tile = item / slabs, slab = item % slabs;
-                const int e = p.tiles[tile].x;
-                for (int ks = 0; ks < ksteps; ++ks, ++g) {
-                    const int s = g % RS;
-                    if (g >= RS && !mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, p.error)) { failed = true; break; }
-                    uint8_t *st = smem + St::raw_off + s * St::raw_bytes;
-                    mbar_arrive_expect_tx(&raw_full[s],
-                                          M * (kRowsKB * kRowsM * 16 + St::wins * kRowsM * 16) + bbytes + sbytes);
-                    for (int m = 0; m < M; ++m) {
-                        const int mat = Down ? 2 : m;
-                        // code copies: down blocks 4ks..4ks+3 at once; gate/up blocks (2ks, 2ks+1), then (+32, +33)
-                        for (int c = 0; c < kRowsKB / St::bpc; ++c) {
-                            const int b0 = Down ? kRowsKB * ks : 2 * ks + 32 * c;
-                            uint8_t *dst = st + St::codes + (m * kRowsKB + c * St::bpc) * kRowsM * 16;
-                            if (p.raw_rowmajor)
-                                tma_load_3d(dst, &p.maps.codes[mat], b0 * 16, slab * kRowsM, e, &raw_full[s]);
-                            else
-                                tma_load_4d(dst, &p.maps.codes[mat], 0, slab * kRowsM, b0, e, &raw_full[s]);
-                        }
-                        for (int w = 0; w < St::wins; ++w) {
-                            const int b0 = Down ? kRowsKB * ks : 2 * ks + 32 * w;
-                            tma_load_3d(st + St::scales + (m * St::wins + w) * kRowsM * 16, &p.maps.scales[mat],
-                                        b0 & ~7, slab * kRowsM, e, &raw_full[s]);
-                        }
+            const int total_g = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x * ksteps : 0;
+            // per-ring cursors, advanced stage by stage (the tile record is read once per item)
+            struct Cursor {
+                int item, ks, tile, slab, e;
+            };
+            auto start = [&](Cursor &c, int item) {
+                c.item = item;
+                c.ks = 0;
+                c.tile = item / slabs;
+                c.slab = item - c.tile * slabs;
+                c.e = item < total ? p.tiles[c.tile].x : 0;
+            };
+            auto advance = [&](Cursor &c) {
+                if (++c.ks == ksteps) start(c, c.item + gridDim.x);
+            };
+            Cursor cc_, cs_;
+            start(cc_, blockIdx.x);
+            cs_ = cc_;
+            int gc = 0, gs = 0;          // next stage of the code ring, of the side ring
+            uint32_t idle = 0;
+            while (gs < total_g) {
+                bool progress = false;
+                if (gc < total_g && (gc < CS || mbar_test(bars.code_empty(gc % CS), ((gc / CS) & 1) ^ 1))) {
+                    const int mat = Down ? 2 : cc_.ks / nodes, kk = cc_.ks % nodes, c = gc % CS;
+                    uint8_t *dst0 = smem + St::codes_off + c * St::codes_bytes;
+                    mbar_arrive_expect_tx(bars.code_full(c), St::codes_bytes);
+                    // down blocks 4kk..4kk+3 in one copy; gate/up blocks (2kk, 2kk+1), then (+32, +33)
+                    for (int cp = 0; cp < kRowsKB / St::bpc; ++cp) {
+                        const int b0 = Down ? kRowsKB * kk : 2 * kk + 32 * cp;
+                        uint8_t *dst = dst0 + cp * St::bpc * kRowsM * 16;
+                        if (p.raw_rowmajor)
+                            tma_load_3d(dst, &p.maps.codes[mat], b0 * 16, cc_.slab * kRowsM, cc_.e, bars.code_full(c));
+                        else
+                            tma_load_4d(dst, &p.maps.codes[mat], 0, cc_.slab * kRowsM, b0, cc_.e, bars.code_full(c));
                     }
-                    bulk_g2s(st + St::b, p.b_arr + static_cast<size_t>(tile) * bslot + static_cast<size_t>(ks) * bbytes,
-                             bbytes, &raw_full[s]);
-                    bulk_g2s(st + St::bsc,
-                             p.bsc_arr + static_cast<size_t>(tile) * sslot +
-                                 static_cast<size_t>(ks) * kRowsKB * St::cwords * kTcTile,
-                             sbytes, &raw_full[s]);
+                    ++gc;
+                    advance(cc_);
+                    progress = true;
+                }
+                if (gs < gc) {
+                    const int mat = Down ? 2 : cs_.ks / nodes, ks = cs_.ks % nodes, sd = gs % SS;
+                    const int q = gs / St::spw, qs = q % QS;
+                    const bool group = ks % St::spw == 0;   // also the scale windows of this stage group
+                    if ((gs < SS || mbar_test(bars.side_empty(sd), ((gs / SS) & 1) ^ 1)) &&
+                        (!group || q < QS || mbar_test(bars.sc_empty(qs), ((q / QS) & 1) ^ 1))) {
+                        uint8_t *st = smem + St::side_off + sd * St::side_bytes;
+                        mbar_arrive_expect_tx(bars.side_full(sd), bbytes + sbytes);
+                        bulk_g2s(st + St::b,
+                                 p.b_arr + static_cast<size_t>(cs_.tile) * bslot + static_cast<size_t>(ks) * bbytes,
+                                 bbytes, bars.side_full(sd));
+                        bulk_g2s(st + St::bsc,
+                                 p.bsc_arr + static_cast<size_t>(cs_.tile) * sslot +
+                                     static_cast<size_t>(ks) * kRowsKB * St::cwords * kTcTile,
+                                 sbytes, bars.side_full(sd));
+                        if (group) {
+                            // gate/up blocks 8j and 32 + 8j of the stage's matrix, down blocks 8j
+                            mbar_arrive_expect_tx(bars.sc_full(qs), St::sc_bytes);
+                            for (int w = 0; w < St::wins; ++w) {
+                                const int b0 = Down ? kRowsKB * ks : 2 * ks + 32 * w;
+                                tma_load_3d(smem + St::sc_off + qs * St::sc_bytes + w * kRowsM * 16, &p.maps.scales[mat],
+                                            b0 & ~7, cs_.slab * kRowsM, cs_.e, bars.sc_full(qs));
+                            }
+                        }
+                        ++gs;
+                        advance(cs_);
+                        progress = true;
+                    }
+                }
+                if (progress) {
+                    idle = 0;
+                } else {
+                    if (++idle > kProducerIdleLimit) {   // the consumers stopped (a bounded wait gave up)
+                        atomicOr(p.error, kFlagTimeout);
+                        break;
+                    }
+                    __nanosleep(64);
                 }
             }
             // keep the CTA alive until every issued copy has landed
-            for (int k = g - RS > 0 ? g - RS : 0; k < g; ++k) mbar_wait(&raw_full[k % RS], (k / RS) & 1, p.error);
+            for (int g = gc - CS > 0 ? gc - CS : 0; g < gc; ++g)
+                mbar_wait(bars.code_full(g % CS), (g / CS) & 1, p.error);
+            for (int g = gs - SS > 0 ? gs - SS : 0; g < gs; ++g)
+                mbar_wait(bars.side_full(g % SS), (g / SS) & 1, p.error);
+            const int nq = (gs + St::spw - 1) / St::spw;
+            for (int q = nq - QS > 0 ? nq - QS : 0; q < nq; ++q)
+                mbar_wait(bars.sc_full(q % QS), (q / QS) & 1, p.error);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = rows_idesc(kRowsM, St::brows);
+            const uint32_t idesc_mg = magic_idesc(kRowsM, St::reg_cols);
+            const uint64_t amg = smem_desc(smem_u32(smem + St::magic_off), 128, 256);
+            const uint64_t bmg = smem_desc(smem_u32(smem + St::magic_off + kRowsM * 32), 128, 256);
             int g = 0;
             uint32_t kseq = 0;
             bool failed = false;
             for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
                 for (int ks = 0; ks < ksteps && !failed; ++ks, ++g) {
-                    const int sr = g % RS, sa = g % AS;
-                    if (!mbar_wait(&a_full[sa], (g / AS) & 1, p.error) ||
-                        !mbar_wait(&raw_full[sr], (g / RS) & 1, p.error)) {
+                    const int sr = g % SS, sa = g % AS;
+                    if (!mbar_wait(bars.a_full(sa), (g / AS) & 1, p.error) ||
+                        !mbar_wait(bars.side_full(sr), (g / SS) & 1, p.error)) {
                         failed = true;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t a_st = smem_u32(smem + St::a_off + sa * St::a_bytes);
-                    const uint32_t b_st = smem_u32(smem + St::raw_off + sr * St::raw_bytes + St::b);
-                    for (int h = 0; h < St::regions_per_stage; ++h, ++kseq) {
+                    const uint32_t b_st = smem_u32(smem + St::side_off + sr * St::side_bytes + St::b);
+                    {
                         const int r = static_cast<int>(kseq % R);
-                        if (!mbar_wait(&tm_empty[r], (kseq / R) & 1, p.error)) { failed = true; break; }
-                        tc_fence_after();
-                        if (Down) {
-                            // the stage's 4 blocks into the region's columns [16 kb, 16 kb + 16)
-#pragma unroll
-                            for (int kb = 0; kb < kRowsKB; ++kb) {
-                                const uint64_t ad = smem_desc(a_st + kb * kRowsM * 32, 128, 256);
-                                const uint64_t bd = smem_desc(b_st + kb * St::brows * 32, 128, 256);
-                                mma_i8(tmem + r * St::reg_cols + kb * kTcTile, ad, bd, idesc, 0u);
-                            }
-                        } else {
-                            // stage slots h (block 2k+h) and 2+h (block 2k+32+h): columns [0,32) and [32,64)
-                            // of gate, +64 for up
-#pragma unroll
-                            for (int m = 0; m < 2; ++m)
-#pragma unroll
-                                for (int q = 0; q < 2; ++q) {
-                                    const int slot = h + 2 * q;
-                                    const uint64_t ad = smem_desc(a_st + (m * kRowsKB + slot) * kRowsM * 32, 128, 256);
-                                    const uint64_t bd = smem_desc(b_st + slot * St::brows * 32, 128, 256);
-                                    mma_i8(tmem + r * St::reg_cols + m * 64 + q * 32, ad, bd, idesc, 0u);
-                                }
+                        if (!mbar_wait(bars.tm_empty(r), (kseq / R) & 1, p.error)) {
+                            failed = true;
+                            break;
                         }
-                        mma_commit(&tm_full[r]);
+                        ++kseq;
+                        tc_fence_after();
+                        // every column of the region = 1.5 * 2^23 (f32), then the integer dots added onto it:
+                        // stage slot kb (gate/up blocks 2k, 2k+1, 2k+32, 2k+33; down 4k..4k+3) into columns
+                        // [brows kb, brows (kb + 1))
+                        mma_bf16(tmem + r * St::reg_cols, amg, bmg, idesc_mg);
+#pragma unroll
+                        for (int kb = 0; kb < kRowsKB; ++kb) {
+                            const uint64_t ad = smem_desc(a_st + kb * kRowsM * 32, 128, 256);
+                            const uint64_t bd = smem_desc(b_st + kb * St::brows * 32, 128, 256);
+                            mma_i8(tmem + r * St::reg_cols + kb * St::brows, ad, bd, idesc, 1u);
+                        }
+                        mma_commit(bars.tm_full(r));
                     }
-                    mma_commit(&a_empty[sa]);
-                    mma_commit(&raw_empty[sr]);
+                    mma_commit(bars.a_empty(sa));
+                    mma_commit(bars.side_empty(sr));
                 }
             }
             // every MMA of this CTA has completed before teardown
@@ -614,61 +799,25 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
         }
     } else if (warp < 2 + kRowsUnpackWarps) {
         // ---------------- unpack: raw nibbles -> u8 K-major core matrices ----------------
-        const int ut = threadIdx.x - 64;
-        constexpr int kUnits = M * kRowsKB * kRowsM;
-        constexpr int copies = kRowsKB / St::bpc;
-        static_assert(kUnits % (32 * kRowsUnpackWarps) == 0, "whole unpack rounds");
         const bool rowmajor = p.raw_rowmajor != 0;
         int g = 0;
-        bool failed = false;
-        for (int item = blockIdx.x; item < total && !failed; item += gridDim.x) {
-            for (int ks = 0; ks < ksteps; ++ks, ++g) {
-                const int sr = g % RS, sa = g % AS;
-                if (!mbar_wait(&raw_full[sr], (g / RS) & 1, p.error) ||
-                    (g >= AS && !mbar_wait(&a_empty[sa], ((g / AS) & 1) ^ 1, p.error))) {
-                    failed = true;
-                    break;
-                }
-                const uint8_t *raw = smem + St::raw_off + sr * St::raw_bytes + St::codes;
-                uint8_t *a = smem + St::a_off + sa * St::a_bytes;
-#pragma unroll
-                for (int i = 0; i < kUnits / (32 * kRowsUnpackWarps); ++i) {
-                    const int u = ut + i * 32 * kRowsUnpackWarps;
-                    const int m = u / (kRowsKB * kRowsM), kb = (u / kRowsM) % kRowsKB, row = u % kRowsM;
-                    const int src = rowmajor ? ((m * copies + kb / St::bpc) * kRowsM + row) * St::bpc + kb % St::bpc
-                                             : (m * kRowsKB + kb) * kRowsM + row;
-                    const uint4 w = reinterpret_cast<const uint4 *>(raw)[src];
-                    const uint4 lo = make_uint4(w.x & 0x0f0f0f0fu, w.y & 0x0f0f0f0fu, w.z & 0x0f0f0f0fu,
-                                                w.w & 0x0f0f0f0fu);
-                    const uint4 hi = make_uint4((w.x >> 4) & 0x0f0f0f0fu, (w.y >> 4) & 0x0f0f0f0fu,
-                                                (w.z >> 4) & 0x0f0f0f0fu, (w.w >> 4) & 0x0f0f0f0fu);
-                    uint8_t *dst = a + (m * kRowsKB + kb) * kRowsM * 32;
-                    *reinterpret_cast<uint4 *>(dst + tile_off(row, 0)) = lo;
-                    *reinterpret_cast<uint4 *>(dst + tile_off(row, 1)) = hi;
-                }
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&a_full[sa]);
-                    mbar_arrive(&raw_empty[sr]);
-                }
-            }
-        }
+        bool ok = true;
+        for (int item = blockIdx.x; item < total && ok; item += gridDim.x)
+            for (int ks = 0; ks < ksteps && ok; ++ks, ++g)
+                ok = rows_unpack<Down>(smem, bars, g, threadIdx.x - 64, rowmajor, lane, p.error);
     } else {
         // ---------------- epilogue ----------------
-        const int ew = warp - 2 - kRowsUnpackWarps;   // 0..15
+        const int ew = warp - 2 - kRowsUnpackWarps;       // 0..15
         const int quarter = warp & 3, chunk = ew >> 2;    // TMEM lane quarter, pair chunk of kRowsCW
         const uint32_t tq = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         if (lane == 0)   // every region starts free
-            for (int r = 0; r < R; ++r) mbar_arrive(&tm_empty[r]);
+            for (int r = 0; r < R; ++r) mbar_arrive(bars.tm_empty(r));
         RowsSeq sq;
-        for (int item = blockIdx.x; item < total; item += gridDim.x) {
+        bool ok = true;
+        for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
             const int4 td = p.tiles[item / slabs];
-            const bool ok = Down ? dn_epilogue_item<Tap>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item,
-                                                         td, lane, quarter, chunk)
-                                 : gu_epilogue_item<Tap>(p, smem, raw_full, raw_empty, tm_full, tm_empty, tq, sq, item,
-                                                         td, lane, quarter, chunk);
-            if (!ok) break;
+            ok = Down ? dn_epilogue_item<Tap>(p, smem, bars, tq, sq, item, td, lane, quarter, chunk)
+                      : gu_epilogue_item<Tap>(p, smem, bars, tq, sq, item, td, lane, quarter, chunk);
         }
     }
     // teardown: every role is done with TMEM before warp 0 frees it
@@ -681,9 +830,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
 }
 
 // Gate/up B operand of every tile: for pair r < n of tile t (token
-// pair_token[p0 + r]), row r = its Q8_1 codes of fragment 0 (elements 0..7
-// and 16..23, the rest zero) and row 16 + r those of fragment 1, blocks in
-// stage order, and the constants d8[16] then -4*s8[16]; pairs n..15 are zero.
+// pair_token[p0 + r]), row tc_gu_brow(r, 0) = its Q8_1 codes of fragment 0
+// (elements 0..7 and 16..23, the rest zero) and row tc_gu_brow(r, 1) those of
+// fragment 1, blocks in stage order, and the constants d8[16] then
+// -4*s8[16]; pairs n..15 are zero.
 // CTA (t, g): 32 threads (fragment rows) x blocks 8g..8g+7.
 __global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 *tiles, const int *num_tiles,
                                                                      const int32_t *pair_token, Q8Planar xq, int H,
@@ -717,8 +867,8 @@ __global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 
         for (int i = 0; i < 8; ++i) {
             const int pos = tc_gu_pos(b0 + i);
             uint8_t *dst = slot + static_cast<size_t>(pos) * 2 * kTcTile * 32;
-            *reinterpret_cast<uint4 *>(dst + tile_off(frag * kTcTile + pr, 0)) = v[2 * i];
-            *reinterpret_cast<uint4 *>(dst + tile_off(frag * kTcTile + pr, 1)) = v[2 * i + 1];
+            *reinterpret_cast<uint4 *>(dst + tile_off(tc_gu_brow(pr, frag), 0)) = v[2 * i];
+            *reinterpret_cast<uint4 *>(dst + tile_off(tc_gu_brow(pr, frag), 1)) = v[2 * i + 1];
             if (!frag) {
                 ss[pos * 2 * kTcTile + pr] = c[i].x;
                 ss[pos * 2 * kTcTile + kTcTile + pr] = -(4.0f * c[i].y);

@@ -43,7 +43,8 @@ enum moe_status {
     MOE_NOT_SUPPORTED = 2,    /* reference: hipErrorNotSupported */
     MOE_CUDA_ERROR = 3,       /* reference: std::runtime_error from a HIP call */
     MOE_NUMERIC_ERROR = 4,    /* a sticky numeric flag was raised */
-    MOE_NCCL_ERROR = 5,
+    /* 5 is reserved (the library makes no NCCL call; expert parallelism runs
+     * over CUDA IPC peer memory) */
     MOE_TIMEOUT = 6,
     MOE_OUT_OF_MEMORY = 7
 };
