@@ -2,7 +2,11 @@
 // (src/session.hip:1412-1556) for a stack of MoE layers, through the C ABI
 // of libqwen_moe_b200.so: one layer workspace shared by every layer (the
 // reference's Session device buffers), one weights object per layer, the
-// residual stream on the device, and per layer
+// residual stream on the device.  Layer::ffn reads the normalised hidden
+// state and its output is added into the residual; the normalisation belongs
+// to the attention side of the session, so here the host applies an
+// unweighted RMS norm (per token: h / sqrt(mean(h^2) + 1e-6)) to the
+// residual to form each layer's input.  Per layer
 //   * the router taps the reference records under a probe (router logits,
 //     src/session.hip:1420-1428) -- here moe_router_logits, whose output the
 //     test routes with;
@@ -11,7 +15,7 @@
 //     10*H over tokens) -- here moe_forward_contributions, which stores the
 //     reference's [T][10][H] contribution layout and folds it in the
 //     reference's rank order;
-//   * the fast path: residual += ffn(residual) with moe_forward_hidden
+//   * the fast path: residual += ffn(input) with moe_forward_hidden
 //     (router GEMM, routing, experts and the scatter-add on the device, no
 //     host round trip), MOE_OUT_ACCUMULATE into the next residual buffer;
 //   * the per-layer flag check (the reference's d.check after each layer's
@@ -25,19 +29,19 @@
 //     gate_<l>.bin      float [hidden], layer l's shared-expert gate vector
 //   Expert weights of layer l are the library's seeded synthetic Q4_0
 //   experts (moe_weights_synthesize(seed, l)).  Writes, per layer l,
-//   x_<l>.bin (its input), logits_<l>.bin, det_<l>.bin (the trace-mode
-//   output, overwrite), ffn_expert_down_unweighted_rank_<N>_<l>.bin
-//   (float [tokens][hidden]) and x_<layers>.bin (the final residual);
-//   prints "ok".
+//   res_<l>.bin (the residual before it), x_<l>.bin (its input),
+//   logits_<l>.bin, det_<l>.bin (the trace-mode output, overwrite),
+//   ffn_expert_down_unweighted_rank_<N>_<l>.bin (float [tokens][hidden]) and
+//   res_<layers>.bin (the final residual); prints "ok".
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
 #include <iterator>
 #include <stdexcept>
 #include <string>
-#include <utility>
 #include <vector>
 
 #include "qwen_moe_b200.h"
@@ -105,15 +109,25 @@ int run(const std::string &dir) {
     moe(moe_layer_create(&desc, &layer), "moe_layer_create");
 
     const size_t n = size_t(T) * H;
-    DeviceFloats cur(n), next(n), logits(size_t(T) * 512), contrib(size_t(T) * 10 * H), shared(n), det(n);
+    DeviceFloats res(n), xin(n), logits(size_t(T) * 512), contrib(size_t(T) * 10 * H), shared(n), det(n);
     {
         const auto x0 = read_as<float>(dir + "/x0.bin", n);
-        cuda(cudaMemcpyAsync(cur.p, x0.data(), n * sizeof(float), cudaMemcpyHostToDevice, stream), "H2D");
+        cuda(cudaMemcpyAsync(res.p, x0.data(), n * sizeof(float), cudaMemcpyHostToDevice, stream), "H2D");
     }
-    float *a = cur.p, *b = next.p;
+    float *a = xin.p;
     for (int l = 0; l < L; ++l) {
         const std::string tag = "_" + std::to_string(l) + ".bin";
-        write_floats(dir + "/x" + tag, to_host(a, n, stream).data(), n);
+        // the layer's input: the RMS-normalised residual
+        std::vector<float> h = to_host(res.p, n, stream);
+        write_floats(dir + "/res" + tag, h.data(), n);
+        for (int t = 0; t < T; ++t) {
+            double ss = 0.0;
+            for (int i = 0; i < H; ++i) ss += double(h[size_t(t) * H + i]) * h[size_t(t) * H + i];
+            const float inv = static_cast<float>(1.0 / std::sqrt(ss / H + 1e-6));
+            for (int i = 0; i < H; ++i) h[size_t(t) * H + i] *= inv;
+        }
+        cuda(cudaMemcpyAsync(a, h.data(), n * sizeof(float), cudaMemcpyHostToDevice, stream), "H2D");
+        write_floats(dir + "/x" + tag, h.data(), n);
         // probe taps: router logits, then the deterministic trace pass
         moe(moe_router_logits(weights[l], a, T, logits.p, stream), "moe_router_logits");
         write_floats(dir + "/logits" + tag, to_host(logits.p, size_t(T) * 512, stream).data(), size_t(T) * 512);
@@ -128,15 +142,13 @@ int run(const std::string &dir) {
             write_floats(dir + "/ffn_expert_down_unweighted_rank_" + std::to_string(rank) + tag, rows.data(), n);
         }
         write_floats(dir + "/det" + tag, to_host(det.p, n, stream).data(), n);
-        // the fast path: next = residual + ffn(residual), all on the device
-        cuda(cudaMemcpyAsync(b, a, n * sizeof(float), cudaMemcpyDeviceToDevice, stream), "D2D");
-        moe(moe_forward_hidden(layer, weights[l], a, T, b, MOE_OUT_ACCUMULATE, stream), "moe_forward_hidden");
+        // the fast path: residual += ffn(input), all on the device
+        moe(moe_forward_hidden(layer, weights[l], a, T, res.p, MOE_OUT_ACCUMULATE, stream), "moe_forward_hidden");
         int flags = 0;
         moe(moe_layer_read_flags(layer, &flags, 1, stream), "moe_layer_read_flags");
         if (flags != 0) throw std::runtime_error("layer " + std::to_string(l) + " raised flags " + std::to_string(flags));
-        std::swap(a, b);
     }
-    write_floats(dir + "/x_" + std::to_string(L) + ".bin", to_host(a, n, stream).data(), n);
+    write_floats(dir + "/res_" + std::to_string(L) + ".bin", to_host(res.p, n, stream).data(), n);
 
     moe(moe_layer_destroy(layer), "moe_layer_destroy");
     for (auto w : weights) moe(moe_weights_destroy(w), "moe_weights_destroy");

@@ -7,12 +7,15 @@ ffn_expert_down_unweighted_rank_N trace taps (src/session.hip:1420-1428,
 
 CPU: the program compiles as C++20 against include/qwen_moe_b200.h and the
 CUDA runtime and links against libqwen_moe_b200.so.
+The program forms each layer's input as the unweighted RMS norm of the
+residual (the session's pre-FFN norm, which is not on this path) and adds the
+FFN output into the residual.
 GPU: every layer is checked against the oracle on that layer's own input (the
-residual the program fed it) and router logits:
+normalised residual the program fed it) and router logits:
 * the logits against fp64 within an fp32 accumulation bound (the reference's
   router is a BLAS GEMM of unspecified order);
-* the fast path's residual update x[l+1] - x[l] and the trace pass's output
-  against the oracle layer within 1e-3 * RMS;
+* the fast path's residual update res[l+1] - res[l] and the trace pass's
+  output against the oracle layer within 1e-3 * RMS;
 * each rank's unweighted down rows against the oracle's CPU expert for that
   token's expert of that rank (1e-3 * RMS), the trace layout of the reference.
 """
@@ -73,17 +76,20 @@ def test_session_layer_stack(pkg, O, tmp_path, T):
     def load(name, shape):
         return np.fromfile(os.path.join(tmp_path, name), np.float32).reshape(shape)
 
-    xs = [load(f"x_{l}.bin", (T, H)) for l in range(L + 1)]
-    assert np.array_equal(xs[0], x0)
+    res = [load(f"res_{l}.bin", (T, H)) for l in range(L + 1)]
+    assert np.array_equal(res[0], x0)
     for l in range(L):
-        x, lg = xs[l], load(f"logits_{l}.bin", (T, E))
+        x, lg = load(f"x_{l}.bin", (T, H)), load(f"logits_{l}.bin", (T, E))
+        r64 = res[l].astype(np.float64)
+        want_x = r64 / np.sqrt(np.mean(r64 ** 2, axis=1, keepdims=True) + 1e-6)
+        assert np.max(np.abs(x - want_x)) <= 1e-5 * np.max(np.abs(want_x)), f"layer {l} input norm"
         ref64 = x.astype(np.float64) @ routers[l].astype(np.float64).T
         bound = 2e-5 * (np.abs(x).astype(np.float64) @ np.abs(routers[l]).astype(np.float64).T)
         assert np.all(np.abs(lg - ref64) <= bound), f"layer {l} router logits"
         want, ids, _, flags = O.moe_layer(x, lg, lambda e: O.synth_expert(seed, l, e), O.synth_expert(seed, l, 512),
                                           gates[l], threads=8)
         assert flags == 0
-        ffn = (xs[l + 1].astype(np.float64) - x).astype(np.float32)
+        ffn = (res[l + 1].astype(np.float64) - res[l]).astype(np.float32)
         assert_close(ffn, want)
         assert_close(load(f"det_{l}.bin", (T, H)), want)
         xq, _ = O.quantize(x)
