@@ -359,10 +359,10 @@ int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, 
     const TcrParams prm = tcr_params(h, w, out, down, tap);
     cudaError_t e;
     if (down)
-        e = launch_overlapped(tap ? tc_rows_kernel<true, true> : tc_rows_kernel<true, false>, grid, kRowsThreads,
+        e = launch_overlapped(tap ? tc_rows_kernel<true, true> : tc_rows_kernel<true, false>, grid, RowsStage<true>::threads,
                               RowsStage<true>::smem, s, prm);
     else
-        e = launch_overlapped(tap ? tc_rows_kernel<false, true> : tc_rows_kernel<false, false>, grid, kRowsThreads,
+        e = launch_overlapped(tap ? tc_rows_kernel<false, true> : tc_rows_kernel<false, false>, grid, RowsStage<false>::threads,
                               RowsStage<false>::smem, s, prm);
     return cuda_status(e, "tc_rows_kernel");
 }

@@ -36,13 +36,14 @@
 // acc += d4 * (dot * d8 - 8 * s8) per block in fp32, then a router-weighted
 // red.add into the residual (lane = output row: coalesced).
 //
-// Warp roles (20 warps):
+// Warp roles (gate/up 20 warps, down 12):
 //   warp 0      TMEM allocation; lane 0 issues the TMA copies: raw weight
 //               codes and scales through tensor maps, the tile's pre-arranged
 //               activation operand as 1-D bulk copies;
 //   warp 1      lane 0 issues the MMAs;
 //   warps 2-3   unpack raw Q4_0 codes shared -> shared into the MMA layout;
-//   warps 4-19  epilogue: four per TMEM lane quarter, 4 pairs each.
+//   warps 4-    epilogue: gate/up four per TMEM lane quarter with 4 pairs
+//               each, down two per quarter with 8 pairs each.
 // Every barrier wait is bounded (ptx.cuh); a wait that gives up sets the
 // timeout flag and the role leaves its loop.
 #pragma once
@@ -57,11 +58,7 @@ namespace qmoe {
 
 constexpr int kRowsM = 128;            // weight rows per MMA (TMEM lanes)
 constexpr int kRowsKB = 4;             // quantisation blocks per pipeline stage
-constexpr int kRowsCW = kTcTile / 4;   // pairs per epilogue warp (four warps per TMEM lane quarter)
 constexpr int kRowsUnpackWarps = 2;
-constexpr int kRowsEpiWarps = 16;
-constexpr int kRowsWarps = 2 + kRowsUnpackWarps + kRowsEpiWarps;
-constexpr int kRowsThreads = 32 * kRowsWarps;
 constexpr int kRowsMinGroup = 1;       // batches above decode size: every group on this path
 constexpr int kRowsHidden = 2048;      // the gate/up stage order pairs blocks b and b + 32 of 64
 constexpr float kMagicF = 12582912.0f; // 1.5 * 2^23 (bits 0x4B400000)
@@ -109,6 +106,12 @@ constexpr int kRowsBarSlots = 16;   // entries per barrier array
 template <bool Down>
 struct RowsStage {
     static constexpr int M = Down ? 1 : 2;                                    // matrices per item (one per stage)
+    // epilogue warps (per TMEM lane quarter: epi_warps / 4) and pairs per warp: gate/up runs
+    // dependent fp32 chains per pair and needs the warps to hide their latency, down the fewer
+    // per-warp fixed costs of wider warps
+    static constexpr int epi_warps = Down ? 8 : 16;
+    static constexpr int cw = kTcTile * 4 / epi_warps;
+    static constexpr int threads = 32 * (2 + kRowsUnpackWarps + epi_warps);
     static constexpr int wins = Down ? 1 : 2;                                 // 8-block scale windows per group
     static constexpr int spw = Down ? 2 : 4;                                  // stages per scale group
     static constexpr int brows = Down ? kTcTile : 2 * kTcTile;                // B rows per block
@@ -167,6 +170,21 @@ __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
 }
 
 // 8 consecutive TMEM columns of this warp's lane quarter (one 32-bit value each).
+// 16 consecutive TMEM columns of this warp's lane quarter.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tie16(uint32_t *r) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t *r) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -308,9 +326,9 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
                                                  uint32_t tq, RowsSeq &sq, int item, int4 td,
                                                  int lane, int quarter, int chunk) {
     using St = RowsStage<false>;
-    constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile, U = CW / 2;
+    constexpr int R = St::regions, CW = St::cw, NP = kTcTile, U = CW / 2;
     constexpr int kNodes = kRowsHidden / 32 / kRowsKB;        // 16 stages (level-2 nodes) per matrix
-    static_assert(CW == 4 && U == 2, "one x8 load per block: 4 pairs x 2 fragments");
+    static_assert(CW == 4 || CW == 8, "one x8 / x16 load per block: 1 or 2 chunks x (4 pairs x 2 fragments)");
     const int I = p.inter;
     const int nb = kRowsHidden / 32, slabs = I / kRowsM;
     const int slab = item % slabs, tile = item / slabs;
@@ -340,17 +358,25 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
         const int r = static_cast<int>(sq.k % R);
         if (!mbar_wait(bars.tm_full(r), (sq.k / R) & 1, p.error)) return false;
         tc_fence_after();
-        const uint32_t tr = tq + r * St::reg_cols + chunk * 8;
+        const uint32_t tr = tq + r * St::reg_cols + chunk * 2 * CW;
         uint64_t node[U], la[U];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {   // leaf h: block 2kk+h (slot h) and 2kk+32+h (slot 2+h)
-            // columns: fragment 0 of the 4 pairs, then fragment 1
-            uint32_t va[8], vb[8];
-            tmem_ld8(tr + h * 32, va);
-            tmem_ld8(tr + (2 + h) * 32, vb);
-            tmem_wait_ld();
-            tie8(va);
-            tie8(vb);
+            // columns: per chunk of 4 pairs, fragment 0 of the pairs, then fragment 1
+            uint32_t va[2 * CW], vb[2 * CW];
+            if constexpr (CW == 8) {
+                tmem_ld16(tr + h * 32, va);
+                tmem_ld16(tr + (2 + h) * 32, vb);
+                tmem_wait_ld();
+                tie16(va);
+                tie16(vb);
+            } else {
+                tmem_ld8(tr + h * 32, va);
+                tmem_ld8(tr + (2 + h) * 32, vb);
+                tmem_wait_ld();
+                tie8(va);
+                tie8(vb);
+            }
             if (h == 1) region_release(bars.tm_empty(r), lane);
             // pair constants d8 and m4 = -4 s8 of block 2kk+h (slot h) and 2kk+32+h (slot 2+h), as pair units
             const uint64_t *ka = reinterpret_cast<const uint64_t *>(
@@ -364,10 +390,11 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
             for (int u = 0; u < U; ++u) {
                 if (u >= units) break;
                 // exact fragment dots of the unit's two pairs: block a (2kk+h) and b (2kk+32+h)
-                const uint64_t ta0 = from_magic2(va[2 * u], va[2 * u + 1]);
-                const uint64_t ta1 = from_magic2(va[4 + 2 * u], va[5 + 2 * u]);
-                const uint64_t tb0 = from_magic2(vb[2 * u], vb[2 * u + 1]);
-                const uint64_t tb1 = from_magic2(vb[4 + 2 * u], vb[5 + 2 * u]);
+                const int c0 = (u >> 1) * 8 + (u & 1) * 2;   // fragment 0 of the unit's pairs; fragment 1 at +4
+                const uint64_t ta0 = from_magic2(va[c0], va[c0 + 1]);
+                const uint64_t ta1 = from_magic2(va[c0 + 4], va[c0 + 5]);
+                const uint64_t tb0 = from_magic2(vb[c0], vb[c0 + 1]);
+                const uint64_t tb1 = from_magic2(vb[c0 + 4], vb[c0 + 5]);
                 const uint64_t d8a = ka[u], m4a = ka[NP / 2 + u], d8b = kb[u], m4b = kb[NP / 2 + u];
                 // MMVQ lanes 2b+f (terms of block a) and 2b+f+64 (block b), summed, then the fragments
                 const uint64_t leaf = add2(add2(mmvq_term2(ta0, d4ap, d8a, m4a, zero2),
@@ -444,15 +471,13 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
         uv[j] = operand((j & 1) ? u1 : u0, fj[j]);
         ng[j] = -gv[j];
     }
-    {   // two at a time: the loads of a pair of lookups overlap, the register peak stays low
-        const float n0[2] = {ng[0], ng[1]}, n1[2] = {ng[2], ng[3]};
-        float x0[2], x1[2];
-        expf_ref_n<2>(n0, x0);
-        expf_ref_n<2>(n1, x1);
-        ex[0] = x0[0];
-        ex[1] = x0[1];
-        ex[2] = x1[0];
-        ex[3] = x1[1];
+#pragma unroll
+    for (int j = 0; j < CW; j += 2) {   // two at a time: the lookups overlap, the register peak stays low
+        const float nj[2] = {ng[j], ng[j + 1]};
+        float xj[2];
+        expf_ref_n<2>(nj, xj);
+        ex[j] = xj[0];
+        ex[j + 1] = xj[1];
     }
 #pragma unroll
     for (int j = 0; j < CW; ++j) {
@@ -491,8 +516,8 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
                                                  uint32_t tq, RowsSeq &sq, int item, int4 td,
                                                  int lane, int quarter, int chunk) {
     using St = RowsStage<true>;
-    constexpr int R = St::regions, CW = kRowsCW, NP = kTcTile;
-    static_assert(CW == 4, "one x4 load per block");
+    constexpr int R = St::regions, CW = St::cw, NP = kTcTile;
+    static_assert(CW == 8, "one x8 load per block");
     const int H = p.hidden, I = p.inter;
     const int nb = I / 32, slabs = H / kRowsM;
     const int slab = item % slabs;
@@ -521,10 +546,10 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
         tc_fence_after();
         uint32_t v[kRowsKB][CW];
 #pragma unroll
-        for (int kb = 0; kb < kRowsKB; ++kb) tmem_ld4(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
+        for (int kb = 0; kb < kRowsKB; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
         tmem_wait_ld();
 #pragma unroll
-        for (int kb = 0; kb < kRowsKB; ++kb) tie4(v[kb]);
+        for (int kb = 0; kb < kRowsKB; ++kb) tie8(v[kb]);
         region_release(bars.tm_empty(r), lane);
         const float *cb = reinterpret_cast<const float *>(st + St::bsc);
 #pragma unroll
@@ -533,9 +558,11 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
             const float d4 = (kb & 1) ? hi_half(hw) : lo_half(hw);
             const uint64_t d4p = pkf2(d4, d4);
             const uint4 d8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + pc0);
+            const uint4 d8h = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + pc0 + 4);
             const uint4 m8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + NP + pc0);
-            const uint64_t d8p[2] = {pk2(d8.x, d8.y), pk2(d8.z, d8.w)};
-            const uint64_t m8p[2] = {pk2(m8.x, m8.y), pk2(m8.z, m8.w)};
+            const uint4 m8h = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + NP + pc0 + 4);
+            const uint64_t d8p[4] = {pk2(d8.x, d8.y), pk2(d8.z, d8.w), pk2(d8h.x, d8h.y), pk2(d8h.z, d8h.w)};
+            const uint64_t m8p[4] = {pk2(m8.x, m8.y), pk2(m8.z, m8.w), pk2(m8h.x, m8h.y), pk2(m8h.z, m8h.w)};
 #pragma unroll
             for (int u = 0; u < CW / 2; ++u) {
                 const uint64_t t = from_magic2(v[kb][2 * u], v[kb][2 * u + 1]);   // exact dots
@@ -588,7 +615,7 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
 
 // ---- the kernel ------------------------------------------------------------
 template <bool Down, bool Tap>
-__global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_constant__ TcrParams p) {
+__global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(const __grid_constant__ TcrParams p) {
     using St = RowsStage<Down>;
     constexpr int CS = St::code_stages, SS = St::side_stages, QS = St::sc_stages, AS = St::a_stages;
     constexpr int R = St::regions;
@@ -609,11 +636,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
         }
         for (int s = 0; s < SS; ++s) {
             mbar_init(bars.side_full(s), 1);
-            mbar_init(bars.side_empty(s), kRowsEpiWarps + 1);   // + the MMAs' commit (B operand)
+            mbar_init(bars.side_empty(s), St::epi_warps + 1);   // + the MMAs' commit (B operand)
         }
         for (int s = 0; s < QS; ++s) {
             mbar_init(bars.sc_full(s), 1);
-            mbar_init(bars.sc_empty(s), kRowsEpiWarps);
+            mbar_init(bars.sc_empty(s), St::epi_warps);
         }
         for (int s = 0; s < AS; ++s) {
             mbar_init(bars.a_full(s), kRowsUnpackWarps);
@@ -621,7 +648,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
         }
         for (int r = 0; r < R; ++r) {
             mbar_init(bars.tm_full(r), 1);
-            mbar_init(bars.tm_empty(r), kRowsEpiWarps);
+            mbar_init(bars.tm_empty(r), St::epi_warps);
         }
         mbar_init(fin, 1);
         mbar_fence_init();
@@ -807,8 +834,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) tc_rows_kernel(const __grid_c
                 ok = rows_unpack<Down>(smem, bars, g, threadIdx.x - 64, rowmajor, lane, p.error);
     } else {
         // ---------------- epilogue ----------------
-        const int ew = warp - 2 - kRowsUnpackWarps;       // 0..15
-        const int quarter = warp & 3, chunk = ew >> 2;    // TMEM lane quarter, pair chunk of kRowsCW
+        const int ew = warp - 2 - kRowsUnpackWarps;       // 0 .. epi_warps - 1
+        const int quarter = warp & 3, chunk = ew >> 2;    // TMEM lane quarter, pair chunk of St::cw pairs
         const uint32_t tq = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         if (lane == 0)   // every region starts free
             for (int r = 0; r < R; ++r) mbar_arrive(bars.tm_empty(r));
