@@ -5,15 +5,15 @@ Contract (one JSON line from rank 0):
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
 Workload (synthetic, seeded):
-  config 2 (default): ragged decode batch of T=8 tokens, uniform top-10 routing
-  from logits ~N(0,1), 512 experts + 1 shared, H=2048, I=512, Q4_0 experts.
-  A step pushes the batch through a stack of L=48 MoE layers with independent
-  seeded weights (43.6 GB, far above the 126 MB L2), each layer adding its FFN
-  output into the residual stream: MoE-layer tokens/s = T * L * K / time.
-  config 1: T=1; config 3: T=4096 with Zipf(1.1) routing; config 5: T=32768
-  mixed batch.  (Config 4 -- 48 layers x 16 ubatches of 1024 tokens -- is
-  --config 4.)
-
+  config 4 (default, the largest single-GPU config): 16 micro-batches of 1,024
+  tokens through a stack of L=48 MoE layers with independent seeded weights
+  (43.6 GB, far above the 126 MB L2), uniform top-10 routing from logits
+  ~N(0,1), 512 experts + 1 shared, H=2048, I=512, Q4_0 experts; each layer
+  adds its FFN output into the residual stream: MoE-layer tokens/s =
+  tokens x layers x K / time.  config 1: decode T=1; config 2: ragged decode
+  T=8; config 3: T=4096 with Zipf(1.1) routing; config 5: T=32768 mixed
+  batch (8 layers).  With --gpus N > 1 (torchrun) the layer is
+  expert-parallel: rank r owns experts [r*512/N, (r+1)*512/N).
 Timing: W warm-up steps, then K steps bracketed by a barrier and
 torch.cuda.synchronize() on both sides, CUDA events on the launching stream,
 max over ranks.  Each step is one CUDA-graph replay of the L layer forwards.
