@@ -166,6 +166,30 @@ __device__ __forceinline__ float warp_tree_sum(float v) {
     for (int m = 1; m < 32; m <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
     return v;
 }
+// warp_tree_sum of V values at once (V a power of two <= 32), bit-identical
+// to V separate calls: recursive halving over masks 1 .. V/2 (at the level of
+// mask m a lane keeps the values whose index bit matches its lane bit and
+// sends the others, so every total is summed over the same lane pairs in the
+// same order), then a plain butterfly over the remaining masks; V - 1 + 5 -
+// log2(V) shuffles instead of 5 V.  On return lane l holds the total of
+// value l % V.
+template <int V>
+__device__ __forceinline__ float warp_tree_sum_n(float (&v)[V], int lane) {
+#pragma unroll
+    for (int m = 1, n = V; m < V; m <<= 1, n >>= 1) {
+        const bool hi = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = hi ? v[2 * i] : v[2 * i + 1];
+            const float keep = hi ? v[2 * i + 1] : v[2 * i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+        }
+    }
+    float t = v[0];
+#pragma unroll
+    for (int m = V; m < 32; m <<= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, m));
+    return t;
+}
 
 // The C library's expf, bit for bit: the reference's CPU SiLU computes
 // g / (1 + expf(-g)) (src/cpu_expert.cpp:248-259), and a middle Q8_1 that is

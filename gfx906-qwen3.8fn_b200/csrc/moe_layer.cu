@@ -191,7 +191,9 @@ int tiles_bound(int tokens, int has_shared) {
 size_t gate_up_smem(int H) { return static_cast<size_t>(kGemvTile) * H + kGemvTile * (H / 32) * 8 + kGemvTile * 32 * 4; }
 size_t down_smem(int I) { return static_cast<size_t>(kGemvTile) * I + kGemvTile * (I / 32) * 8 + 2 * kGemvTile * 4; }
 
-size_t stream_gu_smem(int H, int stages) { return 128 + 2 * kGemvTile * 32 * 4 + size_t(stages) * GuStage(H).bytes; }
+size_t stream_gu_smem(int H, int stages) {
+    return 128 + kGuGroupsMax * 2 * kGemvTile * 32 * 4 + size_t(stages) * GuStage(H).bytes;
+}
 constexpr int kGuStagesMax = 3;
 size_t stream_dn_smem(int I, int stages) { return 128 + size_t(stages) * DnStage(I).bytes; }
 
@@ -203,14 +205,16 @@ int configure_kernels(moe_layer_s *h, int H, int I) {
     MOE_CUDA(cudaFuncSetAttribute(down_kernel<kGemvTile>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(down_smem(I))));
     // The streaming kernels need at least two stages in shared memory.
-    h->gu_stages = stream_stages(GuStage(H).bytes + 256, kGuStagesMax);
+    h->gu_stages = stream_stages(GuStage(H).bytes + 1024, kGuStagesMax);   // + the middle buffers
     h->dn_stages = stream_stages(DnStage(I).bytes, 5);
     if (h->gu_stages < 2 || h->dn_stages < 2) h->gu_stages = h->dn_stages = 0;
     if (h->gu_stages) {
         const int gu = static_cast<int>(stream_gu_smem(H, h->gu_stages));
         const int dn = static_cast<int>(stream_dn_smem(I, h->dn_stages));
-        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
-        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
+        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
+        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
+        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
+        MOE_CUDA(cudaFuncSetAttribute(stream_gate_up_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu));
         MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn));
         MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn));
         MOE_CUDA(cudaFuncSetAttribute(stream_down_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn));
@@ -401,8 +405,11 @@ int launch_experts(moe_layer_s *h, const moe_weights_s *w, float *out, int max_t
         if (stream_groups) {
             sp.stages = h->gu_stages;
             sp.stage_bytes = GuStage(L.hidden).bytes;
-            MOE_CUDA(launch_overlapped(tap ? stream_gate_up_kernel<true> : stream_gate_up_kernel<false>,
-                                       std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
+            // two items in flight per CTA when the CTAs have about one item each (decode of 1-2 tokens)
+            const bool two = gu_items <= 2 * h->sms;
+            auto gu_kernel = two ? (tap ? stream_gate_up_kernel<2, true> : stream_gate_up_kernel<2, false>)
+                                 : (tap ? stream_gate_up_kernel<1, true> : stream_gate_up_kernel<1, false>);
+            MOE_CUDA(launch_overlapped(gu_kernel, std::max(1, std::min(gu_items, h->sms)), kStreamThreads,
                                        stream_gu_smem(L.hidden, sp.stages), s, sp));
         }
         if (tc_tiles)

@@ -24,9 +24,8 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kStreamThreads = 32 + kConsumerThreads;
 constexpr int kGuRows = 32;    // gate rows and up rows per item: one Q8_1 middle block
 constexpr int kDnRows = 128;   // down rows per item
-constexpr int kGuWarpRows = kGuRows / kConsumerWarps;         // gate (and up) rows per consumer warp
+constexpr int kGuGroupsMax = 2;   // gate/up items in flight per CTA: 1 or 2 (stream_gate_up_kernel<G>)
 constexpr int kDnLaneRows = kDnRows / (8 * kConsumerWarps);   // down rows per consumer lane
-static_assert(kGuWarpRows >= 1 && kGuRows % kConsumerWarps == 0, "gate/up rows split evenly over warps");
 static_assert(kDnLaneRows >= 1 && kDnRows % (8 * kConsumerWarps) == 0, "down rows split evenly over lanes");
 constexpr int kMaxStages = 8;  // ring slots (two mbarriers each in the first 128 bytes)
 
@@ -145,18 +144,23 @@ __device__ __forceinline__ void stream_producer(const StreamParams &p, uint8_t *
         mbar_wait(&full[k % p.stages], (k / p.stages) & 1, p.error);
 }
 
-__device__ __forceinline__ void init_ring(uint64_t *full, uint64_t *empty, int stages) {
+__device__ __forceinline__ void init_ring(uint64_t *full, uint64_t *empty, int stages, int consumers) {
     if (threadIdx.x == 0) {
-        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], consumers); }
         mbar_fence_init();
     }
     __syncthreads();
 }
 
 // ---- gate/up + SiLU*up + Q8_1 middle ---------------------------------------
-// Consumer warp cw owns gate rows and up rows R*cw .. R*cw+R-1 of the slab
-// (R = kGuWarpRows); lane l owns blocks l, l+32, ...
-template <int N, bool Tap>
+// The consumer warps form G groups that take the CTA's items in turn (item i
+// goes to group i % G), so that G items are in flight; with two, one item's
+// latencies (activation loads, butterflies, the SiLU's exp lookups, the Q8_1
+// reductions) overlap the other's, which pays when a CTA has about one item
+// (decode of one or two tokens) and costs when it has many.  Warp cw of a
+// group owns gate rows and up rows R*cw .. R*cw+R-1 of the slab (R = 4 G);
+// lane l owns blocks l, l+32, ...
+template <int N, int R, bool Tap>
 __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_t *st, const GuStage &L,
                                              const int4 *const *xr, const float2 *const *sr, int cw, int lane,
                                              uint64_t *empty_bar, float *mid, const ItemTap &tap) {
@@ -165,79 +169,95 @@ __device__ __forceinline__ void gate_up_item(const StreamParams &p, const uint8_
     const uint4 *uc = reinterpret_cast<const uint4 *>(st + L.ucodes);
     const uint16_t *gs = reinterpret_cast<const uint16_t *>(st + L.gsc);
     const uint16_t *us = reinterpret_cast<const uint16_t *>(st + L.usc);
-    constexpr int R = kGuWarpRows;
     // Every (row, pair) value in the reference's MMVQ reduction order, so the
     // middle Q8_1 is bit-identical to the reference CPU expert's.  Lane l takes
     // the blocks b % 64 in {l, l + 32}: a0 accumulates b % 64 == l, a1 b % 64 ==
     // l + 32, each as (fragment 0, fragment 1); rows 0..R-1 gate, R..2R-1 up.
-    float acc[2 * R][N];
+    // After each pair's butterflies lane r < R holds gate and up of row R*cw + r.
+    static_assert(R <= 32, "a matrix's rows fit one reduce-scatter");
+    float gsel[N], usel[N];
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-        uint64_t a0[2 * R], a1[2 * R];
 #pragma unroll
-        for (int r = 0; r < 2 * R; ++r) a0[r] = a1[r] = 0ull;
-        for (int b0 = lane; b0 < nb; b0 += 64) {
+        for (int mtx = 0; mtx < 2; ++mtx) {   // gate rows, then up rows
+            const uint4 *cd = mtx ? uc : gc;
+            const uint16_t *sd = mtx ? us : gs;
+            uint64_t a0[R], a1[R];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int b = b0 + 32 * half;
-                if (b >= nb) break;
-                const int4 lo = __ldg(xr[j] + 2 * b), hi = __ldg(xr[j] + 2 * b + 1);
-                const float2 sc = __ldg(sr[j] + b);
-                const float m4 = -(4.0f * sc.y);
-                const uint64_t d8 = pkf2(sc.x, sc.x), m4p = pkf2(m4, m4);
+            for (int r = 0; r < R; ++r) a0[r] = a1[r] = 0ull;
+            for (int b0 = lane; b0 < nb; b0 += 64) {
 #pragma unroll
-                for (int r = 0; r < 2 * R; ++r) {
-                    const int blk = (cw * R + (r % R)) * nb + b;
-                    const uint4 w = r < R ? gc[blk] : uc[blk];
-                    const float d4 = h2f(r < R ? gs[blk] : us[blk]);
-                    int f0, f1;
-                    frag_dots(w, lo, hi, f0, f1);
-                    const uint64_t dots = pkf2(small_int_to_float(f0), small_int_to_float(f1));
-                    if (half) a1[r] = mmvq_term2(dots, pkf2(d4, d4), d8, m4p, a1[r]);
-                    else a0[r] = mmvq_term2(dots, pkf2(d4, d4), d8, m4p, a0[r]);
-                    if constexpr (Tap) {
-                        if (tap.dst0) tap.put(r < R ? tap.dst0 : tap.dst1, j, cw * R + (r % R), b, f0 + f1);
+                for (int half = 0; half < 2; ++half) {
+                    const int b = b0 + 32 * half;
+                    if (b >= nb) break;
+                    const int4 lo = __ldg(xr[j] + 2 * b), hi = __ldg(xr[j] + 2 * b + 1);
+                    const float2 sc = __ldg(sr[j] + b);
+                    const float m4 = -(4.0f * sc.y);
+                    const uint64_t d8 = pkf2(sc.x, sc.x), m4p = pkf2(m4, m4);
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const int blk = (cw * R + r) * nb + b;
+                        const uint4 w = cd[blk];
+                        const float d4 = h2f(sd[blk]);
+                        int f0, f1;
+                        frag_dots(w, lo, hi, f0, f1);
+                        const uint64_t dots = pkf2(small_int_to_float(f0), small_int_to_float(f1));
+                        if (half) a1[r] = mmvq_term2(dots, pkf2(d4, d4), d8, m4p, a1[r]);
+                        else a0[r] = mmvq_term2(dots, pkf2(d4, d4), d8, m4p, a0[r]);
+                        if constexpr (Tap) {
+                            if (tap.dst0) tap.put(mtx ? tap.dst1 : tap.dst0, j, cw * R + r, b, f0 + f1);
+                        }
                     }
                 }
             }
-        }
+            float leaf[R];
 #pragma unroll
-        for (int r = 0; r < 2 * R; ++r) acc[r][j] = warp_tree_sum(mmvq_leaf(a0[r], a1[r]));
+            for (int r = 0; r < R; ++r) leaf[r] = mmvq_leaf(a0[r], a1[r]);
+            const float tot = warp_tree_sum_n<R>(leaf, lane);   // lane l: row l % R
+            if (mtx) usel[j] = tot;
+            else gsel[j] = tot;
+        }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar);   // slab fully read by this warp
     // SiLU(gate) * up with the reference's sanitisation (session_ops.hip:250-262):
-    // lane r < R finishes row R*cw + r.
+    // lane r < R finishes row R*cw + r, the exponentials of the item's pairs together.
     if (lane < R) {
+        int fl[N];
+        float gv[N], uv[N], ng[N], ex[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-            float g = acc[0][j], u = acc[R][j];
+            fl[j] = 0;
+            gv[j] = operand(gsel[j], fl[j]);
+            uv[j] = operand(usel[j], fl[j]);
+            ng[j] = -gv[j];
+        }
+        expf_ref_n<N>(ng, ex);
 #pragma unroll
-            for (int r = 1; r < R; ++r)
-                if (lane == r) { g = acc[r][j]; u = acc[R + r][j]; }
-            int flags = 0;
-            g = operand(g, flags);
-            u = operand(u, flags);
-            const float act = arithmetic(__fdiv_rn(g, __fadd_rn(1.0f, expf_ref(-g))), flags);
-            const float v = arithmetic(__fmul_rn(act, u), flags);
+        for (int j = 0; j < N; ++j) {
+            int flags = fl[j];
+            const float act = arithmetic(__fdiv_rn(gv[j], __fadd_rn(1.0f, ex[j])), flags);
+            const float v = arithmetic(__fmul_rn(act, uv[j]), flags);
             mid[j * 32 + cw * R + lane] = flags ? 0.0f : v;
             report(flags, p.error);
         }
     }
 }
 
-template <bool Tap>
+template <int G, bool Tap>
 __global__ void __launch_bounds__(kStreamThreads, 1)
 stream_gate_up_kernel(StreamParams p) {
+    static_assert(G >= 1 && G <= kGuGroupsMax && kConsumerWarps % G == 0, "consumer groups");
+    constexpr int kGroupWarps = kConsumerWarps / G, R = kGuRows / kGroupWarps;
     extern __shared__ __align__(128) uint8_t smem[];
     const int H = p.layout.hidden, I = p.layout.inter, nb = H / 32, slabs = I / kGuRows;
     const GuStage L(H);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
-    float *smid = reinterpret_cast<float *>(smem + 128);                 // [2][kGemvTile][32]
-    uint8_t *stages = smem + 128 + 2 * kGemvTile * 32 * 4;
+    float *smid = reinterpret_cast<float *>(smem + 128);                 // [groups][2][kGemvTile][32]
+    uint8_t *stages = smem + 128 + kGuGroupsMax * 2 * kGemvTile * 32 * 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    init_ring(full, empty, p.stages);
+    init_ring(full, empty, p.stages, kGroupWarps);
     grid_dependency_wait();     // tile list and x codes of the routing kernels
     grid_launch_dependents();   // the down kernel may take SMs as this grid's CTAs finish
     const ItemOrder order = item_order(p.num_tiles, slabs);
@@ -258,11 +278,12 @@ stream_gate_up_kernel(StreamParams p) {
         return;
     }
 
-    const int cw = warp - 1;
+    const int grp = (warp - 1) / kGroupWarps, cw = (warp - 1) % kGroupWarps;
     bool failed = false;
     int i = 0;
     const int tap_base = (Tap && p.tap.expert >= 0) ? *p.tap.pair0 : 0;
     for (int pos = blockIdx.x; pos < order.total; pos += gridDim.x, ++i) {
+        if (i % G != grp) continue;   // the other group's item
         const int item = order(pos);
         const TileRec rec = load_tile(p.tiles + item / slabs);
         const int n = rec.n < kGemvTile ? rec.n : kGemvTile;
@@ -280,7 +301,7 @@ stream_gate_up_kernel(StreamParams p) {
         }
         const int s = i % p.stages;
         if (!failed && !mbar_wait(&full[s], (i / p.stages) & 1, p.error)) failed = true;
-        float *mid = smid + (i & 1) * kGemvTile * 32;
+        float *mid = smid + (grp * 2 + ((i / G) & 1)) * kGemvTile * 32;
         ItemTap tap;
         if (Tap && rec.e == p.tap.expert) {
             tap.dst0 = p.tap.gate;
@@ -294,16 +315,16 @@ stream_gate_up_kernel(StreamParams p) {
         if (!failed) {
             const uint8_t *st = stages + static_cast<size_t>(s) * p.stage_bytes;
             switch (n) {
-            case 1: gate_up_item<1, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
-            case 2: gate_up_item<2, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
-            case 3: gate_up_item<3, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
-            default: gate_up_item<4, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
+            case 1: gate_up_item<1, R, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
+            case 2: gate_up_item<2, R, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
+            case 3: gate_up_item<3, R, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
+            default: gate_up_item<4, R, Tap>(p, st, L, xr, sr, cw, lane, &empty[s], mid, tap); break;
             }
         }
-        named_barrier(1, kConsumerThreads);         // every consumer warp, even after a failed wait
+        named_barrier(1 + grp, kGroupWarps * 32);   // every warp of the group, even after a failed wait
         if (failed) continue;
         const int slab = item % slabs;
-        for (int j = cw; j < n; j += kConsumerWarps) {
+        for (int j = cw; j < n; j += kGroupWarps) {
             const Q8Lane q = quantize_lane(mid[j * 32 + lane]);
             const size_t pair = static_cast<size_t>(rec.p0 + j);
             p.mid.codes[pair * I + slab * 32 + lane] = q.code;
@@ -448,7 +469,7 @@ stream_down_kernel(StreamParams p) {
     uint64_t *empty = full + kMaxStages;
     uint8_t *stages = smem + 128;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    init_ring(full, empty, p.stages);
+    init_ring(full, empty, p.stages, kConsumerWarps);
     grid_launch_dependents();   // the next layer's routing CTAs may take the SMs' spare room and wait
     const ItemOrder order = item_order(p.num_tiles, slabs);
 

@@ -1,8 +1,9 @@
 """Bit-exact per-block dot parity of the kernels the forward actually runs.
 
 moe_debug_block_dots runs an ordinary forward through the same kernels a
-batch of that size uses -- the streaming dp4a kernels at decode sizes, the
-tcgen05 tensor-core kernels above -- and records, for one expert's pairs, every
+batch of that size uses -- the streaming dp4a kernels at decode sizes (two
+items in flight per CTA at T=1, one at T=8), the tcgen05 tensor-core kernels
+above -- and records, for one expert's pairs, every
 per-block int32 dot those kernels formed plus the middle Q8_1 the gate/up
 kernel produced.  The checks mirror the reference's own producer-kernel
 comparison against its CPU expert (src/cpu_expert_shadow.hip:333-341) and its
@@ -68,7 +69,8 @@ def tap_and_check(O, torch, c, expert, max_pairs=None):
     return n
 
 
-@pytest.mark.parametrize("T,kind,pick", [(8, "normal", "first"), (8, "normal", "shared"),
+@pytest.mark.parametrize("T,kind,pick", [(1, "normal", "first"), (1, "normal", "shared"),
+                                         (8, "normal", "first"), (8, "normal", "shared"),
                                          (1024, "normal", "largest"), (1024, "normal", "smallest"),
                                          (1024, "normal", "shared"), (4096, "zipf", "largest"),
                                          (4096, "zipf", "median")])

@@ -11,7 +11,9 @@ The test calls it through the C ABI twice in a row per case -- up to the
 array's 1024-token limit, and a skewed routing whose tile list nears the
 array's tile capacity -- checks that the device's free memory does not change
 across a call, and compares every output with the allocating entry point
-(moe_route through a layer workspace).  Routing results are compared exactly
+(moe_route through a layer workspace).  It also captures the call in a CUDA
+graph (after one eager call, as the header requires) and replays the graph
+on new logits written into the captured input.  Routing results are compared exactly
 -- the tolerance the other routing tests use.  This file is collected last on
 purpose.
 """
@@ -58,12 +60,7 @@ def _raw_call(pkg, torch, logits, outs):
 @pytest.mark.parametrize("T,kind", [(8, "normal"), (300, "normal"), (1024, "normal"), (1024, "skewed")])
 def test_noalloc_route_matches_allocating_route_twice(pkg, torch, T, kind):
     layer = pkg.MoeLayer(pkg.make_desc(max_tokens=T))
-    outs = dict(ids=torch.empty(T, 10, dtype=torch.int32, device="cuda"),
-                weights=torch.empty(T, 10, device="cuda"),
-                offsets=torch.empty(513, dtype=torch.int32, device="cuda"),
-                token=torch.empty(T * 10, dtype=torch.int32, device="cuda"),
-                rank=torch.empty(T * 10, dtype=torch.int32, device="cuda"),
-                error=torch.zeros(1, dtype=torch.int32, device="cuda"))
+    outs = _outputs(torch, T)
     # the first call on a device resolves the static array's address; after it,
     # calls allocate nothing: the device's free memory is unchanged around them
     _raw_call(pkg, torch, _logits(torch, T, kind, 1), outs)
@@ -86,6 +83,43 @@ def test_noalloc_route_matches_allocating_route_twice(pkg, torch, T, kind):
         if T == 1024:   # the tile list (<= 4 pairs per tile) nears the array's 3072-tile capacity
             counts = np.diff(want["offsets"].cpu().numpy())
             assert int(np.sum((counts + 3) // 4)) > 2600
+
+
+def _outputs(torch, T):
+    return dict(ids=torch.empty(T, 10, dtype=torch.int32, device="cuda"),
+                weights=torch.empty(T, 10, device="cuda"),
+                offsets=torch.empty(513, dtype=torch.int32, device="cuda"),
+                token=torch.empty(T * 10, dtype=torch.int32, device="cuda"),
+                rank=torch.empty(T * 10, dtype=torch.int32, device="cuda"),
+                error=torch.zeros(1, dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("T", [8, 300])
+def test_noalloc_route_captured_in_cuda_graph(pkg, torch, T):
+    layer = pkg.MoeLayer(pkg.make_desc(max_tokens=T))
+    outs = _outputs(torch, T)
+    logits = torch.empty(T, 512, device="cuda")
+    logits.copy_(_logits(torch, T, "normal", 5))
+    _raw_call(pkg, torch, logits, outs)          # the eager first call resolves the array's address
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):   # the call is enqueued on the capturing stream
+        _raw_call(pkg, torch, logits, outs)
+    for replay in range(2):
+        logits.copy_(_logits(torch, T, "normal", 77 + replay))
+        outs["error"].zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        want = layer.route(logits)
+        torch.cuda.synchronize()
+        assert int(outs["error"].item()) == 0
+        assert np.array_equal(outs["ids"].cpu().numpy(), want["ids"].cpu().numpy())
+        assert np.array_equal(_bits(outs["weights"]), _bits(want["weights"]))
+        assert np.array_equal(outs["offsets"].cpu().numpy(), want["offsets"].cpu().numpy())
+        assert np.array_equal(outs["token"].cpu().numpy(), want["token"].cpu().numpy())
+        assert np.array_equal(outs["rank"].cpu().numpy(), want["rank"].cpu().numpy())
+    del graph
 
 
 def test_noalloc_python_wrapper_checks_arguments(pkg, torch):
