@@ -15,7 +15,7 @@
 namespace qmoe {
 
 constexpr int kChunk = 32;         // tokens per routing chunk (one bit each in a 32-bit mask)
-constexpr int kRouteThreads = 256; // 8 warps; each warp routes tokens w, w+8, w+16, w+24 of a chunk
+constexpr int kRouteThreads = 1024; // 32 warps: one per token of a chunk
 
 // Exponential used by the router softmax.  The same operation sequence is
 // the specification in the CPU oracle: Cody-Waite reduction with ln2 split
