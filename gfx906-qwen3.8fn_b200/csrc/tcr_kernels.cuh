@@ -57,7 +57,7 @@
 namespace qmoe {
 
 constexpr int kRowsM = 128;            // weight rows per MMA (TMEM lanes)
-constexpr int kRowsKB = 4;             // quantisation blocks per pipeline stage
+constexpr int kRowsKB = 4;             // quantisation blocks per gate/up pipeline stage
 constexpr int kRowsUnpackWarps = 2;
 constexpr int kRowsMinGroup = 1;       // batches above decode size: every group on this path
 constexpr int kRowsHidden = 2048;      // the gate/up stage order pairs blocks b and b + 32 of 64
@@ -112,30 +112,31 @@ struct RowsStage {
     static constexpr int epi_warps = Down ? 8 : 16;
     static constexpr int cw = kTcTile * 4 / epi_warps;
     static constexpr int threads = 32 * (2 + kRowsUnpackWarps + epi_warps);
+    static constexpr int kb = Down ? 8 : kRowsKB;                             // quantisation blocks per stage
     static constexpr int wins = Down ? 1 : 2;                                 // 8-block scale windows per group
-    static constexpr int spw = Down ? 2 : 4;                                  // stages per scale group
+    static constexpr int spw = Down ? 1 : 4;                                  // stages per scale group
     static constexpr int brows = Down ? kTcTile : 2 * kTcTile;                // B rows per block
     static constexpr int bpc = Down ? 4 : 2;                                  // blocks per code copy
     static constexpr int cwords = 2;                                          // constants per pair and block
-    static constexpr uint32_t codes_bytes = kRowsKB * kRowsM * 16;
-    static constexpr uint32_t b = 0;                                          // side: [4][brows][32]
-    static constexpr uint32_t bsc = b + kRowsKB * brows * 32;                 // side: [4][cwords][kTcTile] fp32
-    static constexpr uint32_t side_bytes = bsc + kRowsKB * cwords * kTcTile * 4;
+    static constexpr uint32_t codes_bytes = kb * kRowsM * 16;
+    static constexpr uint32_t b = 0;                                          // side: [kb][brows][32]
+    static constexpr uint32_t bsc = b + kb * brows * 32;                      // side: [kb][cwords][kTcTile] fp32
+    static constexpr uint32_t side_bytes = bsc + kb * cwords * kTcTile * 4;
     static constexpr uint32_t sc_bytes = wins * kRowsM * 16;                  // [wins][128][8] half
-    static constexpr uint32_t a_bytes = kRowsKB * kRowsM * 32;                // unpacked A tiles
-    static constexpr int code_stages = 8;                // powers of two: cheap slot and phase arithmetic
+    static constexpr uint32_t a_bytes = kb * kRowsM * 32;                     // unpacked A tiles
+    static constexpr int code_stages = Down ? 4 : 8;     // powers of two: cheap slot and phase arithmetic
     static constexpr int side_stages = 8;
     static constexpr int sc_stages = 4;
-    static constexpr int a_stages = 4;
+    static constexpr int a_stages = Down ? 3 : 4;
     static constexpr uint32_t codes_off = 2048;
     static constexpr uint32_t side_off = codes_off + code_stages * codes_bytes;
     static constexpr uint32_t sc_off = (side_off + side_stages * side_bytes + 1023) / 1024 * 1024;
     static constexpr uint32_t a_off = sc_off + sc_stages * sc_bytes;
     static constexpr uint32_t magic_off = a_off + a_stages * a_bytes;        // bf16 A [128][16], B [128][16]
     static constexpr uint32_t smem = magic_off + 2 * kRowsM * 32;
-    // TMEM columns per region = one stage: 4 blocks x brows (down 16 pairs,
-    // gate/up 16 pairs x 2 fragments)
-    static constexpr int reg_cols = kRowsKB * brows;
+    // TMEM columns per region = one stage: kb blocks x brows (down 8 x 16
+    // pairs, gate/up 4 x 16 pairs x 2 fragments)
+    static constexpr int reg_cols = kb * brows;
     static constexpr int regions = 512 / reg_cols;
     static_assert(side_bytes % 128 == 0 && sc_bytes % 1024 == 0 && codes_bytes % 1024 == 0, "ring alignment");
     static_assert((side_off % 1024) == 0 && (sc_off % 1024) == 0 && (a_off % 1024) == 0, "ring alignment");
@@ -280,7 +281,7 @@ __device__ __forceinline__ bool rows_unpack(uint8_t *smem, const RowsBars &b, in
     if (g >= St::a_stages && !mbar_wait(b.a_empty(sa), ((g / St::a_stages) & 1) ^ 1, error)) return false;
     const uint8_t *raw = smem + St::codes_off + sr * St::codes_bytes;
     uint8_t *a = smem + St::a_off + sa * St::a_bytes;
-    constexpr int kUnits = kRowsKB * kRowsM;
+    constexpr int kUnits = St::kb * kRowsM;
     static_assert(kUnits % kThreads == 0, "whole unpack rounds");
 #pragma unroll
     for (int i = 0; i < kUnits / kThreads; ++i) {
@@ -531,30 +532,30 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
     int tap_base = 0;
     if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
 
-    for (int ks = 0; ks < nb / kRowsKB; ++ks, ++sq.g) {
+    for (int ks = 0; ks < nb / St::kb; ++ks, ++sq.g) {
         const int s = sq.g % St::side_stages;
         const uint8_t *st = smem + St::side_off + s * St::side_bytes;
         if (!mbar_wait(bars.side_full(s), (sq.g / St::side_stages) & 1, p.error)) return false;
         const int q = sq.g / St::spw, qs = q % St::sc_stages;
         if (ks % St::spw == 0 && !mbar_wait(bars.sc_full(qs), (q / St::sc_stages) & 1, p.error)) return false;
-        // d4 of blocks 4ks..4ks+3: columns (ks & 1) * 4 .. + 3 of the 8-block window
-        const uint2 d4q =
-            *reinterpret_cast<const uint2 *>(smem + St::sc_off + qs * St::sc_bytes + lrow * 16 + (ks & 1) * 8);
+        // d4 of the stage's blocks 8ks..8ks+7: the whole 8-block window of this row
+        static_assert(St::kb == 8 && St::spw == 1, "one scale window per stage");
+        const uint4 d4q = *reinterpret_cast<const uint4 *>(smem + St::sc_off + qs * St::sc_bytes + lrow * 16);
         const int r = static_cast<int>(sq.k % R);
         ++sq.k;
         if (!mbar_wait(bars.tm_full(r), ((sq.k - 1) / R) & 1, p.error)) return false;
         tc_fence_after();
-        uint32_t v[kRowsKB][CW];
+        uint32_t v[St::kb][CW];
 #pragma unroll
-        for (int kb = 0; kb < kRowsKB; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
+        for (int kb = 0; kb < St::kb; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
         tmem_wait_ld();
 #pragma unroll
-        for (int kb = 0; kb < kRowsKB; ++kb) tie8(v[kb]);
+        for (int kb = 0; kb < St::kb; ++kb) tie8(v[kb]);
         region_release(bars.tm_empty(r), lane);
         const float *cb = reinterpret_cast<const float *>(st + St::bsc);
 #pragma unroll
-        for (int kb = 0; kb < kRowsKB; ++kb) {
-            const uint32_t hw = (kb < 2) ? d4q.x : d4q.y;
+        for (int kb = 0; kb < St::kb; ++kb) {
+            const uint32_t hw = kb < 2 ? d4q.x : kb < 4 ? d4q.y : kb < 6 ? d4q.z : d4q.w;
             const float d4 = (kb & 1) ? hi_half(hw) : lo_half(hw);
             const uint64_t d4p = pkf2(d4, d4);
             const uint4 d8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + pc0);
@@ -576,7 +577,7 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
                         const int j = 2 * u + jj;
                         const int pl = p0 + pc0 + j - tap_base;
                         if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs)
-                            p.tap.down[(static_cast<size_t>(pl) * H + row) * nb + ks * kRowsKB + kb] =
+                            p.tap.down[(static_cast<size_t>(pl) * H + row) * nb + ks * St::kb + kb] =
                                 static_cast<int32_t>(tt[jj]);
                     }
                 }
@@ -621,7 +622,7 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
     constexpr int R = St::regions;
     extern __shared__ __align__(128) uint8_t smem[];
     const int H = p.hidden, I = p.inter;
-    const int K = Down ? I : H, nb = K / 32, nodes = nb / kRowsKB;
+    const int K = Down ? I : H, nb = K / 32, nodes = nb / St::kb;
     const int ksteps = Down ? nodes : 2 * nodes;     // gate/up: the gate pass, then the up pass
     const int slabs = (Down ? H : I) / kRowsM;
     RowsBars bars{reinterpret_cast<uint64_t *>(smem)};
@@ -685,7 +686,7 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                 tma_prefetch_map(&p.maps.codes[Down ? 2 : m]);
                 tma_prefetch_map(&p.maps.scales[Down ? 2 : m]);
             }
-            constexpr uint32_t bbytes = kRowsKB * St::brows * 32, sbytes = kRowsKB * St::cwords * kTcTile * 4;
+            constexpr uint32_t bbytes = St::kb * St::brows * 32, sbytes = St::kb * St::cwords * kTcTile * 4;
             const size_t bslot = Down ? tc_dn_slot(K) : tc_gu_slot(K);
             const size_t sslot = Down ? tc_dn_sc_slot(K) : tc_gu_sc_slot(K);
             const int total_g = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x * ksteps : 0;
@@ -715,8 +716,8 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                     uint8_t *dst0 = smem + St::codes_off + c * St::codes_bytes;
                     mbar_arrive_expect_tx(bars.code_full(c), St::codes_bytes);
                     // down blocks 4kk..4kk+3 in one copy; gate/up blocks (2kk, 2kk+1), then (+32, +33)
-                    for (int cp = 0; cp < kRowsKB / St::bpc; ++cp) {
-                        const int b0 = Down ? kRowsKB * kk : 2 * kk + 32 * cp;
+                    for (int cp = 0; cp < St::kb / St::bpc; ++cp) {
+                        const int b0 = Down ? St::kb * kk + St::bpc * cp : 2 * kk + 32 * cp;
                         uint8_t *dst = dst0 + cp * St::bpc * kRowsM * 16;
                         if (p.raw_rowmajor)
                             tma_load_3d(dst, &p.maps.codes[mat], b0 * 16, cc_.slab * kRowsM, cc_.e, bars.code_full(c));
@@ -740,13 +741,13 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                                  bbytes, bars.side_full(sd));
                         bulk_g2s(st + St::bsc,
                                  p.bsc_arr + static_cast<size_t>(cs_.tile) * sslot +
-                                     static_cast<size_t>(ks) * kRowsKB * St::cwords * kTcTile,
+                                     static_cast<size_t>(ks) * St::kb * St::cwords * kTcTile,
                                  sbytes, bars.side_full(sd));
                         if (group) {
                             // gate/up blocks 8j and 32 + 8j of the stage's matrix, down blocks 8j
                             mbar_arrive_expect_tx(bars.sc_full(qs), St::sc_bytes);
                             for (int w = 0; w < St::wins; ++w) {
-                                const int b0 = Down ? kRowsKB * ks : 2 * ks + 32 * w;
+                                const int b0 = Down ? St::kb * ks : 2 * ks + 32 * w;
                                 tma_load_3d(smem + St::sc_off + qs * St::sc_bytes + w * kRowsM * 16, &p.maps.scales[mat],
                                             b0 & ~7, cs_.slab * kRowsM, cs_.e, bars.sc_full(qs));
                             }
@@ -809,7 +810,7 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                         // [brows kb, brows (kb + 1))
                         mma_bf16(tmem + r * St::reg_cols, amg, bmg, idesc_mg);
 #pragma unroll
-                        for (int kb = 0; kb < kRowsKB; ++kb) {
+                        for (int kb = 0; kb < St::kb; ++kb) {
                             const uint64_t ad = smem_desc(a_st + kb * kRowsM * 32, 128, 256);
                             const uint64_t bd = smem_desc(b_st + kb * St::brows * 32, 128, 256);
                             mma_i8(tmem + r * St::reg_cols + kb * St::brows, ad, bd, idesc, 1u);
