@@ -260,10 +260,9 @@ EncodeTiledFn encode_tiled() {
 
 // Tensor maps over every expert of a weights object for the TMA loads of the
 // tensor-core kernels: per matrix the code bytes as {16 bytes, row, block,
-// expert} (box 16 x 128 rows x 2 blocks for gate/up, 4 for down: a copy lands
-// block-major, each block's 128 rows contiguous) -- or, where the driver
-// refuses that stride order, as {row bytes, row, expert} (box 32 or 64 bytes x
-// 128 rows) -- and the half scales as {block, row, expert} (box 8 blocks x
+// expert} (box 16 x 128 rows x 4 blocks: a copy lands block-major, each
+// block's 128 rows contiguous) -- or, where the driver refuses that stride
+// order, as {row bytes, row, expert} (box 64 bytes x 128 rows) -- and the half scales as {block, row, expert} (box 8 blocks x
 // 128 rows).  Weights of other shapes (the gate/up stage order is that of 64
 // blocks, H = 2048; I a multiple of 256) or with Q4_1 down matrices run every
 // group on the streaming kernels instead.
@@ -287,14 +286,14 @@ int build_maps(moe_weights_s *w) {
             if (!rowmajor) {
                 const cuuint64_t dims[4] = {16, rows[m], nbm[m], E};
                 const cuuint64_t strides[3] = {nbm[m] * 16, 16, EB};
-                const cuuint32_t box[4] = {16, kRowsM, cuuint32_t(m == 2 ? 4 : 2), 1};
+                const cuuint32_t box[4] = {16, kRowsM, cuuint32_t(kRowsBlocksPerCopy), 1};
                 r = enc(&w->maps.codes[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w->base + code_off[m], dims, strides, box,
                         one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             } else {
                 const cuuint64_t dims[3] = {nbm[m] * 16, rows[m], E};
                 const cuuint64_t strides[2] = {nbm[m] * 16, EB};
-                const cuuint32_t box[3] = {cuuint32_t(m == 2 ? 64 : 32), kRowsM, 1};
+                const cuuint32_t box[3] = {cuuint32_t(16 * kRowsBlocksPerCopy), kRowsM, 1};
                 r = enc(&w->maps.codes[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w->base + code_off[m], dims, strides, box,
                         one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -77,8 +77,8 @@ __host__ __device__ constexpr size_t tc_dn_slot(int K) { return static_cast<size
 __host__ __device__ constexpr size_t tc_gu_sc_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile; }
 __host__ __device__ constexpr size_t tc_dn_sc_slot(int K) { return static_cast<size_t>(K / 32) * 2 * kTcTile; }
 // Position of gate/up block b (of 64) in the stage order: stage k holds blocks
-// 2k, 2k+1, 2k+32, 2k+33.
-__host__ __device__ constexpr int tc_gu_pos(int b) { return 4 * ((b & 31) >> 1) + 2 * (b >> 5) + (b & 1); }
+// 4k..4k+3, then 4k+32..4k+35.
+__host__ __device__ constexpr int tc_gu_pos(int b) { return 8 * ((b & 31) >> 2) + 4 * (b >> 5) + (b & 3); }
 
 // Tensor-core path of one layer workspace: the tile list ({expert, first pair,
 // count, 0}: each group in tiles of kTcTile pairs, the last one partial) and

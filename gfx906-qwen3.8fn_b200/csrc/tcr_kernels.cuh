@@ -25,9 +25,9 @@
 // gives every epilogue warp its 4 pairs x 2 fragments as 8 adjacent columns
 // and the fp32 arithmetic runs as f32x2 over pairs; blocks b and b + 32 land
 // in one TMEM region and form the tree's leaves; a pipeline stage carries
-// blocks 2k, 2k+1, 2k+32, 2k+33 (one level-2 node of the tree), and the 16
-// nodes of an item are summed as a binary tree with a four-slot stack in
-// registers.  Each epilogue thread owns one weight row (its TMEM lane) of gate
+// blocks 4k..4k+3 and 4k+32..4k+35 (four leaves: one node two levels above
+// them), and the 8 nodes of a matrix are summed as a binary tree with a
+// four-slot stack in registers.  Each epilogue thread owns one weight row (its TMEM lane) of gate
 // and of up for 4 pairs; the item end runs SiLU(gate) * up and the Q8_1 of
 // each 32-row middle block (one warp = one block per pair: lane = element,
 // the reference's butterfly order) and writes the down pass's operand.
@@ -57,7 +57,8 @@
 namespace qmoe {
 
 constexpr int kRowsM = 128;            // weight rows per MMA (TMEM lanes)
-constexpr int kRowsKB = 4;             // quantisation blocks per gate/up pipeline stage
+constexpr int kRowsKB = 8;             // quantisation blocks per pipeline stage
+constexpr int kRowsBlocksPerCopy = 4;  // blocks per TMA code copy (gate/up: two copies per stage)
 constexpr int kRowsUnpackWarps = 2;
 constexpr int kRowsMinGroup = 1;       // batches above decode size: every group on this path
 constexpr int kRowsHidden = 2048;      // the gate/up stage order pairs blocks b and b + 32 of 64
@@ -95,13 +96,13 @@ constexpr int kRowsBarSlots = 16;   // entries per barrier array
 
 // Shared-memory rings of one CTA.  Each feeds its own consumers, so every
 // ring is released as soon as they are done with it:
-//   codes  the slab's raw Q4_0 codes of one stage (4 blocks x 128 rows x
+//   codes  the slab's raw Q4_0 codes of one stage (8 blocks x 128 rows x
 //          16 B of one matrix), read by the unpack warps;
 //   side   the tile's arranged activation operand (B, read by the MMAs) and
 //          per-pair constants (read by the epilogue) of one stage;
 //   scale  the weight rows' half scales of a stage group (gate/up: blocks
-//          8j..8j+7 and 32+8j..32+8j+7 of one matrix = 4 stages; down: blocks
-//          8j..8j+7 = 2 stages), read by the epilogue;
+//          8j..8j+7 and 32+8j..32+8j+7 of one matrix = 2 stages; down: blocks
+//          8j..8j+7 = 1 stage), read by the epilogue;
 //   A      the unpacked A operand of one stage (u8, K-major core matrices).
 template <bool Down>
 struct RowsStage {
@@ -112,11 +113,11 @@ struct RowsStage {
     static constexpr int epi_warps = Down ? 8 : 16;
     static constexpr int cw = kTcTile * 4 / epi_warps;
     static constexpr int threads = 32 * (2 + kRowsUnpackWarps + epi_warps);
-    static constexpr int kb = Down ? 8 : kRowsKB;                             // quantisation blocks per stage
+    static constexpr int kb = kRowsKB;                                        // quantisation blocks per stage
     static constexpr int wins = Down ? 1 : 2;                                 // 8-block scale windows per group
-    static constexpr int spw = Down ? 1 : 4;                                  // stages per scale group
+    static constexpr int spw = Down ? 1 : 2;                                  // stages per scale group
     static constexpr int brows = Down ? kTcTile : 2 * kTcTile;                // B rows per block
-    static constexpr int bpc = Down ? 4 : 2;                                  // blocks per code copy
+    static constexpr int bpc = kRowsBlocksPerCopy;                            // blocks per code copy
     static constexpr int cwords = 2;                                          // constants per pair and block
     static constexpr uint32_t codes_bytes = kb * kRowsM * 16;
     static constexpr uint32_t b = 0;                                          // side: [kb][brows][32]
@@ -124,10 +125,10 @@ struct RowsStage {
     static constexpr uint32_t side_bytes = bsc + kb * cwords * kTcTile * 4;
     static constexpr uint32_t sc_bytes = wins * kRowsM * 16;                  // [wins][128][8] half
     static constexpr uint32_t a_bytes = kb * kRowsM * 32;                     // unpacked A tiles
-    static constexpr int code_stages = Down ? 4 : 8;     // powers of two: cheap slot and phase arithmetic
-    static constexpr int side_stages = 8;
+    static constexpr int code_stages = 4;                // powers of two: cheap slot and phase arithmetic
+    static constexpr int side_stages = Down ? 8 : 4;
     static constexpr int sc_stages = 4;
-    static constexpr int a_stages = Down ? 3 : 4;
+    static constexpr int a_stages = 3;
     static constexpr uint32_t codes_off = 2048;
     static constexpr uint32_t side_off = codes_off + code_stages * codes_bytes;
     static constexpr uint32_t sc_off = (side_off + side_stages * side_bytes + 1023) / 1024 * 1024;
@@ -135,7 +136,7 @@ struct RowsStage {
     static constexpr uint32_t magic_off = a_off + a_stages * a_bytes;        // bf16 A [128][16], B [128][16]
     static constexpr uint32_t smem = magic_off + 2 * kRowsM * 32;
     // TMEM columns per region = one stage: kb blocks x brows (down 8 x 16
-    // pairs, gate/up 4 x 16 pairs x 2 fragments)
+    // pairs = 4 regions, gate/up 8 x 16 pairs x 2 fragments = 2 regions)
     static constexpr int reg_cols = kb * brows;
     static constexpr int regions = 512 / reg_cols;
     static_assert(side_bytes % 128 == 0 && sc_bytes % 1024 == 0 && codes_bytes % 1024 == 0, "ring alignment");
@@ -328,7 +329,9 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
                                                  int lane, int quarter, int chunk) {
     using St = RowsStage<false>;
     constexpr int R = St::regions, CW = St::cw, NP = kTcTile, U = CW / 2;
-    constexpr int kNodes = kRowsHidden / 32 / kRowsKB;        // 16 stages (level-2 nodes) per matrix
+    constexpr int kNodes = kRowsHidden / 32 / St::kb;        // 8 stages per matrix
+    constexpr int kLeaves = St::kb / 2;                      // leaves per stage: blocks b and b + 32
+    static_assert(kLeaves == 4, "a stage is one node two levels above the leaves");
     static_assert(CW == 4 || CW == 8, "one x8 / x16 load per block: 1 or 2 chunks x (4 pairs x 2 fragments)");
     const int I = p.inter;
     const int nb = kRowsHidden / 32, slabs = I / kRowsM;
@@ -339,7 +342,7 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
     const int lrow = quarter * 32 + lane;                     // row within the slab
     const int row = slab * kRowsM + lrow;                     // middle row of this lane
     const uint64_t zero2 = 0ull;
-    // binary-tree stack over the 16 level-2 nodes of the current matrix, per unit (s3 ends as the
+    // binary-tree stack over the 8 stage nodes of the current matrix, per unit (s3 ends as the
     // total); the gate totals wait in gt while the up pass runs
     uint64_t s0[U], s1[U], s2[U], s3[U], gt[U];
 #pragma unroll
@@ -354,56 +357,70 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
         if (!mbar_wait(bars.side_full(s), (sq.g / St::side_stages) & 1, p.error)) return false;
         const int q = sq.g / St::spw, qs = q % St::sc_stages;   // scale group (its windows stay for spw stages)
         if (kk % St::spw == 0 && !mbar_wait(bars.sc_full(qs), (q / St::sc_stages) & 1, p.error)) return false;
-        // d4 of this row: window 0 holds blocks 2kk, 2kk+1 at columns c0, c0+1, window 1 blocks 2kk+32, 2kk+33
-        const uint8_t *d4row = smem + St::sc_off + qs * St::sc_bytes + lrow * 16 + ((2 * kk) % 8) * 2;
+        // d4 of this row: window 0 holds blocks 4kk..4kk+3 at columns 4 (kk % 2) .., window 1 blocks 4kk+32..
+        const uint8_t *d4row = smem + St::sc_off + qs * St::sc_bytes + lrow * 16 + (kk & 1) * 8;
+        const uint2 d4w0 = *reinterpret_cast<const uint2 *>(d4row);
+        const uint2 d4w1 = *reinterpret_cast<const uint2 *>(d4row + kRowsM * 16);
         const int r = static_cast<int>(sq.k % R);
         if (!mbar_wait(bars.tm_full(r), (sq.k / R) & 1, p.error)) return false;
         tc_fence_after();
         const uint32_t tr = tq + r * St::reg_cols + chunk * 2 * CW;
-        uint64_t node[U], la[U];
+        uint64_t node[U], la[U], lc[U];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {   // leaf h: block 2kk+h (slot h) and 2kk+32+h (slot 2+h)
+        for (int h = 0; h < kLeaves; ++h) {   // leaf h: block 4kk+h (slot h) and 4kk+32+h (slot 4+h)
             // columns: per chunk of 4 pairs, fragment 0 of the pairs, then fragment 1
             uint32_t va[2 * CW], vb[2 * CW];
             if constexpr (CW == 8) {
                 tmem_ld16(tr + h * 32, va);
-                tmem_ld16(tr + (2 + h) * 32, vb);
+                tmem_ld16(tr + (kLeaves + h) * 32, vb);
                 tmem_wait_ld();
                 tie16(va);
                 tie16(vb);
             } else {
                 tmem_ld8(tr + h * 32, va);
-                tmem_ld8(tr + (2 + h) * 32, vb);
+                tmem_ld8(tr + (kLeaves + h) * 32, vb);
                 tmem_wait_ld();
                 tie8(va);
                 tie8(vb);
             }
-            if (h == 1) region_release(bars.tm_empty(r), lane);
-            // pair constants d8 and m4 = -4 s8 of block 2kk+h (slot h) and 2kk+32+h (slot 2+h), as pair units
-            const uint64_t *ka = reinterpret_cast<const uint64_t *>(
-                reinterpret_cast<const float *>(st + St::bsc) + h * 2 * NP + pc0);
-            const uint64_t *kb = reinterpret_cast<const uint64_t *>(
-                reinterpret_cast<const float *>(st + St::bsc) + (2 + h) * 2 * NP + pc0);
-            const float d4a = h2f(*reinterpret_cast<const uint16_t *>(d4row + 2 * h));
-            const float d4b = h2f(*reinterpret_cast<const uint16_t *>(d4row + kRowsM * 16 + 2 * h));
+            if (h == kLeaves - 1) region_release(bars.tm_empty(r), lane);
+            // pair constants d8 and m4 = -4 s8 of block 4kk+h (slot h) and 4kk+32+h (slot 4+h), as pair units
+            const uint4 *ka = reinterpret_cast<const uint4 *>(reinterpret_cast<const float *>(st + St::bsc) +
+                                                              h * 2 * NP + pc0);
+            const uint4 *kb = reinterpret_cast<const uint4 *>(reinterpret_cast<const float *>(st + St::bsc) +
+                                                              (kLeaves + h) * 2 * NP + pc0);
+            uint64_t d8a[U], m4a[U], d8b[U], m4b[U];
+#pragma unroll
+            for (int v = 0; v < U / 2; ++v) {
+                const uint4 xa = ka[v], ya = ka[NP / 4 + v], xb = kb[v], yb = kb[NP / 4 + v];
+                d8a[2 * v] = pk2(xa.x, xa.y), d8a[2 * v + 1] = pk2(xa.z, xa.w);
+                m4a[2 * v] = pk2(ya.x, ya.y), m4a[2 * v + 1] = pk2(ya.z, ya.w);
+                d8b[2 * v] = pk2(xb.x, xb.y), d8b[2 * v + 1] = pk2(xb.z, xb.w);
+                m4b[2 * v] = pk2(yb.x, yb.y), m4b[2 * v + 1] = pk2(yb.z, yb.w);
+            }
+            const uint32_t wa = (h < 2) ? d4w0.x : d4w0.y, wb = (h < 2) ? d4w1.x : d4w1.y;
+            const float d4a = (h & 1) ? hi_half(wa) : lo_half(wa);
+            const float d4b = (h & 1) ? hi_half(wb) : lo_half(wb);
             const uint64_t d4ap = pkf2(d4a, d4a), d4bp = pkf2(d4b, d4b);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 if (u >= units) break;
-                // exact fragment dots of the unit's two pairs: block a (2kk+h) and b (2kk+32+h)
+                // exact fragment dots of the unit's two pairs: block a (4kk+h) and b (4kk+32+h)
                 const int c0 = (u >> 1) * 8 + (u & 1) * 2;   // fragment 0 of the unit's pairs; fragment 1 at +4
                 const uint64_t ta0 = from_magic2(va[c0], va[c0 + 1]);
                 const uint64_t ta1 = from_magic2(va[c0 + 4], va[c0 + 5]);
                 const uint64_t tb0 = from_magic2(vb[c0], vb[c0 + 1]);
                 const uint64_t tb1 = from_magic2(vb[c0 + 4], vb[c0 + 5]);
-                const uint64_t d8a = ka[u], m4a = ka[NP / 2 + u], d8b = kb[u], m4b = kb[NP / 2 + u];
                 // MMVQ lanes 2b+f (terms of block a) and 2b+f+64 (block b), summed, then the fragments
-                const uint64_t leaf = add2(add2(mmvq_term2(ta0, d4ap, d8a, m4a, zero2),
-                                                mmvq_term2(tb0, d4bp, d8b, m4b, zero2)),
-                                           add2(mmvq_term2(ta1, d4ap, d8a, m4a, zero2),
-                                                mmvq_term2(tb1, d4bp, d8b, m4b, zero2)));
+                const uint64_t leaf = add2(add2(mmvq_term2(ta0, d4ap, d8a[u], m4a[u], zero2),
+                                                mmvq_term2(tb0, d4bp, d8b[u], m4b[u], zero2)),
+                                           add2(mmvq_term2(ta1, d4ap, d8a[u], m4a[u], zero2),
+                                                mmvq_term2(tb1, d4bp, d8b[u], m4b[u], zero2)));
+                // node kk = (L(4kk) + L(4kk+1)) + (L(4kk+2) + L(4kk+3))
                 if (h == 0) la[u] = leaf;
-                else node[u] = add2(la[u], leaf);   // node kk = L(2kk) + L(2kk+1)
+                else if (h == 1) la[u] = add2(la[u], leaf);
+                else if (h == 2) lc[u] = leaf;
+                else node[u] = add2(la[u], add2(lc[u], leaf));
                 if constexpr (Tap) {
                     float a0, a1, c0, c1, b0, b1, e0, e1;
                     upk2(ta0, a0, a1);
@@ -418,8 +435,8 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
                         if (e == p.tap.expert && pc0 + j < n && pl >= 0 && pl < p.tap.max_pairs) {
                             int32_t *dst = m == 0 ? p.tap.gate : p.tap.up;
                             const size_t base = (static_cast<size_t>(pl) * I + row) * nb;
-                            dst[base + 2 * kk + h] = static_cast<int32_t>(da[jj]);
-                            dst[base + 2 * kk + 32 + h] = static_cast<int32_t>(db[jj]);
+                            dst[base + 4 * kk + h] = static_cast<int32_t>(da[jj]);
+                            dst[base + 4 * kk + 32 + h] = static_cast<int32_t>(db[jj]);
                         }
                     }
                 }
@@ -430,7 +447,7 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
             mbar_arrive(bars.side_empty(s));
             if (kk % St::spw == St::spw - 1) mbar_arrive(bars.sc_empty(qs));
         }
-        // push node kk into the binary tree over kk = 0..15 (one warp-uniform branch nest)
+        // push node kk into the binary tree over kk = 0..7 (one warp-uniform branch nest)
         if (!(kk & 1)) {
 #pragma unroll
             for (int u = 0; u < U; ++u) s0[u] = node[u];
@@ -442,10 +459,7 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
             for (int u = 0; u < U; ++u) s2[u] = add2(s1[u], add2(s0[u], node[u]));
         } else {
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const uint64_t x = add2(s2[u], add2(s1[u], add2(s0[u], node[u])));
-                s3[u] = (kk & 8) ? add2(s3[u], x) : x;
-            }
+            for (int u = 0; u < U; ++u) s3[u] = add2(s2[u], add2(s1[u], add2(s0[u], node[u])));
             if (ks == kNodes - 1) {
 #pragma unroll
                 for (int u = 0; u < U; ++u) gt[u] = s3[u];
@@ -715,9 +729,9 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                     const int mat = Down ? 2 : cc_.ks / nodes, kk = cc_.ks % nodes, c = gc % CS;
                     uint8_t *dst0 = smem + St::codes_off + c * St::codes_bytes;
                     mbar_arrive_expect_tx(bars.code_full(c), St::codes_bytes);
-                    // down blocks 4kk..4kk+3 in one copy; gate/up blocks (2kk, 2kk+1), then (+32, +33)
+                    // down blocks 8kk..8kk+3, 8kk+4..8kk+7; gate/up blocks 4kk..4kk+3, then 4kk+32..4kk+35
                     for (int cp = 0; cp < St::kb / St::bpc; ++cp) {
-                        const int b0 = Down ? St::kb * kk + St::bpc * cp : 2 * kk + 32 * cp;
+                        const int b0 = Down ? St::kb * kk + St::bpc * cp : St::bpc * kk + 32 * cp;
                         uint8_t *dst = dst0 + cp * St::bpc * kRowsM * 16;
                         if (p.raw_rowmajor)
                             tma_load_3d(dst, &p.maps.codes[mat], b0 * 16, cc_.slab * kRowsM, cc_.e, bars.code_full(c));
@@ -747,7 +761,7 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                             // gate/up blocks 8j and 32 + 8j of the stage's matrix, down blocks 8j
                             mbar_arrive_expect_tx(bars.sc_full(qs), St::sc_bytes);
                             for (int w = 0; w < St::wins; ++w) {
-                                const int b0 = Down ? St::kb * ks : 2 * ks + 32 * w;
+                                const int b0 = Down ? St::kb * ks : St::bpc * ks + 32 * w;
                                 tma_load_3d(smem + St::sc_off + qs * St::sc_bytes + w * kRowsM * 16, &p.maps.scales[mat],
                                             b0 & ~7, cs_.slab * kRowsM, cs_.e, bars.sc_full(qs));
                             }
@@ -780,7 +794,7 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = rows_idesc(kRowsM, St::brows);
-            const uint32_t idesc_mg = magic_idesc(kRowsM, St::reg_cols);
+            const uint32_t idesc_mg = magic_idesc(kRowsM, kRowsM);   // the offset MMA: 128 columns at a time
             const uint64_t amg = smem_desc(smem_u32(smem + St::magic_off), 128, 256);
             const uint64_t bmg = smem_desc(smem_u32(smem + St::magic_off + kRowsM * 32), 128, 256);
             int g = 0;
@@ -806,9 +820,11 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                         ++kseq;
                         tc_fence_after();
                         // every column of the region = 1.5 * 2^23 (f32), then the integer dots added onto it:
-                        // stage slot kb (gate/up blocks 2k, 2k+1, 2k+32, 2k+33; down 4k..4k+3) into columns
+                        // stage slot kb (gate/up blocks 4k..4k+3, 4k+32..4k+35; down 8k..8k+7) into columns
                         // [brows kb, brows (kb + 1))
-                        mma_bf16(tmem + r * St::reg_cols, amg, bmg, idesc_mg);
+                        static_assert(St::reg_cols % kRowsM == 0, "whole offset MMAs per region");
+#pragma unroll
+                        for (int c = 0; c < St::reg_cols; c += kRowsM) mma_bf16(tmem + r * St::reg_cols + c, amg, bmg, idesc_mg);
 #pragma unroll
                         for (int kb = 0; kb < St::kb; ++kb) {
                             const uint64_t ad = smem_desc(a_st + kb * kRowsM * 32, 128, 256);
