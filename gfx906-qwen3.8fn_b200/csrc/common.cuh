@@ -101,6 +101,18 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// Both elements rounded to half (RNE) and back to fp32.
+__device__ __forceinline__ uint64_t round_half2(uint64_t v) {
+    float a, b;
+    upk2(v, a, b);
+    const float2 f = __half22float2(__floats2half2_rn(a, b));
+    return pkf2(f.x, f.y);
+}
 // block_term for two weight rows against the same activation block, as
 // packed f32x2 operations with the scalar form's per-element rounding (the
 // results are bit-identical to two block_term calls).

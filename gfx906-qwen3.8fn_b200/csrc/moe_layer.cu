@@ -262,14 +262,15 @@ EncodeTiledFn encode_tiled() {
 // tensor-core kernels: per matrix the code bytes as {16 bytes, row, block,
 // expert} (box 16 x 128 rows x 4 blocks: a copy lands block-major, each
 // block's 128 rows contiguous) -- or, where the driver refuses that stride
-// order, as {row bytes, row, expert} (box 64 bytes x 128 rows) -- and the half scales as {block, row, expert} (box 8 blocks x
-// 128 rows).  Weights of other shapes (the gate/up stage order is that of 64
-// blocks, H = 2048; I a multiple of 256) or with Q4_1 down matrices run every
-// group on the streaming kernels instead.
+// order, as {row bytes, row, expert} (box 64 bytes x 128 rows) -- and the
+// half scales (and the minima of Q4_1 down matrices) as {block, row, expert}
+// (box 8 blocks x 128 rows).  Weights of other shapes (the gate/up stage order
+// is that of 64 blocks, H = 2048; I a multiple of 256) run every group on the
+// streaming kernels instead.
 int build_maps(moe_weights_s *w) {
     const ExpertLayout &L = w->layout;
     w->tc_ok = false;
-    if (L.down_type != kDownQ4_0 || L.hidden != kRowsHidden || L.inter % (2 * kRowsM)) return MOE_OK;
+    if (L.hidden != kRowsHidden || L.inter % (2 * kRowsM)) return MOE_OK;
     const EncodeTiledFn enc = encode_tiled();
     if (!enc) return fail(MOE_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
     const size_t code_off[3] = {L.gate_codes, L.up_codes, L.down_codes};
@@ -311,6 +312,15 @@ int build_maps(moe_weights_s *w) {
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return fail(MOE_CUDA_ERROR, "cuTensorMapEncodeTiled refused the weight scale maps");
+    }
+    if (L.down_type == kDownQ4_1) {
+        const cuuint64_t dims[3] = {nbm[2], rows[2], E};
+        const cuuint64_t strides[2] = {nbm[2] * 2, EB};
+        const cuuint32_t box[3] = {8, kRowsM, 1};
+        if (enc(&w->maps.down_mins, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, w->base + L.down_mins, dims, strides, box, one,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return fail(MOE_CUDA_ERROR, "cuTensorMapEncodeTiled refused the down minima map");
     }
     w->raw_rowmajor = rowmajor;
     w->tc_ok = true;
@@ -361,7 +371,10 @@ int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, 
     const int grid = std::max(1, std::min(items, h->sms));
     const TcrParams prm = tcr_params(h, w, out, down, tap);
     cudaError_t e;
-    if (down)
+    if (down && L.down_type == kDownQ4_1)
+        e = launch_overlapped(tap ? tc_rows_kernel<true, true, true> : tc_rows_kernel<true, false, true>, grid,
+                              RowsStage<true>::threads, RowsStage<true>::smem, s, prm);
+    else if (down)
         e = launch_overlapped(tap ? tc_rows_kernel<true, true> : tc_rows_kernel<true, false>, grid, RowsStage<true>::threads,
                               RowsStage<true>::smem, s, prm);
     else
@@ -371,8 +384,8 @@ int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, 
 }
 
 // gate/up + down over the tile lists already in the workspace: the streaming
-// dp4a kernels for the small tiles (`stream_groups`: decode sizes, Q4_1 down
-// matrices, trace mode) and the tensor-core kernels for `tc_tiles` (an upper
+// dp4a kernels for the small tiles (`stream_groups`: decode sizes, trace
+// mode) and the tensor-core kernels for `tc_tiles` (an upper
 // bound on the device-written count).  `events` (optional, three entries) are
 // recorded before the gate/up kernels, between gate/up and down, and after
 // down.  `tap` records one expert's per-block dots (parity taps).
@@ -505,7 +518,6 @@ int launch_route(moe_layer_s *h, const moe_weights_s *w, const float *x, const f
     sp.max_tiles = h->tiles_max;
     sp.error = h->error;
     if (x && allow_tc && w && w->tc_ok) {   // forward above decode size: the groups go to the tensor-core kernels
-        // (Q4_1 down matrices run every group on the dp4a kernels)
         sp.tc_min = kRowsMinGroup;
         sp.tc_tile = kTcTile;
         sp.tc_max = h->tc.max_tiles;
@@ -1662,7 +1674,7 @@ int moe_ep_forward(moe_ep_t ep, moe_weights_t w, const float *x, const float *lo
         sp.shared_w = shared_w;
         sp.shared_token0 = ep->rank * ep->t_max;
         sp.shared_expert = ep->ecount;
-        if (ep->tc && w->tc_ok) {   // Q4_1 down: every group on the dp4a kernels
+        if (ep->tc && w->tc_ok) {   // above decode size: every group on the tensor-core kernels
             sp.tc_min = kRowsMinGroup;
             sp.tc_tile = kTcTile;
             sp.tc_max = r.tc.max_tiles;

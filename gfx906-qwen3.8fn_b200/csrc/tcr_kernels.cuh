@@ -33,8 +33,9 @@
 // the reference's butterfly order) and writes the down pass's operand.
 //
 // Down (its output is never requantised) uses whole-block dots and
-// acc += d4 * (dot * d8 - 8 * s8) per block in fp32, then a router-weighted
-// red.add into the residual (lane = output row: coalesced).
+// acc += d4 * (dot * d8 - 8 * s8) per block in fp32 -- for Q4_1 down matrices
+// the reference's block term acc + fma(dot, half(d4 d8), half(m4 s8)) -- then
+// a router-weighted red.add into the residual (lane = output row: coalesced).
 //
 // Warp roles (gate/up 20 warps, down 12):
 //   warp 0      TMEM allocation; lane 0 issues the TMA copies: raw weight
@@ -73,6 +74,7 @@ __host__ __device__ constexpr int tc_gu_brow(int p, int f) { return (p >> 2) * 8
 struct alignas(64) TcrMaps {
     CUtensorMap codes[3];    // gate, up, down code bytes
     CUtensorMap scales[3];   // gate, up, down half scales
+    CUtensorMap down_mins;   // Q4_1 down matrices: half minima (layout of the down scales)
 };
 
 struct TcrParams {
@@ -102,7 +104,7 @@ constexpr int kRowsBarSlots = 16;   // entries per barrier array
 //          per-pair constants (read by the epilogue) of one stage;
 //   scale  the weight rows' half scales of a stage group (gate/up: blocks
 //          8j..8j+7 and 32+8j..32+8j+7 of one matrix = 2 stages; down: blocks
-//          8j..8j+7 = 1 stage), read by the epilogue;
+//          8j..8j+7 = 1 stage, and their minima for Q4_1), read by the epilogue;
 //   A      the unpacked A operand of one stage (u8, K-major core matrices).
 template <bool Down>
 struct RowsStage {
@@ -114,7 +116,7 @@ struct RowsStage {
     static constexpr int cw = kTcTile * 4 / epi_warps;
     static constexpr int threads = 32 * (2 + kRowsUnpackWarps + epi_warps);
     static constexpr int kb = kRowsKB;                                        // quantisation blocks per stage
-    static constexpr int wins = Down ? 1 : 2;                                 // 8-block scale windows per group
+    static constexpr int wins = 2;   // 8-block windows per group (gate/up: blocks 8j.., 32+8j..; down: scales, Q4_1 minima)
     static constexpr int spw = Down ? 1 : 2;                                  // stages per scale group
     static constexpr int brows = Down ? kTcTile : 2 * kTcTile;                // B rows per block
     static constexpr int bpc = kRowsBlocksPerCopy;                            // blocks per code copy
@@ -123,7 +125,8 @@ struct RowsStage {
     static constexpr uint32_t b = 0;                                          // side: [kb][brows][32]
     static constexpr uint32_t bsc = b + kb * brows * 32;                      // side: [kb][cwords][kTcTile] fp32
     static constexpr uint32_t side_bytes = bsc + kb * cwords * kTcTile * 4;
-    static constexpr uint32_t sc_bytes = wins * kRowsM * 16;                  // [wins][128][8] half
+    static constexpr uint32_t sc_win = kRowsM * 16;                           // [128][8] half
+    static constexpr uint32_t sc_bytes = wins * sc_win;
     static constexpr uint32_t a_bytes = kb * kRowsM * 32;                     // unpacked A tiles
     static constexpr int code_stages = 4;                // powers of two: cheap slot and phase arithmetic
     static constexpr int side_stages = Down ? 8 : 4;
@@ -526,7 +529,8 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
 }
 
 // ---- down epilogue of one item ---------------------------------------------
-template <bool Tap>
+// Q41: Q4_1 down matrices (minima in the stage group's second window).
+template <bool Tap, bool Q41>
 __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *smem, const RowsBars &bars,
                                                  uint32_t tq, RowsSeq &sq, int item, int4 td,
                                                  int lane, int quarter, int chunk) {
@@ -555,6 +559,9 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
         // d4 of the stage's blocks 8ks..8ks+7: the whole 8-block window of this row
         static_assert(St::kb == 8 && St::spw == 1, "one scale window per stage");
         const uint4 d4q = *reinterpret_cast<const uint4 *>(smem + St::sc_off + qs * St::sc_bytes + lrow * 16);
+        uint4 m4q = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (Q41)
+            m4q = *reinterpret_cast<const uint4 *>(smem + St::sc_off + qs * St::sc_bytes + St::sc_win + lrow * 16);
         const int r = static_cast<int>(sq.k % R);
         ++sq.k;
         if (!mbar_wait(bars.tm_full(r), ((sq.k - 1) / R) & 1, p.error)) return false;
@@ -578,10 +585,24 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
             const uint4 m8h = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + NP + pc0 + 4);
             const uint64_t d8p[4] = {pk2(d8.x, d8.y), pk2(d8.z, d8.w), pk2(d8h.x, d8h.y), pk2(d8h.z, d8h.w)};
             const uint64_t m8p[4] = {pk2(m8.x, m8.y), pk2(m8.z, m8.w), pk2(m8h.x, m8h.y), pk2(m8h.z, m8h.w)};
+            uint64_t m4p = 0ull;
+            if constexpr (Q41) {
+                const uint32_t mw = kb < 2 ? m4q.x : kb < 4 ? m4q.y : kb < 6 ? m4q.z : m4q.w;
+                const float m4 = (kb & 1) ? hi_half(mw) : lo_half(mw);
+                m4p = pkf2(m4, m4);
+            }
 #pragma unroll
             for (int u = 0; u < CW / 2; ++u) {
                 const uint64_t t = from_magic2(v[kb][2 * u], v[kb][2 * u + 1]);   // exact dots
-                acc[u] = fma2(d4p, fma2(t, d8p[u], m8p[u]), acc[u]);
+                if constexpr (Q41) {
+                    // s8 = -m8 / 8 exactly; half(d4 d8) and half(m4 s8) of exact fp32 products
+                    const uint64_t s8 = mul2(m8p[u], pkf2(-0.125f, -0.125f));
+                    const uint64_t dd = round_half2(mul2(d4p, d8p[u]));
+                    const uint64_t ms = round_half2(mul2(m4p, s8));
+                    acc[u] = add2(acc[u], fma2(t, dd, ms));
+                } else {
+                    acc[u] = fma2(d4p, fma2(t, d8p[u], m8p[u]), acc[u]);
+                }
                 if constexpr (Tap) {
                     float t0, t1;
                     upk2(t, t0, t1);
@@ -629,7 +650,7 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
 }
 
 // ---- the kernel ------------------------------------------------------------
-template <bool Down, bool Tap>
+template <bool Down, bool Tap, bool Q41 = false>
 __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(const __grid_constant__ TcrParams p) {
     using St = RowsStage<Down>;
     constexpr int CS = St::code_stages, SS = St::side_stages, QS = St::sc_stages, AS = St::a_stages;
@@ -699,6 +720,7 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
             for (int m = 0; m < St::M; ++m) {
                 tma_prefetch_map(&p.maps.codes[Down ? 2 : m]);
                 tma_prefetch_map(&p.maps.scales[Down ? 2 : m]);
+                if (Down && Q41) tma_prefetch_map(&p.maps.down_mins);
             }
             constexpr uint32_t bbytes = St::kb * St::brows * 32, sbytes = St::kb * St::cwords * kTcTile * 4;
             const size_t bslot = Down ? tc_dn_slot(K) : tc_gu_slot(K);
@@ -758,12 +780,16 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
                                      static_cast<size_t>(ks) * St::kb * St::cwords * kTcTile,
                                  sbytes, bars.side_full(sd));
                         if (group) {
-                            // gate/up blocks 8j and 32 + 8j of the stage's matrix, down blocks 8j
-                            mbar_arrive_expect_tx(bars.sc_full(qs), St::sc_bytes);
-                            for (int w = 0; w < St::wins; ++w) {
+                            // gate/up blocks 8j and 32 + 8j of the stage's matrix; down blocks 8j (and
+                            // their minima for Q4_1)
+                            constexpr int wins = Down && !Q41 ? 1 : St::wins;
+                            mbar_arrive_expect_tx(bars.sc_full(qs), wins * St::sc_win);
+#pragma unroll
+                            for (int w = 0; w < wins; ++w) {
                                 const int b0 = Down ? St::kb * ks : St::bpc * ks + 32 * w;
-                                tma_load_3d(smem + St::sc_off + qs * St::sc_bytes + w * kRowsM * 16, &p.maps.scales[mat],
-                                            b0 & ~7, cs_.slab * kRowsM, cs_.e, bars.sc_full(qs));
+                                const CUtensorMap *map = Down && w == 1 ? &p.maps.down_mins : &p.maps.scales[mat];
+                                tma_load_3d(smem + St::sc_off + qs * St::sc_bytes + w * St::sc_win, map, b0 & ~7,
+                                            cs_.slab * kRowsM, cs_.e, bars.sc_full(qs));
                             }
                         }
                         ++gs;
@@ -860,7 +886,7 @@ __global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(co
         bool ok = true;
         for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
             const int4 td = p.tiles[item / slabs];
-            ok = Down ? dn_epilogue_item<Tap>(p, smem, bars, tq, sq, item, td, lane, quarter, chunk)
+            ok = Down ? dn_epilogue_item<Tap, Q41>(p, smem, bars, tq, sq, item, td, lane, quarter, chunk)
                       : gu_epilogue_item<Tap>(p, smem, bars, tq, sq, item, td, lane, quarter, chunk);
         }
     }
@@ -923,14 +949,13 @@ __global__ void __launch_bounds__(2 * kTcTile) tc_rows_gather_kernel(const int4 
 
 inline int tc_rows_configure() {
     const int gu = static_cast<int>(RowsStage<false>::smem), dn = static_cast<int>(RowsStage<true>::smem);
-    if (cudaFuncSetAttribute(tc_rows_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(tc_rows_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gu) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(tc_rows_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(tc_rows_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dn) !=
-            cudaSuccess)
+    const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    if (cudaFuncSetAttribute(tc_rows_kernel<false, false>, a, gu) != cudaSuccess ||
+        cudaFuncSetAttribute(tc_rows_kernel<false, true>, a, gu) != cudaSuccess ||
+        cudaFuncSetAttribute(tc_rows_kernel<true, false>, a, dn) != cudaSuccess ||
+        cudaFuncSetAttribute(tc_rows_kernel<true, true>, a, dn) != cudaSuccess ||
+        cudaFuncSetAttribute(tc_rows_kernel<true, false, true>, a, dn) != cudaSuccess ||
+        cudaFuncSetAttribute(tc_rows_kernel<true, true, true>, a, dn) != cudaSuccess)
         return MOE_CUDA_ERROR;
     return MOE_OK;
 }

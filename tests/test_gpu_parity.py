@@ -224,10 +224,10 @@ def test_q4_1_weights_generator_and_roundtrip(pkg, O, torch):
         assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("T,kind", [(1, "normal"), (8, "normal"), (33, "normal"), (300, "zipf")])
+@pytest.mark.parametrize("T,kind", [(1, "normal"), (8, "normal"), (33, "normal"), (300, "zipf"), (1024, "normal")])
 def test_q4_1_forward_matches_oracle(pkg, O, torch, T, kind):
-    """Decode sizes on the streaming kernels and prefill sizes (all groups on
-    the dp4a kernels: no tensor-core path for Q4_1 down)."""
+    """Decode sizes on the streaming kernels, prefill sizes on the tensor-core
+    kernels (the down kernel with the Q4_1 block term)."""
     c = LayerCase(pkg, O, torch, T, seed=500 + T, logits_kind=kind, down_type=pkg.MOE_Q4_1)
     out = torch.zeros(T, H, device="cuda")
     c.layer.forward(c.weights, c.xd, c.ld, out, accumulate=False)

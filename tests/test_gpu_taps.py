@@ -11,8 +11,9 @@ comparison against its CPU expert (src/cpu_expert_shadow.hip:333-341) and its
 
 * gate and up dots == the oracle's uncentred block dots of that expert's
   weights against the quantised x rows of its pairs (bit-exact);
-* down dots == the oracle's block dots of the down matrix against the
-  middle Q8_1 the GPU itself produced (bit-exact);
+* down dots == the oracle's block dots of the down matrix (Q4_0, or Q4_1 as
+  in the reference's layers 0-5) against the middle Q8_1 the GPU itself
+  produced (bit-exact);
 * that middle Q8_1 is byte-identical to the oracle's CPU-expert middle: the
   gate/up kernels sum in the reference's MMVQ order and the SiLU's exp is
   correctly rounded, so the fp32 gate and up values are the reference's.
@@ -56,12 +57,14 @@ def tap_and_check(O, torch, c, expert, max_pairs=None):
     mid["d"] = ds & 0xffff
     mid["s"] = ds >> 16
     mid["qs"] = r["mid_codes"].cpu().numpy().reshape(n, I // 32, 32)
-    assert np.array_equal(r["down"].cpu().numpy(), O.block_dots(d, mid, H, I // 32)), "down dots on the GPU's middle"
+    down_dots = O.block_dots_q4_1 if c.down_type == O.Q4_1 else O.block_dots
+    assert np.array_equal(r["down"].cpu().numpy(), down_dots(d, mid, H, I // 32)), "down dots on the GPU's middle"
     # the GPU's middle against the CPU expert's own middle Q8_1
     mq = np.zeros(n * I // 32, O.Q8_DTYPE)
     scratch = np.empty(n * I * 3, np.float32)
     out = np.empty(n * H, np.float32)
-    O.lib().o_expert_whole(O.ptr(g), O.ptr(u), O.ptr(d), H, I, O.ptr(xs), n, O.ptr(out), O.ptr(scratch), O.ptr(mq))
+    O.lib().o_expert_whole_typed(O.ptr(g), O.ptr(u), O.ptr(d), c.down_type, H, I, O.ptr(xs), n, O.ptr(out),
+                                 O.ptr(scratch), O.ptr(mq))
     mq = mq.reshape(n, I // 32)
     flips = int(np.sum(mid["qs"] != mq["qs"]))
     assert flips == 0, f"{flips} middle codes differ from the CPU expert's"
@@ -91,4 +94,16 @@ def test_block_dots_of_forward_kernels(pkg, O, torch, T, kind, pick):
         live = np.nonzero(counts)[0]
         expert = int(live[np.argsort(counts[live])[len(live) // 2]])
     # the shared expert of a large batch: its first 160 pairs (three tiles)
+    assert tap_and_check(O, torch, c, expert, max_pairs=160 if expert == 512 else None) >= 1
+
+
+@pytest.mark.parametrize("T,kind,pick", [(300, "zipf", "largest"), (1024, "normal", "largest"),
+                                         (1024, "normal", "shared")])
+def test_block_dots_q4_1_down(pkg, O, torch, T, kind, pick):
+    """Q4_1 down matrices on the tensor-core down kernel: its dots on the
+    GPU's own middle, bit-exact."""
+    c = LayerCase(pkg, O, torch, T, seed=650 + T, logits_kind=kind, down_type=pkg.MOE_Q4_1)
+    probs, _ = O.router_softmax(c.logits)
+    ids, _ = O.select_routes(probs)
+    expert = 512 if pick == "shared" else int(np.argmax(np.bincount(ids.ravel(), minlength=512)))
     assert tap_and_check(O, torch, c, expert, max_pairs=160 if expert == 512 else None) >= 1
