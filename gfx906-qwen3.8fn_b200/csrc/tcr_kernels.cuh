@@ -325,7 +325,9 @@ struct MidQ {
 
 // ---- gate/up epilogue of one item (exact MMVQ order) -----------------------
 // Pairs are handled two at a time (unit u = pairs pc0 + 2u, pc0 + 2u + 1) as
-// packed f32x2 values; units without a real pair are skipped.
+// packed f32x2 values.  Units without a real pair run the same arithmetic on
+// the tile's zero padding (zero B rows and constants: every term is 0), which
+// costs less than a branch per unit and leaf.
 template <bool Tap>
 __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *smem, const RowsBars &bars,
                                                  uint32_t tq, RowsSeq &sq, int item, int4 td,
@@ -341,7 +343,6 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
     const int slab = item % slabs, tile = item / slabs;
     const int e = td.x, p0 = td.y, n = td.z;
     const int pc0 = chunk * CW;                               // this warp's first pair
-    const int units = min(U, max(0, (n - pc0 + 1) / 2));      // units holding a real pair
     const int lrow = quarter * 32 + lane;                     // row within the slab
     const int row = slab * kRowsM + lrow;                     // middle row of this lane
     const uint64_t zero2 = 0ull;
@@ -349,7 +350,7 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
     // total); the gate totals wait in gt while the up pass runs
     uint64_t s0[U], s1[U], s2[U], s3[U], gt[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) s3[u] = gt[u] = 0ull;   // units without a real pair stay 0
+    for (int u = 0; u < U; ++u) s3[u] = gt[u] = 0ull;
     int tap_base = 0;
     if constexpr (Tap) tap_base = (e == p.tap.expert) ? *p.tap.pair0 : 0;
 
@@ -407,7 +408,6 @@ __device__ __forceinline__ bool gu_epilogue_item(const TcrParams &p, uint8_t *sm
             const uint64_t d4ap = pkf2(d4a, d4a), d4bp = pkf2(d4b, d4b);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                if (u >= units) break;
                 // exact fragment dots of the unit's two pairs: block a (4kk+h) and b (4kk+32+h)
                 const int c0 = (u >> 1) * 8 + (u & 1) * 2;   // fragment 0 of the unit's pairs; fragment 1 at +4
                 const uint64_t ta0 = from_magic2(va[c0], va[c0 + 1]);
