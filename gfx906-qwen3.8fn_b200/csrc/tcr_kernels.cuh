@@ -566,16 +566,25 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
         ++sq.k;
         if (!mbar_wait(bars.tm_full(r), ((sq.k - 1) / R) & 1, p.error)) return false;
         tc_fence_after();
+        // the first half's loads, then the second half's in flight while the first half computes
         uint32_t v[St::kb][CW];
+        constexpr int KH = St::kb / 2;
 #pragma unroll
-        for (int kb = 0; kb < St::kb; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
+        for (int kb = 0; kb < KH; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
         tmem_wait_ld();
 #pragma unroll
-        for (int kb = 0; kb < St::kb; ++kb) tie8(v[kb]);
-        region_release(bars.tm_empty(r), lane);
+        for (int kb = 0; kb < KH; ++kb) tie8(v[kb]);
+#pragma unroll
+        for (int kb = KH; kb < St::kb; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
         const float *cb = reinterpret_cast<const float *>(st + St::bsc);
 #pragma unroll
         for (int kb = 0; kb < St::kb; ++kb) {
+            if (kb == KH) {
+                tmem_wait_ld();
+#pragma unroll
+                for (int k2 = KH; k2 < St::kb; ++k2) tie8(v[k2]);
+                region_release(bars.tm_empty(r), lane);
+            }
             const uint32_t hw = kb < 2 ? d4q.x : kb < 4 ? d4q.y : kb < 6 ? d4q.z : d4q.w;
             const float d4 = (kb & 1) ? hi_half(hw) : lo_half(hw);
             const uint64_t d4p = pkf2(d4, d4);
