@@ -373,7 +373,7 @@ int launch_tc(moe_layer_s *h, const moe_weights_s *w, float *out, int tc_tiles, 
     cudaError_t e;
     if (down && L.down_type == kDownQ4_1)
         e = launch_overlapped(tap ? tc_rows_kernel<true, true, true> : tc_rows_kernel<true, false, true>, grid,
-                              RowsStage<true>::threads, RowsStage<true>::smem, s, prm);
+                              RowsStage<true, true>::threads, RowsStage<true, true>::smem, s, prm);
     else if (down)
         e = launch_overlapped(tap ? tc_rows_kernel<true, true> : tc_rows_kernel<true, false>, grid, RowsStage<true>::threads,
                               RowsStage<true>::smem, s, prm);

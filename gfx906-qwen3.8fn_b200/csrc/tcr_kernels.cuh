@@ -106,13 +106,14 @@ constexpr int kRowsBarSlots = 16;   // entries per barrier array
 //          8j..8j+7 and 32+8j..32+8j+7 of one matrix = 2 stages; down: blocks
 //          8j..8j+7 = 1 stage, and their minima for Q4_1), read by the epilogue;
 //   A      the unpacked A operand of one stage (u8, K-major core matrices).
-template <bool Down>
+// Q41: the down kernel of Q4_1 matrices (same layout, more epilogue warps).
+template <bool Down, bool Q41 = false>
 struct RowsStage {
     static constexpr int M = Down ? 1 : 2;                                    // matrices per item (one per stage)
-    // epilogue warps (per TMEM lane quarter: epi_warps / 4) and pairs per warp: gate/up runs
-    // dependent fp32 chains per pair and needs the warps to hide their latency, down the fewer
-    // per-warp fixed costs of wider warps
-    static constexpr int epi_warps = Down ? 8 : 16;
+    // epilogue warps (per TMEM lane quarter: epi_warps / 4) and pairs per warp: gate/up and the
+    // Q4_1 down term run longer dependent fp32 chains per pair and need the warps to hide their
+    // latency, the Q4_0 down term the fewer per-warp fixed costs of wider warps
+    static constexpr int epi_warps = Down && !Q41 ? 8 : 16;
     static constexpr int cw = kTcTile * 4 / epi_warps;
     static constexpr int threads = 32 * (2 + kRowsUnpackWarps + epi_warps);
     static constexpr int kb = kRowsKB;                                        // quantisation blocks per stage
@@ -224,6 +225,18 @@ __device__ __forceinline__ void tie8(uint32_t *r) {
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
                  :
                  : "memory");
+}
+
+// CW consecutive TMEM columns of this warp's lane quarter (CW = 4 or 8), and their tie.
+template <int CW>
+__device__ __forceinline__ void tmem_ld_cw(uint32_t taddr, uint32_t *r) {
+    if constexpr (CW == 8) tmem_ld8(taddr, r);
+    else tmem_ld4(taddr, r);
+}
+template <int CW>
+__device__ __forceinline__ void tie_cw(uint32_t *r) {
+    if constexpr (CW == 8) tie8(r);
+    else tie4(r);
 }
 
 // Instruction descriptor: kind::i8, A unsigned 8-bit (weight codes), B signed
@@ -534,9 +547,9 @@ template <bool Tap, bool Q41>
 __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *smem, const RowsBars &bars,
                                                  uint32_t tq, RowsSeq &sq, int item, int4 td,
                                                  int lane, int quarter, int chunk) {
-    using St = RowsStage<true>;
+    using St = RowsStage<true, Q41>;
     constexpr int R = St::regions, CW = St::cw, NP = kTcTile;
-    static_assert(CW == 8, "one x8 load per block");
+    static_assert(CW == 4 || CW == 8, "one x4 / x8 load per block");
     const int H = p.hidden, I = p.inter;
     const int nb = I / 32, slabs = H / kRowsM;
     const int slab = item % slabs;
@@ -570,30 +583,34 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
         uint32_t v[St::kb][CW];
         constexpr int KH = St::kb / 2;
 #pragma unroll
-        for (int kb = 0; kb < KH; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
+        for (int kb = 0; kb < KH; ++kb) tmem_ld_cw<CW>(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
         tmem_wait_ld();
 #pragma unroll
-        for (int kb = 0; kb < KH; ++kb) tie8(v[kb]);
+        for (int kb = 0; kb < KH; ++kb) tie_cw<CW>(v[kb]);
 #pragma unroll
-        for (int kb = KH; kb < St::kb; ++kb) tmem_ld8(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
+        for (int kb = KH; kb < St::kb; ++kb) tmem_ld_cw<CW>(tq + r * St::reg_cols + kb * NP + pc0, v[kb]);
         const float *cb = reinterpret_cast<const float *>(st + St::bsc);
 #pragma unroll
         for (int kb = 0; kb < St::kb; ++kb) {
             if (kb == KH) {
                 tmem_wait_ld();
 #pragma unroll
-                for (int k2 = KH; k2 < St::kb; ++k2) tie8(v[k2]);
+                for (int k2 = KH; k2 < St::kb; ++k2) tie_cw<CW>(v[k2]);
                 region_release(bars.tm_empty(r), lane);
             }
             const uint32_t hw = kb < 2 ? d4q.x : kb < 4 ? d4q.y : kb < 6 ? d4q.z : d4q.w;
             const float d4 = (kb & 1) ? hi_half(hw) : lo_half(hw);
             const uint64_t d4p = pkf2(d4, d4);
-            const uint4 d8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + pc0);
-            const uint4 d8h = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + pc0 + 4);
-            const uint4 m8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + NP + pc0);
-            const uint4 m8h = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + NP + pc0 + 4);
-            const uint64_t d8p[4] = {pk2(d8.x, d8.y), pk2(d8.z, d8.w), pk2(d8h.x, d8h.y), pk2(d8h.z, d8h.w)};
-            const uint64_t m8p[4] = {pk2(m8.x, m8.y), pk2(m8.z, m8.w), pk2(m8h.x, m8h.y), pk2(m8h.z, m8h.w)};
+            uint64_t d8p[CW / 2], m8p[CW / 2];
+#pragma unroll
+            for (int c = 0; c < CW / 4; ++c) {
+                const uint4 d8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + pc0 + 4 * c);
+                const uint4 m8 = *reinterpret_cast<const uint4 *>(cb + kb * 2 * NP + NP + pc0 + 4 * c);
+                d8p[2 * c] = pk2(d8.x, d8.y);
+                d8p[2 * c + 1] = pk2(d8.z, d8.w);
+                m8p[2 * c] = pk2(m8.x, m8.y);
+                m8p[2 * c + 1] = pk2(m8.z, m8.w);
+            }
             uint64_t m4p = 0ull;
             if constexpr (Q41) {
                 const uint32_t mw = kb < 2 ? m4q.x : kb < 4 ? m4q.y : kb < 6 ? m4q.z : m4q.w;
@@ -660,8 +677,8 @@ __device__ __forceinline__ bool dn_epilogue_item(const TcrParams &p, uint8_t *sm
 
 // ---- the kernel ------------------------------------------------------------
 template <bool Down, bool Tap, bool Q41 = false>
-__global__ void __launch_bounds__(RowsStage<Down>::threads, 1) tc_rows_kernel(const __grid_constant__ TcrParams p) {
-    using St = RowsStage<Down>;
+__global__ void __launch_bounds__(RowsStage<Down, Q41>::threads, 1) tc_rows_kernel(const __grid_constant__ TcrParams p) {
+    using St = RowsStage<Down, Q41>;
     constexpr int CS = St::code_stages, SS = St::side_stages, QS = St::sc_stages, AS = St::a_stages;
     constexpr int R = St::regions;
     extern __shared__ __align__(128) uint8_t smem[];
