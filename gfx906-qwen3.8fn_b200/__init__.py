@@ -41,7 +41,7 @@ EXPORTED = [
     "moe_ep_open_peers", "moe_ep_forward", "moe_ep_read_flags",
     "moe_weights_create_typed", "moe_ep_weights_create_typed", "moe_q4_1_linear", "moe_expert_create_typed",
     "moe_forward_contributions", "moe_weights_upload_router", "moe_forward_hidden", "moe_router_logits",
-    "moe_ep_forward_hidden", "moe_debug_block_dots",
+    "moe_ep_forward_hidden", "moe_debug_block_dots", "moe_debug_expf",
 ]
 
 
@@ -122,6 +122,7 @@ def library(path=LIB_PATH):
         "moe_ep_forward": (I, [P, P, P, P, I, P, I, P]),
         "moe_ep_read_flags": (I, [P, ctypes.POINTER(I), I, P]),
         "moe_debug_block_dots": (I, [P, P, P, P, I, I, I, P, P, P, P, P, P, P]),
+        "moe_debug_expf": (I, [ctypes.c_uint32, ctypes.c_uint32, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -101,6 +101,12 @@ constexpr int kExpfDevices = 64;
 std::mutex g_expf_mutex;
 bool g_expf_loaded[kExpfDevices] = {};
 
+// out[i] = expf_ref of the float with bits first + i (the SiLU's exponential).
+__global__ void debug_expf_kernel(uint32_t first, uint32_t count, float *out) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x)
+        out[i] = expf_ref(__uint_as_float(first + i));
+}
+
 // Fill the current device's g_expf_fix hash table (once per device).
 int expf_table_upload() {
     int device = 0;
@@ -847,6 +853,18 @@ extern "C" {
 int moe_forward_profiled(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens,
                          float *out, int flags, void *stream, void *const *events) {
     return forward_impl(h, w, x, logits, tokens, out, flags, stream, events, nullptr);
+}
+
+int moe_debug_expf(uint32_t first_bits, uint32_t count, float *out, void *stream) {
+    if (!out) return fail(MOE_INVALID_ARGUMENT, "null output");
+    if (count == 0) return MOE_OK;
+    if (static_cast<uint64_t>(first_bits) + count - 1 > 0xffffffffull)
+        return fail(MOE_INVALID_ARGUMENT, "the input range passes 0xffffffff");
+    if (const int st = expf_table_upload()) return st;
+    int device = 0;
+    MOE_CUDA(cudaGetDevice(&device));
+    debug_expf_kernel<<<sm_count(device) * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(first_bits, count, out);
+    return cuda_status(cudaGetLastError(), "debug_expf_kernel");
 }
 
 int moe_debug_block_dots(moe_layer_t h, moe_weights_t w, const float *x, const float *logits, int tokens, int expert,

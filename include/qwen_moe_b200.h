@@ -282,6 +282,14 @@ int moe_quantize_q8_1(const float *x_dev, int width, int columns, void *q8_dev, 
 int moe_debug_block_dots(moe_layer_t h, moe_weights_t w, const float *x_dev, const float *logits_dev, int tokens,
                          int expert, int max_pairs, int32_t *gate_dots, int32_t *up_dots, int32_t *down_dots,
                          int8_t *mid_codes, uint32_t *mid_ds, float *out_dev, void *stream);
+/* The exponential of the gate/up kernels' SiLU over a range of inputs:
+ * out_dev[i] = exp of the float whose bit pattern is first_bits + i (i < count,
+ * no wrap past 0xffffffff), computed as the expert kernels compute it: exp in
+ * double precision rounded once to float, then the build's table of the C
+ * library's expf corrections.  The parity tap for the SiLU, whose reference is
+ * the C library's expf in the reference's CPU expert
+ * (src/cpu_expert.cpp:248-259). */
+int moe_debug_expf(uint32_t first_bits, uint32_t count, float *out_dev, void *stream);
 /* Q4_0 x Q8_1 linear: out[c][r] = sum_b d4*(dot*d8 - 8*s8) for canonical
  * Q4_0 weights [rows][K/32] and canonical Q8_1 input [columns][K/32].
  * Replaces launch_quantized_linear{,_short,_tiled} (src/hip/linear.hip:445-490).

@@ -72,6 +72,7 @@ def lib():
             "o_quantize_q8_1": (I, [P, SZ, P]),
             "o_block_dot": (I, [P, P]),
             "o_block_dots": (None, [P, P, I, I, I, P]),
+            "o_expf_mismatches": (ctypes.c_int64, [P, ctypes.c_uint32, ctypes.c_uint32, P]),
             "o_matrix_serial": (None, [P, P, I, I, I, P]),
             "o_matrix_mmvq": (None, [P, P, I, I, I, P]),
             "o_expert_whole": (I, [P, P, P, I, I, P, I, P, P, P]),

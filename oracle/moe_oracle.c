@@ -629,3 +629,26 @@ O_EXPORT void o_fixture_xorshift_q4_1(uint32_t seed, size_t nblocks, uint8_t *ou
         }
     }
 }
+
+/* Exhaustive check of an expf implementation against the C library's expf,
+ * the exponential of the reference CPU expert's SiLU (src/cpu_expert.cpp:248-259,
+ * the same call as o_expert_whole above): the number of i < count where y[i]
+ * differs in bits from expf of the float with bit pattern first + i (two NaNs
+ * compare equal); *first_bad receives the first such input's bits. */
+O_EXPORT int64_t o_expf_mismatches(const float *y, uint32_t first, uint32_t count, uint32_t *first_bad) {
+    int64_t bad = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint32_t xb = first + i;
+        float x, want;
+        memcpy(&x, &xb, 4);
+        want = expf(x);
+        uint32_t a, b;
+        memcpy(&a, &want, 4);
+        memcpy(&b, &y[i], 4);
+        if (a != b && !(want != want && y[i] != y[i])) {
+            if (bad == 0 && first_bad) *first_bad = xb;
+            ++bad;
+        }
+    }
+    return bad;
+}
