@@ -37,14 +37,14 @@
 // the reference's block term acc + fma(dot, half(d4 d8), half(m4 s8)) -- then
 // a router-weighted red.add into the residual (lane = output row: coalesced).
 //
-// Warp roles (gate/up 20 warps, down 12):
+// Warp roles (gate/up and Q4_1 down 20 warps, Q4_0 down 12):
 //   warp 0      TMEM allocation; lane 0 issues the TMA copies: raw weight
 //               codes and scales through tensor maps, the tile's pre-arranged
 //               activation operand as 1-D bulk copies;
 //   warp 1      lane 0 issues the MMAs;
-//   warps 2-3   unpack raw Q4_0 codes shared -> shared into the MMA layout;
-//   warps 4-    epilogue: gate/up four per TMEM lane quarter with 4 pairs
-//               each, down two per quarter with 8 pairs each.
+//   warps 2-3   unpack raw 4-bit codes shared -> shared into the MMA layout;
+//   warps 4-    epilogue: gate/up and Q4_1 down four per TMEM lane quarter
+//               with 4 pairs each, Q4_0 down two per quarter with 8 pairs each.
 // Every barrier wait is bounded (ptx.cuh); a wait that gives up sets the
 // timeout flag and the role leaves its loop.
 #pragma once
